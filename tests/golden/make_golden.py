@@ -1,0 +1,201 @@
+"""Generate golden vectors from the unmodified reference STEPQuant (torch CPU path).
+
+Run from the repository root in a container where the reference checkout is
+available (its path is given by ``--reference``; it defaults to the
+read-only mount used when these fixtures were produced):
+
+    python tests/golden/make_golden.py --reference <path to the STEPQuant checkout>
+
+The GPU box never runs this script; tests read the committed ``*.npz`` /
+``layouts.json`` files only.  Everything is seeded.  torch runs with one
+thread, although the reference's sums give identical bits with eight.
+
+Files written next to this script:
+* ``layouts.json``   -- ``stepquant.kernels.pool.packed_layout`` tables.
+* ``fit_<case>.npz`` -- ``stepquant.quantization.fit_state`` outputs and the
+                        ``StateCodec.encode`` byte streams for a seeded state.
+* ``pack.npz``       -- ``stepquant.packing.pack`` outputs.
+* ``delta.npz``      -- ``stepquant.core.delta_step`` outputs.
+* ``config0.npz``    -- the CPU reference plumbing case (GDN, B=4, H=HK=4,
+                        K=V=128, seed 0): warm-up state, calibrated plan,
+                        decode inputs, the updated state and its fitted codes.
+"""
+import argparse
+import json
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _bits_mixed(arch, heads_bits, keys):
+    bits = torch.tensor(heads_bits)[:, None].expand(len(heads_bits), keys).clone()
+    return bits
+
+
+def fit_cases():
+    """(name, arch, bits[H,K], group, batch, values, scale, seed)."""
+    cases = []
+    g5 = [2, 4, 6, 8, 16]
+    cases.append(("gdn_mixed_k32", "gdn", _bits_mixed("gdn", g5, 32), 32, 2, 32, 1.0, 31))
+    cases.append(("gdn_mixed_k32_g8", "gdn", _bits_mixed("gdn", g5, 32), 8, 2, 32, 1.0, 32))
+    kb = _bits_mixed("kda", g5, 32).roll(1, 0)
+    kb[:, ::3] = 16
+    kb[:, 1::4] = 2
+    cases.append(("kda_mixed_k32", "kda", kb, 32, 2, 32, 1.0, 33))
+    cases.append(("gdn_k128", "gdn", _bits_mixed("gdn", [4, 6, 8, 16, 2], 128), 32, 2, 128, 0.1, 34))
+    gen = torch.Generator().manual_seed(35)
+    kb = torch.tensor([2, 4, 6, 8])[torch.randint(0, 4, (3, 128), generator=gen)]
+    kb[torch.rand(3, 128, generator=gen) < 0.05] = 16
+    cases.append(("kda_k128", "kda", kb, 32, 2, 128, 0.1, 36))
+    cases.append(("gdn_k128_v64", "gdn", _bits_mixed("gdn", [4, 6, 8, 2], 128), 32, 2, 64, 0.1, 37))
+    cases.append(("gdn_k128_v16", "gdn", _bits_mixed("gdn", [4, 6, 8, 2], 128), 16, 2, 16, 0.1, 38))
+    cases.append(("kda_k64_v8", "kda", torch.tensor([4, 6, 8, 16, 2])[torch.randint(0, 5, (2, 64), generator=gen)], 32, 3, 8, 1.0, 39))
+    cases.append(("gdn_k4_v8", "gdn", _bits_mixed("gdn", g5, 4), 8, 2, 8, 1.0, 40))
+    cases.append(("kda_k4_v4_half", "kda", torch.tensor([[2, 4, 8, 16]]), 32, 3, 4, 1.0, 41))
+    cases.append(("kda_k16_v32", "kda", torch.tensor([[4, 6, 8] * 5 + [16]] * 2), 32, 2, 32, 1.0, 42))
+    return cases
+
+
+def layout_cases():
+    cases = []
+    cases.append(("kda", [[2, 4, 6, 16], [16, 16, 16, 16]], 32, 32))
+    cases.append(("kda", [[2, 4, 8, 16]], 4, 32))
+    cases.append(("kda", [[2, 4, 8, 16]], 32, 32))
+    cases.append(("gdn", [[b] * 4 for b in (2, 4, 6, 8, 16)], 8, 8))
+    cases.append(("gdn", [[6] * 128] * 2, 128, 32))
+    cases.append(("kda", [[6] * 128] * 2, 128, 32))
+    gen = torch.Generator().manual_seed(11)
+    widths = [4] * 8 + [6] * 16 + [8] * 8
+    perm = torch.randperm(32, generator=gen).tolist()
+    cases.append(("gdn", [[widths[i]] * 128 for i in perm], 128, 32))
+    cases.append(("gdn", [[widths[i] if n else 16] * 128 for n, i in enumerate(perm)], 128, 32))
+    kb = torch.tensor([2, 4, 6])[torch.multinomial(torch.tensor([.3, .5, .2]), 32 * 128, True, generator=gen)].reshape(32, 128)
+    kb[torch.rand(32, 128, generator=gen) < 0.02] = 16
+    cases.append(("kda", kb.tolist(), 128, 32))
+    return cases
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", default="/root/reference")
+    args = parser.parse_args()
+    sys.path.insert(0, args.reference)
+    torch.set_num_threads(1)
+    from stepquant.quantization import QuantizationPlan, StateCodec, fit_state
+    from stepquant.packing import pack
+    from stepquant.core import delta_step, impact_factors
+    from stepquant.calibration import LayerStatistics
+    from stepquant.kernels.pool import packed_layout
+
+    layouts = []
+    for arch, bits, values, group in layout_cases():
+        b = torch.tensor(bits)
+        plan = QuantizationPlan(arch, b, torch.ones_like(b).float(), group)
+        for storage in ("packed", "byte"):
+            offsets, rows, columns, total = packed_layout(plan, values, storage)
+            layouts.append(dict(architecture=arch, bits=bits, values=values, value_group_size=group,
+                                storage=storage, offsets=offsets, rows=rows, columns=columns,
+                                page_bytes=total))
+    with open(os.path.join(HERE, "layouts.json"), "w") as fh:
+        json.dump(layouts, fh, separators=(",", ":"))
+
+    for name, arch, bits, group, batch, values, scale, seed in fit_cases():
+        torch.manual_seed(seed)
+        heads, keys = bits.shape
+        impact = torch.rand(heads, keys) + 0.25
+        plan = QuantizationPlan(arch, bits, impact, group)
+        x = torch.randn(batch, heads, keys, values) * scale
+        if name == "gdn_k4_v8":
+            x[1] = 0  # an all-zero request
+        z, r, c, r2, recon = fit_state(x, plan)
+        packed = StateCodec(plan).encode(x)
+        out = dict(architecture=np.array(arch), bits=bits.numpy().astype(np.int8), impact=impact.numpy(),
+                   group=np.array(group), x=x.numpy(), z=z.numpy().astype(np.int8), r=r.numpy(), c=c.numpy(),
+                   rows=packed.rows.numpy(), columns=packed.columns.numpy(),
+                   pivots=packed.pivots.numpy())
+        if r2 is not None:
+            out["r2"] = r2.numpy()
+            out["two_bit_rows"] = packed.two_bit_rows.numpy()
+        for b, stream in packed.codes.items():
+            out[f"codes{b}"] = stream.numpy()
+        np.savez_compressed(os.path.join(HERE, f"fit_{name}.npz"), **out)
+
+    torch.manual_seed(5)
+    packs = {}
+    for bits in (2, 4, 6, 8):
+        for n in (0, 1, 7, 128, 513):
+            codes = torch.randint(2 ** bits, (n,))
+            packs[f"codes_{bits}_{n}"] = codes.numpy().astype(np.int16)
+            packs[f"packed_{bits}_{n}"] = pack(codes, bits).numpy()
+    np.savez_compressed(os.path.join(HERE, "pack.npz"), **packs)
+
+    torch.manual_seed(2)
+    deltas = {}
+    for arch in ("gdn", "kda"):
+        b, h, k, v = 3, 4, 16, 8
+        state = torch.randn(b, h, k, v)
+        q = torch.randn(b, h, k)
+        key = torch.nn.functional.normalize(torch.randn(b, h, k), dim=-1)
+        val, beta = torch.randn(b, h, v), torch.rand(b, h)
+        g = -torch.rand(b, h) if arch == "gdn" else -torch.rand(b, h, k)
+        y, s = delta_step(state, q, key, val, g, beta)
+        deltas.update({f"{arch}_{n}": t.numpy() for n, t in
+                       dict(state=state, q=q, k=key, v=val, g=g, beta=beta, out=y, updated=s).items()})
+    np.savez_compressed(os.path.join(HERE, "delta.npz"), **deltas)
+
+    # Config 0: CPU reference plumbing.
+    gen = torch.Generator().manual_seed(0)
+    batch, heads, qk_heads, keys, values = 4, 4, 4, 128, 128
+
+    def draw_inputs():
+        q = torch.randn(batch, qk_heads, keys, generator=gen)
+        k = torch.randn(batch, qk_heads, keys, generator=gen)
+        v = torch.randn(batch, heads, values, generator=gen).bfloat16()
+        a = torch.randn(batch, heads, generator=gen)
+        b = torch.randn(batch, heads, generator=gen)
+        return q, k, v, a, b
+
+    a_log = torch.rand(heads, generator=gen) * math.log(16)
+    dt_bias = torch.zeros(heads)
+
+    def prepare(q, k, a, b):
+        qn = q * torch.rsqrt(q.square().sum(-1, keepdim=True) + 1e-6) * keys ** -0.5
+        kn = k * torch.rsqrt(k.square().sum(-1, keepdim=True) + 1e-6)
+        g = -a_log.exp() * torch.nn.functional.softplus(a + dt_bias)
+        return qn.repeat_interleave(heads // qk_heads, 1), kn.repeat_interleave(heads // qk_heads, 1), g, b.sigmoid()
+
+    stats = LayerStatistics("gdn", sample_every=64, max_snapshots=8)
+    state = torch.zeros(batch, heads, keys, values)
+    for _ in range(256):
+        q, k, v, a, b = draw_inputs()
+        qn, kn, g, beta = prepare(q, k, a, b)
+        _, state = delta_step(state, qn, kn, v.float(), g, beta)
+        stats.observe(qn, kn, v.float(), g, beta, state)
+    impact = impact_factors(stats.export()["omega"])
+    widths = torch.tensor([4, 6, 6, 8])[torch.randperm(heads, generator=gen)]
+    bits = widths[:, None].expand(heads, keys).clone()
+    plan = QuantizationPlan("gdn", bits, impact, 32)
+    codec = StateCodec(plan)
+    packed = codec.encode(state)
+    decoded = codec.decode(packed)
+    q, k, v, a, b = draw_inputs()
+    qn, kn, g, beta = prepare(q, k, a, b)
+    out, updated = delta_step(decoded, qn, kn, v.float(), g, beta)
+    z, r, c, _, recon = fit_state(updated, plan)
+    z0, r0, c0, _, _ = fit_state(state, plan)
+    np.savez_compressed(
+        os.path.join(HERE, "config0.npz"), bits=bits.numpy().astype(np.int8), impact=impact.numpy(),
+        warm_state=state.numpy(), z0=z0.numpy().astype(np.int8), r0=r0.numpy(), c0=c0.numpy(),
+        q=q.numpy(), k=k.numpy(), v=v.float().numpy(), a=a.numpy(), b=b.numpy(),
+        a_log=a_log.numpy(), dt_bias=dt_bias.numpy(), out=out.numpy(), updated=updated.numpy(),
+        z=z.numpy().astype(np.int8), r=r.numpy(), c=c.numpy())
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

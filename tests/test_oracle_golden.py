@@ -1,0 +1,153 @@
+"""The CPU oracle against vectors produced by the unmodified reference.
+
+These pin the oracle before it is trusted as the checker for the CUDA path:
+``fit_state`` codes and fp16 scales, ``StateCodec`` byte streams, ``pack``,
+``packed_layout`` tables, ``delta_step`` and the config-0 plumbing case must
+all agree (bytes exactly; the fp32 recurrent update within 1e-5).
+"""
+import numpy as np
+import pytest
+
+from conftest import golden_fit_cases, load_golden, load_layouts
+from oracle import stepquant_oracle as O
+
+
+def _plan(d):
+    return O.Plan(str(d["architecture"]), d["bits"].astype(np.int64), d["impact"], int(d["group"]))
+
+
+def _same_bits(a, b):
+    a, b = np.ascontiguousarray(a), np.ascontiguousarray(b)
+    return a.shape == b.shape and a.dtype == b.dtype and bool((a.view(np.uint8) == b.view(np.uint8)).all())
+
+
+@pytest.mark.parametrize("case", golden_fit_cases())
+def test_fit_state_matches_reference_bit_for_bit(case):
+    d = load_golden(f"fit_{case}.npz")
+    plan = _plan(d)
+    z, r, c, r2, recon = O.fit_state(d["x"], plan)
+    assert (z == d["z"]).all()
+    assert _same_bits(r, d["r"])
+    assert _same_bits(c, d["c"])
+    if "r2" in d:
+        assert _same_bits(r2, d["r2"])
+    else:
+        assert r2 is None
+    # Pivot rows are exact fp16 copies.
+    pivots = plan.bits == 16
+    assert (recon[:, pivots] == d["x"][:, pivots].astype(np.float16).astype(np.float32)).all()
+
+
+@pytest.mark.parametrize("case", golden_fit_cases())
+def test_codec_streams_match_reference(case):
+    d = load_golden(f"fit_{case}.npz")
+    plan = _plan(d)
+    enc = O.codec_encode(d["x"], plan)
+    for b in (2, 4, 6, 8):
+        assert _same_bits(enc["codes"][b], d[f"codes{b}"]), b
+    assert _same_bits(enc["rows"], d["rows"])
+    assert _same_bits(enc["columns"], d["columns"])
+    assert _same_bits(enc["pivots"], d["pivots"])
+    if "two_bit_rows" in d:
+        assert _same_bits(enc["two_bit_rows"], d["two_bit_rows"])
+    # decode(encode(x)) is fit_state's reconstruction (test_core.py:46-64).
+    recon = O.fit_state(d["x"], plan)[-1]
+    assert (O.codec_decode(enc, plan) == recon).all()
+
+
+@pytest.mark.parametrize("case", golden_fit_cases())
+def test_page_image_round_trip(case):
+    d = load_golden(f"fit_{case}.npz")
+    plan = _plan(d)
+    pages = O.page_encode(d["x"], plan)
+    assert pages.shape[1] == O.packed_layout(plan, d["x"].shape[-1])[-1]
+    recon = O.fit_state(d["x"], plan)[-1]
+    assert (O.page_decode(pages, plan, d["x"].shape[-1]) == recon).all()
+
+
+def test_packed_layout_tables_match_reference():
+    for entry in load_layouts():
+        bits = np.array(entry["bits"])
+        plan = O.Plan(entry["architecture"], bits, np.ones(bits.shape, np.float32), entry["value_group_size"])
+        got = O.packed_layout(plan, entry["values"], entry["storage"])
+        assert list(got) == [entry["offsets"], entry["rows"], entry["columns"], entry["page_bytes"]]
+
+
+def test_byte_layout_known_answer():
+    # test_byte_layout.py:9-20 of the reference, as a known-answer vector.
+    bits = np.array([[2, 4, 6, 16], [16, 16, 16, 16]])
+    plan = O.Plan("kda", bits, np.ones(bits.shape, np.float32))
+    offsets, rows, columns, total = O.packed_layout(plan, 32, "byte")
+    payload = 4 * 32 + 5 * 32 * 2
+    assert offsets[8:] == [0, 192] and offsets[3] == 128
+    assert columns == [payload + 3 * 2, -1]
+    assert rows == [payload, payload + 2, payload + 4, -1, -1, -1, -1, -1]
+    assert total == (payload + 3 * 2 + 32 * 2 + 15) // 16 * 16
+    assert total > O.packed_layout(plan, 32, "packed")[-1]
+
+
+@pytest.mark.parametrize("arch", ["gdn", "kda"])
+def test_six_bit_page_has_no_padding(arch):
+    # test_stepquant6.py:42-53: exactly H*K*V*6/8 + 2H(K+V) bytes.
+    heads, keys, values = 2, 128, 128
+    plan = O.Plan(arch, np.full((heads, keys), 6), np.ones((heads, keys), np.float32))
+    assert O.packed_layout(plan, values)[-1] - 2 * heads * (keys + values) == heads * keys * values * 6 // 8
+
+
+def test_half_aligned_mixed_kda_page():
+    # test_kernel_edges.py:10-32: mixed KDA pages may be only half-aligned.
+    plan = O.Plan("kda", np.array([[2, 4, 8, 16]]), np.ones((1, 4), np.float32))
+    for values in (4, 32):
+        assert O.packed_layout(plan, values)[-1] % 4 == 2
+
+
+def test_pack_matches_reference():
+    d = load_golden("pack.npz")
+    for bits in (2, 4, 6, 8):
+        for n in (0, 1, 7, 128, 513):
+            codes = d[f"codes_{bits}_{n}"]
+            packed = O.pack(codes, bits)
+            assert _same_bits(packed, d[f"packed_{bits}_{n}"])
+            assert (O.unpack(packed, bits, n) == codes).all()
+            assert packed.size <= (n * bits + 7) // 8 + 2
+
+
+def test_delta_step_matches_reference():
+    d = load_golden("delta.npz")
+    for arch in ("gdn", "kda"):
+        g = {k: d[f"{arch}_{k}"] for k in ("state", "q", "k", "v", "g", "beta", "out", "updated")}
+        out, updated = O.delta_step(g["state"], g["q"], g["k"], g["v"], g["g"], g["beta"])
+        np.testing.assert_allclose(out, g["out"], atol=1e-5, rtol=1e-5)
+        np.testing.assert_allclose(updated, g["updated"], atol=1e-5, rtol=1e-5)
+
+
+def test_config0_plumbing_case():
+    """warm state, calibrated plan, one decode step, re-fit."""
+    d = load_golden("config0.npz")
+    plan = O.Plan("gdn", d["bits"].astype(np.int64), d["impact"], 32)
+    z0, r0, c0, _, recon0 = O.fit_state(d["warm_state"], plan)
+    assert (z0 == d["z0"]).all() and _same_bits(r0, d["r0"]) and _same_bits(c0, d["c0"])
+    # The pool path: page image of the warm state, then one decode step.
+    pages = O.page_encode(d["warm_state"], plan)
+    slots = np.arange(1, 5)
+    pool = np.zeros((5, pages.shape[1]), np.uint8)
+    pool[1:] = pages
+    out, new_pool, updated = O.decode_step(
+        pool, slots, plan, 128, d["q"], d["k"], d["v"], d["a"], d["b"],
+        normalize=True, scale=128 ** -0.5, a_log=d["a_log"], dt_bias=d["dt_bias"])
+    np.testing.assert_allclose(out, d["out"], atol=2e-5, rtol=1e-4)
+    np.testing.assert_allclose(updated, d["updated"], atol=2e-5, rtol=1e-4)
+    # Codes are bit-exact given the same fp32 pre-quantization state.
+    z, r, c, _, _ = O.fit_state(d["updated"], plan)
+    assert (z == d["z"]).all() and _same_bits(r, d["r"]) and _same_bits(c, d["c"])
+    assert (new_pool[0] == 0).all()
+
+
+def test_zero_state_encodes_finite():
+    bits = np.array([[2] * 8, [4] * 8, [6] * 8, [8] * 8, [16] * 8])
+    for arch in ("gdn", "kda"):
+        b = bits if arch == "gdn" else bits.T.copy()
+        plan = O.Plan(arch, b, np.full(b.shape, 0.7, np.float32), 4)
+        x = np.zeros((2,) + b.shape + (16,), np.float32)
+        dec = O.codec_decode(O.codec_encode(x, plan), plan)
+        assert np.isfinite(dec).all() and np.abs(dec).max() < 1e-10
