@@ -1,0 +1,39 @@
+// Internal launch interface of the tile kernels (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "sq_common.cuh"
+
+namespace sq {
+
+enum Mode { kEncode = 0, kDecode = 1, kStep = 2, kReadout = 3, kWriteback = 4, kFit = 5 };
+
+struct TileParams {
+    sq_plan plan;
+    uint8_t *pages;
+    int64_t num_slots;
+    const int64_t *slots;  // request slots (stable slots for kWriteback)
+    sq_step_args step;
+    const float *dense_in;    // kEncode / kFit input
+    float *dense_out;         // kDecode output, or the pre-quantization state of kStep / kWriteback
+    float *scratch;           // kReadout writes, kWriteback reads
+    int64_t *stable_slots;    // kReadout writes
+    int64_t scratch_stride;   // floats per request
+    int16_t *fit_z;
+    uint16_t *fit_r;
+    uint16_t *fit_c;
+    uint16_t *fit_r2;
+    float *fit_recon;
+    int32_t *status;
+};
+
+size_t tile_smem_bytes(int K, int V, int groups);
+cudaError_t launch_tile(int mode, const TileParams &p, int items, cudaStream_t stream);
+
+// Register-resident kernels for K = V = 128 GDN heads of width 4, 6 or 8
+// (sq_fast.cu).  Return cudaErrorNotSupported when the plan is not eligible.
+bool fast_eligible(const sq_plan &plan);
+cudaError_t launch_fast(int mode, const TileParams &p, int batch, cudaStream_t stream);
+
+}  // namespace sq
