@@ -10,9 +10,11 @@
  * Conventions
  *  - All tensor pointers are device pointers unless a parameter says "host".
  *    Buffers are owned by the caller; no entry point allocates device memory.
- *  - ``stream`` is a cudaStream_t (0 = legacy default stream).  Every device
- *    entry point only enqueues work: it never synchronizes, never reads device
- *    memory on the host and is therefore legal inside CUDA-graph capture.
+ *  - ``stream`` is a cudaStream_t (0 = legacy default stream).  Each device
+ *    entry point that replaces a reference operation (all but
+ *    sq_step_async_noalloc) only enqueues work: it never synchronizes, never
+ *    reads device memory on the host and is therefore legal inside CUDA-graph
+ *    capture.
  *  - Return value: SQ_OK or an SQ_ERR_* code for argument errors detected on
  *    the host before launch (the reference raises ValueError at the same
  *    points), or SQ_ERR_CUDA when the launch itself failed.
@@ -194,6 +196,25 @@ int32_t sq_writeback(const sq_plan *plan, uint8_t *pages, int64_t num_slots,
  */
 int32_t sq_fit_state(const sq_plan *plan, const float *x, int32_t batch, int16_t *z, uint16_t *r,
                      uint16_t *c, uint16_t *r2, float *recon, sq_stream_t stream);
+
+/*
+ * No counterpart in the reference.  The asynchronous decode step (sq_readout
+ * then sq_writeback on `stream`) for callers that cannot allocate device memory
+ * when they step, e.g. a server that reserves its whole device budget at
+ * start-up, or a binding with no device allocator of its own.  Its scratch is
+ * a 16 MiB file-scope device array of the library (sq_noalloc_scratch_bytes())
+ * instead of caller buffers; a call needs round_up(batch*8, 256) +
+ * batch * sq_scratch_floats(plan) * 4 bytes of it and returns SQ_ERR_CAPACITY
+ * above that.  All calls share the array, so calls that overlap on the GPU
+ * race.  The first call on a device looks up the array's address; make it
+ * before any stream capture.  Writes the same out and page bytes as
+ * sq_readout + sq_writeback.
+ */
+int32_t sq_step_async_noalloc(const sq_plan *plan, uint8_t *pages, int64_t num_slots, const int64_t *slots,
+                              int32_t batch, const sq_step_args *args, int32_t *status, sq_stream_t stream);
+
+/* Size in bytes of the file-scope scratch array used by sq_step_async_noalloc. */
+int64_t sq_noalloc_scratch_bytes(void);
 
 /* packing.pack (stepquant/packing.py:6-14): codes int16 [n] -> little-endian bytes. */
 int32_t sq_pack(const int16_t *codes, int64_t n, int32_t bits, uint8_t *out, sq_stream_t stream);

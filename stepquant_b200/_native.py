@@ -50,6 +50,8 @@ _SIGNATURES = {
     "sq_packed_bytes": (_i64, [_i64, _i32]),
     "sq_unpack": (_i32, [_p, _i64, _i32, _p, _p]),
     "sq_fp32_step": (_i32, [_p, _i64, _i32, _i32, _i32, _i32, _p, _i32, _p, _p, _p]),
+    "sq_step_async_noalloc": (_i32, [_p, _p, _i64, _p, _i32, _p, _p, _p]),
+    "sq_noalloc_scratch_bytes": (_i64, []),
 }
 
 EXPORTED = tuple(_SIGNATURES)
