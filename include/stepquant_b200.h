@@ -63,6 +63,9 @@ enum sq_architecture { SQ_GDN = 0, SQ_KDA = 1 };
  *                                each head's byte stride between value tiles
  *   rows     [heads*keys]        byte offset of each row's fp16 scale(s), -1 = pivot
  *   columns  [heads]             byte offset of each head's fp16 column scales, -1 = none
+ *   bits_host [heads*keys]       optional HOST copy of bits (may be NULL); when
+ *                                given, the host skips launches that no head needs
+ * The tables must be those sq_packed_layout produces for `bits`.
  * Supported shapes: keys, values in {4,...,128} (powers of two); GDN needs
  * values % value_group_size == 0 and at most 32 value groups.
  */
@@ -79,6 +82,7 @@ typedef struct sq_plan {
     const int32_t *offsets;
     const int32_t *rows;
     const int32_t *columns;
+    const int32_t *bits_host;
 } sq_plan;
 
 /*
@@ -233,6 +237,15 @@ int32_t sq_unpack(const uint8_t *data, int64_t count, int32_t bits, int16_t *out
 int32_t sq_fp32_step(float *state, int64_t num_slots, int32_t heads, int32_t keys, int32_t values,
                      int32_t kda, const int64_t *slots, int32_t batch, const sq_step_args *args,
                      int32_t *status, sq_stream_t stream);
+
+/*
+ * Self-test of the division used by the register-resident decode kernels: for
+ * i < n, out[i] = a[i] / b[i] computed with a correctly rounded reciprocal of
+ * the fp16 value b[i] (given as its bits) and one Markstein correction.  It
+ * must equal IEEE round-to-nearest a[i] / b[i] whenever the quotient is a
+ * normal number; tests compare it with the device's IEEE division.
+ */
+int32_t sq_selftest_fp16_division(const float *a, const uint16_t *b, float *out, int64_t n, sq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -407,6 +407,18 @@ def page_store(page, plan: Plan, values, z, r, c, r2, pivots_f16):
     two_index = 0
     for h in range(heads):
         stride = strides[h]
+        b0 = int(plan.bits[h, 0])
+        if (plan.bits[h] == b0).all() and b0 in (4, 6, 8) and stride == keys * tile * b0 // 8:
+            # Uniform head: its code region is one little-endian bitstream in
+            # (value tile, key row, lane) order.
+            codes = z[h].astype(np.int64) + (2 ** (b0 - 1) - 1)
+            stream = codes.reshape(keys, values // tile, tile).transpose(1, 0, 2).reshape(-1)
+            region = pack(stream, b0)
+            page[offsets[h * keys]:offsets[h * keys] + region.size] = region
+            r_bytes = r[h].astype(np.float16).view(np.uint8)
+            page[rows[h * keys]:rows[h * keys] + 2 * keys] = r_bytes
+            page[columns[h]:columns[h] + 2 * values] = c[h].astype(np.float16).view(np.uint8)
+            continue
         for k in range(keys):
             b = int(plan.bits[h, k])
             off = offsets[h * keys + k]
@@ -472,6 +484,17 @@ def page_decode(pages, plan: Plan, values):
             col = np.zeros(values, F32)
             if columns[h] >= 0:
                 col = np.frombuffer(page[columns[h]:columns[h] + 2 * values].tobytes(), np.float16).astype(F32)
+            b0 = int(plan.bits[h, 0])
+            if (plan.bits[h] == b0).all() and b0 in (4, 6, 8) and strides[h] == keys * tile * b0 // 8:
+                nbytes = keys * values * b0 // 8
+                codes = unpack(page[offsets[h * keys]:offsets[h * keys] + nbytes], b0, keys * values)
+                codes = codes.reshape(values // tile, keys, tile).transpose(1, 0, 2).reshape(keys, values)
+                zz = (codes.astype(np.int64) - ((1 << (b0 - 1)) - 1)).astype(F32)
+                if plan.architecture == "kda":
+                    zz = zz * F32(1 << (8 - b0))
+                rr = np.frombuffer(page[rows[h * keys]:rows[h * keys] + 2 * keys].tobytes(), np.float16).astype(F32)
+                out[i, h] = ((rr[:, None] * col[None, :]).astype(F32) * zz).astype(F32)
+                continue
             for k in range(keys):
                 b = int(plan.bits[h, k])
                 off = offsets[h * keys + k]

@@ -25,7 +25,8 @@ _i64 = ctypes.c_int64
 class SqPlan(ctypes.Structure):
     _fields_ = [("architecture", _i32), ("heads", _i32), ("keys", _i32), ("values", _i32),
                 ("value_group_size", _i32), ("reserved", _i32), ("page_bytes", _i64),
-                ("bits", _p), ("impact", _p), ("offsets", _p), ("rows", _p), ("columns", _p)]
+                ("bits", _p), ("impact", _p), ("offsets", _p), ("rows", _p), ("columns", _p),
+                ("bits_host", _p)]
 
 
 class SqStepArgs(ctypes.Structure):
@@ -52,6 +53,7 @@ _SIGNATURES = {
     "sq_fp32_step": (_i32, [_p, _i64, _i32, _i32, _i32, _i32, _p, _i32, _p, _p, _p]),
     "sq_step_async_noalloc": (_i32, [_p, _p, _i64, _p, _i32, _p, _p, _p]),
     "sq_noalloc_scratch_bytes": (_i64, []),
+    "sq_selftest_fp16_division": (_i32, [_p, _p, _p, _i64, _p]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

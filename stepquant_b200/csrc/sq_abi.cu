@@ -14,6 +14,7 @@ cudaError_t launch_unpack(const uint8_t *data, int64_t count, int bits, int16_t 
 int64_t packed_bytes(int64_t n, int bits);
 cudaError_t launch_fp32_step(float *state, int64_t num_slots, int H, int K, int V, int kda, const int64_t *slots,
                              int batch, const sq_step_args &a, int32_t *status, cudaStream_t stream);
+cudaError_t launch_division_selftest(const float *a, const uint16_t *b, float *out, int64_t n, cudaStream_t stream);
 }  // namespace sq
 
 namespace {
@@ -55,16 +56,26 @@ sq::TileParams base_params(const sq_plan *plan, uint8_t *pages, int64_t num_slot
     return t;
 }
 
-int32_t run(int mode, const sq::TileParams &t, int32_t batch, cudaStream_t stream) {
+// Step, readout and writeback go to the register-resident kernels for the heads
+// they handle (GDN, K = V = 128, widths 4/6/8) and to the tile kernel for the
+// rest; with a host copy of the bits the tile launch is skipped when no head
+// needs it.  Every other mode runs on the tile kernel.
+int32_t run(int mode, sq::TileParams t, int32_t batch, cudaStream_t stream) {
     const int items = batch * t.plan.heads;
     if (items <= 0) return SQ_OK;
-    cudaError_t e = cudaErrorNotSupported;
-    if (sq::fast_eligible(t.plan)) e = sq::launch_fast(mode, t, batch, stream);
-    if (e == cudaErrorNotSupported) {
-        cudaGetLastError();
-        e = sq::launch_tile(mode, t, items, stream);
+    const bool fast_mode = mode == sq::kStep || mode == sq::kReadout || mode == sq::kWriteback;
+    if (fast_mode && sq::fast_eligible(t.plan, t.pages)) {
+        if (cudaError_t e = sq::launch_fast(mode, t, batch, stream)) return cuda_status(e);
+        bool rest = true;
+        if (t.plan.bits_host) {
+            rest = false;
+            for (int h = 0; h < t.plan.heads; ++h)
+                rest = rest || !sq::fast_head(t.plan, t.plan.bits_host[h * t.plan.keys]);
+        }
+        if (!rest) return SQ_OK;
+        t.skip_fast = 1;
     }
-    return cuda_status(e);
+    return cuda_status(sq::launch_tile(mode, t, items, stream));
 }
 
 }  // namespace
@@ -272,6 +283,11 @@ int32_t sq_fp32_step(float *state, int64_t num_slots, int32_t heads, int32_t key
     if (int32_t e = check_step(&p, args)) return e;
     return cuda_status(sq::launch_fp32_step(state, num_slots, heads, keys, values, kda, slots, batch, *args, status,
                                             stream));
+}
+
+int32_t sq_selftest_fp16_division(const float *a, const uint16_t *b, float *out, int64_t n, sq_stream_t stream) {
+    if (n < 0 || (n > 0 && (!a || !b || !out))) return SQ_ERR_ARGUMENT;
+    return cuda_status(sq::launch_division_selftest(a, b, out, n, stream));
 }
 
 }  // extern "C"

@@ -26,14 +26,21 @@ struct TileParams {
     uint16_t *fit_r2;
     float *fit_recon;
     int32_t *status;
+    int skip_fast;  // tile kernel: leave heads that fast_head() accepts to the fast kernel
 };
 
 size_t tile_smem_bytes(int K, int V, int groups);
 cudaError_t launch_tile(int mode, const TileParams &p, int items, cudaStream_t stream);
 
 // Register-resident kernels for K = V = 128 GDN heads of width 4, 6 or 8
-// (sq_fast.cu).  Return cudaErrorNotSupported when the plan is not eligible.
-bool fast_eligible(const sq_plan &plan);
+// (sq_fast.cu) for the step, readout and writeback modes.  fast_eligible():
+// the plan's shape and the page alignment allow them; fast_head(): a head of
+// that width is handled by them (the tile kernel handles the others).
+bool fast_eligible(const sq_plan &plan, const void *pages);
+__host__ __device__ inline bool fast_head(const sq_plan &plan, int width) {
+    return plan.architecture == SQ_GDN && plan.keys == 128 && plan.values == 128 &&
+           (width == 4 || width == 6 || width == 8);
+}
 cudaError_t launch_fast(int mode, const TileParams &p, int batch, cudaStream_t stream);
 
 }  // namespace sq
