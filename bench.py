@@ -27,7 +27,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -63,56 +62,51 @@ def parse_args():
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+    """SM clock and throttle reasons sampled every 2 ms (NVML) while the timed region runs."""
 
-    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
-             "clocks_event_reasons.sw_power_cap"
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
+        self.samples = []
+        self.max_mhz = None
 
     def __enter__(self):
+        import threading
+        self.stop = threading.Event()
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+
+            def run():
+                while not self.stop.is_set():
+                    try:
+                        self.samples.append((pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM),
+                                             pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)))
+                    except pynvml.NVMLError:
+                        pass
+                    self.stop.wait(0.002)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+        except Exception:  # NVML missing: no samples
+            self.thread = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is None:
-            self.lines = []
-            return
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        self.lines = [line for line in out.splitlines() if line.strip()]
+        self.stop.set()
+        if self.thread is not None:
+            self.thread.join()
 
     def summary(self):
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                smax.append(float(parts[1]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[4:8]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
+        reasons = sorted(name for name, bit in self.REASONS.items() if any(r & bit for _, r in self.samples))
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
 
 
 def measured_peak():

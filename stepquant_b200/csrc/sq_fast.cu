@@ -43,7 +43,8 @@ struct FastSmem {
     unsigned char stage[kTiles * (FK * 16 + kStagePad)];  // old packed codes, padded per tile
     unsigned char plane[kPlaneBytes];                     // row partials, then new code bytes
     float red[2][8][FV];                                  // per-warp column partials
-    float4 rowc[FK];                                      // per-row constants
+    float4 rowa[FK];                                      // per-row constants, duplicated pairs:
+    float4 rowb[FK];                                      //   P1: {rd, rd, k, k} {q, q, -, -}; P3-P5: {r, r, 1/r, 1/r} {-r, -r, w2, w2}
     float colc[4][FV];                                    // per-column constants
     __half rold[FK];
     __half cold[FV];
@@ -62,6 +63,15 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.wait_group 0;\n" ::);
 }
 
+// Packed f32x2 arithmetic (sm_100): two independent IEEE round-to-nearest lanes.
+// Caution: ptxas (CUDA 12.9) fuses a packed multiply whose result feeds a
+// packed add into one packed FMA even with -fmad=false and explicit .rn, which
+// changes the rounding.  Every sum the quantizer must reproduce bit for bit is
+// therefore accumulated with scalar __fadd_rn (ptxas keeps those separate).
+__device__ __forceinline__ float2 pmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 pfma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add_lanes(float2 a, float2 b) { return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)); }
+
 // Correctly rounded a / b for b an fp16 value (see the header comment), rb = RN(1/b).
 __device__ __forceinline__ float div_fp16(float a, float b, float rb) {
     const float q = __fmul_rn(a, rb);
@@ -74,28 +84,44 @@ __device__ __forceinline__ float divide(float a, float b, float rb) {
     return SLOW ? __fdiv_rn(a, b) : div_fp16(a, b, rb);
 }
 
-// Signed level (code - offset) of value-lane u of row k in value tile t, read
-// from the staged page; exact small integers built with the 2^23 trick.
+// Two lanes of div_fp16 in packed f32x2 arithmetic (each lane rounds as the
+// scalar operation does); nb = -b.
+template <bool SLOW>
+__device__ __forceinline__ float2 divide2(float2 a, float2 b, float2 rb, float2 nb) {
+    if (SLOW) return make_float2(__fdiv_rn(a.x, b.x), __fdiv_rn(a.y, b.y));
+    const float2 q = pmul2(a, rb);
+    const float2 r = pfma2(q, nb, a);
+    return pfma2(r, rb, q);
+}
+
+__device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
+
+// Bits of the code of value-lane u in row k of value tile t, read from the
+// staged page, ORed into the float 2^23: with the lane's conversion constants
+// (level_constants) one fused multiply-add gives the exact signed level.
 template <int BITS>
-__device__ __forceinline__ float staged_level(const unsigned char *stage, int t, int k, int u) {
+__device__ __forceinline__ float staged_bits(const unsigned char *stage, int t, int k, int u) {
     const unsigned char *chunk = stage + t * (W<BITS>::tile_bytes + kStagePad) + k * W<BITS>::chunk;
+    uint32_t m;
     if (BITS == 8) {
-        const uint32_t c = chunk[u];
-        return __fsub_rn(__uint_as_float(0x4B000000u | c), 8388608.f + float(W<BITS>::off));
+        m = chunk[u];
     } else if (BITS == 4) {
-        const uint32_t byte = chunk[u >> 1];
-        const int s = 4 * (u & 1);
-        const uint32_t m = byte & (0xFu << s);
-        const float scale = s ? 0.0625f : 1.f;
-        return __fmaf_rn(__uint_as_float(0x4B000000u | m), scale, -(8388608.f * scale + float(W<BITS>::off)));
+        m = uint32_t(chunk[u >> 1]) & (0xFu << (4 * (u & 1)));
     } else {
         const int bit = 6 * u;
-        const int p = bit >> 3, s = bit & 7;
-        const uint32_t w = uint32_t(chunk[p]) | (uint32_t(chunk[p + 1]) << 8);
-        const uint32_t m = w & (0x3Fu << s);
-        const float scale = __uint_as_float(uint32_t(127 - s) << 23);  // 2^-s
-        return __fmaf_rn(__uint_as_float(0x4B000000u | m), scale, -(8388608.f * scale + float(W<BITS>::off)));
+        const uint32_t w = uint32_t(chunk[bit >> 3]) | (uint32_t(chunk[(bit >> 3) + 1]) << 8);
+        m = w & (0x3Fu << (bit & 7));
     }
+    return __uint_as_float(0x4B000000u | m);
+}
+
+// level = bits * 2^-s - (2^(23-s) + offset), s = the code's bit shift inside the loaded unit.
+template <int BITS>
+__device__ __forceinline__ float2 level_constants(int u) {
+    const int s = BITS == 8 ? 0 : BITS == 4 ? 4 * (u & 1) : (6 * u) & 7;
+    const float scale = __uint_as_float(uint32_t(127 - s) << 23);
+    return make_float2(scale, -(8388608.f * scale + float(W<BITS>::off)));
 }
 
 // Pack 16 code bytes (one per value lane) of chunk (t, k) from the plane into
@@ -131,24 +157,30 @@ struct Ctx {
     int off_head;
 };
 
-// P3-P5: column max -> c0; first levels and the weighted least-squares sums
-// -> c1; final levels -> code plane -> packed page chunks; r and c stores.
-template <int BITS, int MODE, bool SLOW>
-__device__ __forceinline__ void fast_quantize(const TileParams &p, FastSmem &s, const Ctx &c, float (&X)[16][4]) {
-    const sq_plan &P = p.plan;
+// P3-P5 (shared by every width): column max -> c0; first levels and the
+// weighted least-squares sums -> c1; final code bytes -> plane.  X holds the
+// updated state on entry and x / r on exit.  Packed f32x2 lanes are the column
+// pairs (l, l+32) and (l+64, l+96).
+template <bool SLOW>
+__device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 (&X)[16][2], float qmax) {
     const int warp = c.warp, lane = c.lane, tid = c.tid;
-    constexpr float qmax = float(W<BITS>::off);
     // P3: c0 = fp16(max_k |x / r| / qmax) (uniform width: one division per column).
     {
-        float m[4] = {0.f, 0.f, 0.f, 0.f};
+        float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
-            const float4 rc = s.rowc[warp * 16 + r];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], fabsf(divide<SLOW>(X[r][i], rc.x, rc.y)));
+            const float4 a = s.rowa[warp * 16 + r], b = s.rowb[warp * 16 + r];
+            const float2 s01 = divide2<SLOW>(X[r][0], lo2(a), hi2(a), lo2(b));
+            const float2 s23 = divide2<SLOW>(X[r][1], lo2(a), hi2(a), lo2(b));
+            m0 = fmaxf(m0, fabsf(s01.x));
+            m1 = fmaxf(m1, fabsf(s01.y));
+            m2 = fmaxf(m2, fabsf(s23.x));
+            m3 = fmaxf(m3, fabsf(s23.y));
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) s.red[0][warp][lane + 32 * i] = m[i];
+        s.red[0][warp][lane] = m0;
+        s.red[0][warp][lane + 32] = m1;
+        s.red[0][warp][lane + 64] = m2;
+        s.red[0][warp][lane + 96] = m3;
     }
     __syncthreads();
     int safe = 1;
@@ -166,32 +198,44 @@ __device__ __forceinline__ void fast_quantize(const TileParams &p, FastSmem &s, 
     const bool no_clamp = __syncthreads_and(safe);
     // P4: first levels, weighted least-squares numerator / denominator (16-row blocks).
     {
-        float c0[4], rc0[4], num[4] = {0.f, 0.f, 0.f, 0.f}, den[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            c0[i] = s.colc[1][lane + 32 * i];
-            rc0[i] = s.colc[2][lane + 32 * i];
-        }
+        const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
+        const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
+        const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
+        const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
+        const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
+        float2 num01 = make_float2(0.f, 0.f), num23 = num01, den01 = num01, den23 = num01;
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
-            const float4 rc = s.rowc[warp * 16 + r];
+            const float4 a = s.rowa[warp * 16 + r], b = s.rowb[warp * 16 + r];
+            const float2 rn = lo2(a), w2 = hi2(b);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float x = X[r][i];
-                const float sn = divide<SLOW>(x, rc.x, rc.y);
-                float z = rintf(divide<SLOW>(sn, c0[i], rc0[i]));
-                if (!no_clamp) z = fminf(fmaxf(z, -qmax), qmax);
-                const float v = __fmul_rn(rc.x, z);
-                num[i] = __fadd_rn(num[i], __fmul_rn(__fmul_rn(rc.z, v), x));
-                den[i] = __fadd_rn(den[i], __fmul_rn(rc.z, __fmul_rn(v, v)));
-                X[r][i] = sn;
+            for (int h = 0; h < 2; ++h) {
+                const float2 x = X[r][h];
+                const float2 sn = divide2<SLOW>(x, rn, hi2(a), lo2(b));
+                const float2 y = divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
+                float2 z = make_float2(rintf(y.x), rintf(y.y));
+                if (!no_clamp) z = make_float2(fminf(fmaxf(z.x, -qmax), qmax), fminf(fmaxf(z.y, -qmax), qmax));
+                const float2 v = pmul2(rn, z);
+                const float2 t = pmul2(pmul2(w2, v), x);
+                const float2 d = pmul2(w2, pmul2(v, v));
+                if (h) {
+                    num23 = add_lanes(num23, t);
+                    den23 = add_lanes(den23, d);
+                } else {
+                    num01 = add_lanes(num01, t);
+                    den01 = add_lanes(den01, d);
+                }
+                X[r][h] = sn;
             }
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            s.red[0][warp][lane + 32 * i] = num[i];
-            s.red[1][warp][lane + 32 * i] = den[i];
-        }
+        s.red[0][warp][lane] = num01.x;
+        s.red[0][warp][lane + 32] = num01.y;
+        s.red[0][warp][lane + 64] = num23.x;
+        s.red[0][warp][lane + 96] = num23.y;
+        s.red[1][warp][lane] = den01.x;
+        s.red[1][warp][lane + 32] = den01.y;
+        s.red[1][warp][lane + 64] = den23.x;
+        s.red[1][warp][lane + 96] = den23.y;
     }
     __syncthreads();
     if (tid < FV) {
@@ -206,40 +250,45 @@ __device__ __forceinline__ void fast_quantize(const TileParams &p, FastSmem &s, 
         s.colc[2][tid] = __frcp_rn(c1);
     }
     __syncthreads();
-    // P5: final levels -> one code byte per value in the plane.
+    // P5: final levels -> one code byte (level + offset) per value in the plane.
     {
-        float c1[4], rc1[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            c1[i] = s.colc[1][lane + 32 * i];
-            rc1[i] = s.colc[2][lane + 32 * i];
-        }
+        const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
+        const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
+        const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
+        const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
+        const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
+        const float2 magic = make_float2(8388608.f + qmax, 8388608.f + qmax);
         const int t0 = lane >> 4, u = lane & 15;
+        unsigned char *plane = s.plane + t0 * (FK * 16 + kStagePad) + u;
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
             const int k = warp * 16 + r;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float z = fminf(fmaxf(rintf(divide<SLOW>(X[r][i], c1[i], rc1[i])), -qmax), qmax);
-                const uint32_t code = __float_as_uint(__fadd_rn(z, 8388608.f + qmax));
-                s.plane[(t0 + 2 * i) * (FK * 16 + kStagePad) + k * 16 + u] = static_cast<unsigned char>(code);
+            for (int h = 0; h < 2; ++h) {
+                const float2 y = divide2<SLOW>(X[r][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
+                const float2 z = make_float2(fminf(fmaxf(rintf(y.x), -qmax), qmax), fminf(fmaxf(rintf(y.y), -qmax), qmax));
+                const float2 code = add_lanes(z, magic);
+                plane[(4 * h) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.x));
+                plane[(4 * h + 2) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.y));
             }
         }
     }
     __syncthreads();
-    // Pack the plane into the page and store the scales.
-    {
-        uint8_t *dst = c.page + c.off_head;
-        const int stride = W<BITS>::tile_bytes;
-        for (int ch = tid; ch < kTiles * FK; ch += kThreads) {
-            const int t = ch / FK, k = ch % FK;
-            store_chunk<BITS>(dst + t * stride + k * W<BITS>::chunk, s.plane + t * (FK * 16 + kStagePad) + k * 16);
-        }
-        if (tid < FK) {
-            reinterpret_cast<__half *>(c.page + P.rows[c.head * FK])[tid] = __float2half_rn(s.rowc[tid].x);
-        } else {
-            reinterpret_cast<__half *>(c.page + P.columns[c.head])[tid - FK] = __float2half_rn(s.colc[1][tid - FK]);
-        }
+}
+
+// Pack the code plane into the page (2*BITS bytes per row-tile chunk) and store r and c.
+template <int BITS>
+__device__ __forceinline__ void fast_store(const TileParams &p, FastSmem &s, const Ctx &c) {
+    const sq_plan &P = p.plan;
+    uint8_t *dst = c.page + c.off_head;
+    for (int ch = c.tid; ch < kTiles * FK; ch += kThreads) {
+        const int t = ch / FK, k = ch % FK;
+        store_chunk<BITS>(dst + t * W<BITS>::tile_bytes + k * W<BITS>::chunk, s.plane + t * (FK * 16 + kStagePad) + k * 16);
+    }
+    if (c.tid < FK) {
+        reinterpret_cast<__half *>(c.page + P.rows[c.head * FK])[c.tid] = __float2half_rn(s.rowa[c.tid].x);
+    } else {
+        reinterpret_cast<__half *>(c.page + P.columns[c.head])[c.tid - FK] = __float2half_rn(s.colc[1][c.tid - FK]);
     }
 }
 
@@ -314,36 +363,46 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c) {
     }
     cp_async_wait_all();
     __syncthreads();
-    if (tid < FK) s.rowc[tid] = make_float4(__fmul_rn(__half2float(s.rold[tid]), decay), s.kv[tid], s.qv[tid], 0.f);
+    if (tid < FK) {
+        const float rd = __fmul_rn(__half2float(s.rold[tid]), decay);
+        s.rowa[tid] = make_float4(rd, rd, s.kv[tid], s.kv[tid]);
+        s.rowb[tid] = make_float4(s.qv[tid], s.qv[tid], 0.f, 0.f);
+    }
     __syncthreads();
 
     // ---- P1: unpack, dequantize, decay; column partials of k^T S and q^T S ---
-    float X[16][4];
-    float colc_old[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) colc_old[i] = __half2float(s.cold[lane + 32 * i]);
+    float2 X[16][2];
     const int t0 = lane >> 4, u = lane & 15;
     {
-        float kx[4] = {0.f, 0.f, 0.f, 0.f}, qx[4] = {0.f, 0.f, 0.f, 0.f};
+        const float2 cl01 = make_float2(__half2float(s.cold[lane]), __half2float(s.cold[lane + 32]));
+        const float2 cl23 = make_float2(__half2float(s.cold[lane + 64]), __half2float(s.cold[lane + 96]));
+        const float2 lc = level_constants<BITS>(u);
+        const float2 lscale = make_float2(lc.x, lc.x), lbias = make_float2(lc.y, lc.y);
+        float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
             const int k = warp * 16 + r;
-            const float4 rc = s.rowc[k];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float z = staged_level<BITS>(s.stage, t0 + 2 * i, k, u);
-                const float x = __fmul_rn(__fmul_rn(z, rc.x), colc_old[i]);
-                X[r][i] = x;
-                kx[i] = __fmaf_rn(rc.y, x, kx[i]);
-                qx[i] = __fmaf_rn(rc.z, x, qx[i]);
-            }
+            const float4 a = s.rowa[k], b = s.rowb[k];
+            const float2 f01 = make_float2(staged_bits<BITS>(s.stage, t0, k, u), staged_bits<BITS>(s.stage, t0 + 2, k, u));
+            const float2 f23 = make_float2(staged_bits<BITS>(s.stage, t0 + 4, k, u), staged_bits<BITS>(s.stage, t0 + 6, k, u));
+            const float2 x01 = pmul2(pmul2(pfma2(f01, lscale, lbias), lo2(a)), cl01);
+            const float2 x23 = pmul2(pmul2(pfma2(f23, lscale, lbias), lo2(a)), cl23);
+            X[r][0] = x01;
+            X[r][1] = x23;
+            kx01 = pfma2(hi2(a), x01, kx01);
+            kx23 = pfma2(hi2(a), x23, kx23);
+            qx01 = pfma2(lo2(b), x01, qx01);
+            qx23 = pfma2(lo2(b), x23, qx23);
         }
         if (MODE != kWriteback) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                s.red[0][warp][lane + 32 * i] = kx[i];
-                s.red[1][warp][lane + 32 * i] = qx[i];
-            }
+            s.red[0][warp][lane] = kx01.x;
+            s.red[0][warp][lane + 32] = kx01.y;
+            s.red[0][warp][lane + 64] = kx23.x;
+            s.red[0][warp][lane + 96] = kx23.y;
+            s.red[1][warp][lane] = qx01.x;
+            s.red[1][warp][lane + 32] = qx01.y;
+            s.red[1][warp][lane + 64] = qx23.x;
+            s.red[1][warp][lane + 96] = qx23.y;
             __syncthreads();
             if (tid < FV) {
                 float ks = 0.f, qs = 0.f;
@@ -369,32 +428,33 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c) {
     }
 
     // ---- P2: rank-1 update; row sums of |x| in torch order; new row scales ---
-    float delta[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) delta[i] = s.colc[0][lane + 32 * i];
-    float *rowpart = reinterpret_cast<float *>(s.plane);
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-        const int k = warp * 16 + r;
-        const float kk = s.rowc[k].y;
-        float a = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            X[r][i] = __fmaf_rn(kk, delta[i], X[r][i]);
-            a = __fadd_rn(a, fabsf(X[r][i]));
-        }
-        rowpart[k * kRowPartStride + lane] = a;
-    }
-    if (MODE == kStep && p.dense_out) {
-        float *dst = p.dense_out + (int64_t(c.req) * H + c.head) * FK * FV;
-#pragma unroll
-        for (int r = 0; r < 16; ++r)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[(warp * 16 + r) * FV + lane + 32 * i] = X[r][i];
-    }
-    if (tid == 0) s.flags = 0;
-    __syncthreads();
     {
+        const float2 d01 = make_float2(s.colc[0][lane], s.colc[0][lane + 32]);
+        const float2 d23 = make_float2(s.colc[0][lane + 64], s.colc[0][lane + 96]);
+        float *rowpart = reinterpret_cast<float *>(s.plane);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int k = warp * 16 + r;
+            const float2 kk = hi2(s.rowa[k]);
+            X[r][0] = pfma2(kk, d01, X[r][0]);
+            X[r][1] = pfma2(kk, d23, X[r][1]);
+            const float a = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, fabsf(X[r][0].x)), fabsf(X[r][0].y)),
+                                                fabsf(X[r][1].x)), fabsf(X[r][1].y));
+            rowpart[k * kRowPartStride + lane] = a;
+        }
+        if (MODE == kStep && p.dense_out) {
+            float *dst = p.dense_out + (int64_t(c.req) * H + c.head) * FK * FV;
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                float *row = dst + (warp * 16 + r) * FV + lane;
+                row[0] = X[r][0].x;
+                row[32] = X[r][0].y;
+                row[64] = X[r][1].x;
+                row[96] = X[r][1].y;
+            }
+        }
+        if (tid == 0) s.flags = 0;
+        __syncthreads();
         // Lanes j and j+16 finish row 16*warp + j: S_l = ((A_l + A_{l+8}) + A_{l+16}) + A_{l+24},
         // total = S_0 + S_1 + ... + S_7 in order.
         const int j = lane & 15, half = lane >> 4;
@@ -414,18 +474,22 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c) {
             total = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(prefix, s0), s1), s2), s3);
             const float w = P.impact[c.head * FK + k];
             const float mean = __fdiv_rn(total, float(FV));
-            const float r = fp16_scale(__fsqrt_rn(__fdiv_rn(fmaxf(mean, 1e-20f), w)));
-            s.rowc[k] = make_float4(r, __frcp_rn(r), __fmul_rn(w, w), 0.f);
+            const float rr = fp16_scale(__fsqrt_rn(__fdiv_rn(fmaxf(mean, 1e-20f), w)));
+            const float rc = __frcp_rn(rr);
+            const float w2 = __fmul_rn(w, w);
+            s.rowa[k] = make_float4(rr, rr, rc, rc);
+            s.rowb[k] = make_float4(-rr, -rr, w2, w2);
             if (!(total <= 7.922816251426434e28f)) atomicOr(&s.flags, 1);  // 2^96, or NaN
         }
     }
     __syncthreads();
     if (s.flags) {
         // Pathological magnitudes: IEEE divisions for the whole tile.
-        fast_quantize<BITS, MODE, true>(p, s, c, X);
+        fast_quantize<true>(s, c, X, float(W<BITS>::off));
     } else {
-        fast_quantize<BITS, MODE, false>(p, s, c, X);
+        fast_quantize<false>(s, c, X, float(W<BITS>::off));
     }
+    fast_store<BITS>(p, s, c);
 }
 
 
@@ -495,10 +559,20 @@ cudaError_t launch_fast(int mode, const TileParams &p, int batch, cudaStream_t s
 
 
 namespace {
+// Lanes are processed in pairs through divide2 (the packed form the decode
+// kernels use); an odd tail element goes through the scalar div_fp16.
 __global__ void division_selftest_kernel(const float *a, const uint16_t *b, float *out, int64_t n) {
-    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
-        const float d = __half2float(__ushort_as_half(b[i]));
-        out[i] = div_fp16(a[i], d, __frcp_rn(d));
+    const int64_t pairs = n / 2;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < pairs; i += int64_t(gridDim.x) * blockDim.x) {
+        const float2 d = make_float2(__half2float(__ushort_as_half(b[2 * i])), __half2float(__ushort_as_half(b[2 * i + 1])));
+        const float2 rd = make_float2(__frcp_rn(d.x), __frcp_rn(d.y));
+        const float2 q = divide2<false>(make_float2(a[2 * i], a[2 * i + 1]), d, rd, make_float2(-d.x, -d.y));
+        out[2 * i] = q.x;
+        out[2 * i + 1] = q.y;
+    }
+    if (n & 1 && blockIdx.x == 0 && threadIdx.x == 0) {
+        const float d = __half2float(__ushort_as_half(b[n - 1]));
+        out[n - 1] = div_fp16(a[n - 1], d, __frcp_rn(d));
     }
 }
 }  // namespace
