@@ -48,8 +48,6 @@ struct FastSmem {
     float colc[4][FV];                                    // per-column constants
     __half rold[FK];
     __half cold[FV];
-    float qv[FK];
-    float kv[FK];
     float misc[64];
     int flags;
 };
@@ -94,6 +92,16 @@ __device__ __forceinline__ float2 divide2(float2 a, float2 b, float2 rb, float2 
     return pfma2(r, rb, q);
 }
 
+// Round-half-even to an integer on the FMA pipe: for |y| <= 2^22,
+// (y + 1.5*2^23) rounds y at the unit place (ties to even: 1.5*2^23 is even),
+// and subtracting the constant back is exact.  The integer also sits in the
+// low mantissa bits of the sum (two's complement low byte for |y| < 128).
+constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+__device__ __forceinline__ float2 round_sum2(float2 y) { return add_lanes(y, make_float2(kRound, kRound)); }
+__device__ __forceinline__ float2 clamp2(float2 y, float q) {
+    return make_float2(fminf(fmaxf(y.x, -q), q), fminf(fmaxf(y.y, -q), q));
+}
+
 __device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); }
 __device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
 
@@ -128,7 +136,15 @@ __device__ __forceinline__ float2 level_constants(int u) {
 // the page's 2*BITS-byte little-endian chunk.
 template <int BITS>
 __device__ __forceinline__ void store_chunk(uint8_t *dst, const unsigned char *plane_chunk) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(plane_chunk);
+    // Plane bytes are signed levels b in [-off, off]; code = b + off per byte:
+    // b ^ 0x80 = b + 128 (mod 256) lies in [128 - off, 128 + off], so
+    // subtracting 128 - off from every byte never borrows across bytes.
+    constexpr uint32_t sub = 0x01010101u * uint32_t(128 - W<BITS>::off);
+    uint4 w = *reinterpret_cast<const uint4 *>(plane_chunk);
+    w.x = (w.x ^ 0x80808080u) - sub;
+    w.y = (w.y ^ 0x80808080u) - sub;
+    w.z = (w.z ^ 0x80808080u) - sub;
+    w.w = (w.w ^ 0x80808080u) - sub;
     if (BITS == 8) {
         *reinterpret_cast<uint4 *>(dst) = w;
     } else if (BITS == 4) {
@@ -212,9 +228,9 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 
             for (int h = 0; h < 2; ++h) {
                 const float2 x = X[r][h];
                 const float2 sn = divide2<SLOW>(x, rn, hi2(a), lo2(b));
-                const float2 y = divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
-                float2 z = make_float2(rintf(y.x), rintf(y.y));
-                if (!no_clamp) z = make_float2(fminf(fmaxf(z.x, -qmax), qmax), fminf(fmaxf(z.y, -qmax), qmax));
+                float2 y = divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
+                if (!no_clamp) y = clamp2(y, qmax);  // rint(clamp(y)) == clamp(rint(y)) for integer bounds
+                const float2 z = add_lanes(round_sum2(y), make_float2(-kRound, -kRound));
                 const float2 v = pmul2(rn, z);
                 const float2 t = pmul2(pmul2(w2, v), x);
                 const float2 d = pmul2(w2, pmul2(v, v));
@@ -250,14 +266,13 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 
         s.colc[2][tid] = __frcp_rn(c1);
     }
     __syncthreads();
-    // P5: final levels -> one code byte (level + offset) per value in the plane.
+    // P5: final levels -> one signed level byte per value in the plane.
     {
         const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
         const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
         const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
         const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
         const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
-        const float2 magic = make_float2(8388608.f + qmax, 8388608.f + qmax);
         const int t0 = lane >> 4, u = lane & 15;
         unsigned char *plane = s.plane + t0 * (FK * 16 + kStagePad) + u;
 #pragma unroll
@@ -265,9 +280,8 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 
             const int k = warp * 16 + r;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const float2 y = divide2<SLOW>(X[r][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
-                const float2 z = make_float2(fminf(fmaxf(rintf(y.x), -qmax), qmax), fminf(fmaxf(rintf(y.y), -qmax), qmax));
-                const float2 code = add_lanes(z, magic);
+                const float2 y = clamp2(divide2<SLOW>(X[r][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), qmax);
+                const float2 code = round_sum2(y);  // low byte: the signed level (two's complement)
                 plane[(4 * h) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.x));
                 plane[(4 * h + 2) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.y));
             }
@@ -318,55 +332,68 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c) {
     }
 
     // ---- per-request inputs ------------------------------------------------
-    float beta = 0.f, qk = 0.f, decay = 1.f;
+    // Every global load is issued before anything waits on one; q, k and the
+    // dot products come out of a single block reduction; the gates are
+    // computed redundantly by every thread (no broadcast barrier).
+    float beta = 0.f, qk = 0.f, decay = 1.f, vin = 0.f, qx = 0.f, kx = 0.f;
     if (MODE == kWriteback) {
         const float *sc = p.scratch + int64_t(c.req) * p.scratch_stride + int64_t(c.head) * (FV + 2 * FK);
         if (tid < FK) {
             s.colc[0][tid] = sc[tid];          // delta
-            s.kv[tid] = sc[FV + tid];          // normalised k
+            kx = sc[FV + tid];                 // normalised k
         }
         decay = sc[FV + FK];
     } else {
         const sq_step_args &a = p.step;
         const int qh = c.head / (H / a.qk_heads);
-        float qq = 0.f, kk = 0.f, qkp = 0.f;
         if (tid < FK) {
-            const float qx = load_as_float(a.q, a.io_dtype, int64_t(c.req) * a.q_stride + int64_t(qh) * FK + tid);
-            const float kx = load_as_float(a.k, a.io_dtype, int64_t(c.req) * a.k_stride + int64_t(qh) * FK + tid);
-            s.qv[tid] = qx;
-            s.kv[tid] = kx;
-            qq = __fmul_rn(qx, qx);
-            kk = __fmul_rn(kx, kx);
-            s.colc[3][tid] = load_as_float(a.v, a.io_dtype, int64_t(c.req) * a.v_stride + int64_t(c.head) * FV + tid);
+            qx = load_as_float(a.q, a.io_dtype, int64_t(c.req) * a.q_stride + int64_t(qh) * FK + tid);
+            kx = load_as_float(a.k, a.io_dtype, int64_t(c.req) * a.k_stride + int64_t(qh) * FK + tid);
+            vin = load_as_float(a.v, a.io_dtype, int64_t(c.req) * a.v_stride + int64_t(c.head) * FV + tid);
         }
-        float qn = 1.f, kn = 1.f;
-        if (a.normalize) {
-            qn = __frsqrt_rn(block_sum(qq, s.misc) + 1e-6f);
-            kn = __frsqrt_rn(block_sum(kk, s.misc) + 1e-6f);
-        }
-        if (tid < FK) {
-            const float qx = __fmul_rn(__fmul_rn(s.qv[tid], qn), a.scale);
-            const float kx = __fmul_rn(s.kv[tid], kn);
-            s.qv[tid] = qx;
-            s.kv[tid] = kx;
-            qkp = __fmul_rn(qx, kx);
-        }
-        qk = block_sum(qkp, s.misc);
         const float braw = load_as_float(a.beta, a.gate_dtype, int64_t(c.req) * H + c.head);
-        beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
         float g = load_as_float(a.g, a.gate_dtype, int64_t(c.req) * H + c.head);
+        const float alog = a.a_log ? a.a_log[c.head] : 0.f;
+        const float bias = a.a_log ? a.dt_bias[c.head] : 0.f;
+        // Sum of q^2, k^2 and q.k over the block: warp shuffles, one barrier.
+        float3 part = make_float3(__fmul_rn(qx, qx), __fmul_rn(kx, kx), __fmul_rn(qx, kx));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            part.x += __shfl_xor_sync(0xffffffffu, part.x, o);
+            part.y += __shfl_xor_sync(0xffffffffu, part.y, o);
+            part.z += __shfl_xor_sync(0xffffffffu, part.z, o);
+        }
+        if (lane == 0) {
+            s.misc[4 * warp] = part.x;
+            s.misc[4 * warp + 1] = part.y;
+            s.misc[4 * warp + 2] = part.z;
+        }
+        beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
         if (a.a_log) {
-            const float u = g + a.dt_bias[c.head];
-            g = -expf(a.a_log[c.head]) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
+            const float u = g + bias;
+            g = -expf(alog) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
         }
         decay = expf(g);
+        __syncthreads();
+        float qq = 0.f, kk = 0.f, dot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) {
+            qq += s.misc[4 * w];
+            kk += s.misc[4 * w + 1];
+            dot += s.misc[4 * w + 2];
+        }
+        const float qn = a.normalize ? __frsqrt_rn(qq + 1e-6f) : 1.f;
+        const float kn = a.normalize ? __frsqrt_rn(kk + 1e-6f) : 1.f;
+        qx = __fmul_rn(__fmul_rn(qx, qn), a.scale);
+        kx = __fmul_rn(kx, kn);
+        qk = __fmul_rn(__fmul_rn(__fmul_rn(dot, qn), kn), a.scale);
     }
     cp_async_wait_all();
     __syncthreads();
     if (tid < FK) {
         const float rd = __fmul_rn(__half2float(s.rold[tid]), decay);
-        s.rowa[tid] = make_float4(rd, rd, s.kv[tid], s.kv[tid]);
-        s.rowb[tid] = make_float4(s.qv[tid], s.qv[tid], 0.f, 0.f);
+        s.rowa[tid] = make_float4(rd, rd, kx, kx);
+        s.rowb[tid] = make_float4(qx, qx, 0.f, 0.f);
     }
     __syncthreads();
 
@@ -411,14 +438,14 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c) {
                     ks = __fadd_rn(ks, s.red[0][w][tid]);
                     qs = __fadd_rn(qs, s.red[1][w][tid]);
                 }
-                const float delta = __fmul_rn(beta, __fsub_rn(s.colc[3][tid], ks));
+                const float delta = __fmul_rn(beta, __fsub_rn(vin, ks));
                 s.colc[0][tid] = delta;
                 const float out = __fmaf_rn(qk, delta, qs);
                 store_from_float(p.step.out, p.step.io_dtype, (int64_t(c.req) * H + c.head) * FV + tid, out);
                 if (MODE == kReadout) {
                     float *sc = p.scratch + int64_t(c.req) * p.scratch_stride + int64_t(c.head) * (FV + 2 * FK);
                     sc[tid] = delta;
-                    sc[FV + tid] = s.kv[tid];
+                    sc[FV + tid] = kx;
                     sc[FV + FK + tid] = decay;
                 }
             }
