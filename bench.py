@@ -34,6 +34,13 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "packed-state decode updates/s"
+_result_out = None
+
+
+def emit(line):
+    out = _result_out or sys.__stdout__
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 UNIT = "updates/s"
 
 
@@ -207,13 +214,15 @@ def reference_arm(args):
     res = cpu_reference(args, args.heads, args.qk_heads, args.steps, args.warmup,
                         max(20.0, args.cpu_seconds * 3))
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup,
+            # one full batch-step at the sampled rate
+            "ms_per_step": args.batch * args.heads / res["value"] * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "gdn-decode-b256-h32-k128 (config 1), CPU port of the reference torch path",
                        "batch": args.batch, "heads": args.heads, "qk_heads": args.qk_heads, "dim": args.dim},
             "cpu_baseline": res, "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -222,6 +231,13 @@ def reference_arm(args):
 
 def main():
     args = parse_args()
+    # Library and NCCL messages written to fd 1 go to stderr; the result line
+    # alone goes to the original stdout.
+    result_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
+    global _result_out
+    _result_out = result_out
     if args.impl == "reference":
         reference_arm(args)
         return
@@ -384,6 +400,11 @@ def main():
 
     page_bytes = pool.page_bytes
     page_io, other_io = algorithmic_bytes(page_bytes, heads_l, qk_l, batch, dim)
+    # Each rank's plan covers its own value heads: job totals are sums over ranks.
+    totals = torch.tensor([page_bytes, page_io + other_io], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(totals)
+    job_page_bytes, step_bytes = (int(t) for t in totals.tolist())
     peak, peak_kind = measured_peak()
     if args.mode == "sync":
         dominant, dom_bytes = "sq_step (fused)", page_io + other_io
@@ -410,7 +431,6 @@ def main():
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         cpu = cpu_reference(args, args.heads, args.qk_heads, 100, 1, args.cpu_seconds)
-    step_bytes = (page_io + other_io) * world
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
@@ -418,7 +438,7 @@ def main():
         "config": {"workload": "gdn-decode-b256-h32-k128 (config 1)", "batch": batch, "heads": args.heads,
                    "qk_heads": args.qk_heads, "dim": dim, "mode": args.mode, "writeback": args.mode == "async",
                    "plan": "stepquant6 synthetic, widths {4,6,8} 25/50/25, pivot heads %d" % args.pivot_heads,
-                   "page_bytes_per_request": page_bytes * world, "l2": "inputs > L2: slots rotate over %d groups "
+                   "page_bytes_per_request": job_page_bytes, "l2": "inputs > L2: slots rotate over %d groups "
                    "(%.0f MB of pages per GPU)" % (args.slot_groups, slots_total * page_bytes / 1e6),
                    "parallelism": f"tp{world} (value heads)"},
         "request_steps_per_s": value / args.heads,
@@ -433,7 +453,7 @@ def main():
         "gpu_launches": args.steps * (2 if args.mode == "async" else 1),
         "cpu_baseline": cpu,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 if __name__ == "__main__":
