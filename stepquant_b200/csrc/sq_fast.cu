@@ -306,11 +306,56 @@ __device__ __forceinline__ void fast_store(const TileParams &p, FastSmem &s, con
     }
 }
 
+// Stage the head's code bytes (cp.async, 16-byte pieces, one padded region per value tile).
+template <int BITS>
+__device__ __forceinline__ void stage_codes(FastSmem &s, const uint8_t *src, int tid) {
+    constexpr int pieces = W<BITS>::head_bytes / 16;
+    constexpr int per_tile = W<BITS>::tile_bytes / 16;
+    for (int j = tid; j < pieces; j += kThreads) {
+        const int t = j / per_tile, within = j % per_tile;
+        cp_async16(s.stage + t * (W<BITS>::tile_bytes + kStagePad) + within * 16, src + j * 16);
+    }
+}
+
+// P1 for one code width: unpack, dequantize and decay the warp's 16 rows into X
+// and accumulate the column partials of k^T S and q^T S.
+template <int BITS>
+__device__ __forceinline__ void unpack_rows(const FastSmem &s, int warp, int lane, float2 (&X)[16][2], float2 (&acc)[4]) {
+    const int t0 = lane >> 4, u = lane & 15;
+    const float2 cl01 = make_float2(__half2float(s.cold[lane]), __half2float(s.cold[lane + 32]));
+    const float2 cl23 = make_float2(__half2float(s.cold[lane + 64]), __half2float(s.cold[lane + 96]));
+    const float2 lc = level_constants<BITS>(u);
+    const float2 lscale = make_float2(lc.x, lc.x), lbias = make_float2(lc.y, lc.y);
+    float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const int k = warp * 16 + r;
+        const float4 a = s.rowa[k], b = s.rowb[k];
+        const float2 f01 = make_float2(staged_bits<BITS>(s.stage, t0, k, u), staged_bits<BITS>(s.stage, t0 + 2, k, u));
+        const float2 f23 = make_float2(staged_bits<BITS>(s.stage, t0 + 4, k, u), staged_bits<BITS>(s.stage, t0 + 6, k, u));
+        const float2 x01 = pmul2(pmul2(pfma2(f01, lscale, lbias), lo2(a)), cl01);
+        const float2 x23 = pmul2(pmul2(pfma2(f23, lscale, lbias), lo2(a)), cl23);
+        X[r][0] = x01;
+        X[r][1] = x23;
+        kx01 = pfma2(hi2(a), x01, kx01);
+        kx23 = pfma2(hi2(a), x23, kx23);
+        qx01 = pfma2(lo2(b), x01, qx01);
+        qx23 = pfma2(lo2(b), x23, qx23);
+    }
+    acc[0] = kx01;
+    acc[1] = kx23;
+    acc[2] = qx01;
+    acc[3] = qx23;
+}
+
 // ---------------------------------------------------------------------------
-// The per-head body.  MODE: kStep (fused), kReadout, kWriteback.
+// The per-head body.  MODE: kStep (fused), kReadout, kWriteback.  Only the
+// staging, unpack and pack steps depend on the code width; the prologue, the
+// update and the quantizer are one copy shared by every width, so CTAs of
+// different widths resident on one SM run the same instructions.
 // ---------------------------------------------------------------------------
-template <int BITS, int MODE>
-__device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c) {
+template <int MODE>
+__device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c, int width) {
     const sq_plan &P = p.plan;
     const int H = P.heads;
     const int warp = c.warp, lane = c.lane, tid = c.tid;
@@ -319,12 +364,9 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c) {
     // ---- stage the head's codes, r and c (cp.async, 16-byte pieces) --------
     {
         const uint8_t *src = page + c.off_head;
-        constexpr int pieces = W<BITS>::head_bytes / 16;
-        constexpr int per_tile = W<BITS>::tile_bytes / 16;
-        for (int j = tid; j < pieces; j += kThreads) {
-            const int t = j / per_tile, within = j % per_tile;
-            cp_async16(s.stage + t * (W<BITS>::tile_bytes + kStagePad) + within * 16, src + j * 16);
-        }
+        if (width == 4) stage_codes<4>(s, src, tid);
+        else if (width == 6) stage_codes<6>(s, src, tid);
+        else stage_codes<8>(s, src, tid);
         const int rowoff = P.rows[c.head * FK];
         const int coloff = P.columns[c.head];
         if (tid < 16) cp_async16(reinterpret_cast<unsigned char *>(s.rold) + tid * 16, page + rowoff + tid * 16);
@@ -399,37 +441,20 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c) {
 
     // ---- P1: unpack, dequantize, decay; column partials of k^T S and q^T S ---
     float2 X[16][2];
-    const int t0 = lane >> 4, u = lane & 15;
     {
-        const float2 cl01 = make_float2(__half2float(s.cold[lane]), __half2float(s.cold[lane + 32]));
-        const float2 cl23 = make_float2(__half2float(s.cold[lane + 64]), __half2float(s.cold[lane + 96]));
-        const float2 lc = level_constants<BITS>(u);
-        const float2 lscale = make_float2(lc.x, lc.x), lbias = make_float2(lc.y, lc.y);
-        float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int k = warp * 16 + r;
-            const float4 a = s.rowa[k], b = s.rowb[k];
-            const float2 f01 = make_float2(staged_bits<BITS>(s.stage, t0, k, u), staged_bits<BITS>(s.stage, t0 + 2, k, u));
-            const float2 f23 = make_float2(staged_bits<BITS>(s.stage, t0 + 4, k, u), staged_bits<BITS>(s.stage, t0 + 6, k, u));
-            const float2 x01 = pmul2(pmul2(pfma2(f01, lscale, lbias), lo2(a)), cl01);
-            const float2 x23 = pmul2(pmul2(pfma2(f23, lscale, lbias), lo2(a)), cl23);
-            X[r][0] = x01;
-            X[r][1] = x23;
-            kx01 = pfma2(hi2(a), x01, kx01);
-            kx23 = pfma2(hi2(a), x23, kx23);
-            qx01 = pfma2(lo2(b), x01, qx01);
-            qx23 = pfma2(lo2(b), x23, qx23);
-        }
+        float2 acc[4];
+        if (width == 4) unpack_rows<4>(s, warp, lane, X, acc);
+        else if (width == 6) unpack_rows<6>(s, warp, lane, X, acc);
+        else unpack_rows<8>(s, warp, lane, X, acc);
         if (MODE != kWriteback) {
-            s.red[0][warp][lane] = kx01.x;
-            s.red[0][warp][lane + 32] = kx01.y;
-            s.red[0][warp][lane + 64] = kx23.x;
-            s.red[0][warp][lane + 96] = kx23.y;
-            s.red[1][warp][lane] = qx01.x;
-            s.red[1][warp][lane + 32] = qx01.y;
-            s.red[1][warp][lane + 64] = qx23.x;
-            s.red[1][warp][lane + 96] = qx23.y;
+            s.red[0][warp][lane] = acc[0].x;
+            s.red[0][warp][lane + 32] = acc[0].y;
+            s.red[0][warp][lane + 64] = acc[1].x;
+            s.red[0][warp][lane + 96] = acc[1].y;
+            s.red[1][warp][lane] = acc[2].x;
+            s.red[1][warp][lane + 32] = acc[2].y;
+            s.red[1][warp][lane + 64] = acc[3].x;
+            s.red[1][warp][lane + 96] = acc[3].y;
             __syncthreads();
             if (tid < FV) {
                 float ks = 0.f, qs = 0.f;
@@ -510,13 +535,16 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c) {
         }
     }
     __syncthreads();
+    const float qmax = float((1 << (width - 1)) - 1);
     if (s.flags) {
         // Pathological magnitudes: IEEE divisions for the whole tile.
-        fast_quantize<true>(s, c, X, float(W<BITS>::off));
+        fast_quantize<true>(s, c, X, qmax);
     } else {
-        fast_quantize<false>(s, c, X, float(W<BITS>::off));
+        fast_quantize<false>(s, c, X, qmax);
     }
-    fast_store<BITS>(p, s, c);
+    if (width == 4) fast_store<4>(p, s, c);
+    else if (width == 6) fast_store<6>(p, s, c);
+    else fast_store<8>(p, s, c);
 }
 
 
@@ -552,9 +580,7 @@ __global__ void __launch_bounds__(kThreads, 2) fast_kernel(TileParams p) {
     }
     c.page = p.pages + c.slot * P.page_bytes;
     c.off_head = P.offsets[c.head * FK];
-    if (width == 4) fast_body<4, MODE>(p, s, c);
-    else if (width == 6) fast_body<6, MODE>(p, s, c);
-    else fast_body<8, MODE>(p, s, c);
+    fast_body<MODE>(p, s, c, width);
 }
 
 template <int MODE>
