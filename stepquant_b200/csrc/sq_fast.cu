@@ -1,7 +1,9 @@
 // Register-resident decode kernels for GDN heads with K = V = 128 and a code
 // width of 4, 6 or 8 bits (the served shape of Qwen-Next-style layers).
 //
-// One 256-thread CTA per (request, value head); two CTAs per SM.  Warp w owns
+// Persistent 256-thread CTAs, two per SM, each walking (request, value head)
+// items; the next item's page bytes and inputs are prefetched (cp.async) into
+// a second stage buffer while the current item is computed.  Warp w owns
 // key rows 16w..16w+15 and lane l owns value columns l, l+32, l+64, l+96, so
 // each thread keeps 64 state elements in registers for the whole step.  That
 // mapping makes both ordered sums of fit_state local:
@@ -17,6 +19,9 @@
 // rounding midpoint, far outside the error of the corrected estimate, so the
 // result equals IEEE a/b (tests/test_gpu_fast.py checks it against __fdiv_rn).
 // Rows whose |x| sum exceeds 2^96 switch the CTA to IEEE divisions.
+#include <algorithm>
+#include <atomic>
+
 #include "sq_tile.cuh"
 
 namespace sq {
@@ -39,16 +44,33 @@ struct W {
     static constexpr int off = (1 << (BITS - 1)) - 1;
 };
 
-struct FastSmem {
-    unsigned char stage[kTiles * (FK * 16 + kStagePad)];  // old packed codes, padded per tile
-    unsigned char plane[kPlaneBytes];                     // row partials, then new code bytes
-    float red[2][8][FV];                                  // per-warp column partials
-    float4 rowa[FK];                                      // per-row constants, duplicated pairs:
-    float4 rowb[FK];                                      //   P1: {rd, rd, k, k} {q, q, -, -}; P3-P5: {r, r, 1/r, 1/r} {-r, -r, w2, w2}
-    float colc[4][FV];                                    // per-column constants
+// What one item needs from global memory, staged by cp.async one item ahead.
+struct FastStage {
+    unsigned char codes[kTiles * (FK * 16 + kStagePad)];  // old packed codes, padded per tile
     __half rold[FK];
     __half cold[FV];
+    float in[3][FK];  // raw q, k, v (io dtype); writeback: delta, k, decay
+    float imp[FK];    // the head's row impact weights
+    float gate[4];    // raw beta and g (fp32 gates)
+};
+
+// Per-head constants, read once per CTA.
+constexpr int kMaxHeads = 128;
+struct HeadInfo {
+    int width, off_head, rows, columns;
+    float a_log, dt_bias;
+};
+
+struct FastSmem {
+    FastStage st[2];
+    unsigned char plane[kPlaneBytes];  // row partials, then new code bytes
+    float red[2][8][FV];               // per-warp column partials
+    float4 rowa[FK];                   // per-row constants, duplicated pairs:
+    float4 rowb[FK];                   //   P1: {r_old, r_old, k, k} {q, q, -, -}; P3-P5: {r, r, 1/r, 1/r} {-r, -r, w2, w2}
+    float colc[4][FV];                 // per-column constants
     float misc[64];
+    HeadInfo head[kMaxHeads];
+    long long slot_ring[3];  // slots of the current and next two items (cp.async)
     int flags;
 };
 
@@ -56,10 +78,17 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\n" ::);
-    asm volatile("cp.async.wait_group 0;\n" ::);
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
 }
+__device__ __forceinline__ void cp_async8(void *smem, const void *gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
 // Packed f32x2 arithmetic (sm_100): two independent IEEE round-to-nearest lanes.
 // Caution: ptxas (CUDA 12.9) fuses a packed multiply whose result feeds a
@@ -173,10 +202,77 @@ struct Ctx {
     int off_head;
 };
 
+// Exact sum terms: a product formed by an FFMA2 with a +0 addend (the same
+// rounding as the product alone; ptxas does not merge it into the following
+// add) accumulated with a packed add.
+__device__ __forceinline__ float2 product_term(float2 a, float2 b) { return pfma2(a, b, make_float2(0.f, 0.f)); }
+
+// P4 body: first levels z = rint(clamp(x / r / c0)) and the weighted
+// least-squares numerator / denominator of the warp's 16-row block.  X holds x
+// on entry and x / r on exit.
+template <bool SLOW, bool CLAMP>
+__device__ __forceinline__ void first_levels(const FastSmem &s, int warp, int lane, float2 (&X)[16][2], float qmax,
+                                             float2 (&num)[2], float2 (&den)[2]) {
+    const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
+    const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
+    const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
+    const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
+    const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
+    const float2 round = make_float2(kRound, kRound), nround = make_float2(-kRound, -kRound);
+    num[0] = num[1] = den[0] = den[1] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const float4 a = s.rowa[warp * 16 + r], b = s.rowb[warp * 16 + r];
+        const float2 rn = lo2(a), w2 = hi2(b);
+        // v = rn * z with z = S - 1.5*2^23: one rounding of rn*S - rn*1.5*2^23,
+        // whose second product is exact (rn has 11 significant bits).
+        const float2 nrk = pmul2(rn, nround);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float2 x = X[r][h];
+            const float2 sn = divide2<SLOW>(x, rn, hi2(a), lo2(b));
+            float2 y = divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
+            if (CLAMP) y = clamp2(y, qmax);  // rint(clamp(y)) == clamp(rint(y)) for integer bounds
+            const float2 v = pfma2(rn, __fadd2_rn(y, round), nrk);
+            num[h] = __fadd2_rn(num[h], product_term(pmul2(w2, v), x));
+            den[h] = __fadd2_rn(den[h], product_term(w2, pmul2(v, v)));
+            X[r][h] = sn;
+        }
+    }
+}
+
+// P5 body: final levels -> one signed level byte per value in the plane.
+template <bool SLOW, bool CLAMP>
+__device__ __forceinline__ void final_levels(FastSmem &s, int warp, int lane, const float2 (&X)[16][2], float qmax) {
+    const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
+    const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
+    const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
+    const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
+    const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
+    const float2 round = make_float2(kRound, kRound);
+    const int t0 = lane >> 4, u = lane & 15;
+    unsigned char *plane = s.plane + t0 * (FK * 16 + kStagePad) + u;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const int k = warp * 16 + r;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float2 y = divide2<SLOW>(X[r][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
+            if (CLAMP) y = clamp2(y, qmax);
+            const float2 code = __fadd2_rn(y, round);  // low byte: the signed level (two's complement)
+            plane[(4 * h) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.x));
+            plane[(4 * h + 2) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.y));
+        }
+    }
+}
+
 // P3-P5 (shared by every width): column max -> c0; first levels and the
 // weighted least-squares sums -> c1; final code bytes -> plane.  X holds the
 // updated state on entry and x / r on exit.  Packed f32x2 lanes are the column
-// pairs (l, l+32) and (l+64, l+96).
+// pairs (l, l+32) and (l+64, l+96).  The clamps to [-qmax, qmax] are skipped
+// when no level of the tile can reach qmax + 1/2: every |x/r| is at most the
+// column maximum M, so |x/r/c| <= RN(M/c) (division and rounding are monotone).
+// The IEEE-division path (huge or NaN rows) always clamps.
 template <bool SLOW>
 __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 (&X)[16][2], float qmax) {
     const int warp = c.warp, lane = c.lane, tid = c.tid;
@@ -200,60 +296,34 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 
     }
     __syncthreads();
     int safe = 1;
+    float mx = 0.f;
     if (tid < FV) {
-        float mx = 0.f;
 #pragma unroll
         for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
         const float ratio = __fdiv_rn(mx, qmax);
         const float c0 = fp16_scale(ratio);
         s.colc[1][tid] = c0;
         s.colc[2][tid] = __frcp_rn(c0);
-        // With c0 a normal, unclamped fp16 value every |x/r/c0| < qmax + 1/2: no clamp needed.
+        // With c0 a normal, unclamped fp16 value every |x/r/c0| < qmax + 1/2.
         safe = (c0 >= 6.103515625e-05f) && (ratio <= 65504.f);
     }
     const bool no_clamp = __syncthreads_and(safe);
     // P4: first levels, weighted least-squares numerator / denominator (16-row blocks).
     {
-        const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
-        const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
-        const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
-        const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
-        const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
-        float2 num01 = make_float2(0.f, 0.f), num23 = num01, den01 = num01, den23 = num01;
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const float4 a = s.rowa[warp * 16 + r], b = s.rowb[warp * 16 + r];
-            const float2 rn = lo2(a), w2 = hi2(b);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const float2 x = X[r][h];
-                const float2 sn = divide2<SLOW>(x, rn, hi2(a), lo2(b));
-                float2 y = divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
-                if (!no_clamp) y = clamp2(y, qmax);  // rint(clamp(y)) == clamp(rint(y)) for integer bounds
-                const float2 z = add_lanes(round_sum2(y), make_float2(-kRound, -kRound));
-                const float2 v = pmul2(rn, z);
-                const float2 t = pmul2(pmul2(w2, v), x);
-                const float2 d = pmul2(w2, pmul2(v, v));
-                if (h) {
-                    num23 = add_lanes(num23, t);
-                    den23 = add_lanes(den23, d);
-                } else {
-                    num01 = add_lanes(num01, t);
-                    den01 = add_lanes(den01, d);
-                }
-                X[r][h] = sn;
-            }
-        }
-        s.red[0][warp][lane] = num01.x;
-        s.red[0][warp][lane + 32] = num01.y;
-        s.red[0][warp][lane + 64] = num23.x;
-        s.red[0][warp][lane + 96] = num23.y;
-        s.red[1][warp][lane] = den01.x;
-        s.red[1][warp][lane + 32] = den01.y;
-        s.red[1][warp][lane + 64] = den23.x;
-        s.red[1][warp][lane + 96] = den23.y;
+        float2 num[2], den[2];
+        if (!SLOW && no_clamp) first_levels<SLOW, false>(s, warp, lane, X, qmax, num, den);
+        else first_levels<SLOW, true>(s, warp, lane, X, qmax, num, den);
+        s.red[0][warp][lane] = num[0].x;
+        s.red[0][warp][lane + 32] = num[0].y;
+        s.red[0][warp][lane + 64] = num[1].x;
+        s.red[0][warp][lane + 96] = num[1].y;
+        s.red[1][warp][lane] = den[0].x;
+        s.red[1][warp][lane + 32] = den[0].y;
+        s.red[1][warp][lane + 64] = den[1].x;
+        s.red[1][warp][lane + 96] = den[1].y;
     }
     __syncthreads();
+    safe = 1;
     if (tid < FV) {
         float num = 0.f, den = 0.f;
 #pragma unroll
@@ -264,29 +334,12 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 
         const float c1 = den > 0.f ? fp16_scale(__fdiv_rn(num, fmaxf(den, 1e-30f))) : s.colc[1][tid];
         s.colc[1][tid] = c1;
         s.colc[2][tid] = __frcp_rn(c1);
+        safe = (c1 >= 6.103515625e-05f) && (__fdiv_rn(mx, c1) < qmax + 0.5f);
     }
-    __syncthreads();
+    const bool no_clamp5 = __syncthreads_and(safe);
     // P5: final levels -> one signed level byte per value in the plane.
-    {
-        const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
-        const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
-        const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
-        const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
-        const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
-        const int t0 = lane >> 4, u = lane & 15;
-        unsigned char *plane = s.plane + t0 * (FK * 16 + kStagePad) + u;
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int k = warp * 16 + r;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const float2 y = clamp2(divide2<SLOW>(X[r][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), qmax);
-                const float2 code = round_sum2(y);  // low byte: the signed level (two's complement)
-                plane[(4 * h) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.x));
-                plane[(4 * h + 2) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.y));
-            }
-        }
-    }
+    if (!SLOW && no_clamp5) final_levels<SLOW, false>(s, warp, lane, X, qmax);
+    else final_levels<SLOW, true>(s, warp, lane, X, qmax);
     __syncthreads();
 }
 
@@ -308,22 +361,21 @@ __device__ __forceinline__ void fast_store(const TileParams &p, FastSmem &s, con
 
 // Stage the head's code bytes (cp.async, 16-byte pieces, one padded region per value tile).
 template <int BITS>
-__device__ __forceinline__ void stage_codes(FastSmem &s, const uint8_t *src, int tid) {
+__device__ __forceinline__ void stage_codes(FastStage &st, const uint8_t *src, int tid) {
     constexpr int pieces = W<BITS>::head_bytes / 16;
     constexpr int per_tile = W<BITS>::tile_bytes / 16;
     for (int j = tid; j < pieces; j += kThreads) {
         const int t = j / per_tile, within = j % per_tile;
-        cp_async16(s.stage + t * (W<BITS>::tile_bytes + kStagePad) + within * 16, src + j * 16);
+        cp_async16(st.codes + t * (W<BITS>::tile_bytes + kStagePad) + within * 16, src + j * 16);
     }
 }
 
-// P1 for one code width: unpack, dequantize and decay the warp's 16 rows into X
-// and accumulate the column partials of k^T S and q^T S.
+// P1 for one code width: unpack the warp's 16 rows into X = level * r_old and
+// accumulate the column partials of k_raw^T X and q_raw^T X.
 template <int BITS>
-__device__ __forceinline__ void unpack_rows(const FastSmem &s, int warp, int lane, float2 (&X)[16][2], float2 (&acc)[4]) {
+__device__ __forceinline__ void unpack_rows(const FastSmem &s, const FastStage &st, int warp, int lane,
+                                            float2 (&X)[16][2], float2 (&acc)[4]) {
     const int t0 = lane >> 4, u = lane & 15;
-    const float2 cl01 = make_float2(__half2float(s.cold[lane]), __half2float(s.cold[lane + 32]));
-    const float2 cl23 = make_float2(__half2float(s.cold[lane + 64]), __half2float(s.cold[lane + 96]));
     const float2 lc = level_constants<BITS>(u);
     const float2 lscale = make_float2(lc.x, lc.x), lbias = make_float2(lc.y, lc.y);
     float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
@@ -331,10 +383,10 @@ __device__ __forceinline__ void unpack_rows(const FastSmem &s, int warp, int lan
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
         const float4 a = s.rowa[k], b = s.rowb[k];
-        const float2 f01 = make_float2(staged_bits<BITS>(s.stage, t0, k, u), staged_bits<BITS>(s.stage, t0 + 2, k, u));
-        const float2 f23 = make_float2(staged_bits<BITS>(s.stage, t0 + 4, k, u), staged_bits<BITS>(s.stage, t0 + 6, k, u));
-        const float2 x01 = pmul2(pmul2(pfma2(f01, lscale, lbias), lo2(a)), cl01);
-        const float2 x23 = pmul2(pmul2(pfma2(f23, lscale, lbias), lo2(a)), cl23);
+        const float2 f01 = make_float2(staged_bits<BITS>(st.codes, t0, k, u), staged_bits<BITS>(st.codes, t0 + 2, k, u));
+        const float2 f23 = make_float2(staged_bits<BITS>(st.codes, t0 + 4, k, u), staged_bits<BITS>(st.codes, t0 + 6, k, u));
+        const float2 x01 = pmul2(pfma2(f01, lscale, lbias), lo2(a));
+        const float2 x23 = pmul2(pfma2(f23, lscale, lbias), lo2(a));
         X[r][0] = x01;
         X[r][1] = x23;
         kx01 = pfma2(hi2(a), x01, kx01);
@@ -348,6 +400,72 @@ __device__ __forceinline__ void unpack_rows(const FastSmem &s, int warp, int lan
     acc[3] = qx23;
 }
 
+// One (request, head) work item of the persistent loop.
+struct WorkItem {
+    int req, head, width;
+    int64_t slot;
+    bool fast;    // code width handled by these kernels (else the tile kernel's)
+    bool active;  // 0 < slot < num_slots
+};
+
+__device__ __forceinline__ WorkItem describe(const TileParams &p, const FastSmem &s, int item, long long slot) {
+    WorkItem it;
+    const int H = p.plan.heads;
+    it.req = item / H;
+    it.head = item - it.req * H;
+    it.slot = slot;
+    it.width = s.head[it.head].width;
+    it.fast = it.width == 4 || it.width == 6 || it.width == 8;
+    it.active = it.slot > 0 && it.slot < p.num_slots;
+    return it;
+}
+
+// Issue the cp.async copies of everything item `it` reads: its code bytes, the
+// old r and c, and (when the host found them 16-byte aligned) the request's
+// q, k, v and fp32 gates, or for the writeback the readout's delta, k and decay.
+// Threads 0-31 copy r and c, 32-127 the inputs, 128-129 the gates, 160-191
+// the impact row.
+template <int MODE>
+__device__ __forceinline__ void prefetch(const TileParams &p, const FastSmem &s, FastStage &st, const WorkItem &it, int tid) {
+    const sq_plan &P = p.plan;
+    const HeadInfo &hi = s.head[it.head];
+    const uint8_t *page = p.pages + it.slot * P.page_bytes;
+    const uint8_t *src = page + hi.off_head;
+    if (it.width == 4) stage_codes<4>(st, src, tid);
+    else if (it.width == 6) stage_codes<6>(st, src, tid);
+    else stage_codes<8>(st, src, tid);
+    if (tid < 16) cp_async16(reinterpret_cast<unsigned char *>(st.rold) + tid * 16, page + hi.rows + tid * 16);
+    else if (tid < 32) cp_async16(reinterpret_cast<unsigned char *>(st.cold) + (tid - 16) * 16, page + hi.columns + (tid - 16) * 16);
+    if (MODE != kReadout && tid >= 160 && tid < 192)
+        cp_async16(reinterpret_cast<unsigned char *>(st.imp) + (tid - 160) * 16, P.impact + int64_t(it.head) * FK + (tid - 160) * 4);
+    if (!p.stage_inputs) return;
+    unsigned char *in = reinterpret_cast<unsigned char *>(st.in);
+    const int j = tid - 32;
+    if (MODE == kWriteback) {
+        // delta[V], k[K], decay: 65 pieces of the request's scratch row.
+        const float *sc = p.scratch + int64_t(it.req) * p.scratch_stride + int64_t(it.head) * (FV + 2 * FK);
+        if (j >= 0 && j < 65) cp_async16(in + j * 16, sc + j * 4);
+    } else {
+        const sq_step_args &a = p.step;
+        const int esize = a.io_dtype == SQ_F32 ? 4 : 2;
+        const int pieces = FK * esize / 16;
+        if (j >= 0 && j < 3 * pieces) {
+            const int which = j / pieces, piece = j - which * pieces;
+            const int qh = it.head / (P.heads / a.qk_heads);
+            const unsigned char *base =
+                which == 0 ? static_cast<const unsigned char *>(a.q) + (int64_t(it.req) * a.q_stride + int64_t(qh) * FK) * esize
+                : which == 1 ? static_cast<const unsigned char *>(a.k) + (int64_t(it.req) * a.k_stride + int64_t(qh) * FK) * esize
+                             : static_cast<const unsigned char *>(a.v) + (int64_t(it.req) * a.v_stride + int64_t(it.head) * FV) * esize;
+            cp_async16(in + which * (FK * 4) + piece * 16, base + piece * 16);
+        }
+        if (p.stage_gates) {
+            const int64_t g = int64_t(it.req) * P.heads + it.head;
+            if (tid == 128) cp_async4(&st.gate[0], static_cast<const float *>(a.beta) + g);
+            else if (tid == 129) cp_async4(&st.gate[1], static_cast<const float *>(a.g) + g);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // The per-head body.  MODE: kStep (fused), kReadout, kWriteback.  Only the
 // staging, unpack and pack steps depend on the code width; the prologue, the
@@ -355,50 +473,50 @@ __device__ __forceinline__ void unpack_rows(const FastSmem &s, int warp, int lan
 // different widths resident on one SM run the same instructions.
 // ---------------------------------------------------------------------------
 template <int MODE>
-__device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c, int width) {
+__device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st, const Ctx &c, int width) {
     const sq_plan &P = p.plan;
     const int H = P.heads;
     const int warp = c.warp, lane = c.lane, tid = c.tid;
-    uint8_t *page = c.page;
 
-    // ---- stage the head's codes, r and c (cp.async, 16-byte pieces) --------
-    {
-        const uint8_t *src = page + c.off_head;
-        if (width == 4) stage_codes<4>(s, src, tid);
-        else if (width == 6) stage_codes<6>(s, src, tid);
-        else stage_codes<8>(s, src, tid);
-        const int rowoff = P.rows[c.head * FK];
-        const int coloff = P.columns[c.head];
-        if (tid < 16) cp_async16(reinterpret_cast<unsigned char *>(s.rold) + tid * 16, page + rowoff + tid * 16);
-        else if (tid < 32) cp_async16(reinterpret_cast<unsigned char *>(s.cold) + (tid - 16) * 16, page + coloff + (tid - 16) * 16);
-    }
-
-    // ---- per-request inputs ------------------------------------------------
-    // Every global load is issued before anything waits on one; q, k and the
-    // dot products come out of a single block reduction; the gates are
-    // computed redundantly by every thread (no broadcast barrier).
-    float beta = 0.f, qk = 0.f, decay = 1.f, vin = 0.f, qx = 0.f, kx = 0.f;
+    // ---- per-request inputs -------------------------------------------------
+    // P1 works on Y = level * r_old (no decay, no column scale) with raw q and
+    // k, so it needs nothing computed here: the gate and norm chains overlap
+    // with the unpack.  The updated state is x' = Y * (c * decay) + k * delta,
+    // and k^T (D S) = kn * (c * decay) * sum_k(k_raw * Y) (likewise for q).
+    float vin = 0.f, kraw = 0.f, braw = 0.f, graw = 0.f;
     if (MODE == kWriteback) {
         const float *sc = p.scratch + int64_t(c.req) * p.scratch_stride + int64_t(c.head) * (FV + 2 * FK);
         if (tid < FK) {
-            s.colc[0][tid] = sc[tid];          // delta
-            kx = sc[FV + tid];                 // normalised k
+            const float delta = p.stage_inputs ? st.in[0][tid] : sc[tid];
+            const float kx = p.stage_inputs ? st.in[1][tid] : sc[FV + tid];  // normalised k
+            const float decay = p.stage_inputs ? st.in[2][0] : sc[FV + FK];
+            const float ro = __half2float(st.rold[tid]);
+            s.rowa[tid] = make_float4(ro, ro, kx, kx);
+            s.colc[0][tid] = delta;
+            s.colc[3][tid] = __fmul_rn(__half2float(st.cold[tid]), decay);
         }
-        decay = sc[FV + FK];
     } else {
         const sq_step_args &a = p.step;
-        const int qh = c.head / (H / a.qk_heads);
+        float qraw = 0.f;
         if (tid < FK) {
-            qx = load_as_float(a.q, a.io_dtype, int64_t(c.req) * a.q_stride + int64_t(qh) * FK + tid);
-            kx = load_as_float(a.k, a.io_dtype, int64_t(c.req) * a.k_stride + int64_t(qh) * FK + tid);
-            vin = load_as_float(a.v, a.io_dtype, int64_t(c.req) * a.v_stride + int64_t(c.head) * FV + tid);
+            if (p.stage_inputs) {
+                qraw = load_as_float(st.in[0], a.io_dtype, tid);
+                kraw = load_as_float(st.in[1], a.io_dtype, tid);
+                vin = load_as_float(st.in[2], a.io_dtype, tid);
+            } else {
+                const int qh = c.head / (H / a.qk_heads);
+                qraw = load_as_float(a.q, a.io_dtype, int64_t(c.req) * a.q_stride + int64_t(qh) * FK + tid);
+                kraw = load_as_float(a.k, a.io_dtype, int64_t(c.req) * a.k_stride + int64_t(qh) * FK + tid);
+                vin = load_as_float(a.v, a.io_dtype, int64_t(c.req) * a.v_stride + int64_t(c.head) * FV + tid);
+            }
+            const float ro = __half2float(st.rold[tid]);
+            s.rowa[tid] = make_float4(ro, ro, kraw, kraw);
+            s.rowb[tid] = make_float4(qraw, qraw, 0.f, 0.f);
         }
-        const float braw = load_as_float(a.beta, a.gate_dtype, int64_t(c.req) * H + c.head);
-        float g = load_as_float(a.g, a.gate_dtype, int64_t(c.req) * H + c.head);
-        const float alog = a.a_log ? a.a_log[c.head] : 0.f;
-        const float bias = a.a_log ? a.dt_bias[c.head] : 0.f;
-        // Sum of q^2, k^2 and q.k over the block: warp shuffles, one barrier.
-        float3 part = make_float3(__fmul_rn(qx, qx), __fmul_rn(kx, kx), __fmul_rn(qx, kx));
+        braw = p.stage_gates ? st.gate[0] : load_as_float(a.beta, a.gate_dtype, int64_t(c.req) * H + c.head);
+        graw = p.stage_gates ? st.gate[1] : load_as_float(a.g, a.gate_dtype, int64_t(c.req) * H + c.head);
+        // Per-warp sums of q^2, k^2 and q.k (combined after the next barrier).
+        float3 part = make_float3(__fmul_rn(qraw, qraw), __fmul_rn(kraw, kraw), __fmul_rn(qraw, kraw));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             part.x += __shfl_xor_sync(0xffffffffu, part.x, o);
@@ -410,43 +528,18 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c, int wi
             s.misc[4 * warp + 1] = part.y;
             s.misc[4 * warp + 2] = part.z;
         }
-        beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
-        if (a.a_log) {
-            const float u = g + bias;
-            g = -expf(alog) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
-        }
-        decay = expf(g);
-        __syncthreads();
-        float qq = 0.f, kk = 0.f, dot = 0.f;
-#pragma unroll
-        for (int w = 0; w < kThreads / 32; ++w) {
-            qq += s.misc[4 * w];
-            kk += s.misc[4 * w + 1];
-            dot += s.misc[4 * w + 2];
-        }
-        const float qn = a.normalize ? __frsqrt_rn(qq + 1e-6f) : 1.f;
-        const float kn = a.normalize ? __frsqrt_rn(kk + 1e-6f) : 1.f;
-        qx = __fmul_rn(__fmul_rn(qx, qn), a.scale);
-        kx = __fmul_rn(kx, kn);
-        qk = __fmul_rn(__fmul_rn(__fmul_rn(dot, qn), kn), a.scale);
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    if (tid < FK) {
-        const float rd = __fmul_rn(__half2float(s.rold[tid]), decay);
-        s.rowa[tid] = make_float4(rd, rd, kx, kx);
-        s.rowb[tid] = make_float4(qx, qx, 0.f, 0.f);
     }
     __syncthreads();
 
-    // ---- P1: unpack, dequantize, decay; column partials of k^T S and q^T S ---
+    // ---- P1: unpack; column partials of k_raw^T Y and q_raw^T Y ---------------
     float2 X[16][2];
     {
         float2 acc[4];
-        if (width == 4) unpack_rows<4>(s, warp, lane, X, acc);
-        else if (width == 6) unpack_rows<6>(s, warp, lane, X, acc);
-        else unpack_rows<8>(s, warp, lane, X, acc);
+        if (width == 4) unpack_rows<4>(s, st, warp, lane, X, acc);
+        else if (width == 6) unpack_rows<6>(s, st, warp, lane, X, acc);
+        else unpack_rows<8>(s, st, warp, lane, X, acc);
         if (MODE != kWriteback) {
+            const sq_step_args &a = p.step;
             s.red[0][warp][lane] = acc[0].x;
             s.red[0][warp][lane + 32] = acc[0].y;
             s.red[0][warp][lane + 64] = acc[1].x;
@@ -455,7 +548,28 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c, int wi
             s.red[1][warp][lane + 32] = acc[2].y;
             s.red[1][warp][lane + 64] = acc[3].x;
             s.red[1][warp][lane + 96] = acc[3].y;
+            // Gates (every thread; independent of the unpack above).
+            const float alog = s.head[c.head].a_log;
+            const float bias = s.head[c.head].dt_bias;
+            const float beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
+            float g = graw;
+            if (a.a_log) {
+                const float u = g + bias;
+                g = -expf(alog) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
+            }
+            const float decay = expf(g);
             __syncthreads();
+            float qq = 0.f, kk = 0.f, dot = 0.f;
+#pragma unroll
+            for (int w = 0; w < kThreads / 32; ++w) {
+                qq += s.misc[4 * w];
+                kk += s.misc[4 * w + 1];
+                dot += s.misc[4 * w + 2];
+            }
+            const float qn = a.normalize ? __frsqrt_rn(qq + 1e-6f) : 1.f;
+            const float kn = a.normalize ? __frsqrt_rn(kk + 1e-6f) : 1.f;
+            const float qscale = __fmul_rn(qn, a.scale);
+            const float qk = __fmul_rn(__fmul_rn(__fmul_rn(dot, qn), kn), a.scale);
             if (tid < FV) {
                 float ks = 0.f, qs = 0.f;
 #pragma unroll
@@ -463,10 +577,16 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c, int wi
                     ks = __fadd_rn(ks, s.red[0][w][tid]);
                     qs = __fadd_rn(qs, s.red[1][w][tid]);
                 }
-                const float delta = __fmul_rn(beta, __fsub_rn(vin, ks));
+                const float cd = __fmul_rn(__half2float(st.cold[tid]), decay);
+                const float kS = __fmul_rn(__fmul_rn(ks, kn), cd);      // k^T (D S)
+                const float qS = __fmul_rn(__fmul_rn(qs, qscale), cd);  // q^T (D S)
+                const float delta = __fmul_rn(beta, __fsub_rn(vin, kS));
+                const float kx = __fmul_rn(kraw, kn);  // row tid of the normalised k
                 s.colc[0][tid] = delta;
-                const float out = __fmaf_rn(qk, delta, qs);
-                store_from_float(p.step.out, p.step.io_dtype, (int64_t(c.req) * H + c.head) * FV + tid, out);
+                s.colc[3][tid] = cd;
+                s.rowa[tid].z = kx;
+                s.rowa[tid].w = kx;
+                store_from_float(a.out, a.io_dtype, (int64_t(c.req) * H + c.head) * FV + tid, __fmaf_rn(qk, delta, qS));
                 if (MODE == kReadout) {
                     float *sc = p.scratch + int64_t(c.req) * p.scratch_stride + int64_t(c.head) * (FV + 2 * FK);
                     sc[tid] = delta;
@@ -483,13 +603,15 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c, int wi
     {
         const float2 d01 = make_float2(s.colc[0][lane], s.colc[0][lane + 32]);
         const float2 d23 = make_float2(s.colc[0][lane + 64], s.colc[0][lane + 96]);
+        const float2 cd01 = make_float2(s.colc[3][lane], s.colc[3][lane + 32]);
+        const float2 cd23 = make_float2(s.colc[3][lane + 64], s.colc[3][lane + 96]);
         float *rowpart = reinterpret_cast<float *>(s.plane);
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
             const int k = warp * 16 + r;
             const float2 kk = hi2(s.rowa[k]);
-            X[r][0] = pfma2(kk, d01, X[r][0]);
-            X[r][1] = pfma2(kk, d23, X[r][1]);
+            X[r][0] = pfma2(kk, d01, pmul2(X[r][0], cd01));
+            X[r][1] = pfma2(kk, d23, pmul2(X[r][1], cd23));
             const float a = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, fabsf(X[r][0].x)), fabsf(X[r][0].y)),
                                                 fabsf(X[r][1].x)), fabsf(X[r][1].y));
             rowpart[k * kRowPartStride + lane] = a;
@@ -524,7 +646,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c, int wi
         const float prefix = __shfl_sync(0xffffffffu, total, j);
         if (half) {
             total = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(prefix, s0), s1), s2), s3);
-            const float w = P.impact[c.head * FK + k];
+            const float w = st.imp[k];
             const float mean = __fdiv_rn(total, float(FV));
             const float rr = fp16_scale(__fsqrt_rn(__fdiv_rn(fmaxf(mean, 1e-20f), w)));
             const float rc = __frcp_rn(rr);
@@ -547,9 +669,12 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const Ctx &c, int wi
     else fast_store<8>(p, s, c);
 }
 
-
+// Persistent loop: CTA b takes items b, b + gridDim.x, ... (item = request * H
+// + head).  While one item is computed the next one's data is in flight into
+// the other stage buffer, and the slot of the item after that into a small
+// ring, so each item starts with its page, scales and inputs on chip.
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 2) fast_kernel(TileParams p) {
+__global__ void __launch_bounds__(kThreads, MODE == kReadout ? 3 : 2) fast_kernel(TileParams p, int items) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FastSmem &s = *reinterpret_cast<FastSmem *>(smem_raw);
     const sq_plan &P = p.plan;
@@ -558,50 +683,133 @@ __global__ void __launch_bounds__(kThreads, 2) fast_kernel(TileParams p) {
     c.tid = threadIdx.x;
     c.warp = c.tid >> 5;
     c.lane = c.tid & 31;
-    c.req = blockIdx.x / H;
-    c.head = blockIdx.x % H;
-    c.slot = p.slots[c.req];
-    if (MODE == kReadout && c.head == 0 && c.tid == 0) p.stable_slots[c.req] = c.slot;
-    const int width = P.bits[c.head * FK];
-    if (width != 4 && width != 6 && width != 8) return;  // handled by the tile kernel
-    bool active = c.slot > 0;
-    if (active && c.slot >= p.num_slots) {
-        if (c.tid == 0) flag(p.status, SQ_STATUS_SLOT_RANGE);
-        active = false;
+    int item = blockIdx.x;
+    if (item >= items) return;
+    const int stride = gridDim.x;
+    for (int h = c.tid; h < H; h += kThreads) {
+        HeadInfo hi;
+        hi.width = P.bits[h * FK];
+        hi.off_head = P.offsets[h * FK];
+        hi.rows = P.rows[h * FK];
+        hi.columns = P.columns[h];
+        const bool gates = MODE != kWriteback && p.step.a_log;
+        hi.a_log = gates ? p.step.a_log[h] : 0.f;
+        hi.dt_bias = gates ? p.step.dt_bias[h] : 0.f;
+        s.head[h] = hi;
     }
-    if (!active) {
-        if (MODE != kWriteback && c.tid < FV)
-            store_from_float(p.step.out, p.step.io_dtype, (int64_t(c.req) * H + c.head) * FV + c.tid, 0.f);
-        if (MODE == kStep && p.dense_out) {
-            float *dst = p.dense_out + (int64_t(c.req) * H + c.head) * FK * FV;
-            for (int e = c.tid; e < FK * FV; e += kThreads) dst[e] = 0.f;
+    if (c.tid == 0) {
+        cp_async8(&s.slot_ring[0], p.slots + item / H);
+        if (item + stride < items) cp_async8(&s.slot_ring[1], p.slots + (item + stride) / H);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    long long slot = s.slot_ring[0];
+    {
+        const WorkItem first = describe(p, s, item, slot);
+        if (first.fast && first.active) prefetch<MODE>(p, s, s.st[0], first, c.tid);
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+    }
+    // Invariant at the top of round r: the current item's data is in s.st[buf],
+    // and the next item's slot is in slot_ring[(r + 1) % 3].  Round r fills
+    // entry (r + 2) % 3, last read before the barrier that ended round r - 1.
+    int buf = 0, ring = 0;  // ring = r % 3
+    for (; item < items; item += stride) {
+        const int ring1 = ring == 2 ? 0 : ring + 1, ring2 = ring1 == 2 ? 0 : ring1 + 1;
+        const int next_item = item + stride;
+        if (next_item < items) {
+            const WorkItem nxt = describe(p, s, next_item, s.slot_ring[ring1]);
+            if (nxt.fast && nxt.active) prefetch<MODE>(p, s, s.st[buf ^ 1], nxt, c.tid);
+            if (c.tid == 0 && next_item + stride < items)
+                cp_async8(&s.slot_ring[ring2], p.slots + (next_item + stride) / H);
         }
-        return;
+        cp_async_commit();
+        const WorkItem cur = describe(p, s, item, slot);
+        c.req = cur.req;
+        c.head = cur.head;
+        c.slot = cur.slot;
+        if (MODE == kReadout && c.head == 0 && c.tid == 0) p.stable_slots[c.req] = c.slot;
+        if (cur.fast) {
+            if (cur.active) {
+                c.page = p.pages + c.slot * P.page_bytes;
+                c.off_head = s.head[c.head].off_head;
+                fast_body<MODE>(p, s, s.st[buf], c, cur.width);
+            } else {
+                if (cur.slot > 0 && c.tid == 0) flag(p.status, SQ_STATUS_SLOT_RANGE);
+                if (MODE != kWriteback && c.tid < FV)
+                    store_from_float(p.step.out, p.step.io_dtype, (int64_t(c.req) * H + c.head) * FV + c.tid, 0.f);
+                if (MODE == kStep && p.dense_out) {
+                    float *dst = p.dense_out + (int64_t(c.req) * H + c.head) * FK * FV;
+                    for (int e = c.tid; e < FK * FV; e += kThreads) dst[e] = 0.f;
+                }
+            }
+        }
+        cp_async_wait<0>();  // the next item's data and the slot after it
+        __syncthreads();     // ... visible to all; the stage buffer just read is free
+        slot = s.slot_ring[ring1];
+        buf ^= 1;
+        ring = ring1;
     }
-    c.page = p.pages + c.slot * P.page_bytes;
-    c.off_head = P.offsets[c.head * FK];
-    fast_body<MODE>(p, s, c, width);
 }
+
+// Resident CTAs per device for each mode (set up on the first launch on a device).
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_resident[3][kMaxDevices];
 
 template <int MODE>
 cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream) {
     const int smem = int(sizeof(FastSmem));
-    cudaError_t err = cudaFuncSetAttribute(fast_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
     if (err != cudaSuccess) return err;
-    fast_kernel<MODE><<<items, kThreads, smem, stream>>>(p);
+    std::atomic<int> *resident = device < kMaxDevices ? &g_resident[MODE - kStep][device] : nullptr;
+    int ctas = resident ? resident->load(std::memory_order_relaxed) : 0;
+    if (ctas == 0) {
+        err = cudaFuncSetAttribute(fast_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (err != cudaSuccess) return err;
+        int sms = 0, per_sm = 0;
+        if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return err;
+        if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fast_kernel<MODE>, kThreads, smem)) != cudaSuccess)
+            return err;
+        ctas = sms * std::max(1, per_sm);
+        if (resident) resident->store(ctas, std::memory_order_relaxed);
+    }
+    const int grid = std::max(1, std::min(items, ctas));
+    fast_kernel<MODE><<<grid, kThreads, smem, stream>>>(p, items);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 bool fast_eligible(const sq_plan &plan, const void *pages) {
-    return plan.architecture == SQ_GDN && plan.keys == FK && plan.values == FV && plan.page_bytes % 16 == 0 &&
+    return plan.architecture == SQ_GDN && plan.keys == FK && plan.values == FV && plan.heads <= kMaxHeads &&
+           plan.page_bytes % 16 == 0 &&
            (reinterpret_cast<uintptr_t>(pages) & 15u) == 0;
 }
 
-cudaError_t launch_fast(int mode, const TileParams &p, int batch, cudaStream_t stream) {
-    const int items = batch * p.plan.heads;
+namespace {
+bool aligned16(const void *ptr, int64_t stride_bytes) {
+    return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0 && stride_bytes % 16 == 0;
+}
+}  // namespace
+
+cudaError_t launch_fast(int mode, const TileParams &params, int batch, cudaStream_t stream) {
+    const int items = batch * params.plan.heads;
     if (items <= 0) return cudaSuccess;
+    TileParams p = params;
+    if (mode == kWriteback) {
+        p.stage_inputs = aligned16(p.scratch, p.scratch_stride * 4);
+        p.stage_gates = 0;
+    } else {
+        const sq_step_args &a = p.step;
+        const int64_t esize = a.io_dtype == SQ_F32 ? 4 : 2;
+        p.stage_inputs = aligned16(a.q, a.q_stride * esize) && aligned16(a.k, a.k_stride * esize) &&
+                         aligned16(a.v, a.v_stride * esize);
+        p.stage_gates = a.gate_dtype == SQ_F32 && (reinterpret_cast<uintptr_t>(a.g) & 3u) == 0 &&
+                        (reinterpret_cast<uintptr_t>(a.beta) & 3u) == 0;
+    }
     switch (mode) {
         case kStep: return launch_fast_mode<kStep>(p, items, stream);
         case kReadout: return launch_fast_mode<kReadout>(p, items, stream);

@@ -27,6 +27,8 @@ struct TileParams {
     float *fit_recon;
     int32_t *status;
     int skip_fast;  // tile kernel: leave heads that fast_head() accepts to the fast kernel
+    int stage_inputs;  // fast kernels: q/k/v (or writeback scratch) rows are 16-byte aligned -> cp.async staging
+    int stage_gates;   // fast kernels: fp32 gates -> cp.async staging
 };
 
 size_t tile_smem_bytes(int K, int V, int groups);
