@@ -239,6 +239,53 @@ int32_t sq_fp32_step(float *state, int64_t num_slots, int32_t heads, int32_t key
                      int32_t *status, sq_stream_t stream);
 
 /*
+ * GDN chunked prefill: the state pass that produces each sequence's state
+ * after its prompt.  It replaces the SGLang chunk kernel
+ * (TritonGDNKernel.extend) that stepquant/sglang/runtime.py:193-202 calls
+ * between PackedStatePool.decode and PackedStatePool.encode; the recurrence
+ * is core.delta_step (stepquant/core.py:5-15) applied token by token.
+ * Tokens of num_seqs sequences are concatenated: sequence n owns tokens
+ * [cu_seqlens[n], cu_seqlens[n+1]), clamped to [0, tokens).
+ *   q, k   [tokens, qk_heads, keys] bf16, token rows q_stride / k_stride
+ *          elements apart (16-byte aligned rows)
+ *   v      [tokens, heads, values] bf16, rows v_stride apart
+ *   g      [tokens, heads] fp32 log decay; beta [tokens, heads] fp32
+ *   initial_state [num_seqs, heads, keys, values] fp32, or NULL for zeros
+ *   final_state   [num_seqs, heads, keys, values] fp32 (may equal initial_state)
+ *   out    [tokens, heads, values] bf16: o_t = q_t^T S_t
+ * normalize: q and k are L2 normalised per token (eps 1e-6), q is then
+ * multiplied by scale.  Value head h reads qk head h / (heads / qk_heads).
+ * The pass runs in 64-token chunks in the WY/UT form on tensor cores (bf16
+ * operands, fp32 accumulation; the state is carried in fp32).
+ * keys = values = 128 only (SQ_ERR_UNSUPPORTED otherwise).
+ */
+typedef struct sq_prefill_args {
+    const void *q;
+    const void *k;
+    const void *v;
+    int64_t q_stride;
+    int64_t k_stride;
+    int64_t v_stride;
+    int32_t io_dtype; /* SQ_BF16 */
+    int32_t qk_heads;
+    int32_t heads;
+    int32_t keys;
+    int32_t values;
+    int32_t normalize;
+    float scale;
+    int32_t num_seqs;
+    int32_t tokens;
+    const int32_t *cu_seqlens;
+    const float *g;
+    const float *beta;
+    const float *initial_state;
+    float *final_state;
+    void *out;
+} sq_prefill_args;
+
+int32_t sq_gdn_prefill(const sq_prefill_args *args, sq_stream_t stream);
+
+/*
  * Self-test of the division used by the register-resident decode kernels: for
  * i < n, out[i] = a[i] / b[i] computed with a correctly rounded reciprocal of
  * the fp16 value b[i] (given as its bits) and one Markstein correction.  It

@@ -613,3 +613,39 @@ def impact_factors(omega, gamma=0.25, floor=1e-20):
     """core.py:27-29."""
     log_w = np.log(np.maximum(np.asarray(omega, np.float64), floor)) * (gamma / 2)
     return np.exp(log_w - log_w.mean(-1, keepdims=True)).astype(F32)
+
+
+def prefill_sequential(q, k, v, g, beta, cu_seqlens, initial_state=None, scale=None, normalize=True):
+    """Token-by-token prefill recurrence of adapters.RecurrentKernel (adapters.py:36-60).
+
+    q, k: [tokens, HK, K]; v: [tokens, H, V]; g (log decay), beta: [tokens, H];
+    cu_seqlens: [N + 1] sequence boundaries; initial_state: [N, H, K, V] or None.
+    q and k are L2 normalised (eps 1e-6) when ``normalize``, q is then scaled
+    (default K^-0.5); value head h reads qk head h // (H / HK).  Each token is
+    one core.delta_step.  Returns (out [tokens, H, V], final [N, H, K, V]).
+    """
+    q = np.asarray(q, F32)
+    k = np.asarray(k, F32)
+    v = np.asarray(v, F32)
+    g = np.asarray(g, F32)
+    beta = np.asarray(beta, F32)
+    tokens, hk, keys = q.shape
+    heads, values = v.shape[1], v.shape[2]
+    scale = keys ** -0.5 if scale is None else scale
+    if normalize:
+        q = (q / np.sqrt((q.astype(np.float64) ** 2).sum(-1, keepdims=True) + 1e-6)).astype(F32)
+        k = (k / np.sqrt((k.astype(np.float64) ** 2).sum(-1, keepdims=True) + 1e-6)).astype(F32)
+    q = (q * F32(scale)).astype(F32)
+    q = np.repeat(q, heads // hk, axis=1)
+    k = np.repeat(k, heads // hk, axis=1)
+    bounds = np.asarray(cu_seqlens, np.int64)
+    out = np.zeros((tokens, heads, values), F32)
+    finals = []
+    for n in range(len(bounds) - 1):
+        state = (np.zeros((1, heads, keys, values), F32) if initial_state is None
+                 else np.asarray(initial_state, F32)[n:n + 1].copy())
+        for t in range(bounds[n], bounds[n + 1]):
+            y, state = delta_step(state, q[t:t + 1], k[t:t + 1], v[t:t + 1], g[t:t + 1], beta[t:t + 1])
+            out[t] = y[0]
+        finals.append(state[0])
+    return out, np.stack(finals) if finals else np.zeros((0, heads, keys, values), F32)

@@ -1,0 +1,93 @@
+"""GDN chunked prefill: the state pass that produces a prompt's first state.
+
+The reference runs SGLang's chunk kernel (``TritonGDNKernel.extend``) between
+``PackedStatePool.decode`` and ``PackedStatePool.encode``
+(stepquant/sglang/runtime.py:193-202); the recurrence it evaluates is
+core.delta_step token by token, as the reference's own
+``adapters.RecurrentKernel`` (stepquant/adapters.py:36-60) applies it.  Here
+``sq_gdn_prefill`` evaluates it in 64-token chunks (WY/UT form) on tensor cores
+with bf16 operands and fp32 accumulation and an fp32 state.
+
+``chunk_gated_delta_rule`` keeps the keyword names of that recurrent kernel
+(``initial_state``, ``output_final_state``, ``use_qk_l2norm_in_kernel``,
+``scale``, ``cu_seqlens``); ``PackedStatePool.extend`` is the decode -> chunk
+pass -> encode sequence of the reference hook.
+"""
+import ctypes
+
+import torch
+
+from .. import _native as N
+
+
+def _rows(x, name):
+    """[1, T, heads, dim] or [T, heads, dim] -> bf16 [T, heads, dim] with unit inner stride."""
+    if x.dim() == 4:
+        if x.shape[0] != 1:
+            raise ValueError(f"{name}: expected a leading batch of 1 (concatenated sequences)")
+        x = x[0]
+    if x.dim() != 3:
+        raise ValueError(f"{name}: expected [tokens, heads, dim]")
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    if x.stride(-1) != 1 or x.stride(1) != x.shape[2] or (x.stride(0) * 2) % 16 or x.data_ptr() % 16:
+        x = x.contiguous()
+    return x
+
+
+def _gates(x, tokens, heads, name):
+    if x.dim() == 3:
+        if x.shape[0] != 1:
+            raise ValueError(f"{name}: expected a leading batch of 1")
+        x = x[0]
+    if tuple(x.shape) != (tokens, heads):
+        raise ValueError(f"{name}: expected [tokens, heads] = {(tokens, heads)}, got {tuple(x.shape)}")
+    return x.float().contiguous()
+
+
+def chunk_gated_delta_rule(q, k, v, g, beta, *, scale=None, initial_state=None, output_final_state=True,
+                           use_qk_l2norm_in_kernel=True, cu_seqlens=None):
+    """GDN prefill over concatenated sequences.
+
+    q, k: [1, T, HK, 128] or [T, HK, 128]; v: [.., T, H, 128] (bf16; other
+    dtypes are converted); g (log decay), beta: [.., T, H]; cu_seqlens: int
+    [N + 1] sequence boundaries (default: one sequence of T tokens);
+    initial_state: [N, H, 128, 128] fp32 or None (zeros).  Returns
+    (o [.., T, H, 128] bf16 shaped like v, final_state [N, H, 128, 128] fp32
+    or None when ``output_final_state`` is false).
+    """
+    batched = v.dim() == 4
+    qr, kr, vr = _rows(q, "q"), _rows(k, "k"), _rows(v, "v")
+    tokens, heads, values = vr.shape
+    qk_heads, keys = qr.shape[1], qr.shape[2]
+    if tuple(kr.shape) != (tokens, qk_heads, keys) or qr.shape[0] != tokens:
+        raise ValueError("q, k and v must cover the same tokens, q and k the same heads")
+    if heads % qk_heads:
+        raise ValueError("value heads must be a multiple of qk heads")
+    if keys != 128 or values != 128:
+        raise NotImplementedError("chunked prefill is built for keys = values = 128")
+    device = vr.device
+    N.require_cuda(qr, kr, vr)
+    gr, br = _gates(g, tokens, heads, "g"), _gates(beta, tokens, heads, "beta")
+    if cu_seqlens is None:
+        cu_seqlens = torch.tensor([0, tokens], device=device, dtype=torch.int32)
+    cu = cu_seqlens.to(device=device, dtype=torch.int32).contiguous()
+    seqs = cu.numel() - 1
+    if seqs < 0:
+        raise ValueError("cu_seqlens needs at least one entry")
+    final = torch.empty(seqs, heads, keys, values, device=device, dtype=torch.float32)
+    init = None
+    if initial_state is not None:
+        if tuple(initial_state.shape) != (seqs, heads, keys, values):
+            raise ValueError(f"initial_state must be {(seqs, heads, keys, values)}")
+        init = initial_state.float().contiguous()
+    out = torch.empty(tokens, heads, values, device=device, dtype=torch.bfloat16)
+    args = N.SqPrefillArgs(qr.data_ptr(), kr.data_ptr(), vr.data_ptr(), qr.stride(0), kr.stride(0), vr.stride(0),
+                           N.SQ_BF16, qk_heads, heads, keys, values, 1 if use_qk_l2norm_in_kernel else 0,
+                           keys ** -0.5 if scale is None else float(scale), seqs, tokens, cu.data_ptr(), gr.data_ptr(),
+                           br.data_ptr(), init.data_ptr() if init is not None else None, final.data_ptr(),
+                           out.data_ptr())
+    N.check(N.lib().sq_gdn_prefill(ctypes.byref(args), N.stream_handle()))
+    if batched:
+        out = out.unsqueeze(0)
+    return out, (final if output_final_state else None)

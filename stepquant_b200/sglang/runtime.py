@@ -220,11 +220,16 @@ def kernel_packed_decode(original, self, mixed_qkv, a, b, *, A_log, dt_bias, sca
 
 
 def kernel_extend(original, self, q, k, v, g, beta, *, ssm_states, cache_indices, query_start_loc, **kwargs):
-    """Prefill: decode the active pages, let the native chunk kernel run on the dense
-    V-first state, then encode the final state back into the pages."""
+    """Prefill.  GDN pools with K = V = 128 run the chunked state pass of this
+    library (``PackedStatePool.extend``: decode, chunk pass with in-kernel q/k
+    L2 normalisation, encode).  Other packed pools decode the active pages, let
+    the original chunk kernel update the dense V-first state in place, and
+    encode the final state back into the pages (runtime.py:193-202)."""
     if not isinstance(ssm_states, PackedStatePool):
         return original(self, q, k, v, g, beta, ssm_states=ssm_states, cache_indices=cache_indices,
                         query_start_loc=query_start_loc, **kwargs)
+    if ssm_states.plan.architecture == "gdn" and ssm_states.keys == 128 and ssm_states.values == 128:
+        return ssm_states.extend(q, k, v, g, beta, cache_indices, query_start_loc, normalize=True)
     active = ssm_states.decode(cache_indices).transpose(-1, -2).contiguous()
     indices = torch.arange(cache_indices.numel(), device=cache_indices.device, dtype=cache_indices.dtype)
     output = original(self, q, k, v, g, beta, ssm_states=active, cache_indices=indices,

@@ -1,8 +1,7 @@
 """Generate golden vectors from the unmodified reference STEPQuant (torch CPU path).
 
 Run from the repository root in a container where the reference checkout is
-available (its path is given by ``--reference``; it defaults to the
-read-only mount used when these fixtures were produced):
+available (its path is given by ``--reference``):
 
     python tests/golden/make_golden.py --reference <path to the STEPQuant checkout>
 
@@ -19,6 +18,11 @@ Files written next to this script:
 * ``config0.npz``    -- the CPU reference plumbing case (GDN, B=4, H=HK=4,
                         K=V=128, seed 0): warm-up state, calibrated plan,
                         decode inputs, the updated state and its fitted codes.
+* ``prefill.npz``    -- ``stepquant.adapters.RecurrentKernel`` (the token-by-
+                        token prefill recurrence) on bf16-valued q/k/v with
+                        in-kernel L2 normalisation: outputs and final states.
+
+``--prefill-only`` rewrites ``prefill.npz`` alone.
 """
 import argparse
 import json
@@ -80,11 +84,39 @@ def layout_cases():
     return cases
 
 
+def prefill_cases(RecurrentKernel):
+    """Two sequences' worth of seeded prompts through the reference recurrence."""
+    out = {}
+    gen = torch.Generator().manual_seed(3)
+    for name, tokens, initial in (("a", 150, True), ("b", 64, False)):
+        heads, keys, values = 2, 128, 128
+        q = torch.randn(1, tokens, heads, keys, generator=gen).bfloat16().float()
+        k = torch.randn(1, tokens, heads, keys, generator=gen).bfloat16().float()
+        v = torch.randn(1, tokens, heads, values, generator=gen).bfloat16().float()
+        a_log = torch.rand(heads, generator=gen) * math.log(16)
+        g = -a_log.exp() * torch.nn.functional.softplus(torch.randn(1, tokens, heads, generator=gen))
+        beta = torch.randn(1, tokens, heads, generator=gen).sigmoid()
+        state = torch.randn(1, heads, keys, values, generator=gen) * 0.1 if initial else None
+        o, final = RecurrentKernel("gdn")(q, k, v, g, beta, initial_state=state, output_final_state=True,
+                                          use_qk_l2norm_in_kernel=True)
+        out.update({f"{name}_{n}": t.numpy() for n, t in dict(q=q, k=k, v=v, g=g, beta=beta, out=o, final=final).items()})
+        if initial:
+            out[f"{name}_initial"] = state.numpy()
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="path of the STEPQuant checkout")
+    parser.add_argument("--prefill-only", action="store_true")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
+    if args.prefill_only:
+        from stepquant.adapters import RecurrentKernel
+        torch.set_num_threads(1)
+        np.savez_compressed(os.path.join(HERE, "prefill.npz"), **prefill_cases(RecurrentKernel))
+        print("prefill vectors written to", HERE)
+        return
     torch.set_num_threads(1)
     from stepquant.quantization import QuantizationPlan, StateCodec, fit_state
     from stepquant.packing import pack
@@ -194,6 +226,8 @@ def main():
         q=q.numpy(), k=k.numpy(), v=v.float().numpy(), a=a.numpy(), b=b.numpy(),
         a_log=a_log.numpy(), dt_bias=dt_bias.numpy(), out=out.numpy(), updated=updated.numpy(),
         z=z.numpy().astype(np.int8), r=r.numpy(), c=c.numpy())
+    from stepquant.adapters import RecurrentKernel
+    np.savez_compressed(os.path.join(HERE, "prefill.npz"), **prefill_cases(RecurrentKernel))
     print("golden vectors written to", HERE)
 
 

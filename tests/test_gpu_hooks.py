@@ -5,10 +5,10 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _plan(heads=4, keys=128):
+def _plan(heads=4, keys=128, arch="gdn"):
     from stepquant_b200 import QuantizationPlan
     bits = torch.tensor([4, 6, 8, 6])[:heads, None].expand(heads, keys).clone()
-    return QuantizationPlan("gdn", bits.cuda(), (torch.rand(heads, keys) + 0.5).cuda())
+    return QuantizationPlan(arch, bits.cuda(), (torch.rand(heads, keys) + 0.5).cuda())
 
 
 def test_packed_decode_hook_equals_pool_step():
@@ -35,11 +35,12 @@ def test_packed_decode_hook_equals_pool_step():
 
 
 def test_extend_hook_round_trips_pages_through_native_kernel():
+    """KDA pools: the original chunk kernel runs on the decoded V-first state."""
     from stepquant_b200.kernels.pool import PackedStatePool
     from stepquant_b200.sglang import runtime
     torch.manual_seed(1)
     heads, keys, batch = 4, 128, 3
-    plan = _plan(heads, keys)
+    plan = _plan(heads, keys, "kda")
     pool = PackedStatePool(plan, batch + 1, keys)
     slots = torch.tensor([2, 3, 1], device="cuda")
     seen = {}
@@ -58,6 +59,31 @@ def test_extend_hook_round_trips_pages_through_native_kernel():
     expected = PackedStatePool(plan, batch + 1, keys)
     expected.encode(before * 0.5, slots)
     assert torch.equal(pool.data, expected.data)
+
+
+def test_extend_hook_runs_native_gdn_prefill():
+    """GDN pools: the hook is PackedStatePool.extend (decode, chunk pass, encode)."""
+    from stepquant_b200.kernels.pool import PackedStatePool
+    from stepquant_b200.sglang import runtime
+    torch.manual_seed(3)
+    heads, qk, keys = 4, 2, 128
+    plan = _plan(heads, keys)
+    pools = [PackedStatePool(plan, 5, keys) for _ in range(2)]
+    slots = torch.tensor([3, 1], device="cuda")
+    cu = torch.tensor([0, 70, 90], device="cuda", dtype=torch.int32)
+    q, k = (torch.randn(1, 90, qk, keys, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    v = torch.randn(1, 90, heads, keys, device="cuda", dtype=torch.bfloat16)
+    g = -torch.rand(1, 90, heads, device="cuda")
+    beta = torch.rand(1, 90, heads, device="cuda")
+
+    def original(*args, **kwargs):
+        raise AssertionError("GDN prefill must not call the original kernel")
+
+    out = runtime.kernel_extend(original, None, q, k, v, g, beta, ssm_states=pools[0], cache_indices=slots,
+                                query_start_loc=cu)
+    ref = pools[1].extend(q, k, v, g, beta, slots, cu)
+    assert out.shape == (1, 90, heads, keys)
+    assert torch.equal(out, ref) and torch.equal(pools[0].data, pools[1].data)
 
 
 @pytest.mark.parametrize("arch", ["gdn", "kda"])

@@ -151,3 +151,14 @@ def test_zero_state_encodes_finite():
         x = np.zeros((2,) + b.shape + (16,), np.float32)
         dec = O.codec_decode(O.codec_encode(x, plan), plan)
         assert np.isfinite(dec).all() and np.abs(dec).max() < 1e-10
+
+
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_prefill_oracle_matches_reference_recurrent_kernel(case):
+    """oracle.prefill_sequential vs stepquant.adapters.RecurrentKernel (150 / 64 tokens)."""
+    d = load_golden("prefill.npz")
+    q, k, v, g, beta = (d[f"{case}_{n}"][0] for n in ("q", "k", "v", "g", "beta"))
+    init = d[f"{case}_initial"] if f"{case}_initial" in d else None
+    out, final = O.prefill_sequential(q, k, v, g, beta, [0, q.shape[0]], init)
+    np.testing.assert_allclose(final, d[f"{case}_final"], rtol=0, atol=1e-5 * np.abs(d[f"{case}_final"]).max())
+    np.testing.assert_allclose(out, d[f"{case}_out"][0], rtol=0, atol=1e-5 * np.abs(d[f"{case}_out"]).max())
