@@ -255,8 +255,12 @@ int32_t sq_fp32_step(float *state, int64_t num_slots, int32_t heads, int32_t key
  *   out    [tokens, heads, values] bf16: o_t = q_t^T S_t
  * normalize: q and k are L2 normalised per token (eps 1e-6), q is then
  * multiplied by scale.  Value head h reads qk head h / (heads / qk_heads).
+ *   workspace  caller-owned device buffer of at least
+ *          sq_gdn_prefill_workspace_bytes(tokens, num_seqs, heads) bytes,
+ *          256-byte aligned (per-chunk intermediates; SQ_ERR_CAPACITY if short)
  * The pass runs in 64-token chunks in the WY/UT form on tensor cores (bf16
- * operands, fp32 accumulation; the state is carried in fp32).
+ * operands, fp32 accumulation; the state is carried in fp32): one kernel
+ * prepares every chunk in parallel, a second walks each sequence's chunks.
  * keys = values = 128 only (SQ_ERR_UNSUPPORTED otherwise).
  */
 typedef struct sq_prefill_args {
@@ -281,8 +285,11 @@ typedef struct sq_prefill_args {
     const float *initial_state;
     float *final_state;
     void *out;
+    void *workspace;
+    int64_t workspace_bytes;
 } sq_prefill_args;
 
+int64_t sq_gdn_prefill_workspace_bytes(int32_t tokens, int32_t num_seqs, int32_t heads);
 int32_t sq_gdn_prefill(const sq_prefill_args *args, sq_stream_t stream);
 
 /*

@@ -40,7 +40,8 @@ class SqPrefillArgs(ctypes.Structure):
     _fields_ = [("q", _p), ("k", _p), ("v", _p), ("q_stride", _i64), ("k_stride", _i64), ("v_stride", _i64),
                 ("io_dtype", _i32), ("qk_heads", _i32), ("heads", _i32), ("keys", _i32), ("values", _i32),
                 ("normalize", _i32), ("scale", ctypes.c_float), ("num_seqs", _i32), ("tokens", _i32), ("cu_seqlens", _p),
-                ("g", _p), ("beta", _p), ("initial_state", _p), ("final_state", _p), ("out", _p)]
+                ("g", _p), ("beta", _p), ("initial_state", _p), ("final_state", _p), ("out", _p),
+                ("workspace", _p), ("workspace_bytes", _i64)]
 
 
 _SIGNATURES = {
@@ -62,6 +63,7 @@ _SIGNATURES = {
     "sq_noalloc_scratch_bytes": (_i64, []),
     "sq_selftest_fp16_division": (_i32, [_p, _p, _p, _i64, _p]),
     "sq_gdn_prefill": (_i32, [_p, _p]),
+    "sq_gdn_prefill_workspace_bytes": (_i64, [_i32, _i32, _i32]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -82,11 +82,13 @@ def chunk_gated_delta_rule(q, k, v, g, beta, *, scale=None, initial_state=None, 
             raise ValueError(f"initial_state must be {(seqs, heads, keys, values)}")
         init = initial_state.float().contiguous()
     out = torch.empty(tokens, heads, values, device=device, dtype=torch.bfloat16)
+    workspace = torch.empty(max(N.lib().sq_gdn_prefill_workspace_bytes(tokens, seqs, heads), 1), device=device,
+                            dtype=torch.uint8)
     args = N.SqPrefillArgs(qr.data_ptr(), kr.data_ptr(), vr.data_ptr(), qr.stride(0), kr.stride(0), vr.stride(0),
                            N.SQ_BF16, qk_heads, heads, keys, values, 1 if use_qk_l2norm_in_kernel else 0,
                            keys ** -0.5 if scale is None else float(scale), seqs, tokens, cu.data_ptr(), gr.data_ptr(),
                            br.data_ptr(), init.data_ptr() if init is not None else None, final.data_ptr(),
-                           out.data_ptr())
+                           out.data_ptr(), workspace.data_ptr(), workspace.numel())
     N.check(N.lib().sq_gdn_prefill(ctypes.byref(args), N.stream_handle()))
     if batched:
         out = out.unsqueeze(0)
