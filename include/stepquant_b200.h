@@ -47,7 +47,8 @@ enum sq_error {
 };
 
 enum sq_status_bits {
-    SQ_STATUS_SLOT_RANGE = 1 /* a slot index >= num_slots was skipped */
+    SQ_STATUS_SLOT_RANGE = 1, /* a slot index >= num_slots was skipped */
+    SQ_STATUS_TIMEOUT = 2     /* a bounded device wait gave up (results incomplete) */
 };
 
 enum sq_dtype { SQ_F32 = 0, SQ_BF16 = 1, SQ_F16 = 2 };
@@ -287,6 +288,7 @@ typedef struct sq_prefill_args {
     void *out;
     void *workspace;
     int64_t workspace_bytes;
+    int32_t *status; /* device int32 for SQ_STATUS_* bits, or NULL */
 } sq_prefill_args;
 
 int64_t sq_gdn_prefill_workspace_bytes(int32_t tokens, int32_t num_seqs, int32_t heads);

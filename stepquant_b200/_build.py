@@ -20,12 +20,13 @@ SOURCES = ["sq_abi.cu", "sq_tile.cu", "sq_fast.cu", "sq_pack.cu", "sq_fp32.cu", 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
-    # The quantizer must not contract a*b+c into FMAs (bit-exactness with the
-    # reference fit_state); intended FMAs are written as fmaf().
-    "-fmad=false",
     "-diag-suppress", "128",
-    "-Xcompiler", "-fPIC", "-shared",
+    "-Xcompiler", "-fPIC",
 ]
+# The quantizer must not contract a*b+c into FMAs (bit-exactness with the
+# reference fit_state; intended FMAs are written as fmaf()).  The chunked
+# prefill is toleranced and is built with contraction.
+CONTRACT = {"sq_prefill.cu"}
 
 
 def _nvcc():
@@ -52,14 +53,29 @@ def build(force=False, verbose=False):
     """Compile the native library; returns its path."""
     if not force and up_to_date():
         return LIBRARY
-    os.makedirs(LIBDIR, exist_ok=True)
+    objdir = os.path.join(LIBDIR, "obj")
+    os.makedirs(objdir, exist_ok=True)
+    nvcc = _nvcc()
+    jobs = []
+    for src in SOURCES:
+        obj = os.path.join(objdir, src[:-3] + ".o")
+        fmad = "-fmad=true" if src in CONTRACT else "-fmad=false"
+        cmd = [nvcc, *NVCC_FLAGS, fmad, "-c", "-o", obj, os.path.join(CSRC, src)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        jobs.append((cmd, obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)))
+    failures = []
+    for cmd, obj, proc in jobs:
+        out, _ = proc.communicate()
+        if proc.returncode != 0:
+            failures.append(" ".join(cmd) + "\n" + out)
+    if failures:
+        raise RuntimeError("nvcc failed:\n" + "\n".join(failures))
     tmp = LIBRARY + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, "-o", tmp, *[os.path.join(CSRC, s) for s in SOURCES]]
-    if verbose:
-        print(" ".join(cmd), flush=True)
-    result = subprocess.run(cmd, capture_output=True, text=True)
+    link = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *[obj for _, obj, _ in jobs]]
+    result = subprocess.run(link, capture_output=True, text=True)
     if result.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + result.stdout + result.stderr)
+        raise RuntimeError("nvcc link failed:\n" + result.stdout + result.stderr)
     os.replace(tmp, LIBRARY)
     return LIBRARY
 

@@ -12,6 +12,7 @@ from ._build import LIBRARY
 
 SQ_OK, SQ_ERR_ARGUMENT, SQ_ERR_SHAPE, SQ_ERR_UNSUPPORTED, SQ_ERR_CUDA, SQ_ERR_CAPACITY = range(6)
 SQ_STATUS_SLOT_RANGE = 1
+SQ_STATUS_TIMEOUT = 2
 SQ_F32, SQ_BF16, SQ_F16 = 0, 1, 2
 SQ_GDN, SQ_KDA = 0, 1
 
@@ -41,7 +42,7 @@ class SqPrefillArgs(ctypes.Structure):
                 ("io_dtype", _i32), ("qk_heads", _i32), ("heads", _i32), ("keys", _i32), ("values", _i32),
                 ("normalize", _i32), ("scale", ctypes.c_float), ("num_seqs", _i32), ("tokens", _i32), ("cu_seqlens", _p),
                 ("g", _p), ("beta", _p), ("initial_state", _p), ("final_state", _p), ("out", _p),
-                ("workspace", _p), ("workspace_bytes", _i64)]
+                ("workspace", _p), ("workspace_bytes", _i64), ("status", _p)]
 
 
 _SIGNATURES = {

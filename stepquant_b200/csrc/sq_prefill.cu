@@ -15,11 +15,9 @@
 //
 // prep_kernel (one CTA per chunk and value head, all chunks in parallel)
 // computes everything that does not depend on S -- P, -W, U and the row
-// factors -- into a workspace record; state_kernel (one CTA per sequence and
-// value head) walks the chunks in order with the 128x128 state in fp32
-// registers, prefetching the next chunk's record while it computes D, O and
-// the state update.  Every product is an mma.sync m16n8k16 bf16 tile with fp32
-// accumulation (operands staged in padded shared memory, read with ldmatrix).
+// factors -- into a workspace record (mma.sync bf16 tiles, fp32 inverse);
+// state_kernel (one CTA per sequence and value head) walks the chunks in order
+// with the 128x128 state in tensor memory, on tcgen05 (see its comment).
 // Padded tokens of a last partial chunk have beta = 0 and log decay 0, so they
 // leave the state unchanged.
 #include "sq_common.cuh"
@@ -36,13 +34,14 @@ constexpr int kLdF = 68;  // fp32 row stride of 64x64 tiles
 
 using bf16 = __nv_bfloat16;
 
-// Workspace record of one (chunk, value head), byte offsets.
-constexpr int kRecW = 0;                   // -W   bf16 [64][128]
-constexpr int kRecU = kRecW + PC * PK * 2;  // U    bf16 [64][128]
-constexpr int kRecP = kRecU + PC * PV * 2;  // P    bf16 [64][64]
-constexpr int kRecRo = kRecP + PC * PC * 2; // e^gam nq scale      fp32 [64]
-constexpr int kRecRd = kRecRo + PC * 4;     // e^(gam_C - gam) nk  fp32 [64]
-constexpr int kRecDc = kRecRd + PC * 4;     // e^gam_C             fp32 (16 bytes)
+// Workspace record of one (chunk, value head), byte offsets.  -W and P are
+// stored as the state kernel's shared-memory operand tiles (128-byte swizzle).
+constexpr int kRecW = 0;                     // -W   bf16 [64][128] K-major tile
+constexpr int kRecP = kRecW + PC * PK * 2;    // P    bf16 [64][64]  K-major tile
+constexpr int kRecU = kRecP + PC * PC * 2;    // U    bf16 [64][128] row-major
+constexpr int kRecRo = kRecU + PC * PV * 2;   // e^gam nq scale      fp32 [64]
+constexpr int kRecRd = kRecRo + PC * 4;       // e^(gam_C - gam) nk  fp32 [64]
+constexpr int kRecDc = kRecRd + PC * 4;       // e^gam_C             fp32 (16 bytes)
 constexpr int kRec = (kRecDc + 16 + 255) / 256 * 256;
 constexpr int kOffsetsBytes(int seqs) { return (4 * (seqs + 1) + 255) / 256 * 256; }
 
@@ -95,6 +94,21 @@ __device__ __forceinline__ void load_b_kn(uint32_t (&b)[4], const bf16 (*m)[LD],
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// Byte offset of element (row, k) of a bf16 K-major operand tile with `rows`
+// rows under the 128-byte swizzle: K in atoms of 64 elements (rows * 128 bytes
+// each), rows in groups of 8 (1024 bytes), 16-byte chunk c of row r stored at
+// chunk c ^ (r % 8).
+__device__ __forceinline__ uint32_t sw128(int row, int k, int rows) {
+    const int kin = k & 63;
+    return (k >> 6) * (rows * 128) + (row >> 3) * 1024 + (row & 7) * 128 + ((((kin >> 3) ^ (row & 7))) << 4) + (kin & 7) * 2;
+}
+// The same for an MN-major tile with `krows` K rows: N in groups of 64
+// elements (krows * 128 bytes apart), K rows in groups of 8 (1024 bytes).
+__device__ __forceinline__ uint32_t sw128_mn(int kk, int n, int krows) {
+    const int nin = n & 63;
+    return (n >> 6) * (krows / 8) * 1024 + (kk >> 3) * 1024 + (kk & 7) * 128 + ((((nin >> 3) ^ (kk & 7))) << 4) + (nin & 7) * 2;
 }
 
 // Token range of sequence n, clamped to [0, tokens).
@@ -155,6 +169,7 @@ struct PrepSmem {
     float beta[PC];
     float nq[PC];
     float nk[PC];
+    float fw[PC];  // beta e^gam nk: column factors of Tw
 };
 
 __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const int32_t *offsets,
@@ -238,6 +253,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
         s.gam[2 * lane + 1] = run;
     }
     __syncthreads();
+    if (tid < PC) s.fw[tid] = s.beta[tid] * expf(s.gam[tid]) * s.nk[tid];
 
     // ---- G = K K^T, H = Q K^T (rows 16 (w / 2), columns 32 (w % 2) .. +31) -> L, P
     {
@@ -259,21 +275,30 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
             mma16816(accH[2], aq, b1[0], b1[1]);
             mma16816(accH[3], aq, b1[2], b1[3]);
         }
-        bf16 *prec = reinterpret_cast<bf16 *>(rec + kRecP);
+        float gi[2], li[2], pi[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int i = r0 + g8 + 8 * hh;
+            gi[hh] = s.gam[i];
+            li[hh] = s.beta[i] * s.nk[i];
+            pi[hh] = s.nq[i] * a.scale;
+        }
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
+            const int j = c0 + 8 * nt + 2 * tig;
+            const float gj[2] = {s.gam[j], s.gam[j + 1]}, nkj[2] = {s.nk[j], s.nk[j + 1]};
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                const int i = r0 + g8 + 8 * hh, j = c0 + 8 * nt + 2 * tig;
+                const int i = r0 + g8 + 8 * hh;
                 float pv[2];
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int jj = j + e;
-                    const float dec = jj <= i ? expf(s.gam[i] - s.gam[jj]) : 0.f;
-                    s.l[i][jj] = jj < i ? s.beta[i] * dec * s.nk[i] * s.nk[jj] * accG[nt][2 * hh + e] : 0.f;
-                    pv[e] = dec * s.nq[i] * a.scale * s.nk[jj] * accH[nt][2 * hh + e];
+                    const float dec = jj <= i ? __expf(gi[hh] - gj[e]) * nkj[e] : 0.f;
+                    s.l[i][jj] = jj < i ? li[hh] * dec * accG[nt][2 * hh + e] : 0.f;
+                    pv[e] = pi[hh] * dec * accH[nt][2 * hh + e];
                 }
-                *reinterpret_cast<uint32_t *>(prec + i * PC + j) = pack_bf16(pv[0], pv[1]);
+                *reinterpret_cast<uint32_t *>(rec + kRecP + sw128(i, j, PC)) = pack_bf16(pv[0], pv[1]);
             }
         }
     }
@@ -305,17 +330,30 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
     for (int r = 1; r < 4; ++r) {
         for (int e = tid; e < r * 256; e += 256) {
             const int c = e >> 8, i = (e >> 4) & 15, m = e & 15;
-            float x = 0.f;
-            for (int j = 16 * c; j < 16 * r; ++j) x += s.l[16 * r + i][j] * s.t[j][16 * c + m];
-            s.x[16 * r + i][16 * c + m] = x;
+            const float *lrow = &s.l[16 * r + i][0];
+            float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+            for (int mb = c; mb < r; ++mb) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4) {
+                    const int jj = 16 * mb + j;
+                    x0 += lrow[jj] * s.t[jj][16 * c + m];
+                    x1 += lrow[jj + 1] * s.t[jj + 1][16 * c + m];
+                    x2 += lrow[jj + 2] * s.t[jj + 2][16 * c + m];
+                    x3 += lrow[jj + 3] * s.t[jj + 3][16 * c + m];
+                }
+            }
+            s.x[16 * r + i][16 * c + m] = (x0 + x1) + (x2 + x3);
         }
         __syncthreads();
         for (int e = tid; e < r * 256; e += 256) {
             const int c = e >> 8, i = (e >> 4) & 15, m = e & 15;
-            float t = 0.f;
+            float t0 = 0.f, t1 = 0.f;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) t -= s.t[16 * r + i][16 * r + j] * s.x[16 * r + j][16 * c + m];
-            s.t[16 * r + i][16 * c + m] = t;
+            for (int j = 0; j < 16; j += 2) {
+                t0 -= s.t[16 * r + i][16 * r + j] * s.x[16 * r + j][16 * c + m];
+                t1 -= s.t[16 * r + i][16 * r + j + 1] * s.x[16 * r + j + 1][16 * c + m];
+            }
+            s.t[16 * r + i][16 * c + m] = t0 + t1;
         }
         __syncthreads();
     }
@@ -326,7 +364,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
     for (int e = tid; e < PC * PC; e += 256) {
         const int i = e >> 6, j = e & 63;
         const float t = s.t[i][j];
-        Tw[i][j] = __float2bfloat16_rn(t * (s.beta[j] * expf(s.gam[j]) * s.nk[j]));
+        Tw[i][j] = __float2bfloat16_rn(t * s.fw[j]);
         Tu[i][j] = __float2bfloat16_rn(t * s.beta[j]);
     }
     __syncthreads();
@@ -351,13 +389,12 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
                 mma16816(U[2 * np + 1], au, bv[2], bv[3]);
             }
         }
-        bf16 *wrec = reinterpret_cast<bf16 *>(rec + kRecW);
         bf16 *urec = reinterpret_cast<bf16 *>(rec + kRecU);
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             const int col = c0 + 8 * nt + 2 * tig, i0 = r0 + g8, i1 = i0 + 8;
-            *reinterpret_cast<uint32_t *>(wrec + i0 * PK + col) = pack_bf16(-W[nt][0], -W[nt][1]);
-            *reinterpret_cast<uint32_t *>(wrec + i1 * PK + col) = pack_bf16(-W[nt][2], -W[nt][3]);
+            *reinterpret_cast<uint32_t *>(rec + kRecW + sw128(i0, col, PC)) = pack_bf16(-W[nt][0], -W[nt][1]);
+            *reinterpret_cast<uint32_t *>(rec + kRecW + sw128(i1, col, PC)) = pack_bf16(-W[nt][2], -W[nt][3]);
             *reinterpret_cast<uint32_t *>(urec + i0 * PV + col) = pack_bf16(U[nt][0], U[nt][1]);
             *reinterpret_cast<uint32_t *>(urec + i1 * PV + col) = pack_bf16(U[nt][2], U[nt][3]);
         }
@@ -371,33 +408,133 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
 }
 
 // ---------------------------------------------------------------------------
-// state_kernel: one 512-thread CTA per (sequence, value head).
+// state_kernel: one 512-thread CTA per (sequence, value head), on tcgen05.
+// The transposed products keep every accumulator at M = 128 rows = the value
+// columns: warp w reads TMEM lanes 32 (w % 4) .. +31 (value columns) and the
+// quarter w / 4 of each accumulator's columns.  TMEM columns (fp32):
+//   S^T [0, 128)   the state                     S^T += Dt^T K      (N = 128)
+//   D^T [128, 192) the chunk residuals           D^T  = S^T (-W)^T  (N = 64), + U^T
+//   O1^T [192,256) (Q S)^T                       O1^T = S^T Q^T     (N = 64)
+//   O2^T [256,320) (P D)^T                       O2^T = D^T P^T     (N = 64)
+// Operands are bf16 in shared memory, 128-byte swizzled: S^T, D^T, Dt^T as
+// K-major A tiles written by the threads; -W, P (from the record, bulk copies),
+// raw q (cp.async) as K-major B tiles; raw k as an MN-major B tile.  One
+// thread issues the MMAs; tcgen05.commit arrives on an mbarrier the others
+// wait on (bounded waits: a CTA that gives up sets SQ_STATUS_TIMEOUT and
+// leaves after freeing its tensor memory).
 // ---------------------------------------------------------------------------
-struct StateStage {
-    bf16 w[PC][kLd];  // -W
-    bf16 q[PC][kLd];  // raw q
-    bf16 k[PC][kLd];  // raw k
-    bf16 p[PC][kLdP];
-    bf16 u[PC][PV];
-    float ro[PC];
-    float rd[PC];
-    float dc[4];
+constexpr int kTmemCols = 512;
+constexpr int kColS = 0, kColD = 128, kColO1 = 192, kColO2 = 256;
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+struct TcStage {                 // offsets are multiples of 1024 (swizzle atoms)
+    unsigned char w[16384];      // -W   [t][k]  K-major
+    unsigned char p[8192];       // P    [i][j]  K-major
+    unsigned char u[16384];      // U    [t][v]  bf16 row-major
+    unsigned char q[16384];      // q    [t][k]  K-major
+    unsigned char k[16384];      // k    [t][k]  MN-major (N = k)
+    float ro[PC];                // e^gam nq scale
+    float rd[PC];                // e^(gam_C - gam) nk
+    float dc[4];                 // e^gam_C
+    unsigned char pad[1024 - 528];
+};
+struct TcSmem {
+    TcStage st[2];
+    unsigned char sb[32768];     // S^T bf16 [v][k]
+    unsigned char dm[16384];     // D^T bf16 [v][t]
+    unsigned char dtm[16384];    // Dt^T bf16 [v][t]
 };
 
-struct StateSmem {
-    StateStage st[2];
-    bf16 s[PK][kLd];  // the state in bf16 (operand of W S and Q S)
-    bf16 d[PC][kLd];  // D
-    bf16 dt[PC][kLd]; // diag(e^(gam_C - gam) nk) D
-};
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t((lbo >> 4) & 0x3FFF) << 16) | (uint64_t((sbo >> 4) & 0x3FFF) << 32) |
+           (1ull << 46) | (2ull << 61);  // sm100 descriptor version 1, 128-byte swizzle
+}
+// bf16 x bf16 -> fp32, M = 128, A K-major, B K-major (0) or MN-major (1)
+__device__ __forceinline__ uint32_t idesc_bf16(int n, int b_mn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(b_mn) << 16) | (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+}
+__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile("{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+                 :: "r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" :: "r"(smem_addr(bar)));
+}
+__device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t done = 0;
+    for (uint32_t it = 0; it < kWaitLimit && !done; ++it)
+        asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+                     : "=r"(done) : "r"(smem_addr(bar)), "r"(parity));
+    return done != 0;
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
-// cp.async copies of chunk (t0, n rows) and its record into a stage.
-__device__ __forceinline__ void stage_chunk(const sq_prefill_args &a, StateStage &st, const unsigned char *rec, int t0,
-                                            int n, int qh, int tid) {
+#define SQ_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+#define SQ_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
+// 32 consecutive fp32 columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&out)[32]) {
+    uint32_t r[32];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+                 : SQ_R8(0), SQ_R8(8), SQ_R8(16), SQ_R8(24) : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) out[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&in)[32]) {
+    uint32_t r[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(in[i]);
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+                 "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
+                 :: "r"(taddr), SQ_W8(0), SQ_W8(8), SQ_W8(16), SQ_W8(24) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&out)[16]) {
+    uint32_t r[16];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+                 : SQ_R8(0), SQ_R8(8) : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[i] = __uint_as_float(r[i]);
+}
+#undef SQ_R8
+#undef SQ_W8
+
+// Write N fp32 values (columns c0 .. c0 + N - 1 of row `row`) as bf16 into a K-major SW128 tile.
+template <int N>
+__device__ __forceinline__ void put_row(unsigned char *tile, int rows, int row, int c0, const float (&x)[N], float scale = 1.f) {
+#pragma unroll
+    for (int j = 0; j < N / 8; ++j) {
+        uint4 w;
+        w.x = pack_bf16(scale * x[8 * j], scale * x[8 * j + 1]);
+        w.y = pack_bf16(scale * x[8 * j + 2], scale * x[8 * j + 3]);
+        w.z = pack_bf16(scale * x[8 * j + 4], scale * x[8 * j + 5]);
+        w.w = pack_bf16(scale * x[8 * j + 6], scale * x[8 * j + 7]);
+        *reinterpret_cast<uint4 *>(tile + sw128(row, c0 + 8 * j, rows)) = w;
+    }
+}
+
+// Copies of chunk (t0, n rows) into a stage: the record by three bulk copies
+// completing on `bar` (issued by thread 0), raw q and k rows by cp.async.
+__device__ __forceinline__ void tc_stage(const sq_prefill_args &a, TcStage &st, uint64_t *bar, const unsigned char *rec,
+                                         int t0, int n, int qh, int tid) {
+    if (tid == 0) {
+        const uint32_t bytes = 16384 + 8192 + 16384 + 528;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" :: "r"(smem_addr(bar)), "r"(bytes) : "memory");
+        const unsigned char *src[4] = {rec + kRecW, rec + kRecP, rec + kRecU, rec + kRecRo};
+        void *dst[4] = {st.w, st.p, st.u, st.ro};
+        const uint32_t len[4] = {16384, 8192, 16384, 528};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+                         :: "r"(smem_addr(dst[i])), "l"(src[i]), "r"(len[i]), "r"(smem_addr(bar)) : "memory");
+    }
     const bf16 *qg = static_cast<const bf16 *>(a.q), *kg = static_cast<const bf16 *>(a.k);
     for (int idx = tid; idx < 2 * PC * 16; idx += 512) {
         const int which = idx >> 10, row = (idx >> 4) & 63, piece = idx & 15;
-        bf16 *dst = (which == 0 ? st.q[row] : st.k[row]) + piece * 8;
+        unsigned char *dst = which == 0 ? st.q + sw128(row, 8 * piece, PC) : st.k + sw128_mn(row, 8 * piece, PC);
         if (row < n) {
             const int64_t t = t0 + row;
             cp16(dst, (which == 0 ? qg + t * a.q_stride : kg + t * a.k_stride) + int64_t(qh) * PK + piece * 8);
@@ -405,29 +542,17 @@ __device__ __forceinline__ void stage_chunk(const sq_prefill_args &a, StateStage
             *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
         }
     }
-    for (int idx = tid; idx < PC * 16; idx += 512) {
-        const int row = idx >> 4, piece = idx & 15;
-        cp16(st.w[row] + piece * 8, rec + kRecW + row * PK * 2 + piece * 16);
-        cp16(reinterpret_cast<unsigned char *>(st.u) + idx * 16, rec + kRecU + idx * 16);
-    }
-    for (int idx = tid; idx < PC * 8 + 33; idx += 512) {
-        if (idx < PC * 8) {
-            const int row = idx >> 3, piece = idx & 7;
-            cp16(st.p[row] + piece * 8, rec + kRecP + row * PC * 2 + piece * 16);
-        } else {
-            const int j = idx - PC * 8;  // ro (16 pieces), rd (16), dc (1)
-            cp16(reinterpret_cast<unsigned char *>(j < 16 ? st.ro : j < 32 ? st.rd : st.dc) + (j & 15) * 16,
-                 rec + kRecRo + j * 16);
-        }
-    }
 }
 
 __global__ void __launch_bounds__(512, 1) state_kernel(sq_prefill_args a, const int32_t *offsets,
                                                        const unsigned char *records) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    StateSmem &s = *reinterpret_cast<StateSmem *>(smem_raw);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g8 = lane >> 2, tig = lane & 3;
+    extern __shared__ unsigned char smem_raw[];
+    // 1024-byte aligned (swizzle atoms); offsetting the shared array keeps its address space.
+    TcSmem &s = *reinterpret_cast<TcSmem *>(smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u));
+    __shared__ uint64_t bar_data[2], bar_mma[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag;
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int H = a.heads;
     const int seq = blockIdx.x / H, head = blockIdx.x % H;
     const int qh = head / (H / a.qk_heads);
@@ -435,142 +560,146 @@ __global__ void __launch_bounds__(512, 1) state_kernel(sq_prefill_args a, const 
     const int chunks = (range.y - range.x + PC - 1) / PC;
     const unsigned char *rec0 = records + (int64_t(offsets[seq]) * H + head) * kRec;
     bf16 *og = static_cast<bf16 *>(a.out);
+    const int v = 32 * (warp & 3) + (tid & 31);  // value column = TMEM lane
+    const int cq = warp >> 2;                     // column quarter of every accumulator
 
-    // State fragments: warp w owns rows 16 (w % 8) .. +15 and columns 64 (w / 8) .. +63.
-    const int srow = 16 * (warp & 7), scol = 64 * (warp >> 3);
-    float S[8][4];
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" :: "r"(smem_addr(&tmem_slot)), "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+    }
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" :: "r"(smem_addr(&bar_data[i])));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" :: "r"(smem_addr(&bar_mma[i])));
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        abort_flag = 0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t lane = uint32_t(32 * (warp & 3)) << 16;
+
+    // Initial state: S^T row v = column v of S.
     {
         const float *init = a.initial_state ? a.initial_state + (int64_t(seq) * H + head) * PK * PV : nullptr;
+        const int k0 = 32 * cq;
+        float x[32];
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int row = srow + g8 + 8 * (e >> 1), col = scol + 8 * nt + 2 * tig + (e & 1);
-                S[nt][e] = init ? init[row * PV + col] : 0.f;
-            }
-            const int col = scol + 8 * nt + 2 * tig;
-            *reinterpret_cast<uint32_t *>(&s.s[srow + g8][col]) = pack_bf16(S[nt][0], S[nt][1]);
-            *reinterpret_cast<uint32_t *>(&s.s[srow + g8 + 8][col]) = pack_bf16(S[nt][2], S[nt][3]);
-        }
+        for (int j = 0; j < 32; ++j) x[j] = init ? init[(k0 + j) * PV + v] : 0.f;
+        tmem_st32(tmem + lane + kColS + k0, x);
+        put_row<32>(s.sb, PK, v, k0, x);
+        asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
     }
-    if (chunks > 0) stage_chunk(a, s.st[0], rec0, range.x, min(PC, range.y - range.x), qh, tid);
-    asm volatile("cp.async.commit_group;\n" ::);
-    // Chunk-output fragments: warp w owns rows 16 (w % 4) and columns 32 (w / 4) .. +31.
-    const int orow = 16 * (warp & 3), ocol = 32 * (warp >> 2);
+    if (chunks > 0) tc_stage(a, s.st[0], &bar_data[0], rec0, range.x, min(PC, range.y - range.x), qh, tid);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
 
+    const uint32_t id64 = idesc_bf16(64, 0), id128mn = idesc_bf16(128, 1);
     for (int c = 0; c < chunks; ++c) {
-        StateStage &st = s.st[c & 1];
+        TcStage &st = s.st[c & 1];
         const int t0 = range.x + c * PC, n = min(PC, range.y - t0);
+        // This chunk's copies (issued one chunk ahead) have landed; every thread
+        // is past the previous chunk, whose stage buffer is refilled next.
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        proxy_fence();
+        if (!bar_wait(&bar_data[c & 1], (c >> 1) & 1)) abort_flag = 1;
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (abort_flag) break;
         if (c + 1 < chunks)
-            stage_chunk(a, s.st[(c + 1) & 1], rec0 + int64_t(c + 1) * H * kRec, t0 + PC, min(PC, range.y - t0 - PC), qh, tid);
-        asm volatile("cp.async.commit_group;\ncp.async.wait_group 1;\n" ::);
-        __syncthreads();
+            tc_stage(a, s.st[(c + 1) & 1], &bar_data[(c + 1) & 1], rec0 + int64_t(c + 1) * H * kRec, t0 + PC,
+                     min(PC, range.y - t0 - PC), qh, tid);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
 
-        // ---- D = U - W S, O = diag(e^gam nq scale) Q S
-        float D[4][4], O[4][4] = {};
-        const int i0 = orow + g8, i1 = i0 + 8;
+        // ---- D^T = S^T (-W)^T, O1^T = S^T Q^T
+        if (tid == 0) {
+            const uint32_t sb = smem_addr(s.sb), w = smem_addr(st.w), q = smem_addr(st.q);
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            const int col = ocol + 8 * nt + 2 * tig;
-            const float2 u0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&st.u[i0][col]));
-            const float2 u1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&st.u[i1][col]));
-            D[nt][0] = u0.x;
-            D[nt][1] = u0.y;
-            D[nt][2] = u1.x;
-            D[nt][3] = u1.y;
-        }
-#pragma unroll
-        for (int ks = 0; ks < PK / 16; ++ks) {
-            uint32_t aw[4], aq[4], b0[4], b1[4];
-            load_a<kLd>(aw, st.w, orow, 16 * ks, lane);
-            load_a<kLd>(aq, st.q, orow, 16 * ks, lane);
-            load_b_kn<kLd>(b0, s.s, ocol, 16 * ks, lane);
-            load_b_kn<kLd>(b1, s.s, ocol + 16, 16 * ks, lane);
-            mma16816(D[0], aw, b0[0], b0[1]);
-            mma16816(D[1], aw, b0[2], b0[3]);
-            mma16816(D[2], aw, b1[0], b1[1]);
-            mma16816(D[3], aw, b1[2], b1[3]);
-            mma16816(O[0], aq, b0[0], b0[1]);
-            mma16816(O[1], aq, b0[2], b0[3]);
-            mma16816(O[2], aq, b1[0], b1[1]);
-            mma16816(O[3], aq, b1[2], b1[3]);
-        }
-        {
-            const float o0 = st.ro[i0], o1 = st.ro[i1], d0 = st.rd[i0], d1 = st.rd[i1];
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                const int col = ocol + 8 * nt + 2 * tig;
-                O[nt][0] *= o0;
-                O[nt][1] *= o0;
-                O[nt][2] *= o1;
-                O[nt][3] *= o1;
-                *reinterpret_cast<uint32_t *>(&s.d[i0][col]) = pack_bf16(D[nt][0], D[nt][1]);
-                *reinterpret_cast<uint32_t *>(&s.d[i1][col]) = pack_bf16(D[nt][2], D[nt][3]);
-                *reinterpret_cast<uint32_t *>(&s.dt[i0][col]) = pack_bf16(d0 * D[nt][0], d0 * D[nt][1]);
-                *reinterpret_cast<uint32_t *>(&s.dt[i1][col]) = pack_bf16(d1 * D[nt][2], d1 * D[nt][3]);
+            for (int ks = 0; ks < PK / 16; ++ks) {
+                const uint32_t ao = (ks >> 2) * 16384 + (ks & 3) * 32, bo = (ks >> 2) * 8192 + (ks & 3) * 32;
+                umma(tmem + kColD, sdesc(sb + ao, 16, 1024), sdesc(w + bo, 16, 1024), id64, ks > 0);
+                umma(tmem + kColO1, sdesc(sb + ao, 16, 1024), sdesc(q + bo, 16, 1024), id64, ks > 0);
             }
+            umma_commit(&bar_mma[0]);
         }
-        __syncthreads();
+        if (!bar_wait(&bar_mma[0], c & 1)) abort_flag = 1;
+        tc_fence_after();
 
-        // ---- O += P D; store the chunk's outputs
-#pragma unroll
-        for (int ks = 0; ks < PC / 16; ++ks) {
-            uint32_t ap[4], b0[4], b1[4];
-            load_a<kLdP>(ap, st.p, orow, 16 * ks, lane);
-            load_b_kn<kLd>(b0, s.d, ocol, 16 * ks, lane);
-            load_b_kn<kLd>(b1, s.d, ocol + 16, 16 * ks, lane);
-            mma16816(O[0], ap, b0[0], b0[1]);
-            mma16816(O[1], ap, b0[2], b0[3]);
-            mma16816(O[2], ap, b1[0], b1[1]);
-            mma16816(O[3], ap, b1[2], b1[3]);
-        }
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            const int col = ocol + 8 * nt + 2 * tig;
-            if (i0 < n)
-                *reinterpret_cast<uint32_t *>(og + ((int64_t(t0) + i0) * H + head) * PV + col) = pack_bf16(O[nt][0], O[nt][1]);
-            if (i1 < n)
-                *reinterpret_cast<uint32_t *>(og + ((int64_t(t0) + i1) * H + head) * PV + col) = pack_bf16(O[nt][2], O[nt][3]);
-        }
-
-        // ---- S = e^gam_C S + K^T Dt, then its bf16 copy
+        // ---- D = U + D; D^T and Dt^T tiles; S^T *= e^gam_C
         {
+            const bf16 *u = reinterpret_cast<const bf16 *>(st.u);
+            const int tq = 16 * cq;
+            float d[16], dt[16];
+            tmem_ld16(tmem + lane + kColD + tq, d);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                d[j] += __bfloat162float(u[(tq + j) * PV + v]);
+                dt[j] = st.rd[tq + j] * d[j];
+            }
+            put_row<16>(s.dm, PK, v, tq, d);
+            put_row<16>(s.dtm, PK, v, tq, dt);
             const float dc = st.dc[0];
+            float x[32];
+            tmem_ld32(tmem + lane + kColS + 32 * cq, x);
 #pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) S[nt][e] *= dc;
-            }
+            for (int j = 0; j < 32; ++j) x[j] *= dc;
+            tmem_st32(tmem + lane + kColS + 32 * cq, x);
+            asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+        }
+        proxy_fence();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (abort_flag) break;
+
+        // ---- O2^T = D^T P^T, S^T += Dt^T K
+        if (tid == 0) {
+            const uint32_t dm = smem_addr(s.dm), dtm = smem_addr(s.dtm), p = smem_addr(st.p), k = smem_addr(st.k);
 #pragma unroll
             for (int ks = 0; ks < PC / 16; ++ks) {
-                uint32_t ak[4];
-                load_a_t<kLd>(ak, st.k, srow, 16 * ks, lane);
-#pragma unroll
-                for (int np = 0; np < 4; ++np) {
-                    uint32_t b[4];
-                    load_b_kn<kLd>(b, s.dt, scol + 16 * np, 16 * ks, lane);
-                    mma16816(S[2 * np], ak, b[0], b[1]);
-                    mma16816(S[2 * np + 1], ak, b[2], b[3]);
-                }
+                umma(tmem + kColO2, sdesc(dm + ks * 32, 16, 1024), sdesc(p + ks * 32, 16, 1024), id64, ks > 0);
+                umma(tmem + kColS, sdesc(dtm + ks * 32, 16, 1024), sdesc(k + ks * 2048, 8192, 1024), id128mn, 1);
             }
-#pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-                const int col = scol + 8 * nt + 2 * tig;
-                *reinterpret_cast<uint32_t *>(&s.s[srow + g8][col]) = pack_bf16(S[nt][0], S[nt][1]);
-                *reinterpret_cast<uint32_t *>(&s.s[srow + g8 + 8][col]) = pack_bf16(S[nt][2], S[nt][3]);
-            }
+            umma_commit(&bar_mma[1]);
         }
-        __syncthreads();  // the state copy is complete; this stage is refilled next chunk
-    }
-    asm volatile("cp.async.wait_group 0;\n" ::);
+        if (!bar_wait(&bar_mma[1], c & 1)) abort_flag = 1;
+        tc_fence_after();
 
-    float *fin = a.final_state + (int64_t(seq) * H + head) * PK * PV;
+        // ---- outputs o_t = ro_t (Q S)_t + (P D)_t; the bf16 state tile for the next chunk
+        {
+            const int tq = 16 * cq;
+            float o1[16], o2[16];
+            tmem_ld16(tmem + lane + kColO1 + tq, o1);
+            tmem_ld16(tmem + lane + kColO2 + tq, o2);
+            bf16 *orow = og + ((int64_t(t0) + tq) * H + head) * PV + v;
+            const int64_t ostride = int64_t(H) * PV;
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-        const int col = scol + 8 * nt + 2 * tig;
-        *reinterpret_cast<float2 *>(fin + (srow + g8) * PV + col) = make_float2(S[nt][0], S[nt][1]);
-        *reinterpret_cast<float2 *>(fin + (srow + g8 + 8) * PV + col) = make_float2(S[nt][2], S[nt][3]);
+            for (int j = 0; j < 16; ++j) {
+                if (tq + j < n) orow[j * ostride] = __float2bfloat16_rn(st.ro[tq + j] * o1[j] + o2[j]);
+            }
+            float x[32];
+            tmem_ld32(tmem + lane + kColS + 32 * cq, x);
+            put_row<32>(s.sb, PK, v, 32 * cq, x);
+        }
     }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (abort_flag) {
+        if (tid == 0 && a.status) atomicOr(a.status, SQ_STATUS_TIMEOUT);
+    } else {
+        float *fin = a.final_state + (int64_t(seq) * H + head) * PK * PV;
+        float x[32];
+        tmem_ld32(tmem + lane + kColS + 32 * cq, x);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) fin[(32 * cq + j) * PV + v] = x[j];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" :: "r"(tmem), "r"(kTmemCols));
 }
 
 bool aligned_rows(const void *p, int64_t stride) {
@@ -606,7 +735,7 @@ extern "C" int32_t sq_gdn_prefill(const sq_prefill_args *args, sq_stream_t strea
     int32_t *offsets = static_cast<int32_t *>(a.workspace);
     unsigned char *records = static_cast<unsigned char *>(a.workspace) + sq::kOffsetsBytes(a.num_seqs);
     sq::offsets_kernel<<<1, 1024, 0, s>>>(a, offsets);
-    const int prep_smem = int(sizeof(sq::PrepSmem)), state_smem = int(sizeof(sq::StateSmem));
+    const int prep_smem = int(sizeof(sq::PrepSmem)), state_smem = int(sizeof(sq::TcSmem)) + 1024;
     if (cudaFuncSetAttribute(sq::prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) != cudaSuccess ||
         cudaFuncSetAttribute(sq::state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, state_smem) != cudaSuccess)
         return SQ_ERR_CUDA;

@@ -46,7 +46,7 @@ def _gates(x, tokens, heads, name):
 
 
 def chunk_gated_delta_rule(q, k, v, g, beta, *, scale=None, initial_state=None, output_final_state=True,
-                           use_qk_l2norm_in_kernel=True, cu_seqlens=None):
+                           use_qk_l2norm_in_kernel=True, cu_seqlens=None, check=True):
     """GDN prefill over concatenated sequences.
 
     q, k: [1, T, HK, 128] or [T, HK, 128]; v: [.., T, H, 128] (bf16; other
@@ -54,7 +54,9 @@ def chunk_gated_delta_rule(q, k, v, g, beta, *, scale=None, initial_state=None, 
     [N + 1] sequence boundaries (default: one sequence of T tokens);
     initial_state: [N, H, 128, 128] fp32 or None (zeros).  Returns
     (o [.., T, H, 128] bf16 shaped like v, final_state [N, H, 128, 128] fp32
-    or None when ``output_final_state`` is false).
+    or None when ``output_final_state`` is false).  With ``check`` the call
+    waits for the device and raises RuntimeError if a bounded device wait gave
+    up (SQ_STATUS_TIMEOUT); without it the call is asynchronous.
     """
     batched = v.dim() == 4
     qr, kr, vr = _rows(q, "q"), _rows(k, "k"), _rows(v, "v")
@@ -84,12 +86,15 @@ def chunk_gated_delta_rule(q, k, v, g, beta, *, scale=None, initial_state=None, 
     out = torch.empty(tokens, heads, values, device=device, dtype=torch.bfloat16)
     workspace = torch.empty(max(N.lib().sq_gdn_prefill_workspace_bytes(tokens, seqs, heads), 1), device=device,
                             dtype=torch.uint8)
+    status = torch.zeros(1, device=device, dtype=torch.int32)
     args = N.SqPrefillArgs(qr.data_ptr(), kr.data_ptr(), vr.data_ptr(), qr.stride(0), kr.stride(0), vr.stride(0),
                            N.SQ_BF16, qk_heads, heads, keys, values, 1 if use_qk_l2norm_in_kernel else 0,
                            keys ** -0.5 if scale is None else float(scale), seqs, tokens, cu.data_ptr(), gr.data_ptr(),
                            br.data_ptr(), init.data_ptr() if init is not None else None, final.data_ptr(),
-                           out.data_ptr(), workspace.data_ptr(), workspace.numel())
+                           out.data_ptr(), workspace.data_ptr(), workspace.numel(), status.data_ptr())
     N.check(N.lib().sq_gdn_prefill(ctypes.byref(args), N.stream_handle()))
+    if check and int(status.item()) & N.SQ_STATUS_TIMEOUT:
+        raise RuntimeError("chunked prefill: a bounded device wait gave up; results are incomplete")
     if batched:
         out = out.unsqueeze(0)
     return out, (final if output_final_state else None)
