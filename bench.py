@@ -51,9 +51,12 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("stepquant_b200", "reference"), default="stepquant_b200")
     p.add_argument("--mode", choices=("async", "sync"), default="async")
-    p.add_argument("--batch", type=int, default=256)
+    p.add_argument("--workload", choices=("gdn-decode", "kda-decode", "gdn-prefill"), default="gdn-decode",
+                   help="config 1 (default), config 2, or config 3")
+    p.add_argument("--batch", type=int, default=0, help="default: 256 (config 1), 512 (config 2), 32 (config 3)")
+    p.add_argument("--tokens", type=int, default=2048, help="prompt length (gdn-prefill)")
     p.add_argument("--heads", type=int, default=32)
-    p.add_argument("--qk-heads", type=int, default=16)
+    p.add_argument("--qk-heads", type=int, default=0, help="default: heads / 2 (GDN), heads (KDA)")
     p.add_argument("--dim", type=int, default=128)
     p.add_argument("--pivot-heads", type=int, default=0)
     p.add_argument("--slot-groups", type=int, default=4)
@@ -61,6 +64,7 @@ def parse_args():
     p.add_argument("--seed", type=int, default=1)
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-secondary", action="store_true", help="skip the short config-2 / config-3 measurements")
     return p.parse_args()
 
 
@@ -126,19 +130,23 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
-def measured_peak():
+def measured_peak(key="hbm_gbs"):
+    """(peak, source) from MEASURED_PEAKS.json, else the pool's earlier measurement."""
+    fallback = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as fh:
-            return float(json.load(fh)["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+            data = json.load(fh)
+        if key in data:
+            return float(data[key]), "measured"
+    return fallback[key], "fallback"
 
 
-def algorithmic_bytes(pool_page_bytes, heads_local, qk_local, batch, dim):
+def algorithmic_bytes(pool_page_bytes, heads_local, qk_local, batch, dim, kda=False):
     """Bytes one decode step must move (per rank): pages read+written, bf16 q/k/v in, gates, bf16 out."""
     pages = 2 * pool_page_bytes * batch
     inputs = batch * (2 * qk_local * dim + heads_local * dim) * 2
-    gates = batch * heads_local * 8
+    gates = batch * heads_local * (dim * 4 + 4 if kda else 8)
     output = batch * heads_local * dim * 2
     return pages, inputs + gates + output
 
@@ -229,6 +237,233 @@ def reference_arm(args):
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def _events():
+    import torch
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world, rank, device, barrier,
+                   mode="async", e2e=True, clocks=None, warm_steps=256, slot_groups=4, seed=1):
+    """Decode steps of one layer (GDN config 1 or KDA config 2); returns the measured quantities."""
+    import torch
+    from stepquant_b200 import _native as N
+    from stepquant_b200 import synthetic as S
+    from stepquant_b200.kernels.pool import PackedStatePool
+    from stepquant_b200.quantization import QuantizationPlan
+
+    dim = args.dim
+    heads_l, qk_l = heads_total // world, qk_total // world
+    gen = torch.Generator(device=device).manual_seed(seed * 1000 + rank)
+    cpu_gen = torch.Generator().manual_seed(seed)
+    if kda:
+        bits = S.kda_widths(heads_total, dim, cpu_gen)[rank * heads_l:(rank + 1) * heads_l]
+    else:
+        widths = S.gdn_widths(heads_total, cpu_gen, args.pivot_heads)[rank * heads_l:(rank + 1) * heads_l]
+        bits = widths[:, None].expand(heads_l, dim).clone()
+    a_log, dt_bias = S.gate_parameters(heads_l, dim, kda, gen, device)
+    requests = batch * slot_groups
+    slots_total = requests + 1
+
+    # fp32 warm-up state (the FP32 pool kernel) and row-impact statistics.
+    fp32 = torch.zeros(slots_total, heads_l, dim, dim, device=device)
+    warm_slots = torch.arange(1, slots_total, device=device)
+    out_scratch = torch.empty(requests, heads_l, dim, device=device, dtype=torch.bfloat16)
+    omega = torch.zeros(heads_l, dim, device=device, dtype=torch.float64)
+    for _ in range(warm_steps):
+        inp = S.draw_inputs(requests, heads_l, qk_l, dim, dim, kda, gen, device)
+        st = N.SqStepArgs(inp.q.data_ptr(), inp.k.data_ptr(), inp.v.data_ptr(), inp.q.stride(0), inp.k.stride(0),
+                          inp.v.stride(0), qk_l, N.SQ_BF16, inp.a.data_ptr(), inp.b.data_ptr(), N.SQ_F32, 1,
+                          a_log.data_ptr(), dt_bias.data_ptr(), dim ** -0.5, 0, out_scratch.data_ptr())
+        N.check(N.lib().sq_fp32_step(N.ptr(fp32), slots_total, heads_l, dim, dim, 1 if kda else 0, N.ptr(warm_slots),
+                                     requests, ctypes.byref(st), None, N.stream_handle()))
+        q, k, g, beta = S.prepared(inp, heads_l, dim, kda, a_log, dt_bias)
+        omega += S.row_impact(q, k, g, beta).double().sum(0)
+    impact = S.impact_factors(omega / (warm_steps * requests))
+    plan = QuantizationPlan("kda" if kda else "gdn", bits.to(device), impact.to(device))
+
+    stream = torch.cuda.Stream(device) if mode == "async" else None
+    pool = PackedStatePool(plan, slots_total, dim, writeback_stream=stream)
+    pool.encode(fp32[1:], warm_slots)
+    del fp32
+    groups = [torch.arange(1 + g * batch, 1 + (g + 1) * batch, device=device) for g in range(slot_groups)]
+    inputs = [S.draw_inputs(batch, heads_l, qk_l, dim, dim, kda, gen, device) for _ in range(4)]
+    kw = dict(normalize=True, scale=dim ** -0.5, a_log=a_log, dt_bias=dt_bias)
+
+    # Per-kernel CUDA events on the stream each kernel runs on.
+    marks = {"readout": [], "writeback": [], "step": []}
+    recording = [False]
+    finish = pool._finish_update
+
+    def timed_finish(*tensors, **kwargs):
+        if recording[0]:
+            e0, e1 = _events()
+            e0.record()
+            finish(*tensors, **kwargs)
+            e1.record()
+            marks["writeback"].append((e0, e1))
+        else:
+            finish(*tensors, **kwargs)
+
+    pool._finish_update = timed_finish
+
+    def one_step(i):
+        inp = inputs[i % len(inputs)]
+        pool.wait()
+        if recording[0]:
+            e0, e1 = _events()
+            e0.record()
+        out = pool.step(inp.q, inp.k, inp.v, inp.a, inp.b, groups[i % len(groups)], **kw)
+        if recording[0]:
+            e1.record()
+            marks["readout" if mode == "async" else "step"].append((e0, e1))
+        return out
+
+    for i in range(warmup):
+        one_step(i)
+    pool.wait()
+    barrier()
+    start, end = _events()
+    barrier()
+    if clocks:
+        clocks.start()
+    recording[0] = True
+    start.record()
+    for i in range(steps):
+        one_step(i)
+    pool.wait()
+    end.record()
+    recording[0] = False
+    barrier()
+    if clocks:
+        clocks.stop()
+    res = {"elapsed_ms": start.elapsed_time(end),
+           "kernel_ms": {name: sum(x.elapsed_time(y) for x, y in ev) / max(1, len(ev)) for name, ev in marks.items() if ev}}
+    pool.check_status()
+    res["page_bytes"] = pool.page_bytes
+    res["algorithmic"] = algorithmic_bytes(pool.page_bytes, heads_l, qk_l, batch, dim, kda)
+
+    if e2e:
+        # Each step's inputs (q, k, v bf16; gates fp32) packed in one pinned host
+        # buffer and copied with one H2D transfer; the output comes back with one D2H.
+        fields = [(x.shape, x.dtype) for x in (inputs[0].q, inputs[0].k, inputs[0].v, inputs[0].a, inputs[0].b)]
+        sizes = [math.prod(sh) * torch.tensor([], dtype=dt).element_size() for sh, dt in fields]
+        offsets = [0]
+        for nbytes in sizes:
+            offsets.append(offsets[-1] + (nbytes + 255) // 256 * 256)
+        pinned = []
+        for x in inputs:
+            buf = torch.empty(offsets[-1], dtype=torch.uint8).pin_memory()
+            for t, o, nbytes in zip((x.q, x.k, x.v, x.a, x.b), offsets, sizes):
+                buf[o:o + nbytes].copy_(t.contiguous().view(-1).view(torch.uint8).cpu())
+            pinned.append(buf)
+        dev_buf = torch.empty(offsets[-1], dtype=torch.uint8, device=device)
+        dev_in = tuple(dev_buf[o:o + nbytes].view(dt).view(sh) for (sh, dt), o, nbytes in zip(fields, offsets, sizes))
+        host_out = torch.empty(batch, heads_l, dim, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step(i):
+            dev_buf.copy_(pinned[i % len(pinned)], non_blocking=True)
+            out = pool.step(*dev_in, groups[i % len(groups)], **kw)
+            host_out.copy_(out, non_blocking=True)
+
+        for i in range(warmup):
+            e2e_step(i)
+        pool.wait()
+        barrier()
+        e0, e1 = _events()
+        e0.record()
+        for i in range(steps):
+            e2e_step(i)
+        pool.wait()
+        e1.record()
+        barrier()
+        res.update(e2e_ms=e0.elapsed_time(e1), h2d=sum(sizes), d2h=host_out.numel() * host_out.element_size())
+    return res
+
+
+def measure_prefill(args, batch, tokens, heads_total, qk_total, steps, warmup, world, rank, device, barrier,
+                    e2e=True, clocks=None, seed=3):
+    """Chunked prefill of ``batch`` prompts of ``tokens`` tokens to their first packed states (config 3)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    from stepquant_b200 import synthetic as S
+    from stepquant_b200.kernels.pool import PackedStatePool
+    from stepquant_b200.quantization import QuantizationPlan
+
+    dim = args.dim
+    heads_l, qk_l = heads_total // world, qk_total // world
+    gen = torch.Generator(device=device).manual_seed(seed * 1000 + rank)
+    cpu_gen = torch.Generator().manual_seed(seed)
+    widths = S.gdn_widths(heads_total, cpu_gen)[rank * heads_l:(rank + 1) * heads_l]
+    plan = QuantizationPlan("gdn", widths[:, None].expand(heads_l, dim).clone().to(device),
+                            (torch.rand(heads_l, dim, generator=cpu_gen) + 0.5).to(device))
+    pool = PackedStatePool(plan, batch + 1, dim)
+    slots = torch.arange(1, batch + 1, device=device)
+    total = batch * tokens
+    q = torch.randn(1, total, qk_l, dim, device=device, generator=gen).bfloat16()
+    k = torch.randn(1, total, qk_l, dim, device=device, generator=gen).bfloat16()
+    v = torch.randn(1, total, heads_l, dim, device=device, generator=gen).bfloat16()
+    a_log, _ = S.gate_parameters(heads_l, dim, False, gen, device)
+    g = -a_log.exp() * torch.nn.functional.softplus(torch.randn(1, total, heads_l, device=device, generator=gen))
+    beta = torch.randn(1, total, heads_l, device=device, generator=gen).sigmoid()
+    cu = torch.arange(0, total + 1, tokens, device=device, dtype=torch.int32)
+
+    def one_step():
+        pool.clear(slots)  # new prompts start from the zero state
+        return pool.extend(q, k, v, g, beta, slots, cu)
+
+    for _ in range(warmup):
+        one_step()
+    barrier()
+    start, end = _events()
+    barrier()
+    if clocks:
+        clocks.start()
+    start.record()
+    for _ in range(steps):
+        one_step()
+    end.record()
+    barrier()
+    if clocks:
+        clocks.stop()
+    res = {"elapsed_ms": start.elapsed_time(end)}
+    # per-kernel device times of one step
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        one_step()
+        torch.cuda.synchronize()
+    kernels = {}
+    for ev in prof.key_averages():
+        name = ev.key
+        for short in ("prep_kernel", "state_kernel", "offsets_kernel", "tile_kernel", "fast_kernel"):
+            if short in name:
+                kernels[short] = kernels.get(short, 0.0) + ev.device_time_total / 1e3
+    res["kernel_ms"] = kernels
+    chunk_heads = batch * ((tokens + 63) // 64) * heads_l
+    c, kk, vv = 64, dim, dim
+    res["flops"] = chunk_heads * 2 * (3 * c * c * kk + 2 * c * kk * vv + c * kk * vv + c * c * vv)
+
+    if e2e:
+        pin = [x.cpu().pin_memory() for x in (q, k, v, g, beta)]
+        host_out = torch.empty(v.shape, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            dev = [x.to(device, non_blocking=True) for x in pin]
+            pool.clear(slots)
+            out = pool.extend(*dev, slots, cu)
+            host_out.copy_(out, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        e0, e1 = _events()
+        e0.record()
+        for _ in range(max(1, steps // 4)):
+            e2e_step()
+        e1.record()
+        barrier()
+        res.update(e2e_ms=e0.elapsed_time(e1) / max(1, steps // 4) * steps,
+                   h2d=sum(x.numel() * x.element_size() for x in pin), d2h=host_out.numel() * host_out.element_size())
+    return res
+
+
 def main():
     args = parse_args()
     # Library and NCCL messages written to fd 1 go to stderr; the result line
@@ -254,205 +489,135 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-    if args.heads % world or args.qk_heads % world:
-        raise SystemExit("heads must divide evenly over ranks")
-
-    from stepquant_b200 import _native as N
-    from stepquant_b200 import synthetic as S
-    from stepquant_b200.kernels.pool import PackedStatePool
-    from stepquant_b200.quantization import QuantizationPlan
-
-    heads_l, qk_l, dim, batch = args.heads // world, args.qk_heads // world, args.dim, args.batch
-    gen = torch.Generator(device=device).manual_seed(args.seed * 1000 + rank)
-    cpu_gen = torch.Generator().manual_seed(args.seed)
-    widths = S.gdn_widths(args.heads, cpu_gen, args.pivot_heads)[rank * heads_l:(rank + 1) * heads_l]
-    a_log, dt_bias = S.gate_parameters(heads_l, dim, False, gen, device)
-    requests = batch * args.slot_groups
-    slots_total = requests + 1
-
-    # fp32 warm-up state (the FP32 pool kernel) and row-impact statistics.
-    fp32 = torch.zeros(slots_total, heads_l, dim, dim, device=device)
-    warm_slots = torch.arange(1, slots_total, device=device)
-    out_scratch = torch.empty(requests, heads_l, dim, device=device, dtype=torch.bfloat16)
-    omega = torch.zeros(heads_l, dim, device=device, dtype=torch.float64)
-    for _ in range(args.warm_steps):
-        inp = S.draw_inputs(requests, heads_l, qk_l, dim, dim, False, gen, device)
-        st = N.SqStepArgs(inp.q.data_ptr(), inp.k.data_ptr(), inp.v.data_ptr(), inp.q.stride(0), inp.k.stride(0),
-                          inp.v.stride(0), qk_l, N.SQ_BF16, inp.a.data_ptr(), inp.b.data_ptr(), N.SQ_F32, 1,
-                          a_log.data_ptr(), dt_bias.data_ptr(), dim ** -0.5, 0, out_scratch.data_ptr())
-        N.check(N.lib().sq_fp32_step(N.ptr(fp32), slots_total, heads_l, dim, dim, 0, N.ptr(warm_slots), requests,
-                                     ctypes.byref(st), None, N.stream_handle()))
-        q, k, g, beta = S.prepared(inp, heads_l, dim, False, a_log, dt_bias)
-        omega += S.row_impact(q, k, g, beta).double().sum(0)
-    impact = S.impact_factors(omega / (args.warm_steps * requests))
-    plan = QuantizationPlan("gdn", widths[:, None].expand(heads_l, dim).clone().to(device), impact.to(device))
-
-    stream = torch.cuda.Stream(device) if args.mode == "async" else None
-    pool = PackedStatePool(plan, slots_total, dim, writeback_stream=stream)
-    pool.encode(fp32[1:], warm_slots)
-    del fp32
-    groups = [torch.arange(1 + g * batch, 1 + (g + 1) * batch, device=device) for g in range(args.slot_groups)]
-    inputs = [S.draw_inputs(batch, heads_l, qk_l, dim, dim, False, gen, device) for _ in range(4)]
-    kw = dict(normalize=True, scale=dim ** -0.5, a_log=a_log, dt_bias=dt_bias)
-
-    # Per-kernel CUDA events on the stream each kernel runs on.
-    marks = {"readout": [], "writeback": [], "step": []}
-    recording = [False]
-    finish = pool._finish_update
-
-    def timed_finish(*tensors, **kwargs):
-        if recording[0]:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            finish(*tensors, **kwargs)
-            e1.record()
-            marks["writeback"].append((e0, e1))
-        else:
-            finish(*tensors, **kwargs)
-
-    pool._finish_update = timed_finish
-
-    def one_step(i):
-        inp = inputs[i % len(inputs)]
-        pool.wait()
-        if recording[0]:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-        out = pool.step(inp.q, inp.k, inp.v, inp.a, inp.b, groups[i % len(groups)], **kw)
-        if recording[0]:
-            e1.record()
-            marks["readout" if args.mode == "async" else "step"].append((e0, e1))
-        return out
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
+    def max_over_ranks(*values):
+        t = torch.tensor(values, device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    def sum_over_ranks(*values):
+        t = torch.tensor(values, device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t)
+        return t.tolist()
+
+    workload = args.workload
+    kda = workload == "kda-decode"
+    batch = args.batch if args.batch else (512 if kda else 32 if workload == "gdn-prefill" else 256)
+    heads = args.heads
+    qk_heads = args.qk_heads if args.qk_heads else (heads if kda else heads // 2)
+    if heads % world or qk_heads % world:
+        raise SystemExit("heads must divide evenly over ranks")
     clocks = ClockSampler(local)
-    for i in range(args.warmup):
-        one_step(i)
-    pool.wait()
-    barrier()
+    peak_hbm, peak_hbm_kind = measured_peak()
+    line = {"metric": METRIC, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic"}
 
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    clocks.start()
-    recording[0] = True
-    start.record()
-    for i in range(args.steps):
-        one_step(i)
-    pool.wait()
-    end.record()
-    recording[0] = False
-    barrier()
-    clocks.stop()
-    elapsed_ms = start.elapsed_time(end)
-    kernel_ms = {name: sum(a.elapsed_time(b) for a, b in ev) / max(1, len(ev)) for name, ev in marks.items() if ev}
-    pool.check_status()
-
-    # End to end through the public API with host buffers.
-    # Each step's inputs (q, k, v bf16; a, b fp32) packed in one pinned host
-    # buffer and copied with one H2D transfer; the output comes back with one D2H.
-    fields = [(x.shape, x.dtype) for x in (inputs[0].q, inputs[0].k, inputs[0].v, inputs[0].a, inputs[0].b)]
-    sizes = [math.prod(sh) * torch.tensor([], dtype=dt).element_size() for sh, dt in fields]
-    offsets = [0]
-    for n in sizes:
-        offsets.append(offsets[-1] + (n + 255) // 256 * 256)
-    pinned = []
-    for x in inputs:
-        buf = torch.empty(offsets[-1], dtype=torch.uint8).pin_memory()
-        for t, o, n in zip((x.q, x.k, x.v, x.a, x.b), offsets, sizes):
-            buf[o:o + n].copy_(t.contiguous().view(-1).view(torch.uint8).cpu())
-        pinned.append(buf)
-    dev_buf = torch.empty(offsets[-1], dtype=torch.uint8, device=device)
-    dev_in = tuple(dev_buf[o:o + n].view(dt).view(sh) for (sh, dt), o, n in zip(fields, offsets, sizes))
-    host_out = torch.empty(batch, heads_l, dim, dtype=torch.bfloat16).pin_memory()
-    h2d = sum(sizes)
-    d2h = host_out.numel() * host_out.element_size()
-
-    def e2e_step(i):
-        dev_buf.copy_(pinned[i % len(pinned)], non_blocking=True)
-        out = pool.step(*dev_in, groups[i % len(groups)], **kw)
-        host_out.copy_(out, non_blocking=True)
-
-    for i in range(args.warmup):
-        e2e_step(i)
-    pool.wait()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.steps):
-        e2e_step(i)
-    pool.wait()
-    e1.record()
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
-
-    times = torch.tensor([elapsed_ms, e2e_ms], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms = times.tolist()
-
-    units = args.batch * args.heads * args.steps
-    value = units / (elapsed_ms / 1e3)
-    e2e_value = units / (e2e_ms / 1e3)
-
-    page_bytes = pool.page_bytes
-    page_io, other_io = algorithmic_bytes(page_bytes, heads_l, qk_l, batch, dim)
-    # Each rank's plan covers its own value heads: job totals are sums over ranks.
-    totals = torch.tensor([page_bytes, page_io + other_io], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(totals)
-    job_page_bytes, step_bytes = (int(t) for t in totals.tolist())
-    peak, peak_kind = measured_peak()
-    if args.mode == "sync":
-        dominant, dom_bytes = "sq_step (fused)", page_io + other_io
-        dom_ms = kernel_ms.get("step")
+    if workload == "gdn-prefill":
+        res = measure_prefill(args, batch, args.tokens, heads, qk_heads, args.steps, args.warmup, world, rank, device,
+                              barrier, e2e=True, clocks=clocks)
+        elapsed_ms, e2e_ms = max_over_ranks(res["elapsed_ms"], res["e2e_ms"])
+        flops, = sum_over_ranks(res["flops"])
+        units = batch * args.tokens * args.steps
+        peak_tf, peak_tf_kind = measured_peak("bf16_tflops")
+        kern = res["kernel_ms"]
+        dom_ms = kern.get("prep_kernel", 0.0) + kern.get("state_kernel", 0.0)
+        achieved = flops / world / (dom_ms / 1e3) / 1e12 if dom_ms else None
+        line.update({
+            "metric": "chunked-prefill tokens/s", "unit": "tokens/s", "value": units / (elapsed_ms / 1e3),
+            "ms_per_step": elapsed_ms / args.steps, "dtype": "bf16",
+            "config": {"workload": "gdn-prefill-b%d-t%d-h%d-k128 (config 3)" % (batch, args.tokens, heads),
+                       "batch": batch, "tokens": args.tokens, "chunk": 64, "heads": heads, "qk_heads": qk_heads,
+                       "plan": "stepquant6 synthetic (first packed state)", "parallelism": f"tp{world} (value heads)",
+                       "l2": "inputs > L2 (%.0f MB of q/k/v per GPU)" % ((2 * qk_heads + heads) // world * 128 * 2 * batch * args.tokens / 1e6)},
+            "kernel_ms": kern,
+            "roofline": {"kernel": "prep_kernel + state_kernel", "bound": "tensor", "achieved": achieved, "peak": peak_tf,
+                         "unit": "TFLOP/s", "frac": achieved / peak_tf if achieved else None, "traffic": None,
+                         "peak_source": peak_tf_kind, "algorithmic_flops_per_launch": flops / world},
+            "e2e": {"value": units / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"],
+                    "d2h_bytes_per_step": res["d2h"]},
+            "gpu_launches": args.steps * 5,
+        })
     else:
-        rd, wb = kernel_ms.get("readout", 0.0), kernel_ms.get("writeback", 0.0)
-        if wb >= rd:
-            dominant, dom_bytes, dom_ms = "sq_writeback", page_io, wb
+        res = measure_decode(args, kda, batch, heads, qk_heads, args.steps, args.warmup, world, rank, device, barrier,
+                             mode=args.mode, e2e=True, clocks=clocks, warm_steps=args.warm_steps,
+                             slot_groups=args.slot_groups, seed=2 if kda else args.seed)
+        elapsed_ms, e2e_ms = max_over_ranks(res["elapsed_ms"], res["e2e_ms"])
+        page_io, other_io = res["algorithmic"]
+        job_page_bytes, step_bytes = (int(x) for x in sum_over_ranks(res["page_bytes"], page_io + other_io))
+        units = batch * heads * args.steps
+        kernel_ms = res["kernel_ms"]
+        if args.mode == "sync":
+            dominant, dom_bytes, dom_ms = "sq_step (fused)", page_io + other_io, kernel_ms.get("step")
         else:
-            dominant, dom_bytes, dom_ms = "sq_readout", page_io // 2 + other_io, rd
-    achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms else None
-    # dram read + write bytes per launch from one ncu capture of this workload
-    # (profiles/fast_kernel_gdn_b256.md); None for other shapes.
-    ncu_traffic = {"sq_step (fused)": 160.6e6, "sq_writeback": 162.3e6, "sq_readout": 116.7e6}
-    default_shape = (args.batch, args.heads, args.qk_heads, dim, world) == (256, 32, 16, 128, 1)
-    traffic = ncu_traffic.get(dominant) if default_shape else None
+            rd, wb = kernel_ms.get("readout", 0.0), kernel_ms.get("writeback", 0.0)
+            if wb >= rd:
+                dominant, dom_bytes, dom_ms = "sq_writeback", page_io, wb
+            else:
+                dominant, dom_bytes, dom_ms = "sq_readout", page_io // 2 + other_io, rd
+        achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms else None
+        # dram read + write bytes per launch from one ncu capture of this workload
+        # (profiles/fast_kernel_gdn_b256.md); None for other shapes.
+        ncu_traffic = {"sq_step (fused)": 160.6e6, "sq_writeback": 162.3e6, "sq_readout": 116.7e6}
+        default_shape = (not kda, batch, heads, qk_heads, args.dim, world) == (True, 256, 32, 16, 128, 1)
+        name = ("kda-decode-b%d-h%d-k128 (config 2)" if kda else "gdn-decode-b%d-h%d-k128 (config 1)") % (batch, heads)
+        plan_desc = ("stepquant4 reference-legal twin: row widths {2,4,6} at 30/50/20, 2% fp16 pivot rows" if kda else
+                     "stepquant6 synthetic, widths {4,6,8} 25/50/25, pivot heads %d" % args.pivot_heads)
+        line.update({
+            "value": units / (elapsed_ms / 1e3), "ms_per_step": elapsed_ms / args.steps,
+            "config": {"workload": name, "batch": batch, "heads": heads, "qk_heads": qk_heads, "dim": args.dim,
+                       "mode": args.mode, "writeback": args.mode == "async", "plan": plan_desc,
+                       "page_bytes_per_request": job_page_bytes, "l2": "inputs > L2: slots rotate over %d groups "
+                       "(%.0f MB of pages per GPU)" % (args.slot_groups, (args.slot_groups * batch + 1) * res["page_bytes"] / 1e6),
+                       "parallelism": f"tp{world} (value heads)"},
+            "request_steps_per_s": units / heads / (elapsed_ms / 1e3),
+            "algorithmic_gb_per_s": step_bytes * args.steps / (elapsed_ms / 1e3) / 1e9,
+            "hbm_fraction_whole_step": step_bytes / world * args.steps / (elapsed_ms / 1e3) / 1e9 / peak_hbm,
+            "kernel_ms": kernel_ms,
+            "roofline": {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": peak_hbm, "unit": "GB/s",
+                         "frac": achieved / peak_hbm if achieved else None,
+                         "traffic": ncu_traffic.get(dominant) if default_shape else None, "peak_source": peak_hbm_kind,
+                         "algorithmic_bytes_per_launch": dom_bytes},
+            "e2e": {"value": units / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": res["h2d"],
+                    "d2h_bytes_per_step": res["d2h"]},
+            "gpu_launches": args.steps * (2 if args.mode == "async" else 1),
+        })
+    line["clocks"] = clocks.summary()
+
+    # Short measurements of the other configurations (single GPU, default run only).
+    if world == 1 and workload == "gdn-decode" and not args.no_secondary:
+        sec = {}
+        r2 = measure_decode(args, True, 512, 32, 32, 5, 3, 1, 0, device, barrier, mode="async", e2e=False,
+                            warm_steps=64, slot_groups=2, seed=2)
+        sec["kda-decode-b512-h32-k128 (config 2)"] = {
+            "value": 512 * 32 * 5 / (r2["elapsed_ms"] / 1e3), "unit": UNIT, "ms_per_step": r2["elapsed_ms"] / 5,
+            "kernel_ms": r2["kernel_ms"], "steps": 5, "mode": "async",
+            "note": "tile kernels (no register-resident KDA kernel yet); 64 warm-up steps, 2 slot groups"}
+        r3 = measure_prefill(args, 32, 2048, 32, 16, 5, 2, 1, 0, device, barrier, e2e=False)
+        peak_tf, peak_tf_kind = measured_peak("bf16_tflops")
+        pk = r3["kernel_ms"].get("prep_kernel", 0.0) + r3["kernel_ms"].get("state_kernel", 0.0)
+        sec["gdn-prefill-b32-t2048-h32-k128 (config 3)"] = {
+            "value": 32 * 2048 * 5 / (r3["elapsed_ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r3["elapsed_ms"] / 5,
+            "kernel_ms": r3["kernel_ms"], "steps": 5,
+            "tensor_tflops": r3["flops"] / (pk / 1e3) / 1e12 if pk else None,
+            "tensor_frac": (r3["flops"] / (pk / 1e3) / 1e12 / peak_tf) if pk else None, "peak_source": peak_tf_kind}
+        line["secondary"] = sec
 
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
-
     cpu = None
-    if not args.no_cpu_baseline and world == 1:
-        cpu = cpu_reference(args, args.heads, args.qk_heads, 100, 1, args.cpu_seconds)
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "gdn-decode-b256-h32-k128 (config 1)", "batch": batch, "heads": args.heads,
-                   "qk_heads": args.qk_heads, "dim": dim, "mode": args.mode, "writeback": args.mode == "async",
-                   "plan": "stepquant6 synthetic, widths {4,6,8} 25/50/25, pivot heads %d" % args.pivot_heads,
-                   "page_bytes_per_request": job_page_bytes, "l2": "inputs > L2: slots rotate over %d groups "
-                   "(%.0f MB of pages per GPU)" % (args.slot_groups, slots_total * page_bytes / 1e6),
-                   "parallelism": f"tp{world} (value heads)"},
-        "request_steps_per_s": value / args.heads,
-        "algorithmic_gb_per_s": step_bytes * args.steps / (elapsed_ms / 1e3) / 1e9,
-        "hbm_fraction_whole_step": step_bytes / world * args.steps / (elapsed_ms / 1e3) / 1e9 / peak,
-        "kernel_ms": kernel_ms,
-        "roofline": {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak if achieved else None, "traffic": traffic, "peak_source": peak_kind,
-                     "algorithmic_bytes_per_launch": dom_bytes},
-        "clocks": clocks.summary(),
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps * (2 if args.mode == "async" else 1),
-        "cpu_baseline": cpu,
-    }
+    if not args.no_cpu_baseline and world == 1 and workload == "gdn-decode":
+        cpu = cpu_reference(args, heads, qk_heads, 100, 1, args.cpu_seconds)
+    line["cpu_baseline"] = cpu
     emit(line)
 
 
