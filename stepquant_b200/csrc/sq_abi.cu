@@ -57,14 +57,37 @@ sq::TileParams base_params(const sq_plan *plan, uint8_t *pages, int64_t num_slot
 }
 
 // Step, readout and writeback go to the register-resident kernels for the heads
-// they handle (GDN, K = V = 128, widths 4/6/8) and to the tile kernel for the
-// rest; with a host copy of the bits the tile launch is skipped when no head
+// they handle (GDN, K = V = 128, widths 4/6/8; KDA, K = V = 128, code region
+// within the stage buffer) and to the tile kernel for the rest; with a host copy of the bits the tile launch is skipped when no head
 // needs it.  Every other mode runs on the tile kernel.
+// Host restatement of the KDA head test of fast_head_dev from a head's bits
+// (the packed layout's value-tile stride, tile 4).
+bool kda_head_fast_host(const int32_t *bits, int keys, int values) {
+    int64_t local = 0;
+    bool any_int = false;
+    for (int k = 0; k < keys; ++k) {
+        if (bits[k] == 16) local = (local + 1) / 2 * 2;
+        else any_int = true;
+        local += 4 * bits[k] / 8;
+    }
+    return sq::kda_head_fits((local + 1) / 2 * 2, values, any_int ? 0 : -1);
+}
+
 int32_t run(int mode, sq::TileParams t, int32_t batch, cudaStream_t stream) {
     const int items = batch * t.plan.heads;
     if (items <= 0) return SQ_OK;
     const bool fast_mode = mode == sq::kStep || mode == sq::kReadout || mode == sq::kWriteback;
-    if (fast_mode && sq::fast_eligible(t.plan, t.pages)) {
+    if (fast_mode && sq::kda_fast_eligible(t.plan)) {
+        if (cudaError_t e = sq::launch_fast_kda(mode, t, batch, stream)) return cuda_status(e);
+        bool rest = true;
+        if (t.plan.bits_host) {
+            rest = false;
+            for (int h = 0; h < t.plan.heads; ++h)
+                rest = rest || !kda_head_fast_host(t.plan.bits_host + h * t.plan.keys, t.plan.keys, t.plan.values);
+        }
+        if (!rest) return SQ_OK;
+        t.skip_fast = 1;
+    } else if (fast_mode && sq::fast_eligible(t.plan, t.pages)) {
         if (cudaError_t e = sq::launch_fast(mode, t, batch, stream)) return cuda_status(e);
         bool rest = true;
         if (t.plan.bits_host) {

@@ -1,0 +1,516 @@
+// Register-resident decode kernels for KDA heads with K = V = 128 (the served
+// shape of Kimi-Linear-style layers): per key row a code width of 2, 4, 6 or
+// 8 bits or an fp16 pivot row, per-channel decay, value tile 4.
+//
+// One 256-thread CTA per (request, value head), two CTAs per SM.  The head's
+// code bytes are staged by cp.async; a cooperative pass (P0) unpacks every
+// (row, value tile) chunk into a dense fp16 plane (levels of integer rows,
+// values of pivot rows) laid out so that thread (w, l) reads its four columns
+// l, l+32, l+64, l+96 of a row with one 8-byte load.  From there the mapping
+// is the one of the GDN kernels (warp w owns rows 16w..16w+15, both torch sum
+// orders thread-local): P1 dequantizes and decays (x = level * r_old *
+// 2^(8-b) * decay_k * c, pivot rows value * decay_k) and forms the column
+// partials of k^T S and q^T S, P2 applies the rank-1 update and the row |x|
+// sums, P3-P5 evaluate fit_state for KDA rows (limit = qmax 2^(8-b), y =
+// x / r / c / 2^(8-b), pivot rows excluded from c and the least squares), and a
+// cooperative pass packs the codes.  Divisions by fp16 scales and by the row
+// limits (64, 112, 124, 127: at most 7 significant bits) use the corrected
+// reciprocal of the GDN kernels, exact for such divisors; division by
+// 2^(8-b) is an exact multiplication.
+#include "sq_fast.cuh"
+
+namespace sq {
+namespace {
+
+constexpr int DK = 128;
+constexpr int DV = 128;
+constexpr int DTILES = DV / 4;                 // value tiles of 4
+constexpr int kCodeStage = kKdaCodeCap + 32;    // + 16-byte cover at both ends
+constexpr int kRowPart = 36;                    // floats per row in the row-partial exchange
+
+struct KdaSmem {
+    unsigned char codes[kCodeStage];
+    int bits[DK];
+    int offs[DK];
+    int rows[DK];
+    float imp[DK];
+    union {
+        __half plane[DK * DV];          // P0 -> P1 and P5 -> store: [k][l][i] = column l + 32 i
+        float rowpart[DK * kRowPart];   // P2 row partials
+    } u;
+    float red[2][8][DV];
+    float4 rowa[DK];  // P1: {fa, fa, k, k}          P3-P5: {r, r, 1/r, 1/r}
+    float4 rowb[DK];  // P1: {q, q, isint, -}        P3-P5: {-r, -r, w2, w2}
+    float4 rowc[DK];  // P3-P5: {rn, rn, 2^(b-8), 2^(b-8)}   rn = r 2^(8-b)
+    float4 rowd[DK];  // P3-P5: {limit, 1/limit, qmax, isint}
+    float colc[4][DV];
+    float misc[64];
+    int flags;
+};
+
+__device__ __forceinline__ int qmax_i(int b) { return (1 << ((b > 8 ? 8 : b) - 1)) - 1; }
+
+// P0: unpack every (row, tile) chunk of the staged codes into the fp16 plane.
+template <int MODE>
+__device__ __forceinline__ void kda_unpack(KdaSmem &s, int lead, int off0, int stride, int tid) {
+    for (int idx = tid; idx < DK * DTILES; idx += kThreads) {
+        const int k = idx >> 5, t = idx & 31;
+        const int b = s.bits[k];
+        const unsigned char *src = s.codes + lead + (s.offs[k] - off0) + t * stride;
+        __half h[4];
+        if (b == 16) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                h[j] = MODE == kWriteback ? __float2half_rn(0.f)
+                                          : __ushort_as_half(uint16_t(src[2 * j] | (uint16_t(src[2 * j + 1]) << 8)));
+        } else {
+            uint32_t w = src[0];
+            if (b >= 4) w |= uint32_t(src[1]) << 8;
+            if (b >= 6) w |= uint32_t(src[2]) << 16;
+            if (b == 8) w |= uint32_t(src[3]) << 24;
+            const int off = qmax_i(b), mask = (1 << b) - 1;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) h[j] = __int2half_rn(int((w >> (j * b)) & uint32_t(mask)) - off);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int v = 4 * t + j;
+            s.u.plane[k * DV + (v & 31) * 4 + (v >> 5)] = h[j];
+        }
+    }
+}
+
+template <bool SLOW>
+__device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int tid, float2 (&X)[16][2]) {
+    // P3: c0 = fp16(max over integer rows of |x / r| / limit).
+    {
+        float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int k = warp * 16 + r;
+            const float4 a = s.rowa[k], b = s.rowb[k], d = s.rowd[k];
+            const float2 lim = make_float2(d.x, d.x), rl = make_float2(d.y, d.y), nl = make_float2(-d.x, -d.x);
+            const float keep = d.w;
+            const float2 s01 = divide2<SLOW>(X[r][0], lo2(a), hi2(a), lo2(b));
+            const float2 s23 = divide2<SLOW>(X[r][1], lo2(a), hi2(a), lo2(b));
+            const float2 t01 = divide2<SLOW>(make_float2(fabsf(s01.x), fabsf(s01.y)), lim, rl, nl);
+            const float2 t23 = divide2<SLOW>(make_float2(fabsf(s23.x), fabsf(s23.y)), lim, rl, nl);
+            m0 = fmaxf(m0, t01.x * keep);
+            m1 = fmaxf(m1, t01.y * keep);
+            m2 = fmaxf(m2, t23.x * keep);
+            m3 = fmaxf(m3, t23.y * keep);
+        }
+        s.red[0][warp][lane] = m0;
+        s.red[0][warp][lane + 32] = m1;
+        s.red[0][warp][lane + 64] = m2;
+        s.red[0][warp][lane + 96] = m3;
+    }
+    __syncthreads();
+    if (tid < DV) {
+        float mx = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
+        const float c0 = fp16_scale(mx);
+        s.colc[1][tid] = c0;
+        s.colc[2][tid] = __frcp_rn(c0);
+    }
+    __syncthreads();
+    // P4: first levels and the weighted least-squares sums; X -> x / r (integer rows).
+    {
+        const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
+        const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
+        const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
+        const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
+        const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
+        const float2 round = make_float2(kRound, kRound), nround = make_float2(-kRound, -kRound);
+        float2 num[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}, den[2] = {num[0], num[1]};
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int k = warp * 16 + r;
+            const float4 a = s.rowa[k], b = s.rowb[k], cc = s.rowc[k], d = s.rowd[k];
+            const float2 rn = lo2(cc), inv = hi2(cc), w2 = hi2(b);
+            const float q = d.z;
+            const bool integer = d.w != 0.f;
+            const float2 nrk = pmul2(rn, nround);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float2 x = X[r][h];
+                const float2 sn = divide2<SLOW>(x, lo2(a), hi2(a), lo2(b));
+                float2 y = pmul2(divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), inv);
+                y = clamp2(y, q);
+                const float2 v = pfma2(rn, __fadd2_rn(y, round), nrk);
+                num[h] = __fadd2_rn(num[h], product_term(pmul2(w2, v), x));
+                den[h] = __fadd2_rn(den[h], product_term(w2, pmul2(v, v)));
+                if (integer) X[r][h] = sn;
+            }
+        }
+        s.red[0][warp][lane] = num[0].x;
+        s.red[0][warp][lane + 32] = num[0].y;
+        s.red[0][warp][lane + 64] = num[1].x;
+        s.red[0][warp][lane + 96] = num[1].y;
+        s.red[1][warp][lane] = den[0].x;
+        s.red[1][warp][lane + 32] = den[0].y;
+        s.red[1][warp][lane + 64] = den[1].x;
+        s.red[1][warp][lane + 96] = den[1].y;
+    }
+    __syncthreads();
+    if (tid < DV) {
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            num = __fadd_rn(num, s.red[0][w][tid]);
+            den = __fadd_rn(den, s.red[1][w][tid]);
+        }
+        const float c1 = den > 0.f ? fp16_scale(__fdiv_rn(num, fmaxf(den, 1e-30f))) : s.colc[1][tid];
+        s.colc[1][tid] = c1;
+        s.colc[2][tid] = __frcp_rn(c1);
+    }
+    __syncthreads();
+    // P5: final levels (integer rows) or the fp16 values (pivot rows) -> plane.
+    {
+        const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
+        const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
+        const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
+        const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
+        const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
+        const float2 round = make_float2(kRound, kRound), nround = make_float2(-kRound, -kRound);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int k = warp * 16 + r;
+            const float4 cc = s.rowc[k], d = s.rowd[k];
+            float2 o[2];
+            if (d.w != 0.f) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float2 y = pmul2(divide2<SLOW>(X[r][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), hi2(cc));
+                    y = clamp2(y, d.z);
+                    o[h] = __fadd2_rn(__fadd2_rn(y, round), nround);  // the integer level
+                }
+            } else {
+                o[0] = X[r][0];
+                o[1] = X[r][1];
+            }
+            // interleaved [k][l][i]: i = 0..3 <-> columns l, l+32, l+64, l+96
+            const __half2 h01 = __floats2half2_rn(o[0].x, o[0].y), h23 = __floats2half2_rn(o[1].x, o[1].y);
+            uint2 out;
+            out.x = *reinterpret_cast<const uint32_t *>(&h01);
+            out.y = *reinterpret_cast<const uint32_t *>(&h23);
+            *reinterpret_cast<uint2 *>(&s.u.plane[k * DV + lane * 4]) = out;
+        }
+    }
+    __syncthreads();
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    KdaSmem &s = *reinterpret_cast<KdaSmem *>(smem_raw);
+    const sq_plan &P = p.plan;
+    const int H = P.heads;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int req = blockIdx.x / H, head = blockIdx.x % H;
+    const int64_t slot = p.slots[req];
+    if (MODE == kReadout && head == 0 && tid == 0) p.stable_slots[req] = slot;
+    if (!fast_head_dev(P, head)) return;  // the tile kernel handles this head
+    if (!(slot > 0 && slot < p.num_slots)) {
+        if (slot > 0 && tid == 0) flag(p.status, SQ_STATUS_SLOT_RANGE);
+        if (MODE != kWriteback && tid < DV)
+            store_from_float(p.step.out, p.step.io_dtype, (int64_t(req) * H + head) * DV + tid, 0.f);
+        if (MODE == kStep && p.dense_out) {
+            float *dst = p.dense_out + (int64_t(req) * H + head) * DK * DV;
+            for (int e = tid; e < DK * DV; e += kThreads) dst[e] = 0.f;
+        }
+        return;
+    }
+    uint8_t *page = p.pages + slot * P.page_bytes;
+    const int stride = P.offsets[H * DK + head];
+    const int off0 = P.offsets[head * DK];
+    const int coff = P.columns[head];
+
+    // ---- stage the code region (16-byte cover), per-row tables, inputs ------
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(page + off0);
+    const uintptr_t base = a0 & ~uintptr_t(15);
+    const int lead = int(a0 - base);
+    {
+        const int span = lead + stride * DTILES;
+        for (int j = tid; 16 * j < span; j += kThreads)
+            cp_async16(s.codes + 16 * j, reinterpret_cast<const void *>(base + 16 * uintptr_t(j)));
+    }
+    float qx = 0.f, kx = 0.f, vin = 0.f, ga = 0.f, rold = 1.f, cold = 0.f, decay = 1.f, delta = 0.f;
+    int bk = 16;
+    if (tid < DK) {
+        bk = P.bits[head * DK + tid];
+        s.bits[tid] = bk;
+        s.offs[tid] = P.offsets[head * DK + tid];
+        const int ro = P.rows[head * DK + tid];
+        s.rows[tid] = ro;
+        s.imp[tid] = P.impact[head * DK + tid];
+        if (ro >= 0) rold = half_at(page, ro);
+        cold = half_at(page, coff + 2 * tid);
+        if (MODE == kWriteback) {
+            const float *sc = p.scratch + int64_t(req) * p.scratch_stride + int64_t(head) * (DV + 2 * DK);
+            delta = sc[tid];
+            kx = sc[DV + tid];
+            decay = sc[DV + DK + tid];
+        } else {
+            const sq_step_args &a = p.step;
+            const int qh = head / (H / a.qk_heads);
+            qx = load_as_float(a.q, a.io_dtype, int64_t(req) * a.q_stride + int64_t(qh) * DK + tid);
+            kx = load_as_float(a.k, a.io_dtype, int64_t(req) * a.k_stride + int64_t(qh) * DK + tid);
+            vin = load_as_float(a.v, a.io_dtype, int64_t(req) * a.v_stride + int64_t(head) * DV + tid);
+            ga = load_as_float(a.g, a.gate_dtype, (int64_t(req) * H + head) * DK + tid);
+        }
+    }
+    float beta = 0.f, qk = 0.f;
+    if (MODE != kWriteback) {
+        const sq_step_args &a = p.step;
+        const float braw = load_as_float(a.beta, a.gate_dtype, int64_t(req) * H + head);
+        float3 part = make_float3(__fmul_rn(qx, qx), __fmul_rn(kx, kx), __fmul_rn(qx, kx));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            part.x += __shfl_xor_sync(0xffffffffu, part.x, o);
+            part.y += __shfl_xor_sync(0xffffffffu, part.y, o);
+            part.z += __shfl_xor_sync(0xffffffffu, part.z, o);
+        }
+        if (lane == 0) {
+            s.misc[4 * warp] = part.x;
+            s.misc[4 * warp + 1] = part.y;
+            s.misc[4 * warp + 2] = part.z;
+        }
+        beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
+        if (tid < DK) {
+            float g = ga;
+            if (a.a_log) {
+                const float u = g + a.dt_bias[head * DK + tid];
+                g = -expf(a.a_log[head]) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
+            }
+            decay = expf(g);
+        }
+    }
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+    __syncthreads();
+    if (MODE != kWriteback) {
+        const sq_step_args &a = p.step;
+        float qq = 0.f, kk = 0.f, dot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) {
+            qq += s.misc[4 * w];
+            kk += s.misc[4 * w + 1];
+            dot += s.misc[4 * w + 2];
+        }
+        const float qn = a.normalize ? __frsqrt_rn(qq + 1e-6f) : 1.f;
+        const float kn = a.normalize ? __frsqrt_rn(kk + 1e-6f) : 1.f;
+        qx = __fmul_rn(__fmul_rn(qx, qn), a.scale);
+        kx = __fmul_rn(kx, kn);
+        qk = __fmul_rn(__fmul_rn(__fmul_rn(dot, qn), kn), a.scale);
+    }
+    if (tid < DK) {
+        const bool integer = bk != 16;
+        const float norm = integer ? float(1 << (8 - (bk > 8 ? 8 : bk))) : 1.f;
+        const float fa = integer ? __fmul_rn(__fmul_rn(rold, norm), decay) : decay;
+        s.rowa[tid] = make_float4(fa, fa, kx, kx);
+        s.rowb[tid] = make_float4(qx, qx, integer ? 1.f : 0.f, 0.f);
+        s.colc[3][tid] = cold;
+        if (MODE == kWriteback) s.colc[0][tid] = delta;
+    }
+    kda_unpack<MODE>(s, lead, off0, stride, tid);
+    __syncthreads();
+
+    // ---- P1: dequantize and decay; column partials of k^T S and q^T S -------
+    float2 X[16][2];
+    {
+        const float2 c01 = make_float2(s.colc[3][lane], s.colc[3][lane + 32]);
+        const float2 c23 = make_float2(s.colc[3][lane + 64], s.colc[3][lane + 96]);
+        const float2 one = make_float2(1.f, 1.f);
+        float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int k = warp * 16 + r;
+            const float4 a = s.rowa[k], b = s.rowb[k];
+            const uint2 raw = *reinterpret_cast<const uint2 *>(&s.u.plane[k * DV + lane * 4]);
+            const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+            const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+            const bool integer = b.z != 0.f;
+            const float2 m01 = integer ? c01 : one, m23 = integer ? c23 : one;
+            const float2 x01 = pmul2(pmul2(v01, lo2(a)), m01);
+            const float2 x23 = pmul2(pmul2(v23, lo2(a)), m23);
+            X[r][0] = x01;
+            X[r][1] = x23;
+            kx01 = pfma2(hi2(a), x01, kx01);
+            kx23 = pfma2(hi2(a), x23, kx23);
+            qx01 = pfma2(lo2(b), x01, qx01);
+            qx23 = pfma2(lo2(b), x23, qx23);
+        }
+        if (MODE != kWriteback) {
+            s.red[0][warp][lane] = kx01.x;
+            s.red[0][warp][lane + 32] = kx01.y;
+            s.red[0][warp][lane + 64] = kx23.x;
+            s.red[0][warp][lane + 96] = kx23.y;
+            s.red[1][warp][lane] = qx01.x;
+            s.red[1][warp][lane + 32] = qx01.y;
+            s.red[1][warp][lane + 64] = qx23.x;
+            s.red[1][warp][lane + 96] = qx23.y;
+            __syncthreads();
+            if (tid < DV) {
+                float ks = 0.f, qs = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    ks = __fadd_rn(ks, s.red[0][w][tid]);
+                    qs = __fadd_rn(qs, s.red[1][w][tid]);
+                }
+                const float d = __fmul_rn(beta, __fsub_rn(vin, ks));
+                s.colc[0][tid] = d;
+                store_from_float(p.step.out, p.step.io_dtype, (int64_t(req) * H + head) * DV + tid, __fmaf_rn(qk, d, qs));
+                if (MODE == kReadout) {
+                    float *sc = p.scratch + int64_t(req) * p.scratch_stride + int64_t(head) * (DV + 2 * DK);
+                    sc[tid] = d;
+                    sc[DV + tid] = kx;
+                    sc[DV + DK + tid] = decay;
+                }
+            }
+        }
+        __syncthreads();  // P1 reads of the plane are done before P2 writes row partials over it
+    }
+
+    // ---- P2: rank-1 update; row sums of |x| in torch order; row constants ----
+    {
+        const float2 d01 = make_float2(s.colc[0][lane], s.colc[0][lane + 32]);
+        const float2 d23 = make_float2(s.colc[0][lane + 64], s.colc[0][lane + 96]);
+        float *rowpart = s.u.rowpart;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int k = warp * 16 + r;
+            const float2 kk = hi2(s.rowa[k]);
+            X[r][0] = pfma2(kk, d01, X[r][0]);
+            X[r][1] = pfma2(kk, d23, X[r][1]);
+            const float a = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, fabsf(X[r][0].x)), fabsf(X[r][0].y)),
+                                                fabsf(X[r][1].x)), fabsf(X[r][1].y));
+            rowpart[k * kRowPart + lane] = a;
+        }
+        if (MODE == kStep && p.dense_out) {
+            float *dst = p.dense_out + (int64_t(req) * H + head) * DK * DV;
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                float *row = dst + (warp * 16 + r) * DV + lane;
+                row[0] = X[r][0].x;
+                row[32] = X[r][0].y;
+                row[64] = X[r][1].x;
+                row[96] = X[r][1].y;
+            }
+        }
+        if (MODE == kReadout) {
+            // fp16 pivot rows are final after the update: store them now.
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                const int k = warp * 16 + r;
+                if (s.bits[k] != 16) continue;
+                const float xs[4] = {X[r][0].x, X[r][0].y, X[r][1].x, X[r][1].y};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int v = lane + 32 * i;
+                    reinterpret_cast<__half *>(page + s.offs[k] + (v >> 2) * stride)[v & 3] = __float2half_rn(xs[i]);
+                }
+            }
+            return;
+        }
+        if (tid == 0) s.flags = 0;
+        __syncthreads();
+        const int j = lane & 15, half = lane >> 4;
+        const int k = warp * 16 + j;
+        const float *row = rowpart + k * kRowPart + 4 * half;
+        const float4 a0 = *reinterpret_cast<const float4 *>(row);
+        const float4 a1 = *reinterpret_cast<const float4 *>(row + 8);
+        const float4 a2 = *reinterpret_cast<const float4 *>(row + 16);
+        const float4 a3 = *reinterpret_cast<const float4 *>(row + 24);
+        const float s0 = __fadd_rn(__fadd_rn(__fadd_rn(a0.x, a1.x), a2.x), a3.x);
+        const float s1 = __fadd_rn(__fadd_rn(__fadd_rn(a0.y, a1.y), a2.y), a3.y);
+        const float s2 = __fadd_rn(__fadd_rn(__fadd_rn(a0.z, a1.z), a2.z), a3.z);
+        const float s3 = __fadd_rn(__fadd_rn(__fadd_rn(a0.w, a1.w), a2.w), a3.w);
+        float total = half ? 0.f : __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, s0), s1), s2), s3);
+        const float prefix = __shfl_sync(0xffffffffu, total, j);
+        if (half) {
+            total = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(prefix, s0), s1), s2), s3);
+            const int b = s.bits[k];
+            const bool integer = b != 16;
+            const float w = s.imp[k];
+            const float mean = __fdiv_rn(total, float(DV));
+            float rr = fp16_scale(__fsqrt_rn(__fdiv_rn(fmaxf(mean, 1e-20f), w)));
+            if (!integer) rr = 1.f;
+            const float rc = __frcp_rn(rr);
+            const float w2 = integer ? __fmul_rn(w, w) : 0.f;
+            const int bb = b > 8 ? 8 : b;
+            const float norm = float(1 << (8 - bb)), inv = __uint_as_float(uint32_t(127 - 8 + bb) << 23);
+            const float qm = float(qmax_i(b));
+            const float lim = __fmul_rn(qm, norm);
+            s.rowa[k] = make_float4(rr, rr, rc, rc);
+            s.rowb[k] = make_float4(-rr, -rr, w2, w2);
+            s.rowc[k] = make_float4(__fmul_rn(rr, norm), __fmul_rn(rr, norm), inv, inv);
+            s.rowd[k] = make_float4(lim, __frcp_rn(lim), qm, integer ? 1.f : 0.f);
+            if (integer && !(total <= 7.922816251426434e28f)) atomicOr(&s.flags, 1);  // 2^96, or NaN
+        }
+    }
+    __syncthreads();
+    if (s.flags) kda_quantize<true>(s, warp, lane, tid, X);
+    else kda_quantize<false>(s, warp, lane, tid, X);
+
+    // ---- pack the codes (and, for a fused step, the pivot rows) ------------
+    for (int idx = tid; idx < DK * DTILES; idx += kThreads) {
+        const int k = idx >> 5, t = idx & 31;
+        const int b = s.bits[k];
+        uint8_t *dst = page + s.offs[k] + t * stride;
+        __half h[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int v = 4 * t + j;
+            h[j] = s.u.plane[k * DV + (v & 31) * 4 + (v >> 5)];
+        }
+        if (b == 16) {
+            if (MODE == kStep) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) reinterpret_cast<__half *>(dst)[j] = h[j];
+            }
+        } else {
+            const int off = qmax_i(b);
+            uint32_t w = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) w |= uint32_t(__half2int_rn(h[j]) + off) << (j * b);
+            dst[0] = uint8_t(w);
+            if (b >= 4) dst[1] = uint8_t(w >> 8);
+            if (b >= 6) dst[2] = uint8_t(w >> 16);
+            if (b == 8) dst[3] = uint8_t(w >> 24);
+        }
+    }
+    if (tid < DK) {
+        if (s.rows[tid] >= 0) put_half(page, s.rows[tid], s.rowa[tid].x);
+    } else {
+        put_half(page, coff + 2 * (tid - DK), s.colc[1][tid - DK]);
+    }
+}
+
+template <int MODE>
+cudaError_t launch_kda_mode(const TileParams &p, int items, cudaStream_t stream) {
+    const int smem = int(sizeof(KdaSmem));
+    cudaError_t err = cudaFuncSetAttribute(kda_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return err;
+    kda_kernel<MODE><<<items, kThreads, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool kda_fast_eligible(const sq_plan &plan) {
+    return plan.architecture == SQ_KDA && plan.keys == DK && plan.values == DV;
+}
+
+cudaError_t launch_fast_kda(int mode, const TileParams &p, int batch, cudaStream_t stream) {
+    const int items = batch * p.plan.heads;
+    if (items <= 0) return cudaSuccess;
+    switch (mode) {
+        case kStep: return launch_kda_mode<kStep>(p, items, stream);
+        case kReadout: return launch_kda_mode<kReadout>(p, items, stream);
+        case kWriteback: return launch_kda_mode<kWriteback>(p, items, stream);
+        default: return cudaErrorNotSupported;
+    }
+}
+
+}  // namespace sq

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
     int64_t slot = 1;
     if (MODE != kFit) slot = p.slots[req];
     if (MODE == kReadout && head == 0 && tid == 0) p.stable_slots[req] = slot;
-    if (p.skip_fast && fast_head(P, P.bits[head * K])) return;
+    if (p.skip_fast && fast_head_dev(P, head)) return;
     bool active = slot > 0;
     if (active && MODE != kFit && slot >= p.num_slots) {
         if (head == 0 && tid == 0) flag(p.status, SQ_STATUS_SLOT_RANGE);

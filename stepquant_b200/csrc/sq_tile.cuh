@@ -45,4 +45,22 @@ __host__ __device__ inline bool fast_head(const sq_plan &plan, int width) {
 }
 cudaError_t launch_fast(int mode, const TileParams &p, int batch, cudaStream_t stream);
 
+// Register-resident kernels for KDA heads with K = V = 128 (sq_fast_kda.cu):
+// a head qualifies when it has integer rows and its code region (stride x
+// V / 4 value tiles) fits the kernel's stage buffer.
+constexpr int kKdaCodeCap = 12288;
+__host__ __device__ inline bool kda_head_fits(int64_t stride, int values, int columns_offset) {
+    return columns_offset >= 0 && stride * (values / 4) <= kKdaCodeCap;
+}
+bool kda_fast_eligible(const sq_plan &plan);
+cudaError_t launch_fast_kda(int mode, const TileParams &p, int batch, cudaStream_t stream);
+
+// Device-side: is `head` handled by a register-resident kernel (so the tile
+// kernel, launched with skip_fast, leaves it)?
+__device__ inline bool fast_head_dev(const sq_plan &P, int head) {
+    if (P.architecture == SQ_GDN) return fast_head(P, P.bits[head * P.keys]);
+    return P.keys == 128 && P.values == 128 &&
+           kda_head_fits(P.offsets[P.heads * P.keys + head], P.values, P.columns[head]);
+}
+
 }  // namespace sq
