@@ -51,7 +51,6 @@ struct KdaSmem {
 __device__ __forceinline__ int qmax_i(int b) { return (1 << ((b > 8 ? 8 : b) - 1)) - 1; }
 
 // P0: unpack every (row, tile) chunk of the staged codes into the fp16 plane.
-template <int MODE>
 __device__ __forceinline__ void kda_unpack(KdaSmem &s, int lead, int off0, int stride, int tid) {
     for (int idx = tid; idx < DK * DTILES; idx += kThreads) {
         const int k = idx >> 5, t = idx & 31;
@@ -60,9 +59,7 @@ __device__ __forceinline__ void kda_unpack(KdaSmem &s, int lead, int off0, int s
         __half h[4];
         if (b == 16) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                h[j] = MODE == kWriteback ? __float2half_rn(0.f)
-                                          : __ushort_as_half(uint16_t(src[2 * j] | (uint16_t(src[2 * j + 1]) << 8)));
+            for (int j = 0; j < 4; ++j) h[j] = __ushort_as_half(uint16_t(src[2 * j] | (uint16_t(src[2 * j + 1]) << 8)));
         } else {
             uint32_t w = src[0];
             if (b >= 4) w |= uint32_t(src[1]) << 8;
@@ -313,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
         s.colc[3][tid] = cold;
         if (MODE == kWriteback) s.colc[0][tid] = delta;
     }
-    kda_unpack<MODE>(s, lead, off0, stride, tid);
+    kda_unpack(s, lead, off0, stride, tid);
     __syncthreads();
 
     // ---- P1: dequantize and decay; column partials of k^T S and q^T S -------
@@ -369,6 +366,9 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
                 }
             }
         }
+        // The readout writes no page bytes: the writeback rewrites each head's
+        // code region whole (pivot rows included, recomputed from the same inputs).
+        if (MODE == kReadout) return;
         __syncthreads();  // P1 reads of the plane are done before P2 writes row partials over it
     }
 
@@ -397,21 +397,6 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
                 row[64] = X[r][1].x;
                 row[96] = X[r][1].y;
             }
-        }
-        if (MODE == kReadout) {
-            // fp16 pivot rows are final after the update: store them now.
-#pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                const int k = warp * 16 + r;
-                if (s.bits[k] != 16) continue;
-                const float xs[4] = {X[r][0].x, X[r][0].y, X[r][1].x, X[r][1].y};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int v = lane + 32 * i;
-                    reinterpret_cast<__half *>(page + s.offs[k] + (v >> 2) * stride)[v & 3] = __float2half_rn(xs[i]);
-                }
-            }
-            return;
         }
         if (tid == 0) s.flags = 0;
         __syncthreads();
@@ -453,11 +438,11 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
     if (s.flags) kda_quantize<true>(s, warp, lane, tid, X);
     else kda_quantize<false>(s, warp, lane, tid, X);
 
-    // ---- pack the codes (and, for a fused step, the pivot rows) ------------
+    // ---- pack the codes and the pivot rows into the staged region ----------
     for (int idx = tid; idx < DK * DTILES; idx += kThreads) {
         const int k = idx >> 5, t = idx & 31;
         const int b = s.bits[k];
-        uint8_t *dst = page + s.offs[k] + t * stride;
+        unsigned char *dst = s.codes + lead + (s.offs[k] - off0) + t * stride;
         __half h[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -465,9 +450,11 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
             h[j] = s.u.plane[k * DV + (v & 31) * 4 + (v >> 5)];
         }
         if (b == 16) {
-            if (MODE == kStep) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) reinterpret_cast<__half *>(dst)[j] = h[j];
+            for (int j = 0; j < 4; ++j) {
+                const uint16_t u = __half_as_ushort(h[j]);
+                dst[2 * j] = uint8_t(u);
+                dst[2 * j + 1] = uint8_t(u >> 8);
             }
         } else {
             const int off = qmax_i(b);
@@ -478,6 +465,23 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
             if (b >= 4) dst[1] = uint8_t(w >> 8);
             if (b >= 6) dst[2] = uint8_t(w >> 16);
             if (b == 8) dst[3] = uint8_t(w >> 24);
+        }
+    }
+    __syncthreads();
+    // ---- write the head's code region back: whole 16-byte pieces as vectors,
+    // the ragged first and last pieces byte by byte (their other bytes belong
+    // to neighbouring heads or pages).  Alignment padding inside the region
+    // keeps the staged (prior) bytes.
+    {
+        const uintptr_t a_end = a0 + uintptr_t(stride) * DTILES;
+        for (int j = tid; base + 16 * uintptr_t(j) < a_end; j += kThreads) {
+            const uintptr_t g = base + 16 * uintptr_t(j);
+            if (g >= a0 && g + 16 <= a_end) {
+                *reinterpret_cast<uint4 *>(g) = *reinterpret_cast<const uint4 *>(s.codes + 16 * j);
+            } else {
+                for (int e = 0; e < 16; ++e)
+                    if (g + e >= a0 && g + e < a_end) *reinterpret_cast<uint8_t *>(g + e) = s.codes[16 * j + e];
+            }
         }
     }
     if (tid < DK) {
