@@ -77,6 +77,7 @@ int32_t run(int mode, sq::TileParams t, int32_t batch, cudaStream_t stream) {
     const int items = batch * t.plan.heads;
     if (items <= 0) return SQ_OK;
     const bool fast_mode = mode == sq::kStep || mode == sq::kReadout || mode == sq::kWriteback;
+    const bool gdn_codec = mode == sq::kEncode || mode == sq::kDecode;
     if (fast_mode && sq::kda_fast_eligible(t.plan)) {
         if (cudaError_t e = sq::launch_fast_kda(mode, t, batch, stream)) return cuda_status(e);
         bool rest = true;
@@ -87,7 +88,7 @@ int32_t run(int mode, sq::TileParams t, int32_t batch, cudaStream_t stream) {
         }
         if (!rest) return SQ_OK;
         t.skip_fast = 1;
-    } else if (fast_mode && sq::fast_eligible(t.plan, t.pages)) {
+    } else if ((fast_mode || gdn_codec) && sq::fast_eligible(t.plan, t.pages)) {
         if (cudaError_t e = sq::launch_fast(mode, t, batch, stream)) return cuda_status(e);
         bool rest = true;
         if (t.plan.bits_host) {

@@ -336,6 +336,32 @@ __device__ __forceinline__ void unpack_rows(const FastSmem &s, const FastStage &
     acc[3] = qx23;
 }
 
+// Decode of one width: x = (r * c) * level (the order of the reference codec),
+// written to the dense output.
+template <int BITS>
+__device__ __forceinline__ void decode_rows(const FastStage &st, int warp, int lane, float *dst) {
+    const int t0 = lane >> 4, u = lane & 15;
+    const float2 c01 = make_float2(__half2float(st.cold[lane]), __half2float(st.cold[lane + 32]));
+    const float2 c23 = make_float2(__half2float(st.cold[lane + 64]), __half2float(st.cold[lane + 96]));
+    const float2 lc = level_constants<BITS>(u);
+    const float2 lscale = make_float2(lc.x, lc.x), lbias = make_float2(lc.y, lc.y);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const int k = warp * 16 + r;
+        const float rk = __half2float(st.rold[k]);
+        const float2 rr = make_float2(rk, rk);
+        const float2 f01 = make_float2(staged_bits<BITS>(st.codes, t0, k, u), staged_bits<BITS>(st.codes, t0 + 2, k, u));
+        const float2 f23 = make_float2(staged_bits<BITS>(st.codes, t0 + 4, k, u), staged_bits<BITS>(st.codes, t0 + 6, k, u));
+        const float2 x01 = pmul2(pmul2(rr, c01), pfma2(f01, lscale, lbias));
+        const float2 x23 = pmul2(pmul2(rr, c23), pfma2(f23, lscale, lbias));
+        float *row = dst + k * FV + lane;
+        row[0] = x01.x;
+        row[32] = x01.y;
+        row[64] = x23.x;
+        row[96] = x23.y;
+    }
+}
+
 // One (request, head) work item of the persistent loop.
 struct WorkItem {
     int req, head, width;
@@ -367,14 +393,16 @@ __device__ __forceinline__ void prefetch(const TileParams &p, const FastSmem &s,
     const HeadInfo &hi = s.head[it.head];
     const uint8_t *page = p.pages + it.slot * P.page_bytes;
     const uint8_t *src = page + hi.off_head;
-    if (it.width == 4) stage_codes<4>(st, src, tid);
-    else if (it.width == 6) stage_codes<6>(st, src, tid);
-    else stage_codes<8>(st, src, tid);
-    if (tid < 16) cp_async16(reinterpret_cast<unsigned char *>(st.rold) + tid * 16, page + hi.rows + tid * 16);
-    else if (tid < 32) cp_async16(reinterpret_cast<unsigned char *>(st.cold) + (tid - 16) * 16, page + hi.columns + (tid - 16) * 16);
-    if (MODE != kReadout && tid >= 160 && tid < 192)
+    if (MODE != kEncode) {
+        if (it.width == 4) stage_codes<4>(st, src, tid);
+        else if (it.width == 6) stage_codes<6>(st, src, tid);
+        else stage_codes<8>(st, src, tid);
+        if (tid < 16) cp_async16(reinterpret_cast<unsigned char *>(st.rold) + tid * 16, page + hi.rows + tid * 16);
+        else if (tid < 32) cp_async16(reinterpret_cast<unsigned char *>(st.cold) + (tid - 16) * 16, page + hi.columns + (tid - 16) * 16);
+    }
+    if (MODE != kReadout && MODE != kDecode && tid >= 160 && tid < 192)
         cp_async16(reinterpret_cast<unsigned char *>(st.imp) + (tid - 160) * 16, P.impact + int64_t(it.head) * FK + (tid - 160) * 4);
-    if (!p.stage_inputs) return;
+    if (MODE == kEncode || MODE == kDecode || !p.stage_inputs) return;
     unsigned char *in = reinterpret_cast<unsigned char *>(st.in);
     const int j = tid - 32;
     if (MODE == kWriteback) {
@@ -413,6 +441,13 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
     const sq_plan &P = p.plan;
     const int H = P.heads;
     const int warp = c.warp, lane = c.lane, tid = c.tid;
+    if (MODE == kDecode) {
+        float *dst = p.dense_out + (int64_t(c.req) * H + c.head) * FK * FV;
+        if (width == 4) decode_rows<4>(st, warp, lane, dst);
+        else if (width == 6) decode_rows<6>(st, warp, lane, dst);
+        else decode_rows<8>(st, warp, lane, dst);
+        return;
+    }
 
     // ---- per-request inputs -------------------------------------------------
     // P1 works on Y = level * r_old (no decay, no column scale) with raw q and
@@ -420,7 +455,9 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
     // with the unpack.  The updated state is x' = Y * (c * decay) + k * delta,
     // and k^T (D S) = kn * (c * decay) * sum_k(k_raw * Y) (likewise for q).
     float vin = 0.f, kraw = 0.f, braw = 0.f, graw = 0.f;
-    if (MODE == kWriteback) {
+    if (MODE == kEncode) {
+        // nothing: the state comes from the dense input
+    } else if (MODE == kWriteback) {
         const float *sc = p.scratch + int64_t(c.req) * p.scratch_stride + int64_t(c.head) * (FV + 2 * FK);
         if (tid < FK) {
             const float delta = p.stage_inputs ? st.in[0][tid] : sc[tid];
@@ -469,7 +506,15 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 
     // ---- P1: unpack; column partials of k_raw^T Y and q_raw^T Y ---------------
     float2 X[16][2];
-    {
+    if (MODE == kEncode) {
+        const float *src = p.dense_in + (int64_t(c.req) * H + c.head) * FK * FV;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const float *row = src + (warp * 16 + r) * FV + lane;
+            X[r][0] = make_float2(row[0], row[32]);
+            X[r][1] = make_float2(row[64], row[96]);
+        }
+    } else {
         float2 acc[4];
         if (width == 4) unpack_rows<4>(s, st, warp, lane, X, acc);
         else if (width == 6) unpack_rows<6>(s, st, warp, lane, X, acc);
@@ -546,8 +591,10 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
         for (int r = 0; r < 16; ++r) {
             const int k = warp * 16 + r;
             const float2 kk = hi2(s.rowa[k]);
-            X[r][0] = pfma2(kk, d01, pmul2(X[r][0], cd01));
-            X[r][1] = pfma2(kk, d23, pmul2(X[r][1], cd23));
+            if (MODE != kEncode) {
+                X[r][0] = pfma2(kk, d01, pmul2(X[r][0], cd01));
+                X[r][1] = pfma2(kk, d23, pmul2(X[r][1], cd23));
+            }
             const float a = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, fabsf(X[r][0].x)), fabsf(X[r][0].y)),
                                                 fabsf(X[r][1].x)), fabsf(X[r][1].y));
             rowpart[k * kRowPartStride + lane] = a;
@@ -610,7 +657,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 // the other stage buffer, and the slot of the item after that into a small
 // ring, so each item starts with its page, scales and inputs on chip.
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, MODE == kReadout ? 3 : 2) fast_kernel(TileParams p, int items) {
+__global__ void __launch_bounds__(kThreads, (MODE == kReadout || MODE == kDecode) ? 3 : 2) fast_kernel(TileParams p, int items) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FastSmem &s = *reinterpret_cast<FastSmem *>(smem_raw);
     const sq_plan &P = p.plan;
@@ -674,9 +721,9 @@ __global__ void __launch_bounds__(kThreads, MODE == kReadout ? 3 : 2) fast_kerne
                 fast_body<MODE>(p, s, s.st[buf], c, cur.width);
             } else {
                 if (cur.slot > 0 && c.tid == 0) flag(p.status, SQ_STATUS_SLOT_RANGE);
-                if (MODE != kWriteback && c.tid < FV)
+                if ((MODE == kStep || MODE == kReadout) && c.tid < FV)
                     store_from_float(p.step.out, p.step.io_dtype, (int64_t(c.req) * H + c.head) * FV + c.tid, 0.f);
-                if (MODE == kStep && p.dense_out) {
+                if ((MODE == kStep || MODE == kDecode) && p.dense_out) {
                     float *dst = p.dense_out + (int64_t(c.req) * H + c.head) * FK * FV;
                     for (int e = c.tid; e < FK * FV; e += kThreads) dst[e] = 0.f;
                 }
@@ -692,7 +739,7 @@ __global__ void __launch_bounds__(kThreads, MODE == kReadout ? 3 : 2) fast_kerne
 
 // Resident CTAs per device for each mode (set up on the first launch on a device).
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_resident[3][kMaxDevices];
+std::atomic<int> g_resident[6][kMaxDevices];
 
 template <int MODE>
 cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream) {
@@ -700,7 +747,7 @@ cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream
     int device = 0;
     cudaError_t err = cudaGetDevice(&device);
     if (err != cudaSuccess) return err;
-    std::atomic<int> *resident = device < kMaxDevices ? &g_resident[MODE - kStep][device] : nullptr;
+    std::atomic<int> *resident = device < kMaxDevices ? &g_resident[MODE][device] : nullptr;
     int ctas = resident ? resident->load(std::memory_order_relaxed) : 0;
     if (ctas == 0) {
         err = cudaFuncSetAttribute(fast_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -750,6 +797,8 @@ cudaError_t launch_fast(int mode, const TileParams &params, int batch, cudaStrea
         case kStep: return launch_fast_mode<kStep>(p, items, stream);
         case kReadout: return launch_fast_mode<kReadout>(p, items, stream);
         case kWriteback: return launch_fast_mode<kWriteback>(p, items, stream);
+        case kEncode: return launch_fast_mode<kEncode>(p, items, stream);
+        case kDecode: return launch_fast_mode<kDecode>(p, items, stream);
         default: return cudaErrorNotSupported;
     }
 }
