@@ -91,6 +91,18 @@ __device__ __forceinline__ void load_b_kn(uint32_t (&b)[4], const bf16 (*m)[LD],
     ldsm4t(b, &m[k0 + r + 8 * (i & 1)][n0 + 8 * (i >> 1)]);
 }
 
+__device__ __forceinline__ uint32_t tf32_bits(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+    return r;
+}
+// d += a (16x8, tf32, row-major fragment) * b (8x8, tf32, column fragment); fp32 accumulators.
+__device__ __forceinline__ void mma1688_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<const uint32_t *>(&v);
@@ -158,13 +170,15 @@ __global__ void __launch_bounds__(1024) offsets_kernel(sq_prefill_args a, int32_
 // ---------------------------------------------------------------------------
 // prep_kernel: one 256-thread CTA per (chunk, value head).
 // ---------------------------------------------------------------------------
+constexpr int kLdQ = 144;  // the q tile holds Tw and Tu (bf16 64x72 each) once q is no longer needed
+
 struct PrepSmem {
-    bf16 q[PC][kLd];
+    bf16 q[PC][kLdQ];   // raw q; then Tw (first half) and Tu (second half)
     bf16 k[PC][kLd];
     bf16 v[PC][kLd];
-    float l[PC][kLdF];  // L; then Tu (bf16 [64][72])
+    float l[PC][kLdF];  // L
     float t[PC][kLdF];  // T
-    float x[PC][kLdF];  // block products; then Tw (bf16 [64][72])
+    float x[PC][kLdF];  // off-diagonal block products
     float gam[PC];
     float beta[PC];
     float nq[PC];
@@ -263,7 +277,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
         for (int ks = 0; ks < PK / 16; ++ks) {
             uint32_t ak[4], aq[4], b0[4], b1[4];
             load_a<kLd>(ak, s.k, r0, 16 * ks, lane);
-            load_a<kLd>(aq, s.q, r0, 16 * ks, lane);
+            load_a<kLdQ>(aq, s.q, r0, 16 * ks, lane);
             load_b_nk<kLd>(b0, s.k, c0, 16 * ks, lane);
             load_b_nk<kLd>(b1, s.k, c0 + 16, 16 * ks, lane);
             mma16816(accG[0], ak, b0[0], b0[1]);
@@ -304,10 +318,16 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
     }
     __syncthreads();
 
-    // ---- T = (I + L)^-1: diagonal blocks by substitution, then block rows 1..3
+    // ---- T = (I + L)^-1 in fp32: 16x16 diagonal blocks by substitution, then
+    // block rows r = 1..3 on tensor cores (tf32): T_rc = -T_rr (sum_m L_rm T_mc).
+    // Each block of Tw = T diag(beta e^gam nk) and Tu = T diag(beta) (bf16, in the
+    // dead q tile) is written as soon as the block of T is final.
+    bf16 (*Tw)[kLdP] = reinterpret_cast<bf16 (*)[kLdP]>(&s.q[0][0]);
+    bf16 (*Tu)[kLdP] = reinterpret_cast<bf16 (*)[kLdP]>(&s.q[0][0] + PC * kLdP);
     if (warp < 4) {
         if (lane < 16) {
             const int b = 16 * warp, m = lane;
+            const float fw = s.fw[b + m], fb = s.beta[b + m];
             float t[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -316,58 +336,81 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
                 for (int j = 0; j < i; ++j) val -= s.l[b + i][b + j] * t[j];
                 t[i] = val;
                 s.t[b + i][b + m] = val;
+                Tw[b + i][b + m] = __float2bfloat16_rn(val * fw);
+                Tu[b + i][b + m] = __float2bfloat16_rn(val * fb);
             }
         }
     } else {
+        // zero the blocks of Tw and Tu above the diagonal
         for (int e = tid - 128; e < 6 * 256; e += 128) {
             const int blk = e >> 8, i = (e >> 4) & 15, m = e & 15;
             const int r = blk < 3 ? 0 : blk < 5 ? 1 : 2;
             const int c = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
-            s.t[16 * r + i][16 * c + m] = 0.f;
+            Tw[16 * r + i][16 * c + m] = __float2bfloat16_rn(0.f);
+            Tu[16 * r + i][16 * c + m] = __float2bfloat16_rn(0.f);
         }
     }
     __syncthreads();
     for (int r = 1; r < 4; ++r) {
-        for (int e = tid; e < r * 256; e += 256) {
-            const int c = e >> 8, i = (e >> 4) & 15, m = e & 15;
-            const float *lrow = &s.l[16 * r + i][0];
-            float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+        if (warp < r) {
+            const int c = warp;
+            float X[2][4] = {};
             for (int mb = c; mb < r; ++mb) {
 #pragma unroll
-                for (int j = 0; j < 16; j += 4) {
-                    const int jj = 16 * mb + j;
-                    x0 += lrow[jj] * s.t[jj][16 * c + m];
-                    x1 += lrow[jj + 1] * s.t[jj + 1][16 * c + m];
-                    x2 += lrow[jj + 2] * s.t[jj + 2][16 * c + m];
-                    x3 += lrow[jj + 3] * s.t[jj + 3][16 * c + m];
+                for (int kk = 0; kk < 2; ++kk) {
+                    const int col = 16 * mb + 8 * kk;
+                    uint32_t af[4];
+                    af[0] = tf32_bits(s.l[16 * r + g8][col + tig]);
+                    af[1] = tf32_bits(s.l[16 * r + g8 + 8][col + tig]);
+                    af[2] = tf32_bits(s.l[16 * r + g8][col + tig + 4]);
+                    af[3] = tf32_bits(s.l[16 * r + g8 + 8][col + tig + 4]);
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        const uint32_t b0 = tf32_bits(s.t[col + tig][16 * c + 8 * nt + g8]);
+                        const uint32_t b1 = tf32_bits(s.t[col + tig + 4][16 * c + 8 * nt + g8]);
+                        mma1688_tf32(X[nt], af, b0, b1);
+                    }
                 }
             }
-            s.x[16 * r + i][16 * c + m] = (x0 + x1) + (x2 + x3);
-        }
-        __syncthreads();
-        for (int e = tid; e < r * 256; e += 256) {
-            const int c = e >> 8, i = (e >> 4) & 15, m = e & 15;
-            float t0 = 0.f, t1 = 0.f;
 #pragma unroll
-            for (int j = 0; j < 16; j += 2) {
-                t0 -= s.t[16 * r + i][16 * r + j] * s.x[16 * r + j][16 * c + m];
-                t1 -= s.t[16 * r + i][16 * r + j + 1] * s.x[16 * r + j + 1][16 * c + m];
+            for (int nt = 0; nt < 2; ++nt) {
+                const int col = 16 * c + 8 * nt + 2 * tig;
+                s.x[16 * r + g8][col] = X[nt][0];
+                s.x[16 * r + g8][col + 1] = X[nt][1];
+                s.x[16 * r + g8 + 8][col] = X[nt][2];
+                s.x[16 * r + g8 + 8][col + 1] = X[nt][3];
             }
-            s.t[16 * r + i][16 * c + m] = t0 + t1;
+            __syncwarp();
+            float Y[2][4] = {};
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+                const int col = 16 * r + 8 * kk;
+                uint32_t af[4];
+                af[0] = tf32_bits(s.t[16 * r + g8][col + tig]);
+                af[1] = tf32_bits(s.t[16 * r + g8 + 8][col + tig]);
+                af[2] = tf32_bits(s.t[16 * r + g8][col + tig + 4]);
+                af[3] = tf32_bits(s.t[16 * r + g8 + 8][col + tig + 4]);
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    const uint32_t b0 = tf32_bits(s.x[col + tig][16 * c + 8 * nt + g8]);
+                    const uint32_t b1 = tf32_bits(s.x[col + tig + 4][16 * c + 8 * nt + g8]);
+                    mma1688_tf32(Y[nt], af, b0, b1);
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int i = 16 * r + g8 + 8 * (e >> 1), j = 16 * c + 8 * nt + 2 * tig + (e & 1);
+                    const float tv = -Y[nt][e];
+                    s.t[i][j] = tv;
+                    Tw[i][j] = __float2bfloat16_rn(tv * s.fw[j]);
+                    Tu[i][j] = __float2bfloat16_rn(tv * s.beta[j]);
+                }
+            }
         }
         __syncthreads();
     }
-
-    // ---- Tw = T diag(beta e^gam nk) (into x), Tu = T diag(beta) (into l), bf16
-    bf16 (*Tw)[kLdP] = reinterpret_cast<bf16 (*)[kLdP]>(&s.x[0][0]);
-    bf16 (*Tu)[kLdP] = reinterpret_cast<bf16 (*)[kLdP]>(&s.l[0][0]);
-    for (int e = tid; e < PC * PC; e += 256) {
-        const int i = e >> 6, j = e & 63;
-        const float t = s.t[i][j];
-        Tw[i][j] = __float2bfloat16_rn(t * s.fw[j]);
-        Tu[i][j] = __float2bfloat16_rn(t * s.beta[j]);
-    }
-    __syncthreads();
 
     // ---- -W = -Tw K and U = Tu V (rows 16 (w % 4), columns 64 (w / 4) .. +63)
     {
