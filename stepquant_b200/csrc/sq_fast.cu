@@ -739,7 +739,7 @@ __global__ void __launch_bounds__(kThreads, (MODE == kReadout || MODE == kDecode
 
 // Resident CTAs per device for each mode (set up on the first launch on a device).
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_resident[6][kMaxDevices];
+std::atomic<int> g_resident[kFit + 1][kMaxDevices];  // indexed by Mode
 
 template <int MODE>
 cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream) {

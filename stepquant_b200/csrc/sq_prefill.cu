@@ -172,13 +172,15 @@ __global__ void __launch_bounds__(1024) offsets_kernel(sq_prefill_args a, int32_
 // ---------------------------------------------------------------------------
 constexpr int kLdQ = 144;  // the q tile holds Tw and Tu (bf16 64x72 each) once q is no longer needed
 
+// 70 KB: three CTAs per SM.
 struct PrepSmem {
     bf16 q[PC][kLdQ];   // raw q; then Tw (first half) and Tu (second half)
     bf16 k[PC][kLd];
-    bf16 v[PC][kLd];
-    float l[PC][kLdF];  // L
+    union {
+        float l[PC][kLdF];  // L below the diagonal; the block products X_rc above it (block (c, r))
+        bf16 v[PC][kLd];    // raw v, loaded once T is complete
+    } lv;
     float t[PC][kLdF];  // T
-    float x[PC][kLdF];  // off-diagonal block products
     float gam[PC];
     float beta[PC];
     float nq[PC];
@@ -186,7 +188,7 @@ struct PrepSmem {
     float fw[PC];  // beta e^gam nk: column factors of Tw
 };
 
-__global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const int32_t *offsets,
+__global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const int32_t *offsets,
                                                       unsigned char *records) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     PrepSmem &s = *reinterpret_cast<PrepSmem *>(smem_raw);
@@ -205,18 +207,15 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
     const int qh = head / (H / a.qk_heads);
     unsigned char *rec = records + (int64_t(chunk) * H + head) * kRec;
 
-    // ---- raw q, k, v rows of the chunk (zero rows past the end), gates
+    // ---- raw q, k rows of the chunk (zero rows past the end), gates
     {
         const bf16 *qg = static_cast<const bf16 *>(a.q), *kg = static_cast<const bf16 *>(a.k);
-        const bf16 *vg = static_cast<const bf16 *>(a.v);
-        for (int idx = tid; idx < 3 * PC * 16; idx += 256) {
+        for (int idx = tid; idx < 2 * PC * 16; idx += 256) {
             const int which = idx >> 10, row = (idx >> 4) & 63, piece = idx & 15;
-            bf16 *dst = (which == 0 ? s.q[row] : which == 1 ? s.k[row] : s.v[row]) + piece * 8;
+            bf16 *dst = (which == 0 ? s.q[row] : s.k[row]) + piece * 8;
             if (row < n) {
                 const int64_t t = t0 + row;
-                const bf16 *src = which == 0 ? qg + t * a.q_stride + int64_t(qh) * PK
-                                  : which == 1 ? kg + t * a.k_stride + int64_t(qh) * PK
-                                               : vg + t * a.v_stride + int64_t(head) * PV;
+                const bf16 *src = which == 0 ? qg + t * a.q_stride + int64_t(qh) * PK : kg + t * a.k_stride + int64_t(qh) * PK;
                 cp16(dst, src + piece * 8);
             } else {
                 *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
@@ -309,7 +308,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
                 for (int e = 0; e < 2; ++e) {
                     const int jj = j + e;
                     const float dec = jj <= i ? __expf(gi[hh] - gj[e]) * nkj[e] : 0.f;
-                    s.l[i][jj] = jj < i ? li[hh] * dec * accG[nt][2 * hh + e] : 0.f;
+                    s.lv.l[i][jj] = jj < i ? li[hh] * dec * accG[nt][2 * hh + e] : 0.f;
                     pv[e] = pi[hh] * dec * accH[nt][2 * hh + e];
                 }
                 *reinterpret_cast<uint32_t *>(rec + kRecP + sw128(i, j, PC)) = pack_bf16(pv[0], pv[1]);
@@ -333,7 +332,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
             for (int i = 0; i < 16; ++i) {
                 float val = i == m ? 1.f : 0.f;
 #pragma unroll
-                for (int j = 0; j < i; ++j) val -= s.l[b + i][b + j] * t[j];
+                for (int j = 0; j < i; ++j) val -= s.lv.l[b + i][b + j] * t[j];
                 t[i] = val;
                 s.t[b + i][b + m] = val;
                 Tw[b + i][b + m] = __float2bfloat16_rn(val * fw);
@@ -360,10 +359,10 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
                 for (int kk = 0; kk < 2; ++kk) {
                     const int col = 16 * mb + 8 * kk;
                     uint32_t af[4];
-                    af[0] = tf32_bits(s.l[16 * r + g8][col + tig]);
-                    af[1] = tf32_bits(s.l[16 * r + g8 + 8][col + tig]);
-                    af[2] = tf32_bits(s.l[16 * r + g8][col + tig + 4]);
-                    af[3] = tf32_bits(s.l[16 * r + g8 + 8][col + tig + 4]);
+                    af[0] = tf32_bits(s.lv.l[16 * r + g8][col + tig]);
+                    af[1] = tf32_bits(s.lv.l[16 * r + g8 + 8][col + tig]);
+                    af[2] = tf32_bits(s.lv.l[16 * r + g8][col + tig + 4]);
+                    af[3] = tf32_bits(s.lv.l[16 * r + g8 + 8][col + tig + 4]);
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt) {
                         const uint32_t b0 = tf32_bits(s.t[col + tig][16 * c + 8 * nt + g8]);
@@ -372,13 +371,15 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
                     }
                 }
             }
+            // X_rc (local row i, column m) is kept at l[16 c + i][16 r + m], above the diagonal.
+            float (*xb)[kLdF] = reinterpret_cast<float (*)[kLdF]>(&s.lv.l[16 * c][16 * r]);
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
-                const int col = 16 * c + 8 * nt + 2 * tig;
-                s.x[16 * r + g8][col] = X[nt][0];
-                s.x[16 * r + g8][col + 1] = X[nt][1];
-                s.x[16 * r + g8 + 8][col] = X[nt][2];
-                s.x[16 * r + g8 + 8][col + 1] = X[nt][3];
+                const int col = 8 * nt + 2 * tig;
+                xb[g8][col] = X[nt][0];
+                xb[g8][col + 1] = X[nt][1];
+                xb[g8 + 8][col] = X[nt][2];
+                xb[g8 + 8][col + 1] = X[nt][3];
             }
             __syncwarp();
             float Y[2][4] = {};
@@ -392,8 +393,8 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
                 af[3] = tf32_bits(s.t[16 * r + g8 + 8][col + tig + 4]);
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt) {
-                    const uint32_t b0 = tf32_bits(s.x[col + tig][16 * c + 8 * nt + g8]);
-                    const uint32_t b1 = tf32_bits(s.x[col + tig + 4][16 * c + 8 * nt + g8]);
+                    const uint32_t b0 = tf32_bits(xb[8 * kk + tig][8 * nt + g8]);
+                    const uint32_t b1 = tf32_bits(xb[8 * kk + tig + 4][8 * nt + g8]);
                     mma1688_tf32(Y[nt], af, b0, b1);
                 }
             }
@@ -412,22 +413,52 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
         __syncthreads();
     }
 
-    // ---- -W = -Tw K and U = Tu V (rows 16 (w % 4), columns 64 (w / 4) .. +63)
+    // ---- raw v into the space of L (T is complete), while -W = -Tw K is formed
     {
-        const int r0 = 16 * (warp & 3), c0 = 64 * (warp >> 2);
-        float W[8][4] = {}, U[8][4] = {};
+        const bf16 *vg = static_cast<const bf16 *>(a.v);
+        for (int idx = tid; idx < PC * 16; idx += 256) {
+            const int row = idx >> 4, piece = idx & 15;
+            bf16 *dst = s.lv.v[row] + piece * 8;
+            if (row < n) cp16(dst, vg + (int64_t(t0) + row) * a.v_stride + int64_t(head) * PV + piece * 8);
+            else *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        asm volatile("cp.async.commit_group;\n" ::);
+    }
+    // Rows 16 (w % 4) and columns 64 (w / 4) .. +63 of -W, then of U.
+    const int wr0 = 16 * (warp & 3), wc0 = 64 * (warp >> 2);
+    {
+        float W[8][4] = {};
 #pragma unroll
         for (int ks = 0; ks < PC / 16; ++ks) {
-            uint32_t aw[4], au[4];
-            load_a<kLdP>(aw, Tw, r0, 16 * ks, lane);
-            load_a<kLdP>(au, Tu, r0, 16 * ks, lane);
+            uint32_t aw[4];
+            load_a<kLdP>(aw, Tw, wr0, 16 * ks, lane);
 #pragma unroll
             for (int np = 0; np < 4; ++np) {
-                uint32_t bk[4], bv[4];
-                load_b_kn<kLd>(bk, s.k, c0 + 16 * np, 16 * ks, lane);
-                load_b_kn<kLd>(bv, s.v, c0 + 16 * np, 16 * ks, lane);
+                uint32_t bk[4];
+                load_b_kn<kLd>(bk, s.k, wc0 + 16 * np, 16 * ks, lane);
                 mma16816(W[2 * np], aw, bk[0], bk[1]);
                 mma16816(W[2 * np + 1], aw, bk[2], bk[3]);
+            }
+        }
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            const int col = wc0 + 8 * nt + 2 * tig, i0 = wr0 + g8, i1 = i0 + 8;
+            *reinterpret_cast<uint32_t *>(rec + kRecW + sw128(i0, col, PC)) = pack_bf16(-W[nt][0], -W[nt][1]);
+            *reinterpret_cast<uint32_t *>(rec + kRecW + sw128(i1, col, PC)) = pack_bf16(-W[nt][2], -W[nt][3]);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;\n" ::);
+    __syncthreads();
+    {
+        float U[8][4] = {};
+#pragma unroll
+        for (int ks = 0; ks < PC / 16; ++ks) {
+            uint32_t au[4];
+            load_a<kLdP>(au, Tu, wr0, 16 * ks, lane);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t bv[4];
+                load_b_kn<kLd>(bv, s.lv.v, wc0 + 16 * np, 16 * ks, lane);
                 mma16816(U[2 * np], au, bv[0], bv[1]);
                 mma16816(U[2 * np + 1], au, bv[2], bv[3]);
             }
@@ -435,9 +466,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(sq_prefill_args a, const i
         bf16 *urec = reinterpret_cast<bf16 *>(rec + kRecU);
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
-            const int col = c0 + 8 * nt + 2 * tig, i0 = r0 + g8, i1 = i0 + 8;
-            *reinterpret_cast<uint32_t *>(rec + kRecW + sw128(i0, col, PC)) = pack_bf16(-W[nt][0], -W[nt][1]);
-            *reinterpret_cast<uint32_t *>(rec + kRecW + sw128(i1, col, PC)) = pack_bf16(-W[nt][2], -W[nt][3]);
+            const int col = wc0 + 8 * nt + 2 * tig, i0 = wr0 + g8, i1 = i0 + 8;
             *reinterpret_cast<uint32_t *>(urec + i0 * PV + col) = pack_bf16(U[nt][0], U[nt][1]);
             *reinterpret_cast<uint32_t *>(urec + i1 * PV + col) = pack_bf16(U[nt][2], U[nt][3]);
         }
