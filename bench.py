@@ -17,6 +17,11 @@ in the timed state path.  Requests rotate over 4 groups of slots (a 420 MB pool
 per GPU at N = 1, larger than the 126 MB L2), so each step reads pages that are
 not L2-resident.
 
+Other workloads: ``--workload kda-decode`` (config 2), ``gdn-prefill``
+(config 3: chunked prefill to the first packed state) and ``gdn-stack``
+(config 4: 48 GDN layers decoding through one CUDA graph per token, value heads
+tensor-parallel with an NCCL all-gather of each layer's readout).
+
 Prints one JSON line on rank 0.  ``--impl reference`` times the reference's CPU
 path (StateCodec.decode -> delta_step -> StateCodec.encode, restated in numpy
 by the oracle) on the host cores instead.
@@ -51,9 +56,10 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("stepquant_b200", "reference"), default="stepquant_b200")
     p.add_argument("--mode", choices=("async", "sync"), default="async")
-    p.add_argument("--workload", choices=("gdn-decode", "kda-decode", "gdn-prefill"), default="gdn-decode",
-                   help="config 1 (default), config 2, or config 3")
-    p.add_argument("--batch", type=int, default=0, help="default: 256 (config 1), 512 (config 2), 32 (config 3)")
+    p.add_argument("--workload", choices=("gdn-decode", "kda-decode", "gdn-prefill", "gdn-stack"), default="gdn-decode",
+                   help="config 1 (default), config 2, config 3 or config 4")
+    p.add_argument("--batch", type=int, default=0,
+                   help="default: 256 (config 1), 512 (config 2), 32 (config 3), 512 (config 4)")
     p.add_argument("--tokens", type=int, default=2048, help="prompt length (gdn-prefill)")
     p.add_argument("--heads", type=int, default=32)
     p.add_argument("--qk-heads", type=int, default=0, help="default: heads / 2 (GDN), heads (KDA)")
@@ -65,6 +71,11 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-secondary", action="store_true", help="skip the short config-2 / config-3 measurements")
+    p.add_argument("--layers", type=int, default=48, help="GDN layers of the stack (gdn-stack, config 4)")
+    p.add_argument("--hidden", type=int, default=5120, help="hidden size of the stack's projections (gdn-stack)")
+    p.add_argument("--prompt", type=int, default=128, help="prompt tokens per request before decoding (gdn-stack)")
+    p.add_argument("--writeback-chunk", type=int, default=0,
+                   help="requests per writeback launch (gdn-stack); default: the stepquant6 profile's chunk")
     return p.parse_args()
 
 
@@ -464,6 +475,202 @@ def measure_prefill(args, batch, tokens, heads_total, qk_total, steps, warmup, w
     return res
 
 
+def _rms_norm(x):
+    xf = x.float()
+    return (xf * (xf.square().mean(-1, keepdim=True) + 1e-6).rsqrt()).bfloat16()
+
+
+def measure_stack(args, batch, heads_total, qk_total, steps, warmup, world, rank, device, barrier, clocks=None,
+                  seed=4):
+    """Config 4: a stack of GDN layers decoding one token per request per step.
+
+    Value heads (and their qk heads) are tensor-parallel over the ranks.  Per
+    layer: RMS-normalised residual -> this rank's column slice of a random-init
+    bf16 projection to q, k, v, a, b (cuBLAS) -> ``PackedStatePool.step`` (the
+    readout kernel on the compute stream, requantization and repack on the
+    writeback stream, joined into the graph) -> NCCL all-gather of the
+    readouts [B, H_local * V] -> the gathered readout through a replicated
+    random-init output projection, added to the residual.  The prompt goes
+    through ``PackedStatePool.extend`` (chunked prefill) first; the decode step
+    of all layers is captured once in a CUDA graph (``defer_writeback`` +
+    ``WritebackGraph``, joined) and replayed per token.
+    """
+    import torch
+    import torch.distributed as dist
+    from torch.profiler import ProfilerActivity, profile
+    from stepquant_b200 import synthetic as S
+    from stepquant_b200.kernels.pool import PackedStatePool
+    from stepquant_b200.kernels.profiles import stepquant6_profile
+    from stepquant_b200.kernels.writeback import WritebackGraph, defer_writeback
+    from stepquant_b200.quantization import QuantizationPlan
+
+    dim, hidden, layers, prompt = args.dim, args.hidden, args.layers, args.prompt
+    H, HK = heads_total // world, qk_total // world
+    o_k, o_v, o_a = HK * dim, 2 * HK * dim, 2 * HK * dim + H * dim
+    width = o_a + 2 * H
+    gen = torch.Generator(device=device)
+    wb_stream = torch.cuda.Stream(device)
+    slots = torch.arange(1, batch + 1, device=device)
+    # The profile's chunk is per batch tier; with the heads split over ranks one
+    # launch of that many requests would leave most SMs idle, so it grows with
+    # the rank count (same items per launch as on one GPU).
+    chunk = args.writeback_chunk or min(batch, stepquant6_profile("gdn", min(batch, 512)).chunk * world)
+    stack = []
+    page_bytes = 0
+    for layer in range(layers):
+        cpu_gen = torch.Generator().manual_seed(seed * 1000 + layer)
+        widths = S.gdn_widths(heads_total, cpu_gen)[rank * H:(rank + 1) * H]
+        plan = QuantizationPlan("gdn", widths[:, None].expand(H, dim).clone().to(device),
+                                (torch.rand(heads_total, dim, generator=cpu_gen)[rank * H:(rank + 1) * H] + 0.5).to(device))
+        pool = PackedStatePool(plan, batch + 1, dim, writeback_stream=wb_stream, writeback_chunk=chunk)
+        page_bytes += pool.page_bytes
+        gen.manual_seed((seed * 1000 + layer) * 64 + rank)  # this rank's column slice
+        w_in = (torch.randn(hidden, width, device=device, generator=gen) * hidden ** -0.5).bfloat16()
+        a_log, dt_bias = S.gate_parameters(H, dim, False, gen, device)
+        gen.manual_seed(seed * 1000 + layer + 500_000)  # replicated: identical on every rank
+        w_out = (torch.randn(heads_total * dim, hidden, device=device, generator=gen) * (heads_total * dim) ** -0.5).bfloat16()
+        stack.append((pool, w_in, w_out, a_log, dt_bias))
+
+    def gather(out):
+        """[T, H_local * V] on every rank -> [T, H * V] in global head order."""
+        if world == 1:
+            return out
+        parts = torch.empty(world, *out.shape, device=device, dtype=out.dtype)
+        dist.all_gather_into_tensor(parts, out.contiguous())
+        return parts.permute(1, 0, 2).reshape(out.shape[0], world * out.shape[1])
+
+    # ---- prompt: chunked prefill of every layer (setup, untimed) ----------------
+    tokens = batch * prompt
+    gen.manual_seed(seed * 7919)
+    h = torch.randn(tokens, hidden, device=device, generator=gen).bfloat16()
+    cu = torch.arange(0, tokens + 1, prompt, device=device, dtype=torch.int32)
+    for pool, w_in, w_out, a_log, dt_bias in stack:
+        proj = _rms_norm(h) @ w_in
+        q = proj[:, :o_k].view(1, tokens, HK, dim)
+        k = proj[:, o_k:o_v].view(1, tokens, HK, dim)
+        v = proj[:, o_v:o_a].view(1, tokens, H, dim)
+        a, b = proj[:, o_a:o_a + H].float(), proj[:, o_a + H:].float()
+        g = (-a_log.exp() * torch.nn.functional.softplus(a + dt_bias))[None]
+        out = pool.extend(q, k, v, g, b.sigmoid()[None], slots, cu, scale=dim ** -0.5)
+        h = h + gather(out.reshape(tokens, H * dim)) @ w_out
+        del proj, q, k, v, a, b, g, out
+    prompt_state = float(h.float().square().mean().sqrt())
+    del h
+    torch.cuda.synchronize()
+
+    # ---- decode: one token per request per step, all layers in one graph --------
+    embeds = 4
+    gen.manual_seed(seed * 7919 + 1)
+    inputs = torch.randn(embeds, batch, hidden, device=device, generator=gen).bfloat16()
+    x_in = torch.empty(batch, hidden, device=device, dtype=torch.bfloat16)
+    result = torch.empty(batch, device=device, dtype=torch.float32)
+    pools = [layer[0] for layer in stack]
+
+    def decode_step():
+        h = x_in
+        for pool, w_in, w_out, a_log, dt_bias in stack:
+            proj = _rms_norm(h) @ w_in
+            out = pool.step(proj[:, :o_k], proj[:, o_k:o_v], proj[:, o_v:o_a], proj[:, o_a:o_a + H].float(),
+                            proj[:, o_a + H:].float(), slots, normalize=True, scale=dim ** -0.5, a_log=a_log,
+                            dt_bias=dt_bias)
+            h = h + gather(out.reshape(batch, H * dim)) @ w_out
+        result.copy_(h.float().sum(-1))
+
+    x_in.copy_(inputs[0])
+    decode_step()  # eager: cuBLAS handles, NCCL communicator, pool workspaces
+    for pool in pools:
+        pool.wait()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        with defer_writeback(pools, joined=True) as tasks:
+            decode_step()
+    replay = WritebackGraph(graph, tasks, joined=True)
+
+    def one_step(i):
+        x_in.copy_(inputs[i % embeds])
+        replay.replay()
+
+    for i in range(warmup):
+        one_step(i)
+    barrier()
+    start, end = _events()
+    barrier()
+    if clocks:
+        clocks.start()
+    start.record()
+    for i in range(steps):
+        one_step(i)
+    for pool in pools:
+        pool.wait()
+    end.record()
+    barrier()
+    if clocks:
+        clocks.stop()
+    res = {"elapsed_ms": start.elapsed_time(end), "page_bytes": page_bytes, "prompt_rms": prompt_state, "chunk": chunk,
+           "finite": bool(torch.isfinite(result).all())}
+
+    # Device time of one replay by kernel family (ranks aligned first, so the
+    # all-gather does not absorb another rank's start-up skew).
+    barrier()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        one_step(0)
+        for pool in pools:
+            pool.wait()
+        torch.cuda.synchronize()
+    fam = {"state_readout": 0.0, "state_writeback": 0.0, "gemm": 0.0, "nccl": 0.0, "other": 0.0}
+    launches = 0
+    for ev in prof.key_averages():
+        name, ms = ev.key, ev.device_time_total / 1e3
+        if ms <= 0:
+            continue
+        if "fast_kernel<3>" in name or "fast_kernel<(int)3>" in name:
+            fam["state_readout"] += ms
+            launches += ev.count
+        elif "fast_kernel<4>" in name or "fast_kernel<(int)4>" in name or "tile_kernel" in name:
+            fam["state_writeback"] += ms
+            launches += ev.count
+        elif "sq::" in name:
+            fam["other"] += ms
+            launches += ev.count
+        elif "nccl" in name.lower():
+            fam["nccl"] += ms
+        elif "gemm" in name.lower() or "nvjet" in name.lower() or "cutlass" in name.lower():
+            fam["gemm"] += ms
+        else:
+            fam["other"] += ms
+    res["kernel_ms"] = fam
+    res["sq_launches"] = launches
+
+    # End to end: each step's embeddings from pinned host memory, the step's
+    # per-request result back to the host.
+    pin = inputs.cpu().pin_memory()
+    host_res = torch.empty(batch, dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        x_in.copy_(pin[i % embeds], non_blocking=True)
+        replay.replay()
+        host_res.copy_(result, non_blocking=True)
+
+    e2e_step(0)
+    barrier()
+    e0, e1 = _events()
+    e0.record()
+    for i in range(steps):
+        e2e_step(i)
+    for pool in pools:
+        pool.wait()
+    e1.record()
+    barrier()
+    res.update(e2e_ms=e0.elapsed_time(e1), h2d=batch * hidden * 2, d2h=batch * 4)
+    for pool in pools:
+        pool.wait()
+    torch.cuda.synchronize()
+    # Graphs holding NCCL work are released before the process group goes.
+    del replay, graph, tasks
+    return res
+
+
 def main():
     args = parse_args()
     # Library and NCCL messages written to fd 1 go to stderr; the result line
@@ -509,7 +716,8 @@ def main():
 
     workload = args.workload
     kda = workload == "kda-decode"
-    batch = args.batch if args.batch else (512 if kda else 32 if workload == "gdn-prefill" else 256)
+    batch = args.batch if args.batch else (512 if kda or workload == "gdn-stack" else 32 if workload == "gdn-prefill"
+                                           else 256)
     heads = args.heads
     qk_heads = args.qk_heads if args.qk_heads else (heads if kda else heads // 2)
     if heads % world or qk_heads % world:
@@ -519,7 +727,41 @@ def main():
     line = {"metric": METRIC, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic"}
 
-    if workload == "gdn-prefill":
+    if workload == "gdn-stack":
+        res = measure_stack(args, batch, heads, qk_heads, args.steps, args.warmup, world, rank, device, barrier,
+                            clocks=clocks)
+        elapsed_ms, e2e_ms = max_over_ranks(res["elapsed_ms"], res["e2e_ms"])
+        fam = res["kernel_ms"]
+        state_ms = fam["state_readout"] + fam["state_writeback"]
+        ms_per_step = elapsed_ms / args.steps
+        units = batch * args.steps
+        page_io, other_io = algorithmic_bytes(res["page_bytes"], heads // world, qk_heads // world, batch, args.dim)
+        other_io *= args.layers
+        achieved = (page_io + other_io) / (state_ms / 1e3) / 1e9 if state_ms else None
+        line.update({
+            "metric": "stack decode tokens/s", "unit": "tokens/s", "value": units / (elapsed_ms / 1e3),
+            "ms_per_step": ms_per_step,
+            "config": {"workload": "gdn-stack-l%d-b%d-h%d-hidden%d (config 4)" % (args.layers, batch, heads, args.hidden),
+                       "layers": args.layers, "batch": batch, "hidden": args.hidden, "heads": heads,
+                       "qk_heads": qk_heads, "dim": args.dim, "prompt_tokens": args.prompt,
+                       "decode_tokens_timed": args.steps, "plan": "stepquant6 synthetic per layer",
+                       "parallelism": f"tp{world} (value heads), NCCL all-gather of each layer's readout",
+                       "graph": "one CUDA graph per decode token (all layers), writeback joined",
+                       "writeback_chunk": res["chunk"],
+                       "weights": "random-init bf16 in/out projections",
+                       "l2": "pages of %d layers (%.0f MB per GPU) > L2" % (args.layers, (batch + 1) * res["page_bytes"] / 1e6)},
+            "kernel_ms_per_step": fam,
+            "state_update_share": state_ms / ms_per_step,
+            "roofline": {"kernel": "state kernels (readout + writeback, all layers)", "bound": "hbm",
+                         "achieved": achieved, "peak": peak_hbm, "unit": "GB/s",
+                         "frac": achieved / peak_hbm if achieved else None, "traffic": None,
+                         "peak_source": peak_hbm_kind, "algorithmic_bytes_per_step": page_io + other_io},
+            "e2e": {"value": units / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"],
+                    "d2h_bytes_per_step": res["d2h"]},
+            "gpu_launches": res["sq_launches"] * args.steps,
+            "finite": res["finite"],
+        })
+    elif workload == "gdn-prefill":
         res = measure_prefill(args, batch, args.tokens, heads, qk_heads, args.steps, args.warmup, world, rank, device,
                               barrier, e2e=True, clocks=clocks)
         elapsed_ms, e2e_ms = max_over_ranks(res["elapsed_ms"], res["e2e_ms"])
@@ -564,7 +806,7 @@ def main():
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms else None
         # dram read + write bytes per launch from one ncu capture of this workload
         # (profiles/fast_kernel_gdn_b256.md); None for other shapes.
-        ncu_traffic = {"sq_step (fused)": 160.6e6, "sq_writeback": 162.3e6, "sq_readout": 116.7e6}
+        ncu_traffic = {"sq_step (fused)": 162.3e6, "sq_writeback": 163.1e6, "sq_readout": 116.1e6}
         default_shape = (not kda, batch, heads, qk_heads, args.dim, world) == (True, 256, 32, 16, 128, 1)
         name = ("kda-decode-b%d-h%d-k128 (config 2)" if kda else "gdn-decode-b%d-h%d-k128 (config 1)") % (batch, heads)
         plan_desc = ("stepquant4 reference-legal twin: row widths {2,4,6} at 30/50/20, 2% fp16 pivot rows" if kda else
@@ -598,7 +840,7 @@ def main():
         sec["kda-decode-b512-h32-k128 (config 2)"] = {
             "value": 512 * 32 * 5 / (r2["elapsed_ms"] / 1e3), "unit": UNIT, "ms_per_step": r2["elapsed_ms"] / 5,
             "kernel_ms": r2["kernel_ms"], "steps": 5, "mode": "async",
-            "note": "tile kernels (no register-resident KDA kernel yet); 64 warm-up steps, 2 slot groups"}
+            "note": "register-resident KDA kernels; 64 warm-up steps, 2 slot groups"}
         r3 = measure_prefill(args, 32, 2048, 32, 16, 5, 2, 1, 0, device, barrier, e2e=False)
         peak_tf, peak_tf_kind = measured_peak("bf16_tflops")
         pk = r3["kernel_ms"].get("prep_kernel", 0.0) + r3["kernel_ms"].get("state_kernel", 0.0)

@@ -185,3 +185,55 @@ def test_fast_path_graph_capture():
             assert torch.equal(o, e)
         for p, r in zip(pools, refs):
             assert torch.equal(p.data, r.data)
+
+
+def test_joined_capture_of_chained_layers():
+    """Three layers captured in one graph with joined writeback (the decode
+    stack of the benchmark's config 4): each layer's v is fed by the previous
+    layer's readout; replays equal eager fused steps, outputs and bytes."""
+    from stepquant_b200.kernels.pool import PackedStatePool
+    from stepquant_b200.kernels.writeback import WritebackGraph, defer_writeback
+    gen = torch.Generator().manual_seed(10)
+    plan, _ = _gdn_plan([6, 8, 4, 6], 10)
+    batch, heads, layers = 96, 4, 3
+    stream = torch.cuda.Stream()
+    pools = [PackedStatePool(plan, batch + 1, 128, writeback_stream=stream, writeback_chunk=32) for _ in range(layers)]
+    refs = [PackedStatePool(plan, batch + 1, 128) for _ in range(layers)]
+    slots = torch.randperm(batch, generator=gen).cuda() + 1
+    state = torch.randn(batch, heads, 128, 128, device="cuda") * 0.1
+    for p in pools + refs:
+        p.encode(state, slots)
+    q, k, v, a, b = (t.cuda() for t in _inputs(batch, heads, heads, gen, torch.bfloat16))
+    kw = dict(normalize=True, scale=128 ** -0.5, a_log=torch.rand(heads).cuda(), dt_bias=torch.zeros(heads).cuda())
+    v_in = v.clone()
+
+    def forward(stack):
+        x, outs = v_in, []
+        for p in stack:
+            out = p.step(q, k, x, a, b, slots, **kw)
+            outs.append(out)
+            x = (x.float() + out.float()).bfloat16()
+        return outs
+
+    forward(pools)  # eager warm-up step on both sets
+    forward(refs)
+    for p in pools:
+        p.wait()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        with defer_writeback(pools, joined=True) as tasks:
+            outs = forward(pools)
+    wg = WritebackGraph(graph, tasks, joined=True)
+    assert wg.background is None
+    for step in range(3):
+        v_in.copy_(torch.randn(v.shape, generator=gen).bfloat16())
+        wg.replay()
+        expected = forward(refs)
+        for p in pools:
+            p.wait()
+        torch.cuda.synchronize()
+        for o, e in zip(outs, expected):
+            assert torch.equal(o, e), f"step {step}"
+        for p, r in zip(pools, refs):
+            assert torch.equal(p.data, r.data), f"step {step}"
