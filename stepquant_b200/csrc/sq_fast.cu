@@ -1,12 +1,14 @@
 // Register-resident decode kernels for GDN heads with K = V = 128 and a code
 // width of 4, 6 or 8 bits (the served shape of Qwen-Next-style layers).
 //
-// Persistent 256-thread CTAs, two per SM, each walking (request, value head)
+// Persistent 256-thread CTAs, three per SM, each walking (request, value head)
 // items; the next item's page bytes and inputs are prefetched (cp.async) into
 // a second stage buffer while the current item is computed.  Warp w owns
 // key rows 16w..16w+15 and lane l owns value columns l, l+32, l+64, l+96, so
-// each thread keeps 64 state elements in registers for the whole step.  That
-// mapping makes both ordered sums of fit_state local:
+// each thread owns 64 state elements for the whole step; the step, writeback
+// and encode keep them in the thread's tensor-memory lane between phases and
+// bring 16 at a time into registers (80 registers a thread).  That mapping
+// makes both ordered sums of fit_state local:
 //  * torch sums a row of 128 values as 8 lanes (column % 8), each lane a 4-way
 //    interleaved chain over vectors; the chain of lane (column % 8) over the
 //    columns l + 32 i is exactly what thread l holds -- only the last two
@@ -72,7 +74,16 @@ struct FastSmem {
     HeadInfo head[kMaxHeads];
     long long slot_ring[3];  // slots of the current and next two items (cp.async)
     int flags;
+    uint32_t tmem_slot;      // tensor-memory base of the CTA's state columns
 };
+
+// Step, writeback and encode keep each thread's 64 state values in tensor
+// memory between phases (128 columns per CTA: warps w and w + 4 share a lane
+// quarter, each with 64 columns), so a thread holds only 16 of them in
+// registers at a time and three CTAs fit on an SM.
+constexpr uint32_t kTmCols = 128;
+template <int MODE>
+__host__ __device__ constexpr bool tm_mode() { return MODE == kStep || MODE == kWriteback || MODE == kEncode; }
 
 // Bits of the code of value-lane u in row k of value tile t, read from the
 // staged page, ORed into the float 2^23: with the lane's conversion constants
@@ -140,14 +151,16 @@ struct Ctx {
     int64_t slot;
     uint8_t *page;
     int off_head;
+    uint32_t tm;  // tensor-memory address of the thread's 64 state columns (value (4g+i, h, e) at 16g + 4i + 2h + e)
 };
 
 
 // P4 body: first levels z = rint(clamp(x / r / c0)) and the weighted
-// least-squares numerator / denominator of the warp's 16-row block.  X holds x
-// on entry and x / r on exit.
+// least-squares numerator / denominator of the warp's 16-row block.  The
+// thread's values hold x on entry and x / r on exit; rows go in groups of 4
+// (one 16-column tensor-memory access), in row order.
 template <bool SLOW, bool CLAMP>
-__device__ __forceinline__ void first_levels(const FastSmem &s, int warp, int lane, float2 (&X)[16][2], float qmax,
+__device__ __forceinline__ void first_levels(const FastSmem &s, int warp, int lane, uint32_t tm, float qmax,
                                              float2 (&num)[2], float2 (&den)[2]) {
     const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
     const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
@@ -156,30 +169,37 @@ __device__ __forceinline__ void first_levels(const FastSmem &s, int warp, int la
     const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
     const float2 round = make_float2(kRound, kRound), nround = make_float2(-kRound, -kRound);
     num[0] = num[1] = den[0] = den[1] = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+        tm_ld16(tm + 16 * g, X);
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-        const float4 a = s.rowa[warp * 16 + r], b = s.rowb[warp * 16 + r];
-        const float2 rn = lo2(a), w2 = hi2(b);
-        // v = rn * z with z = S - 1.5*2^23: one rounding of rn*S - rn*1.5*2^23,
-        // whose second product is exact (rn has 11 significant bits).
-        const float2 nrk = pmul2(rn, nround);
+        for (int i = 0; i < 4; ++i) {
+            const float4 a = s.rowa[warp * 16 + 4 * g + i], b = s.rowb[warp * 16 + 4 * g + i];
+            const float2 rn = lo2(a), w2 = hi2(b);
+            // v = rn * z with z = S - 1.5*2^23: one rounding of rn*S - rn*1.5*2^23,
+            // whose second product is exact (rn has 11 significant bits).
+            const float2 nrk = pmul2(rn, nround);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const float2 x = X[r][h];
-            const float2 sn = divide2<SLOW>(x, rn, hi2(a), lo2(b));
-            float2 y = divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
-            if (CLAMP) y = clamp2(y, qmax);  // rint(clamp(y)) == clamp(rint(y)) for integer bounds
-            const float2 v = pfma2(rn, __fadd2_rn(y, round), nrk);
-            num[h] = __fadd2_rn(num[h], product_term(pmul2(w2, v), x));
-            den[h] = __fadd2_rn(den[h], product_term(w2, pmul2(v, v)));
-            X[r][h] = sn;
+            for (int h = 0; h < 2; ++h) {
+                const float2 x = X[i][h];
+                const float2 sn = divide2<SLOW>(x, rn, hi2(a), lo2(b));
+                float2 y = divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
+                if (CLAMP) y = clamp2(y, qmax);  // rint(clamp(y)) == clamp(rint(y)) for integer bounds
+                const float2 v = pfma2(rn, __fadd2_rn(y, round), nrk);
+                num[h] = __fadd2_rn(num[h], product_term(pmul2(w2, v), x));
+                den[h] = __fadd2_rn(den[h], product_term(w2, pmul2(v, v)));
+                X[i][h] = sn;
+            }
         }
+        tm_st16(tm + 16 * g, X);
     }
+    tm_wait_st();
 }
 
 // P5 body: final levels -> one signed level byte per value in the plane.
 template <bool SLOW, bool CLAMP>
-__device__ __forceinline__ void final_levels(FastSmem &s, int warp, int lane, const float2 (&X)[16][2], float qmax) {
+__device__ __forceinline__ void final_levels(FastSmem &s, int warp, int lane, uint32_t tm, float qmax) {
     const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
     const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
     const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
@@ -187,57 +207,108 @@ __device__ __forceinline__ void final_levels(FastSmem &s, int warp, int lane, co
     const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
     const float2 round = make_float2(kRound, kRound);
     const int t0 = lane >> 4, u = lane & 15;
-    unsigned char *plane = s.plane + t0 * (FK * 16 + kStagePad) + u;
+    unsigned char *plane = s.plane + t0 * (FK * 16 + kStagePad) + u + warp * 16 * 16;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+        tm_ld16(tm + 16 * g, X);
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-        const int k = warp * 16 + r;
+        for (int i = 0; i < 4; ++i) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            float2 y = divide2<SLOW>(X[r][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
-            if (CLAMP) y = clamp2(y, qmax);
-            const float2 code = __fadd2_rn(y, round);  // low byte: the signed level (two's complement)
-            plane[(4 * h) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.x));
-            plane[(4 * h + 2) * (FK * 16 + kStagePad) + k * 16] = static_cast<unsigned char>(__float_as_uint(code.y));
+            for (int h = 0; h < 2; ++h) {
+                float2 y = divide2<SLOW>(X[i][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
+                if (CLAMP) y = clamp2(y, qmax);
+                const float2 code = __fadd2_rn(y, round);  // low byte: the signed level (two's complement)
+                plane[(4 * h) * (FK * 16 + kStagePad) + i * 16] = static_cast<unsigned char>(__float_as_uint(code.x));
+                plane[(4 * h + 2) * (FK * 16 + kStagePad) + i * 16] = static_cast<unsigned char>(__float_as_uint(code.y));
+            }
         }
+        plane += 4 * 16;
     }
 }
 
 // P3-P5 (shared by every width): column max -> c0; first levels and the
-// weighted least-squares sums -> c1; final code bytes -> plane.  X holds the
-// updated state on entry and x / r on exit.  Packed f32x2 lanes are the column
-// pairs (l, l+32) and (l+64, l+96).  The clamps to [-qmax, qmax] are skipped
-// when no level of the tile can reach qmax + 1/2: every |x/r| is at most the
-// column maximum M, so |x/r/c| <= RN(M/c) (division and rounding are monotone).
-// The IEEE-division path (huge or NaN rows) always clamps.
-template <bool SLOW>
-__device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 (&X)[16][2], float qmax) {
-    const int warp = c.warp, lane = c.lane, tid = c.tid;
-    // P3: c0 = fp16(max_k |x / r| / qmax) (uniform width: one division per column).
-    {
-        float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+// weighted least-squares sums -> c1; final code bytes -> plane.  The thread's
+// values (tensor memory) hold the updated state on entry and x / r on exit.
+// Packed f32x2 lanes are the column pairs (l, l+32) and (l+64, l+96).  The
+// clamps to [-qmax, qmax] are skipped when no level of the tile can reach
+// qmax + 1/2: every |x/r| is at most the column maximum M, so
+// |x/r/c| <= RN(M/c) (division and rounding are monotone).  The IEEE-division
+// path (huge or NaN rows) always clamps.
+// P3 partial: the warp's column maxima of |x / r| -> s.red[0].  EXACT divides
+// (corrected reciprocal, or IEEE on the SLOW path); otherwise the product
+// x * RN(1/r), within one ulp of the quotient, bounds the maximum.
+template <bool SLOW, bool EXACT>
+__device__ __forceinline__ void column_max(FastSmem &s, int warp, int lane, uint32_t tm) {
+    float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+        tm_ld16(tm + 16 * g, X);
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const float4 a = s.rowa[warp * 16 + r], b = s.rowb[warp * 16 + r];
-            const float2 s01 = divide2<SLOW>(X[r][0], lo2(a), hi2(a), lo2(b));
-            const float2 s23 = divide2<SLOW>(X[r][1], lo2(a), hi2(a), lo2(b));
+        for (int i = 0; i < 4; ++i) {
+            const float4 a = s.rowa[warp * 16 + 4 * g + i], b = s.rowb[warp * 16 + 4 * g + i];
+            const float2 s01 = EXACT ? divide2<SLOW>(X[i][0], lo2(a), hi2(a), lo2(b)) : pmul2(X[i][0], hi2(a));
+            const float2 s23 = EXACT ? divide2<SLOW>(X[i][1], lo2(a), hi2(a), lo2(b)) : pmul2(X[i][1], hi2(a));
             m0 = fmaxf(m0, fabsf(s01.x));
             m1 = fmaxf(m1, fabsf(s01.y));
             m2 = fmaxf(m2, fabsf(s23.x));
             m3 = fmaxf(m3, fabsf(s23.y));
         }
-        s.red[0][warp][lane] = m0;
-        s.red[0][warp][lane + 32] = m1;
-        s.red[0][warp][lane + 64] = m2;
-        s.red[0][warp][lane + 96] = m3;
     }
+    s.red[0][warp][lane] = m0;
+    s.red[0][warp][lane + 32] = m1;
+    s.red[0][warp][lane + 64] = m2;
+    s.red[0][warp][lane + 96] = m3;
+}
+
+// P3-P5 (shared by every width): column max -> c0; first levels and the
+// weighted least-squares sums -> c1; final code bytes -> plane.  The thread's
+// values (tensor memory) hold the updated state on entry and x / r on exit.
+// Packed f32x2 lanes are the column pairs (l, l+32) and (l+64, l+96).  The
+// clamps to [-qmax, qmax] are skipped when no level of the tile can reach
+// qmax + 1/2: every |x/r| is at most the column maximum M, so
+// |x/r/c| <= RN(M/c) (division and rounding are monotone).  The IEEE-division
+// path (huge or NaN rows) always clamps.
+//
+// c0 = fp16(RN(M / qmax)) needs M only up to its fp16 rounding: the maximum M'
+// of the products x * RN(1/r) lies within one ulp of M, and when
+// fp16(RN(prev(M') / qmax)) == fp16(RN(next(M') / qmax)) that value is c0
+// (every step is monotone).  Tiles with a column where the two differ redo
+// the maxima with exact divisions.
+template <bool SLOW>
+__device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float qmax) {
+    const int warp = c.warp, lane = c.lane, tid = c.tid;
+    // P3: c0 = fp16(max_k |x / r| / qmax) (uniform width: one division per column).
+    column_max<SLOW, SLOW>(s, warp, lane, c.tm);
     __syncthreads();
-    int safe = 1;
-    float mx = 0.f;
+    int safe = 1, settled = 1;
+    float mx = 0.f, ratio = 0.f, c0 = 0.f;  // mx: the exact maximum or an upper bound of it
     if (tid < FV) {
+        float m = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
-        const float ratio = __fdiv_rn(mx, qmax);
-        const float c0 = fp16_scale(ratio);
+        for (int w = 0; w < 8; ++w) m = fmaxf(m, s.red[0][w][tid]);
+        if (SLOW) {
+            mx = m;
+        } else {
+            const uint32_t bits = __float_as_uint(m);
+            const float lo = m > 0.f ? __uint_as_float(bits - 1u) : 0.f;
+            mx = __uint_as_float(bits + 1u);
+            settled = fp16_scale(__fdiv_rn(lo, qmax)) == fp16_scale(__fdiv_rn(mx, qmax));
+        }
+    }
+    if (!SLOW && !__syncthreads_and(settled)) {
+        column_max<false, true>(s, warp, lane, c.tm);
+        __syncthreads();
+        if (tid < FV) {
+            mx = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
+        }
+    }
+    if (tid < FV) {
+        ratio = __fdiv_rn(mx, qmax);
+        c0 = fp16_scale(ratio);
         s.colc[1][tid] = c0;
         s.colc[2][tid] = __frcp_rn(c0);
         // With c0 a normal, unclamped fp16 value every |x/r/c0| < qmax + 1/2.
@@ -247,8 +318,8 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 
     // P4: first levels, weighted least-squares numerator / denominator (16-row blocks).
     {
         float2 num[2], den[2];
-        if (!SLOW && no_clamp) first_levels<SLOW, false>(s, warp, lane, X, qmax, num, den);
-        else first_levels<SLOW, true>(s, warp, lane, X, qmax, num, den);
+        if (!SLOW && no_clamp) first_levels<SLOW, false>(s, warp, lane, c.tm, qmax, num, den);
+        else first_levels<SLOW, true>(s, warp, lane, c.tm, qmax, num, den);
         s.red[0][warp][lane] = num[0].x;
         s.red[0][warp][lane + 32] = num[0].y;
         s.red[0][warp][lane + 64] = num[1].x;
@@ -274,8 +345,8 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float2 
     }
     const bool no_clamp5 = __syncthreads_and(safe);
     // P5: final levels -> one signed level byte per value in the plane.
-    if (!SLOW && no_clamp5) final_levels<SLOW, false>(s, warp, lane, X, qmax);
-    else final_levels<SLOW, true>(s, warp, lane, X, qmax);
+    if (!SLOW && no_clamp5) final_levels<SLOW, false>(s, warp, lane, c.tm, qmax);
+    else final_levels<SLOW, true>(s, warp, lane, c.tm, qmax);
     __syncthreads();
 }
 
@@ -334,6 +405,97 @@ __device__ __forceinline__ void unpack_rows(const FastSmem &s, const FastStage &
     acc[1] = kx23;
     acc[2] = qx01;
     acc[3] = qx23;
+}
+
+// P1 of the fused step: as unpack_rows, with Y going to tensor memory.
+template <int BITS>
+__device__ __forceinline__ void unpack_rows_tm(const FastSmem &s, const FastStage &st, int warp, int lane, uint32_t tm,
+                                               float2 (&acc)[4]) {
+    const int t0 = lane >> 4, u = lane & 15;
+    const float2 lc = level_constants<BITS>(u);
+    const float2 lscale = make_float2(lc.x, lc.x), lbias = make_float2(lc.y, lc.y);
+    float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int k = warp * 16 + 4 * g + i;
+            const float4 a = s.rowa[k], b = s.rowb[k];
+            const float2 f01 = make_float2(staged_bits<BITS>(st.codes, t0, k, u), staged_bits<BITS>(st.codes, t0 + 2, k, u));
+            const float2 f23 = make_float2(staged_bits<BITS>(st.codes, t0 + 4, k, u), staged_bits<BITS>(st.codes, t0 + 6, k, u));
+            const float2 x01 = pmul2(pfma2(f01, lscale, lbias), lo2(a));
+            const float2 x23 = pmul2(pfma2(f23, lscale, lbias), lo2(a));
+            X[i][0] = x01;
+            X[i][1] = x23;
+            kx01 = pfma2(hi2(a), x01, kx01);
+            kx23 = pfma2(hi2(a), x23, kx23);
+            qx01 = pfma2(lo2(b), x01, qx01);
+            qx23 = pfma2(lo2(b), x23, qx23);
+        }
+        tm_st16(tm + 16 * g, X);
+    }
+    acc[0] = kx01;
+    acc[1] = kx23;
+    acc[2] = qx01;
+    acc[3] = qx23;
+}
+
+// Row |x| partial of row k in torch's order: one thread's 4 columns l, l+32,
+// l+64, l+96 are one accumulator slot of the 8-lane, 4-way interleaved chain.
+__device__ __forceinline__ void row_partial(float *rowpart, int k, int lane, const float2 (&x)[2]) {
+    rowpart[k * kRowPartStride + lane] =
+        __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, fabsf(x[0].x)), fabsf(x[0].y)), fabsf(x[1].x)), fabsf(x[1].y));
+}
+
+// P1 + P2 of the writeback (delta, k and c * decay are known before the
+// unpack): x' = (level * r_old) * (c * decay) + k * delta, row partials, x' to
+// tensor memory.
+template <int BITS>
+__device__ __forceinline__ void unpack_update_tm(FastSmem &s, const FastStage &st, int warp, int lane, uint32_t tm) {
+    const int t0 = lane >> 4, u = lane & 15;
+    const float2 lc = level_constants<BITS>(u);
+    const float2 lscale = make_float2(lc.x, lc.x), lbias = make_float2(lc.y, lc.y);
+    const float2 d01 = make_float2(s.colc[0][lane], s.colc[0][lane + 32]);
+    const float2 d23 = make_float2(s.colc[0][lane + 64], s.colc[0][lane + 96]);
+    const float2 cd01 = make_float2(s.colc[3][lane], s.colc[3][lane + 32]);
+    const float2 cd23 = make_float2(s.colc[3][lane + 64], s.colc[3][lane + 96]);
+    float *rowpart = reinterpret_cast<float *>(s.plane);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int k = warp * 16 + 4 * g + i;
+            const float4 a = s.rowa[k];
+            const float2 f01 = make_float2(staged_bits<BITS>(st.codes, t0, k, u), staged_bits<BITS>(st.codes, t0 + 2, k, u));
+            const float2 f23 = make_float2(staged_bits<BITS>(st.codes, t0 + 4, k, u), staged_bits<BITS>(st.codes, t0 + 6, k, u));
+            const float2 x01 = pmul2(pfma2(f01, lscale, lbias), lo2(a));
+            const float2 x23 = pmul2(pfma2(f23, lscale, lbias), lo2(a));
+            X[i][0] = pfma2(hi2(a), d01, pmul2(x01, cd01));
+            X[i][1] = pfma2(hi2(a), d23, pmul2(x23, cd23));
+            row_partial(rowpart, k, lane, X[i]);
+        }
+        tm_st16(tm + 16 * g, X);
+    }
+}
+
+// P1 + P2 of the encode: the dense state rows, row partials, to tensor memory.
+__device__ __forceinline__ void load_rows_tm(FastSmem &s, const float *src, int warp, int lane, uint32_t tm) {
+    float *rowpart = reinterpret_cast<float *>(s.plane);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int k = warp * 16 + 4 * g + i;
+            const float *row = src + k * FV + lane;
+            X[i][0] = make_float2(row[0], row[32]);
+            X[i][1] = make_float2(row[64], row[96]);
+            row_partial(rowpart, k, lane, X[i]);
+        }
+        tm_st16(tm + 16 * g, X);
+    }
 }
 
 // Decode of one width: x = (r * c) * level (the order of the reference codec),
@@ -505,21 +667,26 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
     __syncthreads();
 
     // ---- P1: unpack; column partials of k_raw^T Y and q_raw^T Y ---------------
-    float2 X[16][2];
+    // (Encode and writeback fold P2's work into this pass.)
     if (MODE == kEncode) {
-        const float *src = p.dense_in + (int64_t(c.req) * H + c.head) * FK * FV;
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const float *row = src + (warp * 16 + r) * FV + lane;
-            X[r][0] = make_float2(row[0], row[32]);
-            X[r][1] = make_float2(row[64], row[96]);
-        }
+        load_rows_tm(s, p.dense_in + (int64_t(c.req) * H + c.head) * FK * FV, warp, lane, c.tm);
+    } else if (MODE == kWriteback) {
+        if (width == 4) unpack_update_tm<4>(s, st, warp, lane, c.tm);
+        else if (width == 6) unpack_update_tm<6>(s, st, warp, lane, c.tm);
+        else unpack_update_tm<8>(s, st, warp, lane, c.tm);
     } else {
         float2 acc[4];
-        if (width == 4) unpack_rows<4>(s, st, warp, lane, X, acc);
-        else if (width == 6) unpack_rows<6>(s, st, warp, lane, X, acc);
-        else unpack_rows<8>(s, st, warp, lane, X, acc);
-        if (MODE != kWriteback) {
+        if (MODE == kReadout) {
+            float2 X[16][2];  // the readout keeps no state past P1
+            if (width == 4) unpack_rows<4>(s, st, warp, lane, X, acc);
+            else if (width == 6) unpack_rows<6>(s, st, warp, lane, X, acc);
+            else unpack_rows<8>(s, st, warp, lane, X, acc);
+        } else {
+            if (width == 4) unpack_rows_tm<4>(s, st, warp, lane, c.tm, acc);
+            else if (width == 6) unpack_rows_tm<6>(s, st, warp, lane, c.tm, acc);
+            else unpack_rows_tm<8>(s, st, warp, lane, c.tm, acc);
+        }
+        {
             const sq_step_args &a = p.step;
             s.red[0][warp][lane] = acc[0].x;
             s.red[0][warp][lane + 32] = acc[0].y;
@@ -582,34 +749,36 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 
     // ---- P2: rank-1 update; row sums of |x| in torch order; new row scales ---
     {
-        const float2 d01 = make_float2(s.colc[0][lane], s.colc[0][lane + 32]);
-        const float2 d23 = make_float2(s.colc[0][lane + 64], s.colc[0][lane + 96]);
-        const float2 cd01 = make_float2(s.colc[3][lane], s.colc[3][lane + 32]);
-        const float2 cd23 = make_float2(s.colc[3][lane + 64], s.colc[3][lane + 96]);
         float *rowpart = reinterpret_cast<float *>(s.plane);
+        if (MODE == kStep) {
+            const float2 d01 = make_float2(s.colc[0][lane], s.colc[0][lane + 32]);
+            const float2 d23 = make_float2(s.colc[0][lane + 64], s.colc[0][lane + 96]);
+            const float2 cd01 = make_float2(s.colc[3][lane], s.colc[3][lane + 32]);
+            const float2 cd23 = make_float2(s.colc[3][lane + 64], s.colc[3][lane + 96]);
+            float *dst = p.dense_out ? p.dense_out + (int64_t(c.req) * H + c.head) * FK * FV : nullptr;
+#pragma unroll 1
+            for (int g = 0; g < 4; ++g) {
+                float2 X[4][2];
+                tm_ld16(c.tm + 16 * g, X);
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int k = warp * 16 + r;
-            const float2 kk = hi2(s.rowa[k]);
-            if (MODE != kEncode) {
-                X[r][0] = pfma2(kk, d01, pmul2(X[r][0], cd01));
-                X[r][1] = pfma2(kk, d23, pmul2(X[r][1], cd23));
-            }
-            const float a = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, fabsf(X[r][0].x)), fabsf(X[r][0].y)),
-                                                fabsf(X[r][1].x)), fabsf(X[r][1].y));
-            rowpart[k * kRowPartStride + lane] = a;
-        }
-        if (MODE == kStep && p.dense_out) {
-            float *dst = p.dense_out + (int64_t(c.req) * H + c.head) * FK * FV;
-#pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                float *row = dst + (warp * 16 + r) * FV + lane;
-                row[0] = X[r][0].x;
-                row[32] = X[r][0].y;
-                row[64] = X[r][1].x;
-                row[96] = X[r][1].y;
+                for (int i = 0; i < 4; ++i) {
+                    const int k = warp * 16 + 4 * g + i;
+                    const float2 kk = hi2(s.rowa[k]);
+                    X[i][0] = pfma2(kk, d01, pmul2(X[i][0], cd01));
+                    X[i][1] = pfma2(kk, d23, pmul2(X[i][1], cd23));
+                    row_partial(rowpart, k, lane, X[i]);
+                    if (dst) {
+                        float *row = dst + k * FV + lane;
+                        row[0] = X[i][0].x;
+                        row[32] = X[i][0].y;
+                        row[64] = X[i][1].x;
+                        row[96] = X[i][1].y;
+                    }
+                }
+                tm_st16(c.tm + 16 * g, X);
             }
         }
+        tm_wait_st();
         if (tid == 0) s.flags = 0;
         __syncthreads();
         // Lanes j and j+16 finish row 16*warp + j: S_l = ((A_l + A_{l+8}) + A_{l+16}) + A_{l+24},
@@ -643,9 +812,9 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
     const float qmax = float((1 << (width - 1)) - 1);
     if (s.flags) {
         // Pathological magnitudes: IEEE divisions for the whole tile.
-        fast_quantize<true>(s, c, X, qmax);
+        fast_quantize<true>(s, c, qmax);
     } else {
-        fast_quantize<false>(s, c, X, qmax);
+        fast_quantize<false>(s, c, qmax);
     }
     if (width == 4) fast_store<4>(p, s, c);
     else if (width == 6) fast_store<6>(p, s, c);
@@ -657,7 +826,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 // the other stage buffer, and the slot of the item after that into a small
 // ring, so each item starts with its page, scales and inputs on chip.
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, (MODE == kReadout || MODE == kDecode) ? 3 : 2) fast_kernel(TileParams p, int items) {
+__global__ void __launch_bounds__(kThreads, 3) fast_kernel(TileParams p, int items) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FastSmem &s = *reinterpret_cast<FastSmem *>(smem_raw);
     const sq_plan &P = p.plan;
@@ -680,13 +849,19 @@ __global__ void __launch_bounds__(kThreads, (MODE == kReadout || MODE == kDecode
         hi.dt_bias = gates ? p.step.dt_bias[h] : 0.f;
         s.head[h] = hi;
     }
+    if (tm_mode<MODE>() && c.warp == 0) tm_alloc(&s.tmem_slot, kTmCols);
     if (c.tid == 0) {
         cp_async8(&s.slot_ring[0], p.slots + item / H);
         if (item + stride < items) cp_async8(&s.slot_ring[1], p.slots + (item + stride) / H);
     }
     cp_async_commit();
     cp_async_wait<0>();
+    if (tm_mode<MODE>()) tm_fence_before();
     __syncthreads();
+    if (tm_mode<MODE>()) {
+        tm_fence_after();
+        c.tm = s.tmem_slot + (uint32_t(32 * (c.warp & 3)) << 16) + uint32_t(64 * (c.warp >> 2));
+    }
     long long slot = s.slot_ring[0];
     {
         const WorkItem first = describe(p, s, item, slot);
@@ -735,6 +910,12 @@ __global__ void __launch_bounds__(kThreads, (MODE == kReadout || MODE == kDecode
         buf ^= 1;
         ring = ring1;
     }
+    if (tm_mode<MODE>()) {
+        tm_fence_before();
+        __syncthreads();
+        tm_fence_after();
+        if (c.warp == 0) tm_dealloc(s.tmem_slot, kTmCols);
+    }
 }
 
 // Resident CTAs per device for each mode (set up on the first launch on a device).
@@ -754,8 +935,25 @@ cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream
         if (err != cudaSuccess) return err;
         int sms = 0, per_sm = 0;
         if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return err;
-        if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fast_kernel<MODE>, kThreads, smem)) != cudaSuccess)
+        if (tm_mode<MODE>()) {
+            // The occupancy query reports one CTA per SM for a kernel that
+            // allocates tensor memory; resident CTAs are bounded here by
+            // registers, shared memory, threads and the 512 columns.
+            cudaFuncAttributes fa;
+            int regs_sm = 0, smem_sm = 0, threads_sm = 0, reserved = 0;
+            if ((err = cudaFuncGetAttributes(&fa, fast_kernel<MODE>)) != cudaSuccess) return err;
+            if ((err = cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, device)) != cudaSuccess ||
+                (err = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device)) != cudaSuccess ||
+                (err = cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, device)) != cudaSuccess ||
+                (err = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, device)) != cudaSuccess)
+                return err;
+            const int regs_cta = ((fa.numRegs * 32 + 255) / 256 * 256) * (kThreads / 32);
+            per_sm = std::min({regs_sm / std::max(1, regs_cta), smem_sm / (smem + int(fa.sharedSizeBytes) + reserved),
+                               threads_sm / kThreads, int(512 / kTmCols)});
+        } else if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fast_kernel<MODE>, kThreads, smem)) !=
+                   cudaSuccess) {
             return err;
+        }
         ctas = sms * std::max(1, per_sm);
         if (resident) resident->store(ctas, std::memory_order_relaxed);
     }

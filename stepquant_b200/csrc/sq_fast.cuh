@@ -70,6 +70,49 @@ __device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); 
 __device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
 
 
+// ---- tensor memory as state storage --------------------------------------
+// A thread keeps its state values in its own tensor-memory lane (32x32b
+// accesses: warp w reaches lanes 32 (w % 4) .. +31, thread i of the warp lane
+// 32 (w % 4) + i), so no two threads exchange data through it and no fences
+// beyond the allocation's are needed.  Loads tie their destination registers
+// to the wait, so no use can be scheduled ahead of it.
+__device__ __forceinline__ void tm_alloc(uint32_t *slot, uint32_t cols) {  // one full warp
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n"
+                 ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(slot))), "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+}
+__device__ __forceinline__ void tm_dealloc(uint32_t base, uint32_t cols) {  // one full warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(base), "r"(cols));
+}
+__device__ __forceinline__ void tm_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tm_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tm_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+// 16 consecutive fp32 columns of the thread's lane <-> v[i][h] = columns 4i + 2h, 4i + 2h + 1.
+__device__ __forceinline__ void tm_ld16(uint32_t taddr, float2 (&v)[4][2]) {
+    uint32_t r[16];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :: "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[i][0] = make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]));
+        v[i][1] = make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+    }
+}
+__device__ __forceinline__ void tm_st16(uint32_t taddr, const float2 (&v)[4][2]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
+                 ::"r"(taddr), "f"(v[0][0].x), "f"(v[0][0].y), "f"(v[0][1].x), "f"(v[0][1].y), "f"(v[1][0].x),
+                   "f"(v[1][0].y), "f"(v[1][1].x), "f"(v[1][1].y), "f"(v[2][0].x), "f"(v[2][0].y), "f"(v[2][1].x),
+                   "f"(v[2][1].y), "f"(v[3][0].x), "f"(v[3][0].y), "f"(v[3][1].x), "f"(v[3][1].y)
+                 : "memory");
+}
+
 // Exact sum terms: a product formed by an FFMA2 with a +0 addend (the same
 // rounding as the product alone; ptxas does not merge it into the following
 // add) accumulated with a packed add.
