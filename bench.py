@@ -79,6 +79,9 @@ def parse_args():
     p.add_argument("--prompt", type=int, default=128, help="prompt tokens per request before decoding (gdn-stack)")
     p.add_argument("--writeback-chunk", type=int, default=0,
                    help="requests per writeback launch (gdn-stack); default: the stepquant6 profile's chunk")
+    p.add_argument("--writeback-sms", type=int, default=0,
+                   help="SM budget of the writeback stream's green context (gdn-stack); 0 (default): an ordinary "
+                        "stream; -1: the stepquant6 profile's budget")
     return p.parse_args()
 
 
@@ -256,6 +259,69 @@ def _events():
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
+def kernel_times(pool, inputs, groups, kw, mode, launches=8, reps=4):
+    """Average device time (ms) of one launch of each decode kernel.
+
+    ``launches`` launches of one kernel (rotating over the slot groups, so the
+    pages they read exceed L2 as in the timed loop) are captured in a CUDA
+    graph and replayed ``reps`` times between CUDA events on the stream the
+    kernel runs on.  Launch-issue time on the host is thus kept out of the
+    figure at every GPU count.
+    """
+    import torch
+    from stepquant_b200 import _native as N
+
+    batch = groups[0].numel()
+    inp = inputs[0]
+    out = torch.empty(batch, pool.heads, pool.values, device=inp.q.device, dtype=inp.q.dtype)
+    args, keep = pool._step_args(inp.q, inp.k, inp.v, inp.a, inp.b, batch, kw["normalize"], kw["scale"], kw["a_log"],
+                                 kw["dt_bias"], out)
+    lib = N.lib()
+
+    def readout(g):
+        scratch, stable = (t[:batch] for t in pool.scratch)
+        N.check(lib.sq_readout(pool._dp.ref(), N.ptr(pool.data), pool.data.shape[0], N.ptr(groups[g]), batch,
+                               ctypes.byref(args), N.ptr(scratch), N.ptr(stable), N.ptr(pool.status),
+                               N.stream_handle()))
+
+    def writeback(g):
+        # the readout's scratch of group 0, applied to group g's pages
+        N.check(lib.sq_writeback(pool._dp.ref(), N.ptr(pool.data), pool.data.shape[0], N.ptr(groups[g]), batch,
+                                 N.ptr(pool.scratch[0]), None, N.ptr(pool.status), N.stream_handle()))
+
+    def step(g):
+        N.check(lib.sq_step(pool._dp.ref(), N.ptr(pool.data), pool.data.shape[0], N.ptr(groups[g]), batch,
+                            ctypes.byref(args), None, N.ptr(pool.status), N.stream_handle()))
+
+    def timed(launch, stream):
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for j in range(launches):
+                launch(j % len(groups))
+        with torch.cuda.stream(stream):
+            graph.replay()
+            e0, e1 = _events()
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (reps * launches)
+
+    pool.wait()
+    compute = torch.cuda.Stream(inp.q.device)
+    if mode != "async":
+        result = {"step": timed(step, compute)}
+    else:
+        result = {"readout": timed(readout, compute)}
+        readout(0)  # the writeback's inputs
+        torch.cuda.synchronize()
+        result["writeback"] = timed(writeback, torch.cuda.Stream(inp.q.device))
+    del keep
+    return result
+
+
 def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world, rank, device, barrier,
                    mode="async", e2e=True, clocks=None, warm_steps=256, slot_groups=4, seed=1):
     """Decode steps of one layer (GDN config 1 or KDA config 2); returns the measured quantities."""
@@ -305,48 +371,15 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
     inputs = [S.draw_inputs(batch, heads_l, qk_l, dim, dim, kda, gen, device) for _ in range(4)]
     kw = dict(normalize=True, scale=dim ** -0.5, a_log=a_log, dt_bias=dt_bias)
 
-    # Per-kernel CUDA events on the stream each kernel runs on.
-    marks = {"readout": [], "writeback": [], "step": []}
-    recording = [False]
-    finish = pool._finish_update
-
-    def timed_finish(*tensors, **kwargs):
-        if recording[0]:
-            e0, e1 = _events()
-            e0.record()
-            finish(*tensors, **kwargs)
-            e1.record()
-            marks["writeback"].append((e0, e1))
-        else:
-            finish(*tensors, **kwargs)
-
-    pool._finish_update = timed_finish
-
     def one_step(i):
         inp = inputs[i % len(inputs)]
-        pool.wait()
-        if recording[0]:
-            e0, e1 = _events()
-            e0.record()
-        out = pool.step(inp.q, inp.k, inp.v, inp.a, inp.b, groups[i % len(groups)], **kw)
-        if recording[0]:
-            e1.record()
-            marks["readout" if mode == "async" else "step"].append((e0, e1))
-        return out
+        return pool.step(inp.q, inp.k, inp.v, inp.a, inp.b, groups[i % len(groups)], **kw)
 
     for i in range(warmup):
         one_step(i)
     pool.wait()
     barrier()
-    # Per-kernel device times: eager launches bracketed by events on each
-    # kernel's own stream.
-    recording[0] = True
-    for i in range(min(steps, 20)):
-        one_step(i)
-    pool.wait()
-    recording[0] = False
-    torch.cuda.synchronize()
-    kernel_ms = {name: sum(x.elapsed_time(y) for x, y in ev) / max(1, len(ev)) for name, ev in marks.items() if ev}
+    kernel_ms = kernel_times(pool, inputs, groups, kw, mode)
 
     # The timed loop replays one CUDA graph per (inputs, slot group) pair -- the
     # reference benchmark's methodology (bench_formats.py times step(); wait()
@@ -408,29 +441,54 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
             for t, o, nbytes in zip((x.q, x.k, x.v, x.a, x.b), offsets, sizes):
                 buf[o:o + nbytes].copy_(t.contiguous().view(-1).view(torch.uint8).cpu())
             pinned.append(buf)
-        dev_buf = torch.empty(offsets[-1], dtype=torch.uint8, device=device)
-        dev_in = tuple(dev_buf[o:o + nbytes].view(dt).view(sh) for (sh, dt), o, nbytes in zip(fields, offsets, sizes))
-        host_out = torch.empty(batch, heads_l, dim, dtype=torch.bfloat16).pin_memory()
-
-        e2e_graphs = [capture(lambda g=g: pool.step(*dev_in, groups[g], **kw)) for g in range(len(groups))]
+        # Two input buffers: step i + 1's inputs cross PCIe on a copy stream
+        # while step i runs, and each step's output goes back on another, as a
+        # serving loop pipelines them.  One graph per (slot group, buffer).
+        nbuf = 2
+        dev_bufs = [torch.empty(offsets[-1], dtype=torch.uint8, device=device) for _ in range(nbuf)]
+        dev_ins = [tuple(buf[o:o + nbytes].view(dt).view(sh) for (sh, dt), o, nbytes in zip(fields, offsets, sizes))
+                   for buf in dev_bufs]
+        host_outs = [torch.empty(batch, heads_l, dim, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
+        keys = [(g, b) for g in range(len(groups)) for b in range(nbuf)]
+        e2e_graphs = {key: capture(lambda key=key: pool.step(*dev_ins[key[1]], groups[key[0]], **kw)) for key in keys}
+        h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        copied = [torch.cuda.Event() for _ in range(nbuf)]
+        consumed = [torch.cuda.Event() for _ in range(nbuf)]
+        produced = {key: torch.cuda.Event() for key in keys}
+        fetched = {key: torch.cuda.Event() for key in keys}
 
         def e2e_step(i):
-            dev_buf.copy_(pinned[i % len(pinned)], non_blocking=True)
-            graph, out = e2e_graphs[i % len(groups)]
+            b, key = i % nbuf, (i % len(groups), i % nbuf)
+            main = torch.cuda.current_stream()
+            with torch.cuda.stream(h2d):
+                h2d.wait_event(consumed[b])  # the step that last read this buffer has
+                dev_bufs[b].copy_(pinned[i % len(pinned)], non_blocking=True)
+                copied[b].record()
+            main.wait_event(copied[b])
+            main.wait_event(fetched[key])  # this graph's previous output is on the host
+            graph, out = e2e_graphs[key]
             graph.replay()
-            host_out.copy_(out, non_blocking=True)
+            consumed[b].record()
+            produced[key].record()
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(produced[key])
+                host_outs[b].copy_(out, non_blocking=True)
+                fetched[key].record()
 
         for i in range(warmup):
             e2e_step(i)
         pool.wait()
+        torch.cuda.current_stream().wait_stream(d2h)
         barrier()
         e0, e1 = _events()
         e0.record()
         for i in range(steps):
             e2e_step(i)
         pool.wait()
+        torch.cuda.current_stream().wait_stream(d2h)
         e1.record()
         barrier()
+        host_out = host_outs[0]
         res.update(e2e_ms=e0.elapsed_time(e1), h2d=sum(sizes), d2h=host_out.numel() * host_out.element_size())
     return res
 
@@ -545,6 +603,7 @@ def measure_stack(args, batch, heads_total, qk_total, steps, warmup, world, rank
     from stepquant_b200 import synthetic as S
     from stepquant_b200.kernels.pool import PackedStatePool
     from stepquant_b200.kernels.profiles import stepquant6_profile
+    from stepquant_b200.kernels.resources import writeback_resources
     from stepquant_b200.kernels.writeback import WritebackGraph, defer_writeback
     from stepquant_b200.quantization import QuantizationPlan
 
@@ -553,12 +612,14 @@ def measure_stack(args, batch, heads_total, qk_total, steps, warmup, world, rank
     o_k, o_v, o_a = HK * dim, 2 * HK * dim, 2 * HK * dim + H * dim
     width = o_a + 2 * H
     gen = torch.Generator(device=device)
-    wb_stream = torch.cuda.Stream(device)
+    wb_profile = stepquant6_profile("gdn", min(batch, 512))
+    resources = writeback_resources(device, wb_profile.sms if args.writeback_sms < 0 else args.writeback_sms)
+    wb_stream = resources.stream
     slots = torch.arange(1, batch + 1, device=device)
     # The profile's chunk is per batch tier; with the heads split over ranks one
     # launch of that many requests would leave most SMs idle, so it grows with
     # the rank count (same items per launch as on one GPU).
-    chunk = args.writeback_chunk or min(batch, stepquant6_profile("gdn", min(batch, 512)).chunk * world)
+    chunk = args.writeback_chunk or min(batch, wb_profile.chunk * world)
     stack = []
     page_bytes = 0
     for layer in range(layers):
@@ -652,6 +713,7 @@ def measure_stack(args, batch, heads_total, qk_total, steps, warmup, world, rank
     if clocks:
         clocks.stop()
     res = {"elapsed_ms": start.elapsed_time(end), "page_bytes": page_bytes, "prompt_rms": prompt_state, "chunk": chunk,
+           "writeback_sms": resources.actual_sms,
            "finite": bool(torch.isfinite(result).all())}
 
     # Device time of one replay by kernel family (ranks aligned first, so the
@@ -791,7 +853,7 @@ def main():
                        "decode_tokens_timed": args.steps, "plan": "stepquant6 synthetic per layer",
                        "parallelism": f"tp{world} (value heads), NCCL all-gather of each layer's readout",
                        "graph": "one CUDA graph per decode token (all layers), writeback joined",
-                       "writeback_chunk": res["chunk"],
+                       "writeback_chunk": res["chunk"], "writeback_sms": res["writeback_sms"],
                        "weights": "random-init bf16 in/out projections",
                        "l2": "pages of %d layers (%.0f MB per GPU) > L2" % (args.layers, (batch + 1) * res["page_bytes"] / 1e6)},
             "kernel_ms_per_step": fam,

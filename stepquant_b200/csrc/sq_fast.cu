@@ -23,6 +23,10 @@
 // Rows whose |x| sum exceeds 2^96 switch the CTA to IEEE divisions.
 #include <algorithm>
 #include <atomic>
+#include <mutex>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "sq_fast.cuh"
 
@@ -918,9 +922,39 @@ __global__ void __launch_bounds__(kThreads, 3) fast_kernel(TileParams p, int ite
     }
 }
 
-// Resident CTAs per device for each mode (set up on the first launch on a device).
+// Resident CTAs per SM for each mode, and SMs, per device (set up on the first
+// launch on a device).
 constexpr int kMaxDevices = 64;
 std::atomic<int> g_resident[kFit + 1][kMaxDevices];  // indexed by Mode
+std::atomic<int> g_sms[kMaxDevices];
+
+// SMs the kernels of `stream` run on: its green context's SM partition (a
+// writeback stream with an SM budget), else the whole device.  A persistent
+// grid sized for more SMs than its stream owns would leave CTAs waiting for
+// others to exit, each with a fixed share of the items.
+int stream_sms(cudaStream_t stream, int device_sms) {
+    static PFN_cuStreamGetGreenCtx_v12040 get_ctx = nullptr;
+    static PFN_cuGreenCtxGetDevResource_v12040 get_res = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuStreamGetGreenCtx", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_ctx = reinterpret_cast<PFN_cuStreamGetGreenCtx_v12040>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuGreenCtxGetDevResource", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_res = reinterpret_cast<PFN_cuGreenCtxGetDevResource_v12040>(f);
+        (void)cudaGetLastError();
+    });
+    if (!stream || !get_ctx || !get_res) return device_sms;
+    CUgreenCtx green = nullptr;
+    if (get_ctx(reinterpret_cast<CUstream>(stream), &green) != CUDA_SUCCESS || !green) return device_sms;
+    CUdevResource res;
+    if (get_res(green, &res, CU_DEV_RESOURCE_TYPE_SM) != CUDA_SUCCESS) return device_sms;
+    return std::max(1, std::min(device_sms, int(res.sm.smCount)));
+}
 
 template <int MODE>
 cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream) {
@@ -929,11 +963,11 @@ cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream
     cudaError_t err = cudaGetDevice(&device);
     if (err != cudaSuccess) return err;
     std::atomic<int> *resident = device < kMaxDevices ? &g_resident[MODE][device] : nullptr;
-    int ctas = resident ? resident->load(std::memory_order_relaxed) : 0;
-    if (ctas == 0) {
+    int per_sm = resident ? resident->load(std::memory_order_relaxed) : 0;
+    int sms = device < kMaxDevices ? g_sms[device].load(std::memory_order_relaxed) : 0;
+    if (per_sm == 0 || sms == 0) {
         err = cudaFuncSetAttribute(fast_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (err != cudaSuccess) return err;
-        int sms = 0, per_sm = 0;
         if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return err;
         if (tm_mode<MODE>()) {
             // The occupancy query reports one CTA per SM for a kernel that
@@ -954,10 +988,11 @@ cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream
                    cudaSuccess) {
             return err;
         }
-        ctas = sms * std::max(1, per_sm);
-        if (resident) resident->store(ctas, std::memory_order_relaxed);
+        per_sm = std::max(1, per_sm);
+        if (resident) resident->store(per_sm, std::memory_order_relaxed);
+        if (device < kMaxDevices) g_sms[device].store(sms, std::memory_order_relaxed);
     }
-    const int grid = std::max(1, std::min(items, ctas));
+    const int grid = std::max(1, std::min(items, per_sm * stream_sms(stream, sms)));
     fast_kernel<MODE><<<grid, kThreads, smem, stream>>>(p, items);
     return cudaGetLastError();
 }
