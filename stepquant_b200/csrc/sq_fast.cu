@@ -276,10 +276,10 @@ __device__ __forceinline__ void column_max(FastSmem &s, int warp, int lane, uint
 // path (huge or NaN rows) always clamps.
 //
 // c0 = fp16(RN(M / qmax)) needs M only up to its fp16 rounding: the maximum M'
-// of the products x * RN(1/r) lies within one ulp of M, and when
-// fp16(RN(prev(M') / qmax)) == fp16(RN(next(M') / qmax)) that value is c0
-// (every step is monotone).  Tiles with a column where the two differ redo
-// the maxima with exact divisions.
+// of the products x * RN(1/r) lies within one float step of M (two are
+// allowed for), and when fp16(RN(M'' / qmax)) is the same at both ends of that
+// interval it is c0 (every step is monotone).  Tiles with a column where the
+// two differ redo the maxima with exact divisions.
 template <bool SLOW>
 __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float qmax) {
     const int warp = c.warp, lane = c.lane, tid = c.tid;
@@ -296,8 +296,8 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float q
             mx = m;
         } else {
             const uint32_t bits = __float_as_uint(m);
-            const float lo = m > 0.f ? __uint_as_float(bits - 1u) : 0.f;
-            mx = __uint_as_float(bits + 1u);
+            const float lo = bits > 2u ? __uint_as_float(bits - 2u) : 0.f;
+            mx = __uint_as_float(bits + 2u);
             settled = fp16_scale(__fdiv_rn(lo, qmax)) == fp16_scale(__fdiv_rn(mx, qmax));
         }
     }

@@ -46,7 +46,14 @@ struct KdaSmem {
     float colc[4][DV];
     float misc[64];
     int flags;
+    int qmax_max;        // largest qmax of the head's integer rows
+    uint32_t tmem_slot;  // tensor-memory base of the CTA's state columns
 };
+
+// Step and writeback keep each thread's 64 state values in its tensor-memory
+// lane between phases (128 columns per CTA; warps w and w + 4 share a lane
+// quarter with 64 columns each) and bring 16 at a time into registers.
+constexpr uint32_t kTmCols = 128;
 
 __device__ __forceinline__ int qmax_i(int b) { return (1 << ((b > 8 ? 8 : b) - 1)) - 1; }
 
@@ -77,53 +84,65 @@ __device__ __forceinline__ void kda_unpack(KdaSmem &s, int lead, int off0, int s
     }
 }
 
-template <bool SLOW>
-__device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int tid, float2 (&X)[16][2]) {
-    // P3: c0 = fp16(max over integer rows of |x / r| / limit).
-    {
-        float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+// P3 partial: per column, the maximum over the warp's integer rows of
+// |x / r| / limit -> s.red[0].  EXACT divides (corrected reciprocals, IEEE on
+// the SLOW path); otherwise |x| * RN(1/r) * RN(1/limit), whose relative
+// distance from the exact value is below 6 * 2^-24 (six float steps), bounds it.
+template <bool SLOW, bool EXACT>
+__device__ __forceinline__ void kda_column_max(KdaSmem &s, int warp, int lane, uint32_t tm) {
+    float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+        tm_ld16(tm + 16 * g, X);
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int k = warp * 16 + r;
+        for (int i = 0; i < 4; ++i) {
+            const int k = warp * 16 + 4 * g + i;
             const float4 a = s.rowa[k], b = s.rowb[k], d = s.rowd[k];
-            const float2 lim = make_float2(d.x, d.x), rl = make_float2(d.y, d.y), nl = make_float2(-d.x, -d.x);
             const float keep = d.w;
-            const float2 s01 = divide2<SLOW>(X[r][0], lo2(a), hi2(a), lo2(b));
-            const float2 s23 = divide2<SLOW>(X[r][1], lo2(a), hi2(a), lo2(b));
-            const float2 t01 = divide2<SLOW>(make_float2(fabsf(s01.x), fabsf(s01.y)), lim, rl, nl);
-            const float2 t23 = divide2<SLOW>(make_float2(fabsf(s23.x), fabsf(s23.y)), lim, rl, nl);
+            float2 t01, t23;
+            if (EXACT) {
+                const float2 lim = make_float2(d.x, d.x), rl = make_float2(d.y, d.y), nl = make_float2(-d.x, -d.x);
+                const float2 s01 = divide2<SLOW>(X[i][0], lo2(a), hi2(a), lo2(b));
+                const float2 s23 = divide2<SLOW>(X[i][1], lo2(a), hi2(a), lo2(b));
+                t01 = divide2<SLOW>(make_float2(fabsf(s01.x), fabsf(s01.y)), lim, rl, nl);
+                t23 = divide2<SLOW>(make_float2(fabsf(s23.x), fabsf(s23.y)), lim, rl, nl);
+            } else {
+                const float2 rl = make_float2(d.y, d.y);
+                t01 = pmul2(pmul2(make_float2(fabsf(X[i][0].x), fabsf(X[i][0].y)), hi2(a)), rl);
+                t23 = pmul2(pmul2(make_float2(fabsf(X[i][1].x), fabsf(X[i][1].y)), hi2(a)), rl);
+            }
             m0 = fmaxf(m0, t01.x * keep);
             m1 = fmaxf(m1, t01.y * keep);
             m2 = fmaxf(m2, t23.x * keep);
             m3 = fmaxf(m3, t23.y * keep);
         }
-        s.red[0][warp][lane] = m0;
-        s.red[0][warp][lane + 32] = m1;
-        s.red[0][warp][lane + 64] = m2;
-        s.red[0][warp][lane + 96] = m3;
     }
-    __syncthreads();
-    if (tid < DV) {
-        float mx = 0.f;
+    s.red[0][warp][lane] = m0;
+    s.red[0][warp][lane + 32] = m1;
+    s.red[0][warp][lane + 64] = m2;
+    s.red[0][warp][lane + 96] = m3;
+}
+
+// P4 body: first levels and the weighted least-squares sums; the thread's
+// values go from x to x / r (integer rows) in tensor memory.
+template <bool SLOW, bool CLAMP>
+__device__ __forceinline__ void kda_first_levels(const KdaSmem &s, int warp, int lane, uint32_t tm, float2 (&num)[2],
+                                                 float2 (&den)[2]) {
+    const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
+    const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
+    const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
+    const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
+    const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
+    const float2 round = make_float2(kRound, kRound), nround = make_float2(-kRound, -kRound);
+    num[0] = num[1] = den[0] = den[1] = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+        tm_ld16(tm + 16 * g, X);
 #pragma unroll
-        for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
-        const float c0 = fp16_scale(mx);
-        s.colc[1][tid] = c0;
-        s.colc[2][tid] = __frcp_rn(c0);
-    }
-    __syncthreads();
-    // P4: first levels and the weighted least-squares sums; X -> x / r (integer rows).
-    {
-        const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
-        const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
-        const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
-        const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
-        const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
-        const float2 round = make_float2(kRound, kRound), nround = make_float2(-kRound, -kRound);
-        float2 num[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}, den[2] = {num[0], num[1]};
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int k = warp * 16 + r;
+        for (int i = 0; i < 4; ++i) {
+            const int k = warp * 16 + 4 * g + i;
             const float4 a = s.rowa[k], b = s.rowb[k], cc = s.rowc[k], d = s.rowd[k];
             const float2 rn = lo2(cc), inv = hi2(cc), w2 = hi2(b);
             const float q = d.z;
@@ -131,16 +150,110 @@ __device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int
             const float2 nrk = pmul2(rn, nround);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const float2 x = X[r][h];
+                const float2 x = X[i][h];
                 const float2 sn = divide2<SLOW>(x, lo2(a), hi2(a), lo2(b));
                 float2 y = pmul2(divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), inv);
-                y = clamp2(y, q);
+                if (CLAMP) y = clamp2(y, q);
                 const float2 v = pfma2(rn, __fadd2_rn(y, round), nrk);
                 num[h] = __fadd2_rn(num[h], product_term(pmul2(w2, v), x));
                 den[h] = __fadd2_rn(den[h], product_term(w2, pmul2(v, v)));
-                if (integer) X[r][h] = sn;
+                if (integer) X[i][h] = sn;
             }
         }
+        tm_st16(tm + 16 * g, X);
+    }
+    tm_wait_st();
+}
+
+// P5 body: final levels (integer rows) or the fp16 values (pivot rows) -> plane.
+template <bool SLOW, bool CLAMP>
+__device__ __forceinline__ void kda_final_levels(KdaSmem &s, int warp, int lane, uint32_t tm) {
+    const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
+    const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
+    const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
+    const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
+    const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
+    const float2 round = make_float2(kRound, kRound), nround = make_float2(-kRound, -kRound);
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+        tm_ld16(tm + 16 * g, X);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int k = warp * 16 + 4 * g + i;
+            const float4 cc = s.rowc[k], d = s.rowd[k];
+            float2 o[2];
+            if (d.w != 0.f) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float2 y = pmul2(divide2<SLOW>(X[i][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), hi2(cc));
+                    if (CLAMP) y = clamp2(y, d.z);
+                    o[h] = __fadd2_rn(__fadd2_rn(y, round), nround);  // the integer level
+                }
+            } else {
+                o[0] = X[i][0];
+                o[1] = X[i][1];
+            }
+            // interleaved [k][l][i]: i = 0..3 <-> columns l, l+32, l+64, l+96
+            const __half2 h01 = __floats2half2_rn(o[0].x, o[0].y), h23 = __floats2half2_rn(o[1].x, o[1].y);
+            uint2 out;
+            out.x = *reinterpret_cast<const uint32_t *>(&h01);
+            out.y = *reinterpret_cast<const uint32_t *>(&h23);
+            *reinterpret_cast<uint2 *>(&s.u.plane[k * DV + lane * 4]) = out;
+        }
+    }
+}
+
+// P3-P5 on the thread's values in tensor memory.  c0 = fp16(M), M the
+// column's maximum of |x/r|/limit over integer rows: the products bound M
+// within six float steps; when fp16 rounds the whole interval of seven steps
+// either side to one value, that is c0, otherwise the tile redoes the maxima
+// with exact divisions.  Clamps are skipped when they cannot act: with c0 a
+// normal, unclamped fp16 value every |x/r/c0| / 2^(8-b) < qmax_b (1 + 2^-10)
+// < qmax_b + 1/2; for c1, when RN(M'/c1) * qmax_max <= qmax_max + 0.49 with M'
+// the bound of M and qmax_max the head's largest qmax.  The SLOW path (huge
+// or NaN rows) divides in IEEE arithmetic and always clamps.
+template <bool SLOW>
+__device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int tid, uint32_t tm) {
+    kda_column_max<SLOW, SLOW>(s, warp, lane, tm);
+    __syncthreads();
+    int settled = 1;
+    float mx = 0.f;  // the exact maximum, or an upper bound of it
+    if (tid < DV) {
+        float m = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) m = fmaxf(m, s.red[0][w][tid]);
+        if (SLOW) {
+            mx = m;
+        } else {
+            const uint32_t bits = __float_as_uint(m);
+            const float lo = bits > 7u ? __uint_as_float(bits - 7u) : 0.f;
+            mx = __uint_as_float(bits + 7u);
+            settled = fp16_scale(lo) == fp16_scale(mx);
+        }
+    }
+    if (!SLOW && !__syncthreads_and(settled)) {
+        kda_column_max<false, true>(s, warp, lane, tm);
+        __syncthreads();
+        if (tid < DV) {
+            mx = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
+        }
+    }
+    int safe = 1;
+    if (tid < DV) {
+        const float c0 = fp16_scale(mx);
+        s.colc[1][tid] = c0;
+        s.colc[2][tid] = __frcp_rn(c0);
+        safe = (c0 >= 6.103515625e-05f) && (mx <= 65504.f);
+    }
+    const bool no_clamp = __syncthreads_and(safe);
+    // P4: first levels and the weighted least-squares sums.
+    {
+        float2 num[2], den[2];
+        if (!SLOW && no_clamp) kda_first_levels<SLOW, false>(s, warp, lane, tm, num, den);
+        else kda_first_levels<SLOW, true>(s, warp, lane, tm, num, den);
         s.red[0][warp][lane] = num[0].x;
         s.red[0][warp][lane + 32] = num[0].y;
         s.red[0][warp][lane + 64] = num[1].x;
@@ -151,6 +264,7 @@ __device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int
         s.red[1][warp][lane + 96] = den[1].y;
     }
     __syncthreads();
+    safe = 1;
     if (tid < DV) {
         float num = 0.f, den = 0.f;
 #pragma unroll
@@ -161,45 +275,19 @@ __device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int
         const float c1 = den > 0.f ? fp16_scale(__fdiv_rn(num, fmaxf(den, 1e-30f))) : s.colc[1][tid];
         s.colc[1][tid] = c1;
         s.colc[2][tid] = __frcp_rn(c1);
+        const float qm = float(s.qmax_max);
+        safe = (c1 >= 6.103515625e-05f) && (__fmul_rn(__fdiv_rn(mx, c1), qm) <= qm + 0.49f);
     }
-    __syncthreads();
+    const bool no_clamp5 = __syncthreads_and(safe);
     // P5: final levels (integer rows) or the fp16 values (pivot rows) -> plane.
-    {
-        const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
-        const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
-        const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
-        const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
-        const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
-        const float2 round = make_float2(kRound, kRound), nround = make_float2(-kRound, -kRound);
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int k = warp * 16 + r;
-            const float4 cc = s.rowc[k], d = s.rowd[k];
-            float2 o[2];
-            if (d.w != 0.f) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    float2 y = pmul2(divide2<SLOW>(X[r][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), hi2(cc));
-                    y = clamp2(y, d.z);
-                    o[h] = __fadd2_rn(__fadd2_rn(y, round), nround);  // the integer level
-                }
-            } else {
-                o[0] = X[r][0];
-                o[1] = X[r][1];
-            }
-            // interleaved [k][l][i]: i = 0..3 <-> columns l, l+32, l+64, l+96
-            const __half2 h01 = __floats2half2_rn(o[0].x, o[0].y), h23 = __floats2half2_rn(o[1].x, o[1].y);
-            uint2 out;
-            out.x = *reinterpret_cast<const uint32_t *>(&h01);
-            out.y = *reinterpret_cast<const uint32_t *>(&h23);
-            *reinterpret_cast<uint2 *>(&s.u.plane[k * DV + lane * 4]) = out;
-        }
-    }
+    if (!SLOW && no_clamp5) kda_final_levels<SLOW, false>(s, warp, lane, tm);
+    else kda_final_levels<SLOW, true>(s, warp, lane, tm);
     __syncthreads();
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
+__global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
+    constexpr bool kTm = MODE == kStep || MODE == kWriteback;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     KdaSmem &s = *reinterpret_cast<KdaSmem *>(smem_raw);
     const sq_plan &P = p.plan;
@@ -284,8 +372,15 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
             decay = expf(g);
         }
     }
+    if (kTm && warp == 0) tm_alloc(&s.tmem_slot, kTmCols);
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+    if (kTm) tm_fence_before();
     __syncthreads();
+    uint32_t tm = 0;  // the thread's 64 columns: value (row 4g+i, half h, lane e) at 16g + 4i + 2h + e
+    if (kTm) {
+        tm_fence_after();
+        tm = s.tmem_slot + (uint32_t(32 * (warp & 3)) << 16) + uint32_t(64 * (warp >> 2));
+    }
     if (MODE != kWriteback) {
         const sq_step_args &a = p.step;
         float qq = 0.f, kk = 0.f, dot = 0.f;
@@ -314,29 +409,33 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
     __syncthreads();
 
     // ---- P1: dequantize and decay; column partials of k^T S and q^T S -------
-    float2 X[16][2];
     {
         const float2 c01 = make_float2(s.colc[3][lane], s.colc[3][lane + 32]);
         const float2 c23 = make_float2(s.colc[3][lane + 64], s.colc[3][lane + 96]);
         const float2 one = make_float2(1.f, 1.f);
         float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
+#pragma unroll 1
+        for (int g = 0; g < 4; ++g) {
+            float2 X[4][2];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int k = warp * 16 + r;
-            const float4 a = s.rowa[k], b = s.rowb[k];
-            const uint2 raw = *reinterpret_cast<const uint2 *>(&s.u.plane[k * DV + lane * 4]);
-            const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
-            const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
-            const bool integer = b.z != 0.f;
-            const float2 m01 = integer ? c01 : one, m23 = integer ? c23 : one;
-            const float2 x01 = pmul2(pmul2(v01, lo2(a)), m01);
-            const float2 x23 = pmul2(pmul2(v23, lo2(a)), m23);
-            X[r][0] = x01;
-            X[r][1] = x23;
-            kx01 = pfma2(hi2(a), x01, kx01);
-            kx23 = pfma2(hi2(a), x23, kx23);
-            qx01 = pfma2(lo2(b), x01, qx01);
-            qx23 = pfma2(lo2(b), x23, qx23);
+            for (int i = 0; i < 4; ++i) {
+                const int k = warp * 16 + 4 * g + i;
+                const float4 a = s.rowa[k], b = s.rowb[k];
+                const uint2 raw = *reinterpret_cast<const uint2 *>(&s.u.plane[k * DV + lane * 4]);
+                const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+                const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                const bool integer = b.z != 0.f;
+                const float2 m01 = integer ? c01 : one, m23 = integer ? c23 : one;
+                const float2 x01 = pmul2(pmul2(v01, lo2(a)), m01);
+                const float2 x23 = pmul2(pmul2(v23, lo2(a)), m23);
+                X[i][0] = x01;
+                X[i][1] = x23;
+                kx01 = pfma2(hi2(a), x01, kx01);
+                kx23 = pfma2(hi2(a), x23, kx23);
+                qx01 = pfma2(lo2(b), x01, qx01);
+                qx23 = pfma2(lo2(b), x23, qx23);
+            }
+            if (kTm) tm_st16(tm + 16 * g, X);
         }
         if (MODE != kWriteback) {
             s.red[0][warp][lane] = kx01.x;
@@ -377,28 +476,35 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
         const float2 d01 = make_float2(s.colc[0][lane], s.colc[0][lane + 32]);
         const float2 d23 = make_float2(s.colc[0][lane + 64], s.colc[0][lane + 96]);
         float *rowpart = s.u.rowpart;
+        float *dst = MODE == kStep && p.dense_out ? p.dense_out + (int64_t(req) * H + head) * DK * DV : nullptr;
+#pragma unroll 1
+        for (int g = 0; g < 4; ++g) {
+            float2 X[4][2];
+            tm_ld16(tm + 16 * g, X);
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int k = warp * 16 + r;
-            const float2 kk = hi2(s.rowa[k]);
-            X[r][0] = pfma2(kk, d01, X[r][0]);
-            X[r][1] = pfma2(kk, d23, X[r][1]);
-            const float a = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, fabsf(X[r][0].x)), fabsf(X[r][0].y)),
-                                                fabsf(X[r][1].x)), fabsf(X[r][1].y));
-            rowpart[k * kRowPart + lane] = a;
-        }
-        if (MODE == kStep && p.dense_out) {
-            float *dst = p.dense_out + (int64_t(req) * H + head) * DK * DV;
-#pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                float *row = dst + (warp * 16 + r) * DV + lane;
-                row[0] = X[r][0].x;
-                row[32] = X[r][0].y;
-                row[64] = X[r][1].x;
-                row[96] = X[r][1].y;
+            for (int i = 0; i < 4; ++i) {
+                const int k = warp * 16 + 4 * g + i;
+                const float2 kk = hi2(s.rowa[k]);
+                X[i][0] = pfma2(kk, d01, X[i][0]);
+                X[i][1] = pfma2(kk, d23, X[i][1]);
+                rowpart[k * kRowPart + lane] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, fabsf(X[i][0].x)),
+                                                                             fabsf(X[i][0].y)), fabsf(X[i][1].x)),
+                                                         fabsf(X[i][1].y));
+                if (dst) {
+                    float *row = dst + k * DV + lane;
+                    row[0] = X[i][0].x;
+                    row[32] = X[i][0].y;
+                    row[64] = X[i][1].x;
+                    row[96] = X[i][1].y;
+                }
             }
+            tm_st16(tm + 16 * g, X);
         }
-        if (tid == 0) s.flags = 0;
+        tm_wait_st();
+        if (tid == 0) {
+            s.flags = 0;
+            s.qmax_max = 0;
+        }
         __syncthreads();
         const int j = lane & 15, half = lane >> 4;
         const int k = warp * 16 + j;
@@ -431,12 +537,13 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
             s.rowb[k] = make_float4(-rr, -rr, w2, w2);
             s.rowc[k] = make_float4(__fmul_rn(rr, norm), __fmul_rn(rr, norm), inv, inv);
             s.rowd[k] = make_float4(lim, __frcp_rn(lim), qm, integer ? 1.f : 0.f);
+            if (integer) atomicMax(&s.qmax_max, qmax_i(b));
             if (integer && !(total <= 7.922816251426434e28f)) atomicOr(&s.flags, 1);  // 2^96, or NaN
         }
     }
     __syncthreads();
-    if (s.flags) kda_quantize<true>(s, warp, lane, tid, X);
-    else kda_quantize<false>(s, warp, lane, tid, X);
+    if (s.flags) kda_quantize<true>(s, warp, lane, tid, tm);
+    else kda_quantize<false>(s, warp, lane, tid, tm);
 
     // ---- pack the codes and the pivot rows into the staged region ----------
     for (int idx = tid; idx < DK * DTILES; idx += kThreads) {
@@ -488,6 +595,12 @@ __global__ void __launch_bounds__(kThreads, 2) kda_kernel(TileParams p) {
         if (s.rows[tid] >= 0) put_half(page, s.rows[tid], s.rowa[tid].x);
     } else {
         put_half(page, coff + 2 * (tid - DK), s.colc[1][tid - DK]);
+    }
+    if (kTm) {
+        tm_fence_before();
+        __syncthreads();
+        tm_fence_after();
+        if (warp == 0) tm_dealloc(s.tmem_slot, kTmCols);
     }
 }
 
