@@ -153,7 +153,9 @@ __device__ __forceinline__ void kda_first_levels(const KdaSmem &s, int warp, int
                 const float2 x = X[i][h];
                 const float2 sn = divide2<SLOW>(x, lo2(a), hi2(a), lo2(b));
                 float2 y = pmul2(divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), inv);
-                if (CLAMP) y = clamp2(y, q);
+                // Pivot rows (weight 0 in the sums) are always clamped: their
+                // unbounded levels could overflow v * v and turn 0 * inf into NaN.
+                if (CLAMP || !integer) y = clamp2(y, q);
                 const float2 v = pfma2(rn, __fadd2_rn(y, round), nrk);
                 num[h] = __fadd2_rn(num[h], product_term(pmul2(w2, v), x));
                 den[h] = __fadd2_rn(den[h], product_term(w2, pmul2(v, v)));
