@@ -237,3 +237,38 @@ def test_joined_capture_of_chained_layers():
             assert torch.equal(o, e), f"step {step}"
         for p, r in zip(pools, refs):
             assert torch.equal(p.data, r.data), f"step {step}"
+
+
+def test_ieee_path_rows_beyond_2_96():
+    """Rows whose |x| sum exceeds 2^96 switch a tile to IEEE divisions (the
+    kernels' SLOW path, reached by the encode of such a state): the pages equal
+    the oracle's.  The decoded state is bounded by the saturated fp16 scales
+    (65504^2 * qmax), so the following step runs the ordinary path on tiles
+    whose r and c saturate; its bytes equal the oracle's too."""
+    from stepquant_b200.kernels.pool import PackedStatePool
+    gen = torch.Generator().manual_seed(12)
+    plan, oplan = _gdn_plan([4, 6, 8, 6], 12)
+    batch, heads = 6, 4
+    pool = PackedStatePool(plan, batch + 1, 128)
+    slots = torch.arange(1, batch + 1, device="cuda")
+    state = torch.randn(batch, heads, 128, 128, generator=gen) * 0.1
+    state[1, :, 5] *= 1e28   # |x| row sums near 1e29 > 2^96 in every head of request 1
+    state[3, 2, 100] *= 3e27
+    before = pool.data.cpu().numpy()
+    pool.encode(state.cuda(), slots)
+    expected = O.page_encode(state.numpy(), oplan, before[1:])
+    got = pool.data.cpu().numpy()
+    for i in range(batch):
+        assert (got[i + 1] == expected[i]).all(), f"encode, request {i}"
+    q, k, v, a, b = _inputs(batch, heads, heads, gen, torch.float32)
+    upd = torch.empty(batch, heads, 128, 128, device="cuda")
+    before = pool.data.cpu().numpy()
+    pool.step(q.cuda(), k.cuda(), v.cuda(), a.cuda(), b.cuda(), slots, normalize=True, scale=128 ** -0.5,
+              a_log=torch.rand(heads).cuda(), dt_bias=torch.zeros(heads).cuda(), state_out=upd)
+    pool.check_status()
+    u = upd.cpu().numpy()
+    assert np.isfinite(u).all() and np.abs(u).max() > 1e9
+    expected = O.page_encode(u, oplan, before[1:])
+    got = pool.data.cpu().numpy()
+    for i in range(batch):
+        assert (got[i + 1] == expected[i]).all(), f"step, request {i}"

@@ -102,3 +102,32 @@ def test_kda_async_equals_fused():
         torch.cuda.synchronize()
         assert torch.equal(o1, o2)
         assert torch.equal(sync.data, asyn.data), f"step {step}"
+
+
+def test_kda_saturated_scales():
+    """A state with integer rows near 1e27 encodes to saturated fp16 scales
+    (r, c = 65504); the KDA kernel's step from those pages repacks exactly the
+    oracle's fit_state of its own updated state."""
+    from stepquant_b200.kernels.pool import PackedStatePool
+    gen = torch.Generator().manual_seed(24)
+    heads, batch = 4, 6
+    plan, oplan = _kda_plan(heads, 24)
+    pool = PackedStatePool(plan, batch + 1, 128)
+    slots = torch.arange(1, batch + 1, device="cuda")
+    state = torch.randn(batch, heads, 128, 128, generator=gen) * 0.1
+    bits = oplan.bits
+    rows = [k for k in range(128) if bits[1, k] != 16][:2]
+    state[2, 1, rows] *= 1e28
+    pool.encode(state.cuda(), slots)
+    q, k, v, a, b = _inputs(batch, heads, gen, torch.float32)
+    upd = torch.empty(batch, heads, 128, 128, device="cuda")
+    before = pool.data.cpu().numpy()
+    pool.step(q.cuda(), k.cuda(), v.cuda(), a.cuda(), b.cuda(), slots, normalize=True, scale=128 ** -0.5,
+              a_log=(torch.rand(heads) * np.log(16)).cuda(), dt_bias=torch.zeros(heads * 128).cuda(), state_out=upd)
+    pool.check_status()
+    u = upd.cpu().numpy()
+    assert np.isfinite(u).all() and np.abs(u).max() > 1e6
+    expected = O.page_encode(u, oplan, before[1:])
+    got = pool.data.cpu().numpy()
+    for i in range(batch):
+        assert (got[i + 1] == expected[i]).all(), f"request {i}"
