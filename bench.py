@@ -577,6 +577,18 @@ def measure_prefill(args, batch, tokens, heads_total, qk_total, steps, warmup, w
     return res
 
 
+def gather_heads(out, world, group=None):
+    """All-gather of per-rank readouts [T, H_local * V] into [T, H * V] in the
+    global head order (rank r owns heads [r * H_local, (r + 1) * H_local))."""
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return out
+    parts = torch.empty(world * out.shape[0], out.shape[1], device=out.device, dtype=out.dtype)
+    dist.all_gather_into_tensor(parts, out.contiguous(), group=group)  # rank-major concatenation
+    return parts.view(world, *out.shape).permute(1, 0, 2).reshape(out.shape[0], world * out.shape[1])
+
+
 def _rms_norm(x):
     xf = x.float()
     return (xf * (xf.square().mean(-1, keepdim=True) + 1e-6).rsqrt()).bfloat16()
@@ -637,12 +649,7 @@ def measure_stack(args, batch, heads_total, qk_total, steps, warmup, world, rank
         stack.append((pool, w_in, w_out, a_log, dt_bias))
 
     def gather(out):
-        """[T, H_local * V] on every rank -> [T, H * V] in global head order."""
-        if world == 1:
-            return out
-        parts = torch.empty(world, *out.shape, device=device, dtype=out.dtype)
-        dist.all_gather_into_tensor(parts, out.contiguous())
-        return parts.permute(1, 0, 2).reshape(out.shape[0], world * out.shape[1])
+        return gather_heads(out, world)
 
     # ---- prompt: chunked prefill of every layer (setup, untimed) ----------------
     tokens = batch * prompt

@@ -2,7 +2,9 @@
 
 The decode path shards value heads over ranks with no data-path collective;
 what crosses ranks is the slot-count agreement (a MIN over the gloo CPU group,
-sglang/runtime.py:310-317) and the benchmark's max-over-ranks timing.
+sglang/runtime.py:310-317), the benchmark's max-over-ranks timing, and in the
+layer stack (bench.py --workload gdn-stack) the all-gather of each layer's
+readouts back into the global head order.
 """
 import os
 import socket
@@ -51,3 +53,24 @@ def test_two_rank_slot_agreement_sharding_and_timing():
 def test_single_rank_agreement_is_identity():
     from stepquant_b200.sglang.runtime import agree_min
     assert agree_min(17, None) == 17
+
+
+def _gather_worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import bench
+        tokens, heads, dim = 3, 4, 5
+        full = torch.arange(tokens * heads * world * dim, dtype=torch.float32).reshape(tokens, heads * world, dim)
+        local = full[:, rank * heads:(rank + 1) * heads].reshape(tokens, heads * dim)  # this rank's value heads
+        gathered = bench.gather_heads(local, world)
+        results[rank] = torch.equal(gathered, full.reshape(tokens, heads * world * dim))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_readout_gather_keeps_global_head_order():
+    world, port = 2, _free_port()
+    results = mp.Manager().dict()
+    mp.spawn(_gather_worker, args=(world, port, results), nprocs=world, join=True)
+    assert results[0] and results[1]
