@@ -381,37 +381,51 @@ __device__ __forceinline__ void stage_codes(FastStage &st, const uint8_t *src, i
     }
 }
 
-// P1 for one code width: unpack the warp's 16 rows into X = level * r_old and
-// accumulate the column partials of k_raw^T X and q_raw^T X.
+// P1 of the readout, which keeps no state: the column partials of k_raw^T Y
+// and q_raw^T Y, with lane l covering the four consecutive columns 4l..4l+3
+// (one or two word loads per row instead of a byte load per value).  Each
+// column's partial is the same ordered sum over the warp's 16 rows as in
+// unpack_rows_tm, so the results are identical.
 template <int BITS>
-__device__ __forceinline__ void unpack_rows(const FastSmem &s, const FastStage &st, int warp, int lane,
-                                            float2 (&X)[16][2], float2 (&acc)[4]) {
-    const int t0 = lane >> 4, u = lane & 15;
-    const float2 lc = level_constants<BITS>(u);
-    const float2 lscale = make_float2(lc.x, lc.x), lbias = make_float2(lc.y, lc.y);
+__device__ __forceinline__ void readout_rows(FastSmem &s, const FastStage &st, int warp, int lane) {
+    const int gq = lane & 3;
+    const unsigned char *tile = st.codes + (lane >> 2) * (W<BITS>::tile_bytes + kStagePad);
+    constexpr uint32_t mask = (1u << BITS) - 1u;
+    constexpr float bias = -(8388608.f + float(W<BITS>::off));
+    const float2 nbias = make_float2(bias, bias);
     float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
-#pragma unroll
+#pragma unroll 4
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
+        const unsigned char *chunk = tile + k * W<BITS>::chunk;
+        uint32_t v;
+        if (BITS == 8) {
+            v = *reinterpret_cast<const uint32_t *>(chunk + 4 * gq);
+        } else if (BITS == 4) {
+            v = *reinterpret_cast<const uint16_t *>(chunk + 2 * gq);
+        } else {  // 3 bytes at 3 gq: two words and a funnel shift (the second word may be the next chunk's)
+            const uint32_t *words = reinterpret_cast<const uint32_t *>(chunk) + ((3 * gq) >> 2);
+            v = __funnelshift_r(words[0], words[1], (3 * gq & 3) * 8);
+        }
         const float4 a = s.rowa[k], b = s.rowb[k];
-        const float2 f01 = make_float2(staged_bits<BITS>(st.codes, t0, k, u), staged_bits<BITS>(st.codes, t0 + 2, k, u));
-        const float2 f23 = make_float2(staged_bits<BITS>(st.codes, t0 + 4, k, u), staged_bits<BITS>(st.codes, t0 + 6, k, u));
-        const float2 x01 = pmul2(pfma2(f01, lscale, lbias), lo2(a));
-        const float2 x23 = pmul2(pfma2(f23, lscale, lbias), lo2(a));
-        X[r][0] = x01;
-        X[r][1] = x23;
-        kx01 = pfma2(hi2(a), x01, kx01);
-        kx23 = pfma2(hi2(a), x23, kx23);
-        qx01 = pfma2(lo2(b), x01, qx01);
-        qx23 = pfma2(lo2(b), x23, qx23);
+        const float2 f01 = make_float2(__uint_as_float(0x4B000000u | (v & mask)),
+                                       __uint_as_float(0x4B000000u | ((v >> BITS) & mask)));
+        const float2 f23 = make_float2(__uint_as_float(0x4B000000u | ((v >> (2 * BITS)) & mask)),
+                                       __uint_as_float(0x4B000000u | ((v >> (3 * BITS)) & mask)));
+        const float2 y01 = pmul2(__fadd2_rn(f01, nbias), lo2(a));  // exact level, then * r_old
+        const float2 y23 = pmul2(__fadd2_rn(f23, nbias), lo2(a));
+        kx01 = pfma2(hi2(a), y01, kx01);
+        kx23 = pfma2(hi2(a), y23, kx23);
+        qx01 = pfma2(lo2(b), y01, qx01);
+        qx23 = pfma2(lo2(b), y23, qx23);
     }
-    acc[0] = kx01;
-    acc[1] = kx23;
-    acc[2] = qx01;
-    acc[3] = qx23;
+    *reinterpret_cast<float4 *>(&s.red[0][warp][4 * lane]) = make_float4(kx01.x, kx01.y, kx23.x, kx23.y);
+    *reinterpret_cast<float4 *>(&s.red[1][warp][4 * lane]) = make_float4(qx01.x, qx01.y, qx23.x, qx23.y);
 }
 
-// P1 of the fused step: as unpack_rows, with Y going to tensor memory.
+// P1 of the fused step: unpack the warp's 16 rows into Y = level * r_old
+// (to tensor memory) and accumulate the column partials of k_raw^T Y and
+// q_raw^T Y.
 template <int BITS>
 __device__ __forceinline__ void unpack_rows_tm(const FastSmem &s, const FastStage &st, int warp, int lane, uint32_t tm,
                                                float2 (&acc)[4]) {
@@ -679,19 +693,15 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
         else if (width == 6) unpack_update_tm<6>(s, st, warp, lane, c.tm);
         else unpack_update_tm<8>(s, st, warp, lane, c.tm);
     } else {
-        float2 acc[4];
         if (MODE == kReadout) {
-            float2 X[16][2];  // the readout keeps no state past P1
-            if (width == 4) unpack_rows<4>(s, st, warp, lane, X, acc);
-            else if (width == 6) unpack_rows<6>(s, st, warp, lane, X, acc);
-            else unpack_rows<8>(s, st, warp, lane, X, acc);
+            if (width == 4) readout_rows<4>(s, st, warp, lane);
+            else if (width == 6) readout_rows<6>(s, st, warp, lane);
+            else readout_rows<8>(s, st, warp, lane);
         } else {
+            float2 acc[4];
             if (width == 4) unpack_rows_tm<4>(s, st, warp, lane, c.tm, acc);
             else if (width == 6) unpack_rows_tm<6>(s, st, warp, lane, c.tm, acc);
             else unpack_rows_tm<8>(s, st, warp, lane, c.tm, acc);
-        }
-        {
-            const sq_step_args &a = p.step;
             s.red[0][warp][lane] = acc[0].x;
             s.red[0][warp][lane + 32] = acc[0].y;
             s.red[0][warp][lane + 64] = acc[1].x;
@@ -700,6 +710,9 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
             s.red[1][warp][lane + 32] = acc[2].y;
             s.red[1][warp][lane + 64] = acc[3].x;
             s.red[1][warp][lane + 96] = acc[3].y;
+        }
+        {
+            const sq_step_args &a = p.step;
             // Gates (every thread; independent of the unpack above).
             const float alog = s.head[c.head].a_log;
             const float bias = s.head[c.head].dt_bias;
