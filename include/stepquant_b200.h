@@ -76,7 +76,7 @@ typedef struct sq_plan {
     int32_t keys;
     int32_t values;
     int32_t value_group_size;
-    int32_t reserved;
+    int32_t storage;      /* 0: packed codes (tiles of 16 / 4 values); 1: byte carriers */
     int64_t page_bytes;
     const int32_t *bits;
     const float *impact;

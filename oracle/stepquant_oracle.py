@@ -450,27 +450,96 @@ def page_store(page, plan: Plan, values, z, r, c, r2, pivots_f16):
                 _put_half(page, columns[h] + 2 * v, c[h, v])
 
 
-def page_encode(state, plan: Plan, pages=None):
+def page_store_byte(page, plan: Plan, values, z, r, c, r2, pivots_f16):
+    """Byte-carrier page image of one request (storage='byte'), in place.
+
+    Integer rows keep their signed level as one int8 at code_base + k + v*K
+    (KDA: the level times 2^(8-b); fit.py:111-115, kernels/pool.py:37-44);
+    fp16 pivot rows are contiguous at their offset; r (GDN 2-bit: per value
+    group) and c as in packed pages.
+    """
+    heads, keys = plan.bits.shape
+    offsets, rows, columns, _ = packed_layout(plan, values, "byte")
+    kda = plan.architecture == "kda"
+    two_index = 0
+    for h in range(heads):
+        code_base = offsets[heads * keys + h]
+        for k in range(keys):
+            b = int(plan.bits[h, k])
+            off = offsets[h * keys + k]
+            if b == 16:
+                page[off:off + 2 * values] = pivots_f16[h, k].astype(np.float16).view(np.uint8)
+                continue
+            level = z[h, k].astype(np.int64) * ((1 << (8 - min(b, 8))) if kda else 1)
+            idx = code_base + k + np.arange(values) * keys
+            page[idx] = level.astype(np.int8).view(np.uint8)
+            if b == 2 and not kda:
+                for g in range(values // plan.value_group_size):
+                    _put_half(page, rows[h * keys + k] + 2 * g, r2[two_index, k, g])
+            else:
+                _put_half(page, rows[h * keys + k], r[h, k])
+        if not kda and plan.bits[h, 0] == 2:
+            two_index += 1
+        if columns[h] >= 0:
+            page[columns[h]:columns[h] + 2 * values] = c[h].astype(np.float16).view(np.uint8)
+
+
+def page_encode(state, plan: Plan, pages=None, storage="packed"):
     """pool.encode (kernels/pool.py:199-205,334-346): dense fp32 [B,H,K,V] -> pages [B,P].
 
     ``pages`` supplies the prior page contents (kept in alignment padding);
-    zero pages are used when it is None.
+    zero pages are used when it is None.  ``storage`` selects packed codes or
+    byte carriers.
     """
     state = np.asarray(state, F32)
     batch, heads, keys, values = state.shape
-    page_bytes = packed_layout(plan, values)[-1]
+    page_bytes = packed_layout(plan, values, storage)[-1]
     out = np.zeros((batch, page_bytes), np.uint8) if pages is None else np.array(pages, np.uint8)
     if batch == 0:
         return out
     z, r, c, r2, _ = fit_state(state, plan)
     pivots = state.astype(np.float16)
+    store = page_store_byte if storage == "byte" else page_store
     for i in range(batch):
-        page_store(out[i], plan, values, z[i], r[i], c[i], None if r2 is None else r2[i], pivots[i])
+        store(out[i], plan, values, z[i], r[i], c[i], None if r2 is None else r2[i], pivots[i])
     return out
 
 
-def page_decode(pages, plan: Plan, values):
+def page_decode_byte(pages, plan: Plan, values):
+    """byte_codec.py:6-27: byte-carrier pages [B,P] -> dense fp32 [B,H,K,V], x = (r c) z."""
+    pages = np.asarray(pages, np.uint8)
+    heads, keys = plan.bits.shape
+    offsets, rows, columns, _ = packed_layout(plan, values, "byte")
+    group = plan.value_group_size
+    kda = plan.architecture == "kda"
+    out = np.zeros((pages.shape[0], heads, keys, values), F32)
+    for i in range(pages.shape[0]):
+        page = pages[i]
+        for h in range(heads):
+            code_base = offsets[heads * keys + h]
+            col = np.zeros(values, F32)
+            if columns[h] >= 0:
+                col = np.frombuffer(page[columns[h]:columns[h] + 2 * values].tobytes(), np.float16).astype(F32)
+            for k in range(keys):
+                b = int(plan.bits[h, k])
+                off = offsets[h * keys + k]
+                if b == 16:
+                    out[i, h, k] = np.frombuffer(page[off:off + 2 * values].tobytes(), np.float16).astype(F32)
+                    continue
+                zz = page[code_base + k + np.arange(values) * keys].view(np.int8).astype(F32)
+                if b == 2 and not kda:
+                    rr = np.array([_get_half(page, rows[h * keys + k] + 2 * (v // group)) for v in range(values)],
+                                  np.float16).astype(F32)
+                else:
+                    rr = np.full(values, _get_half(page, rows[h * keys + k]), np.float16).astype(F32)
+                out[i, h, k] = ((rr * col).astype(F32) * zz).astype(F32)
+    return out
+
+
+def page_decode(pages, plan: Plan, values, storage="packed"):
     """fused.py:19-59: pages [B,P] uint8 -> dense fp32 [B,H,K,V]."""
+    if storage == "byte":
+        return page_decode_byte(pages, plan, values)
     pages = np.asarray(pages, np.uint8)
     heads, keys = plan.bits.shape
     offsets, rows, columns, _ = packed_layout(plan, values)
@@ -578,7 +647,7 @@ def prepare_inputs(q, k, g, beta, heads, *, kda, normalize=False, scale=1.0, a_l
     return q, k, g, beta
 
 
-def decode_step(pages, slots, plan: Plan, values, q, k, v, g, beta, **prep):
+def decode_step(pages, slots, plan: Plan, values, q, k, v, g, beta, storage="packed", **prep):
     """One packed-state decode step over ``pages[slots]`` (slot <= 0 = padding).
 
     Returns (out [B,H,V] fp32, new_pages copy, updated fp32 state [B,H,K,V]).
@@ -590,12 +659,12 @@ def decode_step(pages, slots, plan: Plan, values, q, k, v, g, beta, **prep):
     active = slots > 0
     state = np.zeros((len(slots), heads, plan.bits.shape[1], values), F32)
     if active.any():
-        state[active] = page_decode(pages[slots[active]], plan, values)
+        state[active] = page_decode(pages[slots[active]], plan, values, storage)
     out, updated = delta_step(state, qp, kp, np.asarray(v, F32).reshape(len(slots), heads, values),
                               log_decay, beta_p)
     out[~active] = 0
     if active.any():
-        pages[slots[active]] = page_encode(updated[active], plan, pages[slots[active]])
+        pages[slots[active]] = page_encode(updated[active], plan, pages[slots[active]], storage)
     return out, pages, updated
 
 

@@ -25,7 +25,7 @@ _i64 = ctypes.c_int64
 
 class SqPlan(ctypes.Structure):
     _fields_ = [("architecture", _i32), ("heads", _i32), ("keys", _i32), ("values", _i32),
-                ("value_group_size", _i32), ("reserved", _i32), ("page_bytes", _i64),
+                ("value_group_size", _i32), ("storage", _i32), ("page_bytes", _i64),
                 ("bits", _p), ("impact", _p), ("offsets", _p), ("rows", _p), ("columns", _p),
                 ("bits_host", _p)]
 

@@ -147,6 +147,13 @@ __device__ __forceinline__ uint32_t read_code(const uint8_t *p, uint32_t bitpos,
     return (v >> shift) & ((1u << bits) - 1u);
 }
 
+// Byte offset of value v of the fp16 pivot row at `off`: packed pages keep the
+// row's values in tiles `stride` apart (pool.py:50-57); byte-carrier pages
+// store the row contiguously (pool.py:37-44).
+__device__ __forceinline__ int64_t pivot_at(int off, int v, int tile, int stride, bool bytes) {
+    return bytes ? int64_t(off) + 2 * v : int64_t(off) + int64_t(v / tile) * stride + 2 * (v % tile);
+}
+
 __device__ __forceinline__ float qmax_of(int bits, bool gdn) {
     if (gdn && bits == 2) return 3.f;
     const int b = bits > 8 ? 8 : bits;

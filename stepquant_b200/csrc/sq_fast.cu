@@ -1013,7 +1013,8 @@ cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream
 }  // namespace
 
 bool fast_eligible(const sq_plan &plan, const void *pages) {
-    return plan.architecture == SQ_GDN && plan.keys == FK && plan.values == FV && plan.heads <= kMaxHeads &&
+    return plan.architecture == SQ_GDN && plan.storage == 0 && plan.keys == FK && plan.values == FV &&
+           plan.heads <= kMaxHeads &&
            plan.page_bytes % 16 == 0 &&
            (reinterpret_cast<uintptr_t>(pages) & 15u) == 0;
 }

@@ -618,7 +618,7 @@ cudaError_t launch_kda_mode(const TileParams &p, int items, cudaStream_t stream)
 }  // namespace
 
 bool kda_fast_eligible(const sq_plan &plan) {
-    return plan.architecture == SQ_KDA && plan.keys == DK && plan.values == DV;
+    return plan.architecture == SQ_KDA && plan.storage == 0 && plan.keys == DK && plan.values == DV;
 }
 
 cudaError_t launch_fast_kda(int mode, const TileParams &p, int batch, cudaStream_t stream) {

@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
     const int stride = P.offsets[H * K + head];
     const int coff = P.columns[head];
     const int tile = min(kda ? 4 : 16, V);
+    const bool bytes = P.storage != 0;  // byte carriers (pool.py:34-49): codes at code_base + k + v K
     const bool gdn2 = !kda && P.bits[head * K] == 2;
     if (MODE == kWriteback && coff < 0) return;  // all-pivot head: finished by sq_readout
     __syncthreads();
@@ -133,14 +134,14 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
         for (int e = tid; e < K * V; e += kThreads) {
             const int k = e / V, v = e % V;
             const int b = s.rbits[k];
-            const int t = v / tile, u = v % tile;
-            const int64_t base = s.roff[k] + int64_t(t) * stride;
             float x;
             if (b == 16) {
-                x = MODE == kWriteback ? 0.f : half_at(page, base + 2 * u);
+                x = MODE == kWriteback ? 0.f : half_at(page, pivot_at(s.roff[k], v, tile, stride, bytes));
             } else {
-                const uint32_t code = read_code(page + base, uint32_t(u * b), b);
-                const float z = level_of(code, b, kda);
+                // byte carriers: the signed level (KDA: times 2^(8-b)) at code_base + k + v K
+                const float z = bytes ? float(reinterpret_cast<const int8_t *>(page)[s.roff[k] + int64_t(v) * K])
+                                      : level_of(read_code(page + s.roff[k] + int64_t(v / tile) * stride,
+                                                           uint32_t((v % tile) * b), b), b, kda);
                 const float r = gdn2 ? s.r2s[k * groups + v / G] : s.rr[k];
                 x = __fmul_rn(__fmul_rn(r, s.cold[v]), z);
             }
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
             for (int e = tid; e < K * V; e += kThreads) {
                 const int k = e / V, v = e % V;
                 if (s.rbits[k] != 16) continue;
-                put_half(page, s.roff[k] + int64_t(v / tile) * stride + 2 * (v % tile), s.xs[e]);
+                put_half(page, pivot_at(s.roff[k], v, tile, stride, bytes), s.xs[e]);
             }
             return;
         }
@@ -245,7 +246,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
             // All-pivot head: no quantization, store the fp16 rows.
             for (int e = tid; e < K * V; e += kThreads) {
                 const int k = e / V, v = e % V;
-                put_half(page, s.roff[k] + int64_t(v / tile) * stride + 2 * (v % tile), s.xs[e]);
+                put_half(page, pivot_at(s.roff[k], v, tile, stride, bytes), s.xs[e]);
             }
             return;
         }
@@ -254,7 +255,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
         __syncthreads();
         for (int e = tid; e < K * V; e += kThreads) {
             const int k = e / V, v = e % V;
-            put_half(page, s.roff[k] + int64_t(v / tile) * stride + 2 * (v % tile), s.xs[e]);
+            put_half(page, pivot_at(s.roff[k], v, tile, stride, bytes), s.xs[e]);
         }
         return;
     }
@@ -364,7 +365,19 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
     }
     // Page stores: codes of integer rows, fp16 pivots, r, c.
     const int tiles = V / tile;
-    for (int ch = tid; ch < K * tiles; ch += kThreads) {
+    if (bytes) {
+        for (int e = tid; e < K * V; e += kThreads) {
+            const int k = e / V, v = e % V;
+            const int b = s.rbits[k];
+            if (b == 16) {
+                if (MODE != kWriteback) put_half(page, pivot_at(s.roff[k], v, tile, stride, bytes), s.xs[e]);
+                continue;
+            }
+            const int z = int(s.zq[e]) * (kda ? (1 << (8 - b)) : 1);  // fit.py:111-115
+            reinterpret_cast<int8_t *>(page)[s.roff[k] + int64_t(v) * K] = int8_t(z);
+        }
+    }
+    for (int ch = tid; !bytes && ch < K * tiles; ch += kThreads) {
         const int k = ch / tiles, t = ch % tiles;
         const int b = s.rbits[k];
         uint8_t *dst = page + s.roff[k] + int64_t(t) * stride;

@@ -58,6 +58,7 @@ cudaError_t launch_fast_kda(int mode, const TileParams &p, int batch, cudaStream
 // Device-side: is `head` handled by a register-resident kernel (so the tile
 // kernel, launched with skip_fast, leaves it)?
 __device__ inline bool fast_head_dev(const sq_plan &P, int head) {
+    if (P.storage != 0) return false;
     if (P.architecture == SQ_GDN) return fast_head(P, P.bits[head * P.keys]);
     return P.keys == 128 && P.values == 128 &&
            kda_head_fits(P.offsets[P.heads * P.keys + head], P.values, P.columns[head]);

@@ -57,8 +57,6 @@ class PackedStatePool:
             raise ValueError("state pool requires CUDA")
         if storage not in ("packed", "byte"):
             raise ValueError("state storage must be packed or byte")
-        if storage == "byte":
-            raise NotImplementedError("byte-carrier storage is not built; use storage='packed'")
         self.storage = storage
         self.early_writeback = True
         self.plan = plan

@@ -74,7 +74,7 @@ class DevicePlan:
         self.bits_host = plan.bits.detach().to("cpu", torch.int32).contiguous()
         self.struct = N.SqPlan(
             N.SQ_KDA if plan.architecture == "kda" else N.SQ_GDN, self.heads, self.keys, values,
-            plan.value_group_size, 0, page_bytes, self.bits.data_ptr(), self.impact.data_ptr(),
+            plan.value_group_size, 1 if storage == "byte" else 0, page_bytes, self.bits.data_ptr(), self.impact.data_ptr(),
             self.offsets.data_ptr(), self.rows.data_ptr(), self.columns.data_ptr(), self.bits_host.data_ptr())
 
     def ref(self):

@@ -162,3 +162,25 @@ def test_prefill_oracle_matches_reference_recurrent_kernel(case):
     out, final = O.prefill_sequential(q, k, v, g, beta, [0, q.shape[0]], init)
     np.testing.assert_allclose(final, d[f"{case}_final"], rtol=0, atol=1e-5 * np.abs(d[f"{case}_final"]).max())
     np.testing.assert_allclose(out, d[f"{case}_out"][0], rtol=0, atol=1e-5 * np.abs(d[f"{case}_out"]).max())
+
+
+def test_byte_carrier_pages_hold_the_packed_levels():
+    """storage='byte' pages (fit.py:111-115, byte_codec.py:6-27): the same
+    fitted levels as packed pages, one int8 per value (KDA: times 2^(8-b)),
+    contiguous fp16 pivot rows; both images decode to the same state."""
+    rng = np.random.default_rng(5)
+    for arch, bits in (("kda", np.array([[2, 4, 6, 16] * 8, [16] * 32])),
+                       ("gdn", np.array([[4] * 32, [2] * 32, [16] * 32, [8] * 32]))):
+        plan = O.Plan(arch, bits, (rng.random(bits.shape) + 0.5).astype(np.float32), 8)
+        state = (rng.standard_normal((2, bits.shape[0], 32, 32)) * 0.1).astype(np.float32)
+        byte_pages = O.page_encode(state, plan, storage="byte")
+        packed_pages = O.page_encode(state, plan)
+        assert byte_pages.shape[1] == O.packed_layout(plan, 32, "byte")[-1]
+        np.testing.assert_array_equal(O.page_decode(byte_pages, plan, 32, "byte"), O.page_decode(packed_pages, plan, 32))
+        z = O.fit_state(state, plan)[0]
+        offsets = O.packed_layout(plan, 32, "byte")[0]
+        code_base = offsets[bits.shape[0] * 32]
+        k = 1 if arch == "kda" else 0  # a 4-bit row of head 0
+        levels = byte_pages[0, code_base + k + np.arange(32) * 32].view(np.int8)
+        expect = z[0, 0, k].astype(np.int64) * (16 if arch == "kda" else 1)
+        np.testing.assert_array_equal(levels, expect)
