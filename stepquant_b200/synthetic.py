@@ -14,6 +14,8 @@ from dataclasses import dataclass
 
 import torch
 
+from .core import impact_factors, row_impact  # noqa: F401  (re-exported for the benchmark)
+
 from .quantization import QuantizationPlan
 
 
@@ -58,18 +60,6 @@ def prepared(inputs, heads, keys, kda, a_log, dt_bias):
     return q, k, g, torch.sigmoid(inputs.b)
 
 
-def row_impact(q, k, log_decay, beta):
-    """core.py:18-24: squared transported read [D(q - beta k (k^T q))]^2."""
-    decay = log_decay.exp()
-    if decay.ndim == q.ndim - 1:
-        decay = decay.unsqueeze(-1)
-    return (decay * (q - beta.unsqueeze(-1) * k * (k * q).sum(-1, keepdim=True))).square()
-
-
-def impact_factors(omega, gamma=0.25, floor=1e-20):
-    """core.py:27-29."""
-    log_w = omega.double().clamp_min(floor).log() * (gamma / 2)
-    return (log_w - log_w.mean(-1, keepdim=True)).exp().float()
 
 
 def gdn_widths(heads, generator, pivot_heads=0):

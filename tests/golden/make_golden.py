@@ -22,7 +22,14 @@ Files written next to this script:
                         token prefill recurrence) on bf16-valued q/k/v with
                         in-kernel L2 normalisation: outputs and final states.
 
-``--prefill-only`` rewrites ``prefill.npz`` alone.
+* ``calibration.npz`` -- ``stepquant.calibration``: the statistics a seeded
+                        run of ``LayerStatistics.observe`` exports (two GDN
+                        and two KDA layers), the plans ``calibrate`` makes from
+                        them, and ``stepquant.allocation`` on seeded cost
+                        tables.
+
+``--prefill-only`` rewrites ``prefill.npz`` alone; ``--calibration-only``
+rewrites ``calibration.npz`` alone.
 """
 import argparse
 import json
@@ -105,12 +112,75 @@ def prefill_cases(RecurrentKernel):
     return out
 
 
+CALIBRATION_CASES = (  # (arch, layers, heads, keys, values, nominal bits, pivots, seed)
+    ("gdn", 2, 6, 32, 32, 6, 2, 41),
+    ("kda", 2, 2, 32, 32, 4, 8, 42),
+)
+
+
+def observe_run(LayerStatistics, arch, heads, keys, values, seed, updates=32, batch=4):
+    """A seeded stream of observe() calls (tests/test_calibration.py replays
+    it); returns the exported statistics."""
+    gen = torch.Generator().manual_seed(seed)
+    stat = LayerStatistics(arch, sample_every=8, max_snapshots=6)
+    for _ in range(updates):
+        q = torch.randn(batch, heads, keys, generator=gen)
+        k = torch.nn.functional.normalize(torch.randn(batch, heads, keys, generator=gen), dim=-1)
+        v = torch.randn(batch, heads, values, generator=gen)
+        shape = (batch, heads) if arch == "gdn" else (batch, heads, keys)
+        log_decay = -torch.rand(shape, generator=gen) * 0.2
+        beta = torch.rand(batch, heads, generator=gen)
+        state = torch.randn(batch, heads, keys, values, generator=gen) * 0.1
+        stat.observe(q, k, v, log_decay, beta, state)
+    return stat.export()
+
+
+def calibration_vectors(reference_modules):
+    LayerStatistics, calibrate, allocate_dp, allocate_lagrangian = reference_modules
+    out = {}
+    for arch, layers, heads, keys, values, nominal, pivots, seed in CALIBRATION_CASES:
+        stats = {}
+        for layer in range(layers):
+            name = f"model.layers.{3 * layer}.mixer"
+            stats[name] = observe_run(LayerStatistics, arch, heads, keys, values, seed + 100 * layer)
+            e = stats[name]
+            for key in ("omega", "log_decay", "snapshots"):
+                out[f"{arch}_{layer}_{key}"] = e[key].numpy()
+            out[f"{arch}_{layer}_counts"] = np.array([e["tokens"], e["sampled_states"]])
+        result = calibrate(stats, nominal_bits=nominal, pivots=pivots, horizon=256, value_group_size=8)
+        for layer, name in enumerate(sorted(stats)):
+            out[f"{arch}_{layer}_bits"] = result["plans"][name]["bits"].numpy().astype(np.int8)
+            out[f"{arch}_{layer}_impact"] = result["plans"][name]["impact"].numpy()
+        st = result["settings"]
+        out[f"{arch}_budget"] = np.array([st["integer_budget"], st["integer_bits_used"]])
+    gen = torch.Generator().manual_seed(43)
+    for name, fn, units in (("dp", allocate_dp, 24), ("lagrangian", allocate_lagrangian, 200)):
+        candidates = [4, 6, 8] if name == "dp" else [2, 4, 6, 8]
+        cost = torch.rand(units, len(candidates), generator=gen).double()
+        cost = torch.sort(cost, dim=1, descending=True).values  # wider is better, mostly
+        cost[::7] = torch.rand(len(cost[::7]), len(candidates), generator=gen).double()  # some non-monotone rows
+        budget = int(units * (5 if name == "dp" else 4))
+        out[f"alloc_{name}_cost"] = cost.numpy()
+        out[f"alloc_{name}_budget"] = np.array(budget)
+        out[f"alloc_{name}_result"] = fn(cost, candidates, budget).numpy()
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path of the STEPQuant checkout")
     parser.add_argument("--prefill-only", action="store_true")
+    parser.add_argument("--calibration-only", action="store_true")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
+    if args.calibration_only:
+        from stepquant.calibration import LayerStatistics, calibrate
+        from stepquant.allocation import allocate_dp, allocate_lagrangian
+        torch.set_num_threads(1)
+        np.savez_compressed(os.path.join(HERE, "calibration.npz"),
+                            **calibration_vectors((LayerStatistics, calibrate, allocate_dp, allocate_lagrangian)))
+        print("calibration vectors written to", HERE)
+        return
     if args.prefill_only:
         from stepquant.adapters import RecurrentKernel
         torch.set_num_threads(1)
