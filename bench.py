@@ -236,15 +236,18 @@ def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    res = cpu_reference(args, args.heads, args.qk_heads, args.steps, args.warmup,
-                        max(20.0, args.cpu_seconds * 3))
+    # The reference arm times config 1 (the default workload's shapes).
+    batch = args.batch or 256
+    qk_heads = args.qk_heads or args.heads // 2
+    res = cpu_reference(args, args.heads, qk_heads, args.steps, args.warmup, max(20.0, args.cpu_seconds * 3))
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup,
             # one full batch-step at the sampled rate
-            "ms_per_step": args.batch * args.heads / res["value"] * 1e3, "higher_is_better": True,
+            "ms_per_step": batch * args.heads / res["value"] * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "gdn-decode-b256-h32-k128 (config 1), CPU port of the reference torch path",
-                       "batch": args.batch, "heads": args.heads, "qk_heads": args.qk_heads, "dim": args.dim},
+            "config": {"workload": "gdn-decode-b%d-h%d-k128 (config 1), CPU port of the reference torch path"
+                                   % (batch, args.heads),
+                       "batch": batch, "heads": args.heads, "qk_heads": qk_heads, "dim": args.dim},
             "cpu_baseline": res, "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0}}
     emit(line)
