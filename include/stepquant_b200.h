@@ -76,7 +76,8 @@ typedef struct sq_plan {
     int32_t keys;
     int32_t values;
     int32_t value_group_size;
-    int32_t storage;      /* 0: packed codes (tiles of 16 / 4 values); 1: byte carriers */
+    int32_t storage;      /* pages: 0 packed codes (tiles of 16 / 4 values), 1 byte carriers;
+                             baseline formats: 2 symmetric groups (sym_int*), 3 dual axis (dsq_int*) */
     int64_t page_bytes;
     const int32_t *bits;
     const float *impact;

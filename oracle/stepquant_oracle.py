@@ -718,3 +718,133 @@ def prefill_sequential(q, k, v, g, beta, cu_seqlens, initial_state=None, scale=N
             out[t] = y[0]
         finals.append(state[0])
     return out, np.stack(finals) if finals else np.zeros((0, heads, keys, values), F32)
+
+
+# ---------------------------------------------------------------------------
+# baseline state formats (stepquant/formats.py, kernels/format_pool.py)
+# ---------------------------------------------------------------------------
+
+def format_spec(name):
+    """formats.py:28-41 get_format -> (kind, bits, group)."""
+    import re
+    if name == "fp32":
+        return "fp32", 32, 32
+    m = re.fullmatch(r"sym_int([468])_g128", name)
+    if m:
+        return "symmetric", int(m[1]), 128
+    m = re.fullmatch(r"dsq_int([46])", name)
+    if m:
+        return "dsq", int(m[1]), 128
+    raise ValueError(f"unknown state format: {name}")
+
+
+def format_layout(heads, keys, values, kind, bits, group):
+    """kernels/format_pool.py:9-27: (offsets, rows, columns, page_bytes) of a
+    baseline-format page: each row's codes as one little-endian bitstream,
+    then per row the symmetric groups' (fp16 scale, fp16 zero) or the DSQ fp16
+    row scale, then per head the DSQ (fp16 column scale, fp16 zero) pairs."""
+    offsets, rows, columns = [], [], []
+    cursor = 0
+    for _ in range(heads * keys):
+        offsets.append(cursor)
+        cursor += values * bits // 8
+    cursor = (cursor + 3) // 4 * 4
+    for _ in range(heads * keys):
+        rows.append(-1 if kind == "fp32" else cursor)
+        cursor += 0 if kind == "fp32" else (2 if kind == "dsq" else values // group * 4)
+    cursor = (cursor + 3) // 4 * 4
+    for _ in range(heads):
+        columns.append(cursor)
+        cursor += values * 4 if kind == "dsq" else 0
+    return offsets, rows, columns, cursor
+
+
+def group_fit(x, bits, group):
+    """formats.py:51-65 (symmetric groupwise absmax): codes, scale, zero, recon."""
+    x = np.asarray(x, F32)
+    y = x.reshape(*x.shape[:-1], -1, group)
+    limit = F32(2 ** (bits - 1) - 1)
+    s = fp16_scale((np.abs(y).max(-1, keepdims=True) / limit).astype(F32))
+    z = np.full_like(s, limit)
+    q = (np.clip(np.rint((y / s).astype(F32)), -limit, limit) + z).astype(F32)
+    return q.reshape(x.shape), s, z, ((q - z) * s).astype(F32).reshape(x.shape)
+
+
+def dual_fit(x, bits, pivots=None):
+    """formats.py:68-82 (Q-Mamba DSQ dual axis): codes, r, c, zero, recon.
+    ``pivots`` (bool [H, K]) marks fp16 rows; the baseline pools have none."""
+    x = np.asarray(x, F32)
+    mask = np.ones(x.shape[1:3], bool)[None, :, :, None] if pivots is None else ~pivots[None, :, :, None]
+    mean = (torch_inner_sum(np.abs(x))[..., None] / F32(x.shape[-1])).astype(F32)
+    r = fp16_scale(np.sqrt(np.maximum(mean, F32(1e-20))))
+    y = (x / r).astype(F32)
+    levels = F32(2 ** (min(bits, 8) - 1) - 1)
+    c = fp16_scale(np.where(mask, (np.abs(y) / levels).astype(F32), F32(0)).max(-2, keepdims=True))
+    q = np.minimum(np.maximum(np.rint((y / c).astype(F32)), -levels), levels).astype(F32)
+    recon = np.where(mask, ((r * c).astype(F32) * q).astype(F32), x.astype(np.float16).astype(F32))
+    return (q + levels).astype(F32), r, c, np.zeros_like(c), recon
+
+
+def _put_codes(page, off, codes, bits):
+    stream = pack(np.asarray(codes, np.int64), bits)
+    page[off:off + stream.size] = stream
+
+
+def format_page_encode(state, name, pages=None):
+    """One page per request of a baseline-format pool (format_pool.py encode,
+    formats.py:8-81 store): codes bit-packed per row, scales as fp16."""
+    kind, bits, group = format_spec(name)
+    state = np.asarray(state, F32)
+    batch, heads, keys, values = state.shape
+    offsets, rows, columns, page_bytes = format_layout(heads, keys, values, kind, bits, group)
+    out = np.zeros((batch, page_bytes), np.uint8) if pages is None else np.array(pages, np.uint8)
+    if kind == "symmetric":
+        codes, s, z, _ = group_fit(state, bits, group)
+    else:
+        codes, r, c, _, _ = dual_fit(state, bits)
+    for i in range(batch):
+        page = out[i]
+        for h in range(heads):
+            for k in range(keys):
+                row = h * keys + k
+                _put_codes(page, offsets[row], codes[i, h, k], bits)
+                if kind == "symmetric":
+                    for g in range(values // group):
+                        _put_half(page, rows[row] + 4 * g, s[i, h, k, g, 0])
+                        _put_half(page, rows[row] + 4 * g + 2, z[i, h, k, g, 0])
+                else:
+                    _put_half(page, rows[row], r[i, h, k, 0])
+            if kind == "dsq":
+                for v in range(values):
+                    _put_half(page, columns[h] + 4 * v, c[i, h, 0, v])
+                    _put_half(page, columns[h] + 4 * v + 2, 0.0)
+    return out
+
+
+def format_page_decode(pages, name, heads, keys, values):
+    """formats.py:15-45 read: symmetric (code - zero) * scale; DSQ (r c)(code - levels)."""
+    kind, bits, group = format_spec(name)
+    pages = np.asarray(pages, np.uint8)
+    offsets, rows, columns, _ = format_layout(heads, keys, values, kind, bits, group)
+    out = np.zeros((pages.shape[0], heads, keys, values), F32)
+    levels = F32(2 ** (bits - 1) - 1)
+    for i in range(pages.shape[0]):
+        page = pages[i]
+        for h in range(heads):
+            col = None
+            if kind == "dsq":
+                col = np.array([_get_half(page, columns[h] + 4 * v) for v in range(values)], np.float16).astype(F32)
+            for k in range(keys):
+                row = h * keys + k
+                nbytes = values * bits // 8
+                codes = unpack(page[offsets[row]:offsets[row] + nbytes], bits, values).astype(F32)
+                if kind == "symmetric":
+                    s = np.repeat(np.array([_get_half(page, rows[row] + 4 * g) for g in range(values // group)],
+                                           np.float16).astype(F32), group)
+                    z = np.repeat(np.array([_get_half(page, rows[row] + 4 * g + 2) for g in range(values // group)],
+                                           np.float16).astype(F32), group)
+                    out[i, h, k] = ((codes - z).astype(F32) * s).astype(F32)
+                else:
+                    rr = np.float16(_get_half(page, rows[row])).astype(F32)
+                    out[i, h, k] = ((rr * col).astype(F32) * (codes - levels).astype(F32)).astype(F32)
+    return out

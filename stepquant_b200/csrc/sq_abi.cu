@@ -25,7 +25,7 @@ int32_t check_plan(const sq_plan *p) {
     if (!p || !p->bits || !p->impact || !p->offsets || !p->rows || !p->columns) return SQ_ERR_ARGUMENT;
     if (p->architecture != SQ_GDN && p->architecture != SQ_KDA) return SQ_ERR_ARGUMENT;
     if (p->heads < 1 || p->page_bytes < 2 || p->value_group_size < 1) return SQ_ERR_ARGUMENT;
-    if (p->storage != 0 && p->storage != 1) return SQ_ERR_ARGUMENT;
+    if (p->storage < 0 || p->storage > 3) return SQ_ERR_ARGUMENT;  // packed, byte, symmetric, DSQ
     if (!pow2_dim(p->keys) || !pow2_dim(p->values)) return SQ_ERR_SHAPE;
     if (p->architecture == SQ_GDN) {
         if (p->values % p->value_group_size) return SQ_ERR_SHAPE;

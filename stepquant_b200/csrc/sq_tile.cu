@@ -63,6 +63,74 @@ size_t tile_smem_bytes(int K, int V, int groups) {
     return size_t(K) * V * 5 + size_t(K) * 9 * 4 + size_t(V) * 5 * 4 + 32 * 4 + size_t(K) * groups * 4;
 }
 
+// Fit one (request, head) tile to a baseline format and store its page bytes
+// (formats.py:51-82 group_fit / dual_fit, format_pool.py:9-27 layout): the
+// symmetric format's per-group scale fp16(absmax / limit) with zero point
+// `limit`; DSQ's row scale r = fp16(sqrt(max(mean |x|, 1e-20))) (torch's row
+// sum order), column scale c = fp16(max_k |x / r| / levels) and codes
+// rint(x / r / c); every division correctly rounded.  Codes go to each row's
+// bitstream as level + limit.
+__device__ void format_store(int fmt, int G, uint8_t *page, Smem &s, int K, int V, int coff, int tid) {
+    const int groups = V / G;
+    for (int k = tid; k < K; k += kThreads) {
+        const float *row = s.xs + k * V;
+        const float limit = float((1 << (s.rbits[k] - 1)) - 1);
+        if (fmt == 2) {
+            for (int g = 0; g < groups; ++g) {
+                float m = 0.f;
+                for (int i = 0; i < G; ++i) m = fmaxf(m, fabsf(row[g * G + i]));
+                const float sc = fp16_scale(__fdiv_rn(m, limit));
+                s.r2s[k * groups + g] = sc;
+                put_half(page, s.rrow[k] + 4 * g, sc);
+                put_half(page, s.rrow[k] + 4 * g + 2, limit);
+            }
+        } else {
+            const float sum = torch_inner_sum(V, [&](int i) { return fabsf(row[i]); });
+            const float r = fp16_scale(__fsqrt_rn(fmaxf(__fdiv_rn(sum, float(V)), 1e-20f)));
+            s.rr[k] = r;
+            put_half(page, s.rrow[k], r);
+        }
+    }
+    __syncthreads();
+    if (fmt == 3) {
+        for (int v = tid; v < V; v += kThreads) {
+            float m = 0.f;
+            for (int k = 0; k < K; ++k) {
+                const float limit = float((1 << (s.rbits[k] - 1)) - 1);
+                m = fmaxf(m, __fdiv_rn(fabsf(__fdiv_rn(s.xs[k * V + v], s.rr[k])), limit));
+            }
+            const float c = fp16_scale(m);
+            s.c1[v] = c;
+            put_half(page, coff + 4 * v, c);
+            put_half(page, coff + 4 * v + 2, 0.f);
+        }
+        __syncthreads();
+    }
+    for (int e = tid; e < K * V; e += kThreads) {
+        const int k = e / V, v = e % V;
+        const float limit = float((1 << (s.rbits[k] - 1)) - 1);
+        const float y = fmt == 2 ? __fdiv_rn(s.xs[e], s.r2s[k * groups + v / G])
+                                 : __fdiv_rn(__fdiv_rn(s.xs[e], s.rr[k]), s.c1[v]);
+        s.zq[e] = int8_t(fminf(fmaxf(rintf(y), -limit), limit));
+    }
+    __syncthreads();
+    for (int k = tid; k < K; k += kThreads) {  // one thread per row bitstream
+        const int b = s.rbits[k], off = (1 << (b - 1)) - 1;
+        uint8_t *dst = page + s.roff[k];
+        uint32_t acc = 0;
+        int nbits = 0, w = 0;
+        for (int v = 0; v < V; ++v) {
+            acc |= uint32_t(int(s.zq[k * V + v]) + off) << nbits;
+            nbits += b;
+            while (nbits >= 8) {
+                dst[w++] = uint8_t(acc & 0xffu);
+                acc >>= 8;
+                nbits -= 8;
+            }
+        }
+    }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -111,7 +179,8 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
     const int stride = P.offsets[H * K + head];
     const int coff = P.columns[head];
     const int tile = min(kda ? 4 : 16, V);
-    const bool bytes = P.storage != 0;  // byte carriers (pool.py:34-49): codes at code_base + k + v K
+    const bool bytes = P.storage == 1;  // byte carriers (pool.py:34-49): codes at code_base + k + v K
+    const int fmt = P.storage >= 2 ? P.storage : 0;  // baseline formats: 2 symmetric groups, 3 dual axis (DSQ)
     const bool gdn2 = !kda && P.bits[head * K] == 2;
     if (MODE == kWriteback && coff < 0) return;  // all-pivot head: finished by sq_readout
     __syncthreads();
@@ -119,6 +188,25 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
     // ---- load the state ----------------------------------------------------
     if (MODE == kEncode || MODE == kFit) {
         for (int e = tid; e < K * V; e += kThreads) s.xs[e] = p.dense_in[tile_index + e];
+    } else if (fmt) {
+        // Baseline formats (formats.py:15-45 read): each row one little-endian
+        // bitstream; symmetric (code - zero) * scale per value group, DSQ
+        // (r c)(code - levels).  No pivot rows.
+        const int G = P.value_group_size;
+        for (int e = tid; e < K * V; e += kThreads) {
+            const int k = e / V, v = e % V;
+            const int b = s.rbits[k];
+            const float code = float(read_code(page + s.roff[k], uint32_t(v * b), b));
+            float x;
+            if (fmt == 2) {
+                const int64_t meta = s.rrow[k] + 4 * int64_t(v / G);
+                x = __fmul_rn(__fsub_rn(code, half_at(page, meta + 2)), half_at(page, meta));
+            } else {
+                const float rc = __fmul_rn(half_at(page, s.rrow[k]), half_at(page, coff + 4 * v));
+                x = __fmul_rn(rc, __fsub_rn(code, float((1 << (b - 1)) - 1)));
+            }
+            s.xs[e] = x;
+        }
     } else {
         for (int v = tid; v < V; v += kThreads) s.cold[v] = coff >= 0 ? half_at(page, coff + 2 * v) : 0.f;
         for (int k = tid; k < K; k += kThreads) {
@@ -260,6 +348,10 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
         return;
     }
     __syncthreads();
+    if (fmt) {
+        format_store(fmt, P.value_group_size, page, s, K, V, coff, tid);
+        return;
+    }
 
     // ---- fit_state (quantization.py:93-137) ----------------------------------
     // Row scales r = fp16(sqrt(max(mean|x|, 1e-20) / w)).

@@ -1,15 +1,17 @@
-"""FP32 state pool: the reference's FP32 baseline format (stepquant/kernels/format_pool.py,
-floating.py:20-53) on the device kernel ``sq_fp32_step``.
+"""Baseline state formats (stepquant/kernels/format_pool.py, floating.py:20-53).
 
-Same slot interface as PackedStatePool (step / encode / decode / wait / clear /
-copy); the state is stored uncompressed as fp32 [slots, H, K, V].  The other
-baseline formats (sym_int*, dsq_*) are not built.
+``Fp32StatePool``: the FP32 baseline on the device kernel ``sq_fp32_step``,
+the state stored uncompressed as fp32 [slots, H, K, V].  ``FormatStatePool``:
+the symmetric groupwise (sym_int4/6/8_g128) and dual-axis (dsq_int4/6)
+formats on the generic tile kernel (``sq_plan.storage`` 2 and 3).  Both keep
+PackedStatePool's slot interface (step / encode / decode / wait / clear / copy).
 """
 import ctypes
 
 import torch
 
 from .. import _native as N
+from .pool import PackedStatePool
 
 
 class Fp32StatePool:
@@ -78,8 +80,79 @@ class Fp32StatePool:
 
 
 def format_layout(plan, values, spec):
-    """Bytes per slot of a baseline-format page (fp32 only in this build)."""
-    if spec.kind != "fp32":
-        raise NotImplementedError(f"state format {spec.name} is not built")
-    heads, keys = plan.bits.shape
-    return None, None, None, heads * keys * values * 4
+    """Page layout of a baseline-format pool (kernels/format_pool.py:9-27):
+    (offsets, rows, columns, page_bytes).  Each key row's codes are one
+    little-endian bitstream of ``values * bits / 8`` bytes; then per row the
+    symmetric groups' (fp16 scale, fp16 zero point) pairs or the DSQ fp16 row
+    scale; then per head the DSQ (fp16 column scale, fp16 zero) pairs."""
+    offsets, rows, columns = [], [], []
+    cursor = 0
+    bits = plan.bits.detach().cpu().flatten().tolist()
+    for b in bits:
+        if b == 16:
+            cursor = (cursor + 1) // 2 * 2
+        offsets.append(cursor)
+        cursor += values * b // 8
+    cursor = (cursor + 3) // 4 * 4
+    floating, dual = spec.kind == "fp32", spec.kind == "dsq"
+    for b in bits:
+        rows.append(cursor if b != 16 and not floating else -1)
+        cursor += 0 if floating or b == 16 else (2 if dual else values // spec.group_size * 4)
+    cursor = (cursor + 3) // 4 * 4
+    for _ in range(plan.bits.shape[0]):
+        columns.append(cursor)
+        cursor += values * 4 if dual else 0
+    return offsets, rows, columns, cursor
+
+
+class FormatStatePool(PackedStatePool):
+    """Baseline-format pages (sym_int*_g128, dsq_int*; kernels/format_pool.py:30-128)
+    with the PackedStatePool slot interface, on the generic tile kernel.
+
+    Synchronous only, like the reference's fused format kernels.  The fp32
+    format returns an ``Fp32StatePool``.  Codes and scales are exactly the
+    reference's ``formats.group_fit`` / ``dual_fit`` of the state.
+    """
+
+    def __new__(cls, plan, slots, value_dim, spec, writeback_stream=None, layout=None):
+        if spec.kind == "fp32":
+            return Fp32StatePool(plan, slots, value_dim, spec, writeback_stream)
+        return super().__new__(cls)
+
+    def __init__(self, plan, slots, value_dim, spec, writeback_stream=None, layout=None):
+        from ..quantization import DevicePlan
+        if writeback_stream is not None:
+            raise ValueError("these fused formats require synchronous writeback")
+        if spec.kind not in ("symmetric", "dsq"):
+            raise ValueError(f"not a baseline state format: {spec.name}")
+        if not (plan.bits == spec.bits).all():
+            raise ValueError(f"precision map incompatible with {spec.name}")
+        if plan.bits.device.type != "cuda":
+            raise ValueError("fused format pool requires CUDA")
+        self.plan, self.spec = plan, spec
+        self.heads, self.keys = plan.bits.shape
+        self.values, self.device = value_dim, plan.bits.device
+        if self.keys & (self.keys - 1) or value_dim & (value_dim - 1) or value_dim % 4:
+            raise ValueError("key/value dimensions must be powers of two, value >= 4")
+        if spec.kind == "dsq" and self.keys > 128:
+            raise ValueError("dual-axis g128 requires key_dim <=128")
+        if spec.kind == "symmetric" and value_dim % spec.group_size:
+            raise ValueError("group size must divide value dimension")
+        if not 4 <= self.keys <= 128 or value_dim > 128:
+            raise NotImplementedError("this build supports key and value dimensions from 4 to 128")
+        offsets, rows, columns, page_bytes = format_layout(plan, value_dim, spec) if layout is None else layout
+        # The device plan's offset table ends with one (unused) stride per head.
+        self._dp = DevicePlan(plan, value_dim, spec.kind, (list(offsets) + [0] * self.heads, rows, columns, page_bytes),
+                              group=spec.group_size if spec.kind == "symmetric" else value_dim)
+        self.page_bytes = page_bytes
+        self.offsets, self.rows, self.columns = self._dp.offsets, self._dp.rows, self._dp.columns
+        self.bits, self.impact = self._dp.bits, self._dp.impact
+        self.storage = spec.kind
+        self.early_writeback = False
+        self._storage = torch.zeros(slots * page_bytes + 64, device=self.device, dtype=torch.uint8)
+        self.data = self._storage[:slots * page_bytes].view(slots, page_bytes)
+        self.status = torch.zeros(1, device=self.device, dtype=torch.int32)
+        self.coefficients = None
+        self.row_tile = 0
+        self._init_writeback(None, 0)
+        self._init_workspace(slots, None)

@@ -56,14 +56,18 @@ class PackedState:
 class DevicePlan:
     """Device tables of a plan plus its page layout, packed into an ``sq_plan``."""
 
-    def __init__(self, plan, values, storage="packed"):
+    # sq_plan.storage codes: STEPQuant packed pages, byte carriers, and the
+    # baseline formats (kernels/format_pool.py) symmetric groups and DSQ.
+    STORAGE = {"packed": 0, "byte": 1, "symmetric": 2, "dsq": 3}
+
+    def __init__(self, plan, values, storage="packed", layout=None, group=None):
         from .kernels.pool import packed_layout
         N.require_cuda(plan.bits)
         self.plan = plan
         self.device = plan.bits.device
         self.heads, self.keys = plan.bits.shape
         self.values = values
-        offsets, rows, columns, page_bytes = packed_layout(plan, values, storage)
+        offsets, rows, columns, page_bytes = layout if layout is not None else packed_layout(plan, values, storage)
         self.page_bytes = page_bytes
         dev = self.device
         self.bits = plan.bits.to(device=dev, dtype=torch.int32).contiguous()
@@ -74,7 +78,8 @@ class DevicePlan:
         self.bits_host = plan.bits.detach().to("cpu", torch.int32).contiguous()
         self.struct = N.SqPlan(
             N.SQ_KDA if plan.architecture == "kda" else N.SQ_GDN, self.heads, self.keys, values,
-            plan.value_group_size, 1 if storage == "byte" else 0, page_bytes, self.bits.data_ptr(), self.impact.data_ptr(),
+            plan.value_group_size if group is None else group, self.STORAGE[storage], page_bytes,
+            self.bits.data_ptr(), self.impact.data_ptr(),
             self.offsets.data_ptr(), self.rows.data_ptr(), self.columns.data_ptr(), self.bits_host.data_ptr())
 
     def ref(self):

@@ -23,7 +23,7 @@ import weakref
 import torch
 
 from ..formats import FormatPlan, get_format
-from ..kernels.format_pool import Fp32StatePool, format_layout
+from ..kernels.format_pool import FormatStatePool, format_layout
 from ..kernels.pool import PackedStatePool
 from ..quantization import QuantizationPlan
 
@@ -122,7 +122,7 @@ def make_pool(plan, size, values, spec, stream, workspace, chunk, storage):
     if spec.kind == "stepquant":
         return PackedStatePool(plan, size + 1, values, writeback_stream=stream, writeback_workspace=workspace,
                                writeback_chunk=chunk, storage=storage)
-    return Fp32StatePool(plan, size + 1, values, spec, writeback_stream=stream)
+    return FormatStatePool(plan, size + 1, values, spec, writeback_stream=stream)
 
 
 def pool_init(original, self, **kwargs):

@@ -28,8 +28,13 @@ Files written next to this script:
                         them, and ``stepquant.allocation`` on seeded cost
                         tables.
 
+* ``formats.npz``  -- ``stepquant.formats`` baseline formats (sym_int*_g128
+                        ``group_fit``, dsq_int* ``dual_fit``) on seeded states,
+                        and ``kernels.format_pool.format_layout`` tables.
+
 ``--prefill-only`` rewrites ``prefill.npz`` alone; ``--calibration-only``
-rewrites ``calibration.npz`` alone.
+rewrites ``calibration.npz`` alone; ``--formats-only`` rewrites
+``formats.npz`` alone.
 """
 import argparse
 import json
@@ -166,13 +171,58 @@ def calibration_vectors(reference_modules):
     return out
 
 
+FORMAT_CASES = ("sym_int4_g128", "sym_int6_g128", "sym_int8_g128", "dsq_int4", "dsq_int6")
+
+
+def format_vectors(get_format, group_fit, dual_fit, format_layout):
+    """Baseline-format fits of one seeded state [2, 2, 16, 128] and their page layouts."""
+    gen = torch.Generator().manual_seed(44)
+    heads, keys, values = 2, 16, 128
+    x = torch.randn(2, heads, keys, values, generator=gen) * 0.1
+    x[1, 0, 3] = 0  # an all-zero row
+    x[1, 1, :, 7] *= 40  # a large column
+    out = {"x": x.numpy()}
+    for name in FORMAT_CASES:
+        spec = get_format(name)
+        bits = torch.full((heads, keys), spec.bits, dtype=torch.long)
+        impact = torch.rand(heads, keys, generator=gen) + 0.5
+        if spec.kind == "symmetric":
+            q, scale, zero, recon = group_fit(x, spec)
+            out[f"{name}_q"] = q.numpy().astype(np.uint8)
+            out[f"{name}_s"] = scale.numpy()
+            out[f"{name}_z"] = zero.numpy()
+        else:
+            q, r, c, zero, recon = dual_fit(x, bits, impact)
+            out[f"{name}_q"] = q.numpy().astype(np.uint8)
+            out[f"{name}_r"] = r.numpy()
+            out[f"{name}_c"] = c.numpy()
+        out[f"{name}_recon"] = recon.numpy()
+
+        class _Plan:  # format_layout reads plan.bits only
+            pass
+        plan = _Plan()
+        plan.bits = bits
+        offsets, rows, columns, total = format_layout(plan, values, spec)
+        out[f"{name}_layout"] = np.array(offsets + rows + columns + [total], dtype=np.int64)
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path of the STEPQuant checkout")
     parser.add_argument("--prefill-only", action="store_true")
     parser.add_argument("--calibration-only", action="store_true")
+    parser.add_argument("--formats-only", action="store_true")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
+    if args.formats_only:
+        from stepquant.formats import get_format, group_fit, dual_fit
+        from stepquant.kernels.format_pool import format_layout
+        torch.set_num_threads(1)
+        np.savez_compressed(os.path.join(HERE, "formats.npz"),
+                            **format_vectors(get_format, group_fit, dual_fit, format_layout))
+        print("format vectors written to", HERE)
+        return
     if args.calibration_only:
         from stepquant.calibration import LayerStatistics, calibrate
         from stepquant.allocation import allocate_dp, allocate_lagrangian

@@ -184,3 +184,29 @@ def test_byte_carrier_pages_hold_the_packed_levels():
         levels = byte_pages[0, code_base + k + np.arange(32) * 32].view(np.int8)
         expect = z[0, 0, k].astype(np.int64) * (16 if arch == "kda" else 1)
         np.testing.assert_array_equal(levels, expect)
+
+
+@pytest.mark.parametrize("name", ["sym_int4_g128", "sym_int6_g128", "sym_int8_g128", "dsq_int4", "dsq_int6"])
+def test_baseline_formats_match_reference(name):
+    """formats.py group_fit / dual_fit and format_pool.format_layout of the
+    reference (tests/golden/formats.npz) against the oracle's restatement;
+    the oracle's page image decodes back to the reference reconstruction."""
+    d = load_golden("formats.npz")
+    x = d["x"]
+    kind, bits, group = O.format_spec(name)
+    if kind == "symmetric":
+        codes, s, z, recon = O.group_fit(x, bits, group)
+        np.testing.assert_array_equal(s, d[f"{name}_s"])
+        np.testing.assert_array_equal(z, d[f"{name}_z"])
+    else:
+        codes, r, c, _, recon = O.dual_fit(x, bits)
+        np.testing.assert_array_equal(r, d[f"{name}_r"])
+        np.testing.assert_array_equal(c, d[f"{name}_c"])
+    np.testing.assert_array_equal(codes, d[f"{name}_q"].astype(np.float32))
+    np.testing.assert_array_equal(recon, d[f"{name}_recon"])
+    heads, keys, values = x.shape[1:]
+    offsets, rows, columns, total = O.format_layout(heads, keys, values, kind, bits, group)
+    np.testing.assert_array_equal(np.array(offsets + rows + columns + [total]), d[f"{name}_layout"])
+    pages = O.format_page_encode(x, name)
+    assert pages.shape == (x.shape[0], total)
+    np.testing.assert_array_equal(O.format_page_decode(pages, name, heads, keys, values), d[f"{name}_recon"])
