@@ -7,10 +7,12 @@ applied, o = S^T q read out, the state requantized (fit_state), repacked and
 written back.  Asynchronous writeback is on (config 1): the readout kernel runs
 on the compute stream and the requantization on a writeback stream, and a
 step is complete when both are.  ``--mode sync`` times the fused single-kernel
-step instead.  The timed loop replays one CUDA graph per step (async steps as
-a foreground graph and a background writeback graph, WritebackGraph), as the
+step instead.  The timed loop replays one CUDA graph per step (async steps
+with their writeback joined; the end-to-end leg pairs a foreground graph with
+a background writeback graph), as the
 reference benchmark times ``step(); wait()`` under CUDA graphs; per-kernel
-device times come from a separate pass of eager launches.
+device times come from graph-captured batches of one kernel's launches timed
+with CUDA events on that kernel's stream.
 
 Workload: Qwen-Next-style layer, 16 qk heads / 32 value heads, K = V = 128,
 batch 256, stepquant6 synthetic plan (seed 1: per-head widths {4, 6, 8} at
@@ -386,13 +388,14 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
 
     # The timed loop replays one CUDA graph per (inputs, slot group) pair -- the
     # reference benchmark's methodology (bench_formats.py times step(); wait()
-    # under CUDA graphs).  Async steps are captured as a foreground graph plus a
-    # background writeback graph on the writeback stream (defer_writeback +
-    # WritebackGraph, paired), so the next step's host-to-device input copy
-    # overlaps the previous step's writeback, as with eager launches.
+    # under CUDA graphs).  Async steps are captured with their writeback
+    # (defer_writeback + WritebackGraph): joined into one graph for the device
+    # throughput; for the end-to-end leg as a foreground graph plus a
+    # background writeback graph on the writeback stream (paired), so the next
+    # step's host-to-device input copy overlaps the previous step's writeback.
     period = math.lcm(len(inputs), len(groups))
 
-    def capture(step_fn):
+    def capture(step_fn, joined):
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         if mode != "async":
@@ -400,13 +403,14 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
                 result = step_fn()
             return graph, result
         with torch.cuda.graph(graph):
-            with defer_writeback([pool]) as tasks:
+            with defer_writeback([pool], joined=joined) as tasks:
                 result = step_fn()
-        return WritebackGraph(graph, tasks), result
+        return WritebackGraph(graph, tasks, joined=joined), result
 
     graphs = [capture(lambda j=j: pool.step(inputs[j % len(inputs)].q, inputs[j % len(inputs)].k,
                                            inputs[j % len(inputs)].v, inputs[j % len(inputs)].a,
-                                           inputs[j % len(inputs)].b, groups[j % len(groups)], **kw))[0]
+                                           inputs[j % len(inputs)].b, groups[j % len(groups)], **kw),
+                      joined=True)[0]
               for j in range(period)]
     for i in range(warmup):
         graphs[i % period].replay()
@@ -453,7 +457,8 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
                    for buf in dev_bufs]
         host_outs = [torch.empty(batch, heads_l, dim, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
         keys = [(g, b) for g in range(len(groups)) for b in range(nbuf)]
-        e2e_graphs = {key: capture(lambda key=key: pool.step(*dev_ins[key[1]], groups[key[0]], **kw)) for key in keys}
+        e2e_graphs = {key: capture(lambda key=key: pool.step(*dev_ins[key[1]], groups[key[0]], **kw), joined=False)
+                      for key in keys}
         h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
         copied = [torch.cuda.Event() for _ in range(nbuf)]
         consumed = [torch.cuda.Event() for _ in range(nbuf)]
