@@ -65,6 +65,10 @@ def test_device_entry_points_reject_bad_arguments_before_launch():
     args = N.SqStepArgs(16, 16, 16, 0, 0, 0, 3, 0, 16, 16, 0, 0, None, None, 1.0, 0, 16)
     assert N.lib().sq_step(ctypes.byref(plan), fake, 4, fake, 1, ctypes.byref(args), None, None, None) == N.SQ_ERR_SHAPE
     assert N.lib().sq_pack(fake, 4, 5, fake, None) == N.SQ_ERR_ARGUMENT
+    # Page storage codes: 0 packed, 1 byte carriers, 2 / 3 baseline formats; others are rejected.
+    for storage, code in ((4, N.SQ_ERR_ARGUMENT), (-1, N.SQ_ERR_ARGUMENT), (3, N.SQ_ERR_SHAPE)):
+        plan = N.SqPlan(0, 2, 96, 128, 32, storage, 1000, fake, fake, fake, fake, fake)
+        assert N.lib().sq_decode(ctypes.byref(plan), fake, 4, fake, 1, fake, None, None) == code
     assert N.lib().sq_packed_bytes(7, 6) == 6 and N.lib().sq_packed_bytes(0, 2) == 0
     # Zero-size work is a no-op that touches no pointer.
     assert N.lib().sq_pack(None, 0, 4, None, None) == N.SQ_OK
