@@ -188,6 +188,36 @@ struct PrepSmem {
     float fw[PC];  // beta e^gam nk: column factors of Tw
 };
 
+// acc (a 16x16 block as two 16x8 tf32 accumulator tiles) += A[ar0.., ac0..] B[br0.., bc0..]
+// over a 16-deep k range (two m16n8k8 steps); fp32 operands rounded to tf32.
+__device__ __forceinline__ void mma_block16(float (&acc)[2][4], const float (*A)[kLdF], int ar0, int ac0,
+                                            const float (*B)[kLdF], int br0, int bc0, int g8, int tig) {
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+        uint32_t af[4];
+        af[0] = tf32_bits(A[ar0 + g8][ac0 + 8 * kk + tig]);
+        af[1] = tf32_bits(A[ar0 + g8 + 8][ac0 + 8 * kk + tig]);
+        af[2] = tf32_bits(A[ar0 + g8][ac0 + 8 * kk + tig + 4]);
+        af[3] = tf32_bits(A[ar0 + g8 + 8][ac0 + 8 * kk + tig + 4]);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            const uint32_t b0 = tf32_bits(B[br0 + 8 * kk + tig][bc0 + 8 * nt + g8]);
+            const uint32_t b1 = tf32_bits(B[br0 + 8 * kk + tig + 4][bc0 + 8 * nt + g8]);
+            mma1688_tf32(acc[nt], af, b0, b1);
+        }
+    }
+}
+__device__ __forceinline__ void store_block16(const float (&acc)[2][4], float (*dst)[kLdF], int g8, int tig) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+        const int col = 8 * nt + 2 * tig;
+        dst[g8][col] = acc[nt][0];
+        dst[g8][col + 1] = acc[nt][1];
+        dst[g8 + 8][col] = acc[nt][2];
+        dst[g8 + 8][col + 1] = acc[nt][3];
+    }
+}
+
 __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const int32_t *offsets,
                                                       unsigned char *records) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -350,65 +380,59 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
         }
     }
     __syncthreads();
-    for (int r = 1; r < 4; ++r) {
-        if (warp < r) {
-            const int c = warp;
-            float X[2][4] = {};
-            for (int mb = c; mb < r; ++mb) {
-#pragma unroll
-                for (int kk = 0; kk < 2; ++kk) {
-                    const int col = 16 * mb + 8 * kk;
-                    uint32_t af[4];
-                    af[0] = tf32_bits(s.lv.l[16 * r + g8][col + tig]);
-                    af[1] = tf32_bits(s.lv.l[16 * r + g8 + 8][col + tig]);
-                    af[2] = tf32_bits(s.lv.l[16 * r + g8][col + tig + 4]);
-                    af[3] = tf32_bits(s.lv.l[16 * r + g8 + 8][col + tig + 4]);
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
-                        const uint32_t b0 = tf32_bits(s.t[col + tig][16 * c + 8 * nt + g8]);
-                        const uint32_t b1 = tf32_bits(s.t[col + tig + 4][16 * c + 8 * nt + g8]);
-                        mma1688_tf32(X[nt], af, b0, b1);
-                    }
-                }
-            }
-            // X_rc (local row i, column m) is kept at l[16 c + i][16 r + m], above the diagonal.
-            float (*xb)[kLdF] = reinterpret_cast<float (*)[kLdF]>(&s.lv.l[16 * c][16 * r]);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                const int col = 8 * nt + 2 * tig;
-                xb[g8][col] = X[nt][0];
-                xb[g8][col + 1] = X[nt][1];
-                xb[g8 + 8][col] = X[nt][2];
-                xb[g8 + 8][col + 1] = X[nt][3];
-            }
-            __syncwarp();
-            float Y[2][4] = {};
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk) {
-                const int col = 16 * r + 8 * kk;
-                uint32_t af[4];
-                af[0] = tf32_bits(s.t[16 * r + g8][col + tig]);
-                af[1] = tf32_bits(s.t[16 * r + g8 + 8][col + tig]);
-                af[2] = tf32_bits(s.t[16 * r + g8][col + tig + 4]);
-                af[3] = tf32_bits(s.t[16 * r + g8 + 8][col + tig + 4]);
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    const uint32_t b0 = tf32_bits(xb[8 * kk + tig][8 * nt + g8]);
-                    const uint32_t b1 = tf32_bits(xb[8 * kk + tig + 4][8 * nt + g8]);
-                    mma1688_tf32(Y[nt], af, b0, b1);
-                }
-            }
+    // Blocks below the diagonal as a blocked inverse in two stages:
+    //   A: T10 = -T11 (L10 T00) (warp 0) and T32 = -T33 (L32 T22) (warp 1);
+    //   B: T[2:4, 0:2] = -T[2:4, 2:4] (L[2:4, 0:2] T[0:2, 0:2]), one block per warp.
+    // The block products X are kept in free blocks above L's diagonal.
+    {
+        float (*L)[kLdF] = s.lv.l;
+        float (*T)[kLdF] = s.t;
+        auto above = [&](int r, int c) { return reinterpret_cast<float (*)[kLdF]>(&L[16 * r][16 * c]); };
+        auto finish = [&](int r, int c, const float (&Y)[2][4]) {  // T_rc = -Y, with its Tw and Tu blocks
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int i = 16 * r + g8 + 8 * (e >> 1), j = 16 * c + 8 * nt + 2 * tig + (e & 1);
                     const float tv = -Y[nt][e];
-                    s.t[i][j] = tv;
+                    T[i][j] = tv;
                     Tw[i][j] = __float2bfloat16_rn(tv * s.fw[j]);
                     Tu[i][j] = __float2bfloat16_rn(tv * s.beta[j]);
                 }
             }
+        };
+        if (warp < 2) {
+            const int r = warp ? 3 : 1, c = r - 1;
+            float (*xb)[kLdF] = above(c, r);
+            float X[2][4] = {}, Y[2][4] = {};
+            mma_block16(X, L, 16 * r, 16 * c, T, 16 * c, 16 * c, g8, tig);
+            store_block16(X, xb, g8, tig);
+            __syncwarp();
+            mma_block16(Y, T, 16 * r, 16 * r, xb, 0, 0, g8, tig);
+            finish(r, c, Y);
+        }
+        __syncthreads();
+        if (warp < 4) {
+            const int i = 2 + (warp >> 1), j = warp & 1;
+            // X_mj = sum over m' = j..1 of L_{m m'} T_{m' j}, for m = 2 (and m = 3 in row 3)
+            float (*x2)[kLdF] = warp == 0 ? above(0, 1) : warp == 1 ? above(0, 2) : warp == 2 ? above(0, 3) : above(1, 3);
+            float (*x3)[kLdF] = warp == 2 ? above(1, 2) : above(2, 3);
+            float X[2][4] = {}, Y[2][4] = {};
+            for (int m = j; m < 2; ++m) mma_block16(X, L, 32, 16 * m, T, 16 * m, 16 * j, g8, tig);
+            store_block16(X, x2, g8, tig);
+            if (i == 3) {
+                float X3[2][4] = {};
+                for (int m = j; m < 2; ++m) mma_block16(X3, L, 48, 16 * m, T, 16 * m, 16 * j, g8, tig);
+                store_block16(X3, x3, g8, tig);
+            }
+            __syncwarp();
+            if (i == 2) {
+                mma_block16(Y, T, 32, 32, x2, 0, 0, g8, tig);  // T22 X_2j
+            } else {
+                mma_block16(Y, T, 48, 32, x2, 0, 0, g8, tig);  // T32 X_2j
+                mma_block16(Y, T, 48, 48, x3, 0, 0, g8, tig);  // + T33 X_3j
+            }
+            finish(i, j, Y);
         }
         __syncthreads();
     }
