@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
 // leaves after freeing its tensor memory).
 // ---------------------------------------------------------------------------
 constexpr int kTmemCols = 512;
-constexpr int kColS = 0, kColD = 128, kColO1 = 192, kColO2 = 256;
+constexpr int kColS = 0, kColD = 128, kColO1 = 192, kColO2 = 256, kColD1 = 320, kColO11 = 384;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 struct TcStage {                 // offsets are multiples of 1024 (swizzle atoms)
@@ -688,38 +688,42 @@ __global__ void __launch_bounds__(512, 1) state_kernel(sq_prefill_args a, const 
         put_row<32>(s.sb, PK, v, k0, x);
         asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
     }
-    if (chunks > 0) tc_stage(a, s.st[0], &bar_data[0], rec0, range.x, min(PC, range.y - range.x), qh, tid);
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-
+    // Chunk c uses D and O1 columns of parity c & 1, so the next chunk's first
+    // MMAs (into the other pair) run while chunk c's outputs are read out.
+    auto col_d = [](int parity) { return parity ? kColD1 : kColD; };
+    auto col_o1 = [](int parity) { return parity ? kColO11 : kColO1; };
     const uint32_t id64 = idesc_bf16(64, 0), id128mn = idesc_bf16(128, 1);
-    for (int c = 0; c < chunks; ++c) {
-        TcStage &st = s.st[c & 1];
-        const int t0 = range.x + c * PC, n = min(PC, range.y - t0);
-        // This chunk's copies (issued one chunk ahead) have landed; every thread
-        // is past the previous chunk, whose stage buffer is refilled next.
+    auto issue_first = [&](const TcStage &st, int parity) {  // D^T = S^T (-W)^T, O1^T = S^T Q^T
+        const uint32_t sb = smem_addr(s.sb), w = smem_addr(st.w), q = smem_addr(st.q);
+#pragma unroll
+        for (int ks = 0; ks < PK / 16; ++ks) {
+            const uint32_t ao = (ks >> 2) * 16384 + (ks & 3) * 32, bo = (ks >> 2) * 8192 + (ks & 3) * 32;
+            umma(tmem + col_d(parity), sdesc(sb + ao, 16, 1024), sdesc(w + bo, 16, 1024), id64, ks > 0);
+            umma(tmem + col_o1(parity), sdesc(sb + ao, 16, 1024), sdesc(q + bo, 16, 1024), id64, ks > 0);
+        }
+        umma_commit(&bar_mma[0]);
+    };
+    if (chunks > 0) {
+        tc_stage(a, s.st[0], &bar_data[0], rec0, range.x, min(PC, range.y - range.x), qh, tid);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
         asm volatile("cp.async.wait_group 0;\n" ::: "memory");
         proxy_fence();
-        if (!bar_wait(&bar_data[c & 1], (c >> 1) & 1)) abort_flag = 1;
+        if (!bar_wait(&bar_data[0], 0)) abort_flag = 1;
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
-        if (abort_flag) break;
-        if (c + 1 < chunks)
-            tc_stage(a, s.st[(c + 1) & 1], &bar_data[(c + 1) & 1], rec0 + int64_t(c + 1) * H * kRec, t0 + PC,
-                     min(PC, range.y - t0 - PC), qh, tid);
+        if (!abort_flag && tid == 0) issue_first(s.st[0], 0);
+        if (chunks > 1)
+            tc_stage(a, s.st[1], &bar_data[1], rec0 + int64_t(H) * kRec, range.x + PC, min(PC, range.y - range.x - PC),
+                     qh, tid);
         asm volatile("cp.async.commit_group;\n" ::: "memory");
+    }
 
-        // ---- D^T = S^T (-W)^T, O1^T = S^T Q^T
-        if (tid == 0) {
-            const uint32_t sb = smem_addr(s.sb), w = smem_addr(st.w), q = smem_addr(st.q);
-#pragma unroll
-            for (int ks = 0; ks < PK / 16; ++ks) {
-                const uint32_t ao = (ks >> 2) * 16384 + (ks & 3) * 32, bo = (ks >> 2) * 8192 + (ks & 3) * 32;
-                umma(tmem + kColD, sdesc(sb + ao, 16, 1024), sdesc(w + bo, 16, 1024), id64, ks > 0);
-                umma(tmem + kColO1, sdesc(sb + ao, 16, 1024), sdesc(q + bo, 16, 1024), id64, ks > 0);
-            }
-            umma_commit(&bar_mma[0]);
-        }
+    for (int c = 0; c < chunks; ++c) {
+        if (abort_flag) break;
+        const int par = c & 1;
+        TcStage &st = s.st[par];
+        const int t0 = range.x + c * PC, n = min(PC, range.y - t0);
         if (!bar_wait(&bar_mma[0], c & 1)) abort_flag = 1;
         tc_fence_after();
 
@@ -728,7 +732,7 @@ __global__ void __launch_bounds__(512, 1) state_kernel(sq_prefill_args a, const 
             const bf16 *u = reinterpret_cast<const bf16 *>(st.u);
             const int tq = 16 * cq;
             float d[16], dt[16];
-            tmem_ld16(tmem + lane + kColD + tq, d);
+            tmem_ld16(tmem + lane + col_d(par) + tq, d);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 d[j] += __bfloat162float(u[(tq + j) * PV + v]);
@@ -752,10 +756,10 @@ __global__ void __launch_bounds__(512, 1) state_kernel(sq_prefill_args a, const 
 
         // ---- O2^T = D^T P^T, S^T += Dt^T K
         if (tid == 0) {
-            const uint32_t dm = smem_addr(s.dm), dtm = smem_addr(s.dtm), p = smem_addr(st.p), k = smem_addr(st.k);
+            const uint32_t dm = smem_addr(s.dm), dtm = smem_addr(s.dtm), pp = smem_addr(st.p), k = smem_addr(st.k);
 #pragma unroll
             for (int ks = 0; ks < PC / 16; ++ks) {
-                umma(tmem + kColO2, sdesc(dm + ks * 32, 16, 1024), sdesc(p + ks * 32, 16, 1024), id64, ks > 0);
+                umma(tmem + kColO2, sdesc(dm + ks * 32, 16, 1024), sdesc(pp + ks * 32, 16, 1024), id64, ks > 0);
                 umma(tmem + kColS, sdesc(dtm + ks * 32, 16, 1024), sdesc(k + ks * 2048, 8192, 1024), id128mn, 1);
             }
             umma_commit(&bar_mma[1]);
@@ -763,11 +767,27 @@ __global__ void __launch_bounds__(512, 1) state_kernel(sq_prefill_args a, const 
         if (!bar_wait(&bar_mma[1], c & 1)) abort_flag = 1;
         tc_fence_after();
 
-        // ---- outputs o_t = ro_t (Q S)_t + (P D)_t; the bf16 state tile for the next chunk
+        // ---- the bf16 state tile for the next chunk; its copies; its first MMAs
+        {
+            float x[32];
+            tmem_ld32(tmem + lane + kColS + 32 * cq, x);
+            put_row<32>(s.sb, PK, v, 32 * cq, x);
+        }
+        if (c + 1 < chunks) {
+            asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+            if (!bar_wait(&bar_data[par ^ 1], ((c + 1) >> 1) & 1)) abort_flag = 1;
+        }
+        proxy_fence();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (c + 1 < chunks && !abort_flag && tid == 0) issue_first(s.st[par ^ 1], par ^ 1);
+
+        // ---- outputs o_t = ro_t (Q S)_t + (P D)_t, while the next chunk's MMAs run
         {
             const int tq = 16 * cq;
             float o1[16], o2[16];
-            tmem_ld16(tmem + lane + kColO1 + tq, o1);
+            tmem_ld16(tmem + lane + col_o1(par) + tq, o1);
             tmem_ld16(tmem + lane + kColO2 + tq, o2);
             bf16 *orow = og + ((int64_t(t0) + tq) * H + head) * PV + v;
             const int64_t ostride = int64_t(H) * PV;
@@ -775,10 +795,15 @@ __global__ void __launch_bounds__(512, 1) state_kernel(sq_prefill_args a, const 
             for (int j = 0; j < 16; ++j) {
                 if (tq + j < n) orow[j * ostride] = __float2bfloat16_rn(st.ro[tq + j] * o1[j] + o2[j]);
             }
-            float x[32];
-            tmem_ld32(tmem + lane + kColS + 32 * cq, x);
-            put_row<32>(s.sb, PK, v, 32 * cq, x);
         }
+        // Every read of this stage buffer is done: refill it with chunk c + 2.
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (c + 2 < chunks)
+            tc_stage(a, st, &bar_data[par], rec0 + int64_t(c + 2) * H * kRec, t0 + 2 * PC,
+                     min(PC, range.y - t0 - 2 * PC), qh, tid);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     tc_fence_before();
