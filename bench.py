@@ -561,6 +561,8 @@ def measure_prefill(args, batch, tokens, heads_total, qk_total, steps, warmup, w
     chunk_heads = batch * ((tokens + 63) // 64) * heads_l
     c, kk, vv = 64, dim, dim
     res["flops"] = chunk_heads * 2 * (3 * c * c * kk + 2 * c * kk * vv + c * kk * vv + c * c * vv)
+    # Bytes the path must move: bf16 q, k, v in, fp32 g and beta in, bf16 outputs, the packed first states.
+    res["bytes"] = total * ((2 * qk_l * dim + 2 * heads_l * dim) * 2 + 2 * heads_l * 4) + batch * pool.page_bytes
 
     if e2e:
         pin = [x.cpu().pin_memory() for x in (q, k, v, g, beta)]
@@ -886,12 +888,23 @@ def main():
         res = measure_prefill(args, batch, args.tokens, heads, qk_heads, args.steps, args.warmup, world, rank, device,
                               barrier, e2e=True, clocks=clocks)
         elapsed_ms, e2e_ms = max_over_ranks(res["elapsed_ms"], res["e2e_ms"])
-        flops, = sum_over_ranks(res["flops"])
+        flops, nbytes = sum_over_ranks(res["flops"], res["bytes"])
         units = batch * args.tokens * args.steps
         peak_tf, peak_tf_kind = measured_peak("bf16_tflops")
+        peak_hbm, peak_hbm_kind = measured_peak("hbm_gbs")
         kern = res["kernel_ms"]
-        dom_ms = kern.get("prep_kernel", 0.0) + kern.get("state_kernel", 0.0)
-        achieved = flops / world / (dom_ms / 1e3) / 1e12 if dom_ms else None
+        dom_ms = sum(kern.values())
+        achieved_tf = flops / world / (dom_ms / 1e3) / 1e12 if dom_ms else None
+        achieved_gbs = nbytes / world / (dom_ms / 1e3) / 1e9 if dom_ms else None
+        # DRAM bytes of prep_kernel + state_kernel per launch from ncu on 4 prompts (259.0 + 296.8 MB), scaled by
+        # the prompts processed: traffic grows in proportion (one record per chunk and head).
+        traffic = 555.8e6 * batch / 4 if (args.tokens, heads // world, qk_heads // world) == (2048, 32, 16) else None
+        # The prefill is reported against the tensor roofline; the HBM view sits beside it, with the resource
+        # that takes longer at its peak (at config 3 the bytes, 0.25 ms, over the flops, 0.21 ms).
+        hbm = {"achieved": achieved_gbs, "peak": peak_hbm, "unit": "GB/s",
+               "frac": achieved_gbs / peak_hbm if achieved_gbs else None, "traffic": traffic,
+               "peak_source": peak_hbm_kind, "algorithmic_bytes_per_launch": nbytes / world}
+        slower = "hbm" if nbytes / (peak_hbm * 1e9) >= flops / (peak_tf * 1e12) else "tensor"
         line.update({
             "metric": "chunked-prefill tokens/s", "unit": "tokens/s", "value": units / (elapsed_ms / 1e3),
             "ms_per_step": elapsed_ms / args.steps, "dtype": "bf16",
@@ -900,9 +913,12 @@ def main():
                        "plan": "stepquant6 synthetic (first packed state)", "parallelism": f"tp{world} (value heads)",
                        "l2": "inputs > L2 (%.0f MB of q/k/v per GPU)" % ((2 * qk_heads + heads) // world * 128 * 2 * batch * args.tokens / 1e6)},
             "kernel_ms": kern,
-            "roofline": {"kernel": "prep_kernel + state_kernel", "bound": "tensor", "achieved": achieved, "peak": peak_tf,
-                         "unit": "TFLOP/s", "frac": achieved / peak_tf if achieved else None, "traffic": None,
-                         "peak_source": peak_tf_kind, "algorithmic_flops_per_launch": flops / world},
+            "roofline": {"kernel": "prep_kernel + state_kernel + offsets_kernel + fast_kernel (one prefill call)",
+                         "bound": "tensor", "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved_tf / peak_tf if achieved_tf else None, "traffic": traffic,
+                         "traffic_unit": "bytes", "peak_source": peak_tf_kind,
+                         "algorithmic_flops_per_launch": flops / world, "hbm": hbm,
+                         "slower_at_peak": slower},
             "e2e": {"value": units / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"]},
             "gpu_launches": args.steps * 5,
@@ -964,10 +980,12 @@ def main():
             "note": "register-resident KDA kernels; 64 warm-up steps, 2 slot groups"}
         r3 = measure_prefill(args, 32, 2048, 32, 16, 5, 2, 1, 0, device, barrier, e2e=False)
         peak_tf, peak_tf_kind = measured_peak("bf16_tflops")
-        pk = r3["kernel_ms"].get("prep_kernel", 0.0) + r3["kernel_ms"].get("state_kernel", 0.0)
+        peak_hbm, _ = measured_peak("hbm_gbs")
+        pk = sum(r3["kernel_ms"].values())
         sec["gdn-prefill-b32-t2048-h32-k128 (config 3)"] = {
             "value": 32 * 2048 * 5 / (r3["elapsed_ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r3["elapsed_ms"] / 5,
             "kernel_ms": r3["kernel_ms"], "steps": 5,
+            "hbm_frac": (r3["bytes"] / (pk / 1e3) / 1e9 / peak_hbm) if pk else None,
             "tensor_tflops": r3["flops"] / (pk / 1e3) / 1e12 if pk else None,
             "tensor_frac": (r3["flops"] / (pk / 1e3) / 1e12 / peak_tf) if pk else None, "peak_source": peak_tf_kind}
         line["secondary"] = sec

@@ -69,7 +69,6 @@ struct HeadInfo {
 
 struct FastSmem {
     FastStage st[2];
-    unsigned char plane[kPlaneBytes];  // row partials, then new code bytes
     float red[2][8][FV];               // per-warp column partials
     float4 rowa[FK];                   // per-row constants, duplicated pairs:
     float4 rowb[FK];                   //   P1: {r_old, r_old, k, k} {q, q, -, -}; P3-P5: {r, r, 1/r, 1/r} {-r, -r, w2, w2}
@@ -79,6 +78,9 @@ struct FastSmem {
     long long slot_ring[3];  // slots of the current and next two items (cp.async)
     int flags;
     uint32_t tmem_slot;      // tensor-memory base of the CTA's state columns
+    // Last, so that the readout and decode, which requantize nothing, launch
+    // without it (four CTAs per SM instead of three).
+    alignas(16) unsigned char plane[kPlaneBytes];  // row partials, then new code bytes
 };
 
 // Step, writeback and encode keep each thread's 64 state values in tensor
@@ -666,8 +668,10 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
             s.rowa[tid] = make_float4(ro, ro, kraw, kraw);
             s.rowb[tid] = make_float4(qraw, qraw, 0.f, 0.f);
         }
-        braw = p.stage_gates ? st.gate[0] : load_as_float(a.beta, a.gate_dtype, int64_t(c.req) * H + c.head);
-        graw = p.stage_gates ? st.gate[1] : load_as_float(a.g, a.gate_dtype, int64_t(c.req) * H + c.head);
+        if (tid < FV) {  // only the value-column threads finish the readout
+            braw = p.stage_gates ? st.gate[0] : load_as_float(a.beta, a.gate_dtype, int64_t(c.req) * H + c.head);
+            graw = p.stage_gates ? st.gate[1] : load_as_float(a.g, a.gate_dtype, int64_t(c.req) * H + c.head);
+        }
         // Per-warp sums of q^2, k^2 and q.k (combined after the next barrier).
         float3 part = make_float3(__fmul_rn(qraw, qraw), __fmul_rn(kraw, kraw), __fmul_rn(qraw, kraw));
 #pragma unroll
@@ -713,29 +717,34 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
         }
         {
             const sq_step_args &a = p.step;
-            // Gates (every thread; independent of the unpack above).
-            const float alog = s.head[c.head].a_log;
-            const float bias = s.head[c.head].dt_bias;
-            const float beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
-            float g = graw;
-            if (a.a_log) {
-                const float u = g + bias;
-                g = -expf(alog) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
-            }
-            const float decay = expf(g);
-            __syncthreads();
-            float qq = 0.f, kk = 0.f, dot = 0.f;
-#pragma unroll
-            for (int w = 0; w < kThreads / 32; ++w) {
-                qq += s.misc[4 * w];
-                kk += s.misc[4 * w + 1];
-                dot += s.misc[4 * w + 2];
-            }
-            const float qn = a.normalize ? __frsqrt_rn(qq + 1e-6f) : 1.f;
-            const float kn = a.normalize ? __frsqrt_rn(kk + 1e-6f) : 1.f;
-            const float qscale = __fmul_rn(qn, a.scale);
-            const float qk = __fmul_rn(__fmul_rn(__fmul_rn(dot, qn), kn), a.scale);
+            // Gates, norms and the column results: the four warps of the value
+            // columns only (the gates are independent of the unpack above).
+            float beta = 0.f, decay = 0.f;
             if (tid < FV) {
+                const float alog = s.head[c.head].a_log;
+                const float bias = s.head[c.head].dt_bias;
+                beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
+                float g = graw;
+                if (a.a_log) {
+                    const float u = g + bias;
+                    g = -expf(alog) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
+                }
+                decay = expf(g);
+            }
+            __syncthreads();
+            if (tid < FV) {
+                float qq = 0.f, kk = 0.f, dot = 0.f;
+#pragma unroll
+                for (int w = 0; w < kThreads / 32; ++w) {
+                    const float4 m = reinterpret_cast<const float4 *>(s.misc)[w];
+                    qq += m.x;
+                    kk += m.y;
+                    dot += m.z;
+                }
+                const float qn = a.normalize ? __frsqrt_rn(qq + 1e-6f) : 1.f;
+                const float kn = a.normalize ? __frsqrt_rn(kk + 1e-6f) : 1.f;
+                const float qscale = __fmul_rn(qn, a.scale);
+                const float qk = __fmul_rn(__fmul_rn(__fmul_rn(dot, qn), kn), a.scale);
                 float ks = 0.f, qs = 0.f;
 #pragma unroll
                 for (int w = 0; w < 8; ++w) {
@@ -971,7 +980,7 @@ int stream_sms(cudaStream_t stream, int device_sms) {
 
 template <int MODE>
 cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream) {
-    const int smem = int(sizeof(FastSmem));
+    const int smem = MODE == kReadout || MODE == kDecode ? int(offsetof(FastSmem, plane)) : int(sizeof(FastSmem));
     int device = 0;
     cudaError_t err = cudaGetDevice(&device);
     if (err != cudaSuccess) return err;

@@ -512,6 +512,8 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
 //   D^T [128, 192) the chunk residuals           D^T  = S^T (-W)^T  (N = 64), + U^T
 //   O1^T [192,256) (Q S)^T                       O1^T = S^T Q^T     (N = 64)
 //   O2^T [256,320) (P D)^T                       O2^T = D^T P^T     (N = 64)
+// Odd chunks keep D^T in [320, 384) and O1^T in [384, 448), so the next
+// chunk's D^T and O1^T products run while this chunk's outputs are read.
 // Operands are bf16 in shared memory, 128-byte swizzled: S^T, D^T, Dt^T as
 // K-major A tiles written by the threads; -W, P (from the record, bulk copies),
 // raw q (cp.async) as K-major B tiles; raw k as an MN-major B tile.  One
