@@ -34,10 +34,6 @@ struct KdaSmem {
     int offs[DK];
     int rows[DK];
     float imp[DK];
-    union {
-        __half plane[DK * DV];          // P0 -> P1 and P5 -> store: [k][l][i] = column l + 32 i
-        float rowpart[DK * kRowPart];   // P2 row partials
-    } u;
     float red[2][8][DV];
     float4 rowa[DK];  // P1: {fa, fa, k, k}          P3-P5: {r, r, 1/r, 1/r}
     float4 rowb[DK];  // P1: {q, q, isint, -}        P3-P5: {-r, -r, w2, w2}
@@ -48,6 +44,11 @@ struct KdaSmem {
     int flags;
     int qmax_max;        // largest qmax of the head's integer rows
     uint32_t tmem_slot;  // tensor-memory base of the CTA's state columns
+    // Last, so that the readout, which goes without it, launches without it.
+    union alignas(16) {
+        __half plane[DK * DV];          // P0 -> P1 and P5 -> store: [k][l][i] = column l + 32 i
+        float rowpart[DK * kRowPart];   // P2 row partials
+    } u;
 };
 
 // Step and writeback keep each thread's 64 state values in its tensor-memory
@@ -82,6 +83,55 @@ __device__ __forceinline__ void kda_unpack(KdaSmem &s, int lead, int off0, int s
             s.u.plane[k * DV + (v & 31) * 4 + (v >> 5)] = h[j];
         }
     }
+}
+
+// P1 of the readout, which keeps no state: lane l covers the four consecutive
+// columns 4l .. 4l + 3 (value tile l), decoded straight from the staged code
+// bytes instead of through the fp16 plane.  Each element is formed with the
+// same operations as in P1 of the step (the level is exact either way), and
+// each column's partial is the same ordered sum over the warp's 16 rows, so
+// the results are identical.
+__device__ __forceinline__ void kda_readout_rows(KdaSmem &s, int lead, int off0, int stride, int warp, int lane) {
+    const float4 c = *reinterpret_cast<const float4 *>(&s.colc[3][4 * lane]);
+    const float2 c01 = make_float2(c.x, c.y), c23 = make_float2(c.z, c.w), one = make_float2(1.f, 1.f);
+    const int base = lead - off0 + lane * stride;
+    float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
+#pragma unroll 2
+    for (int r = 0; r < 16; ++r) {
+        const int k = warp * 16 + r;
+        const int b = s.bits[k];  // one width per row: the branches are warp-uniform
+        const unsigned char *src = s.codes + (base + s.offs[k]);
+        float2 v01, v23;
+        if (b == 16) {
+            const uint32_t h01 = uint32_t(src[0]) | uint32_t(src[1]) << 8 | uint32_t(src[2]) << 16 | uint32_t(src[3]) << 24;
+            const uint32_t h23 = uint32_t(src[4]) | uint32_t(src[5]) << 8 | uint32_t(src[6]) << 16 | uint32_t(src[7]) << 24;
+            v01 = __half22float2(*reinterpret_cast<const __half2 *>(&h01));
+            v23 = __half22float2(*reinterpret_cast<const __half2 *>(&h23));
+        } else {
+            uint32_t w = src[0];
+            if (b >= 4) w |= uint32_t(src[1]) << 8;
+            if (b >= 6) w |= uint32_t(src[2]) << 16;
+            if (b == 8) w |= uint32_t(src[3]) << 24;
+            const uint32_t mask = (1u << b) - 1u;
+            const float bias = -(8388608.f + float(qmax_i(b)));  // 2^23 + code - (2^23 + offset) = level
+            v01 = make_float2(__fadd_rn(__uint_as_float(0x4B000000u | (w & mask)), bias),
+                              __fadd_rn(__uint_as_float(0x4B000000u | ((w >> b) & mask)), bias));
+            v23 = make_float2(__fadd_rn(__uint_as_float(0x4B000000u | ((w >> (2 * b)) & mask)), bias),
+                              __fadd_rn(__uint_as_float(0x4B000000u | ((w >> (3 * b)) & mask)), bias));
+        }
+        const float4 a = s.rowa[k];
+        const float q = s.rowb[k].x;
+        const bool integer = b != 16;
+        const float2 m01 = integer ? c01 : one, m23 = integer ? c23 : one;
+        const float2 x01 = pmul2(pmul2(v01, lo2(a)), m01);
+        const float2 x23 = pmul2(pmul2(v23, lo2(a)), m23);
+        kx01 = pfma2(hi2(a), x01, kx01);
+        kx23 = pfma2(hi2(a), x23, kx23);
+        qx01 = pfma2(make_float2(q, q), x01, qx01);
+        qx23 = pfma2(make_float2(q, q), x23, qx23);
+    }
+    *reinterpret_cast<float4 *>(&s.red[0][warp][4 * lane]) = make_float4(kx01.x, kx01.y, kx23.x, kx23.y);
+    *reinterpret_cast<float4 *>(&s.red[1][warp][4 * lane]) = make_float4(qx01.x, qx01.y, qx23.x, qx23.y);
 }
 
 // P3 partial: per column, the maximum over the warp's integer rows of
@@ -351,7 +401,6 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
     float beta = 0.f, qk = 0.f;
     if (MODE != kWriteback) {
         const sq_step_args &a = p.step;
-        const float braw = load_as_float(a.beta, a.gate_dtype, int64_t(req) * H + head);
         float3 part = make_float3(__fmul_rn(qx, qx), __fmul_rn(kx, kx), __fmul_rn(qx, kx));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -364,8 +413,9 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
             s.misc[4 * warp + 1] = part.y;
             s.misc[4 * warp + 2] = part.z;
         }
-        beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
-        if (tid < DK) {
+        if (tid < DK) {  // DK == DV: the threads that finish the columns
+            const float braw = load_as_float(a.beta, a.gate_dtype, int64_t(req) * H + head);
+            beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
             float g = ga;
             if (a.a_log) {
                 const float u = g + a.dt_bias[head * DK + tid];
@@ -383,14 +433,15 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         tm_fence_after();
         tm = s.tmem_slot + (uint32_t(32 * (warp & 3)) << 16) + uint32_t(64 * (warp >> 2));
     }
-    if (MODE != kWriteback) {
+    if (MODE != kWriteback && tid < DK) {
         const sq_step_args &a = p.step;
         float qq = 0.f, kk = 0.f, dot = 0.f;
 #pragma unroll
         for (int w = 0; w < kThreads / 32; ++w) {
-            qq += s.misc[4 * w];
-            kk += s.misc[4 * w + 1];
-            dot += s.misc[4 * w + 2];
+            const float4 m = reinterpret_cast<const float4 *>(s.misc)[w];
+            qq += m.x;
+            kk += m.y;
+            dot += m.z;
         }
         const float qn = a.normalize ? __frsqrt_rn(qq + 1e-6f) : 1.f;
         const float kn = a.normalize ? __frsqrt_rn(kk + 1e-6f) : 1.f;
@@ -407,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         s.colc[3][tid] = cold;
         if (MODE == kWriteback) s.colc[0][tid] = delta;
     }
-    kda_unpack(s, lead, off0, stride, tid);
+    if (MODE != kReadout) kda_unpack(s, lead, off0, stride, tid);
     __syncthreads();
 
     // ---- P1: dequantize and decay; column partials of k^T S and q^T S -------
@@ -416,8 +467,9 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         const float2 c23 = make_float2(s.colc[3][lane + 64], s.colc[3][lane + 96]);
         const float2 one = make_float2(1.f, 1.f);
         float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
+        if (MODE == kReadout) kda_readout_rows(s, lead, off0, stride, warp, lane);
 #pragma unroll 1
-        for (int g = 0; g < 4; ++g) {
+        for (int g = 0; g < (MODE == kReadout ? 0 : 4); ++g) {
             float2 X[4][2];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -439,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
             }
             if (kTm) tm_st16(tm + 16 * g, X);
         }
-        if (MODE != kWriteback) {
+        if (MODE == kStep) {
             s.red[0][warp][lane] = kx01.x;
             s.red[0][warp][lane + 32] = kx01.y;
             s.red[0][warp][lane + 64] = kx23.x;
@@ -448,6 +500,8 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
             s.red[1][warp][lane + 32] = qx01.y;
             s.red[1][warp][lane + 64] = qx23.x;
             s.red[1][warp][lane + 96] = qx23.y;
+        }
+        if (MODE != kWriteback) {
             __syncthreads();
             if (tid < DV) {
                 float ks = 0.f, qs = 0.f;
@@ -608,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
 
 template <int MODE>
 cudaError_t launch_kda_mode(const TileParams &p, int items, cudaStream_t stream) {
-    const int smem = int(sizeof(KdaSmem));
+    const int smem = MODE == kReadout ? int(offsetof(KdaSmem, u)) : int(sizeof(KdaSmem));
     cudaError_t err = cudaFuncSetAttribute(kda_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return err;
     kda_kernel<MODE><<<items, kThreads, smem, stream>>>(p);
