@@ -95,40 +95,42 @@ __device__ __forceinline__ void kda_readout_rows(KdaSmem &s, int lead, int off0,
     const float4 c = *reinterpret_cast<const float4 *>(&s.colc[3][4 * lane]);
     const float2 c01 = make_float2(c.x, c.y), c23 = make_float2(c.z, c.w), one = make_float2(1.f, 1.f);
     const int base = lead - off0 + lane * stride;
+    const uint32_t *words = reinterpret_cast<const uint32_t *>(s.codes);
     float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
 #pragma unroll 2
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
-        const int b = s.bits[k];  // one width per row: the branches are warp-uniform
-        const unsigned char *src = s.codes + (base + s.offs[k]);
-        float2 v01, v23;
-        if (b == 16) {
-            const uint32_t h01 = uint32_t(src[0]) | uint32_t(src[1]) << 8 | uint32_t(src[2]) << 16 | uint32_t(src[3]) << 24;
-            const uint32_t h23 = uint32_t(src[4]) | uint32_t(src[5]) << 8 | uint32_t(src[6]) << 16 | uint32_t(src[7]) << 24;
-            v01 = __half22float2(*reinterpret_cast<const __half2 *>(&h01));
-            v23 = __half22float2(*reinterpret_cast<const __half2 *>(&h23));
-        } else {
-            uint32_t w = src[0];
-            if (b >= 4) w |= uint32_t(src[1]) << 8;
-            if (b >= 6) w |= uint32_t(src[2]) << 16;
-            if (b == 8) w |= uint32_t(src[3]) << 24;
-            const uint32_t mask = (1u << b) - 1u;
-            const float bias = -(8388608.f + float(qmax_i(b)));  // 2^23 + code - (2^23 + offset) = level
-            v01 = make_float2(__fadd_rn(__uint_as_float(0x4B000000u | (w & mask)), bias),
-                              __fadd_rn(__uint_as_float(0x4B000000u | ((w >> b) & mask)), bias));
-            v23 = make_float2(__fadd_rn(__uint_as_float(0x4B000000u | ((w >> (2 * b)) & mask)), bias),
-                              __fadd_rn(__uint_as_float(0x4B000000u | ((w >> (3 * b)) & mask)), bias));
-        }
         const float4 a = s.rowa[k];
-        const float q = s.rowb[k].x;
-        const bool integer = b != 16;
+        const float4 d = s.rowb[k];  // {q, level bias, code mask (0: fp16 row), byte offset of the row}
+        const int at = base + __float_as_int(d.w);
+        // The chunk's first 4 (fp16: 8) bytes from aligned words; the staged
+        // region has 16 spare bytes past its end, so the reads stay inside it.
+        const uint32_t *w = words + (at >> 2);
+        const uint32_t sh = uint32_t(at & 3) * 8u;
+        const uint32_t w0 = __funnelshift_r(w[0], w[1], sh);
+        const uint32_t mask = __float_as_uint(d.z);
+        float2 v01, v23;
+        if (mask == 0u) {  // fp16 row (the width is the row's: the branch is warp-uniform)
+            const uint32_t w1 = __funnelshift_r(w[1], w[2], sh);
+            v01 = __half22float2(*reinterpret_cast<const __half2 *>(&w0));
+            v23 = __half22float2(*reinterpret_cast<const __half2 *>(&w1));
+        } else {  // 2^23 + code - (2^23 + offset) = level, exactly
+            const int b = __popc(mask);
+            const float2 bias = make_float2(d.y, d.y);
+            v01 = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | (w0 & mask)),
+                                         __uint_as_float(0x4B000000u | ((w0 >> b) & mask))), bias);
+            v23 = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | ((w0 >> (2 * b)) & mask)),
+                                         __uint_as_float(0x4B000000u | ((w0 >> (3 * b)) & mask))), bias);
+        }
+        const bool integer = mask != 0u;
         const float2 m01 = integer ? c01 : one, m23 = integer ? c23 : one;
         const float2 x01 = pmul2(pmul2(v01, lo2(a)), m01);
         const float2 x23 = pmul2(pmul2(v23, lo2(a)), m23);
+        const float2 q = make_float2(d.x, d.x);
         kx01 = pfma2(hi2(a), x01, kx01);
         kx23 = pfma2(hi2(a), x23, kx23);
-        qx01 = pfma2(make_float2(q, q), x01, qx01);
-        qx23 = pfma2(make_float2(q, q), x23, qx23);
+        qx01 = pfma2(q, x01, qx01);
+        qx23 = pfma2(q, x23, qx23);
     }
     *reinterpret_cast<float4 *>(&s.red[0][warp][4 * lane]) = make_float4(kx01.x, kx01.y, kx23.x, kx23.y);
     *reinterpret_cast<float4 *>(&s.red[1][warp][4 * lane]) = make_float4(qx01.x, qx01.y, qx23.x, qx23.y);
@@ -454,7 +456,11 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         const float norm = integer ? float(1 << (8 - (bk > 8 ? 8 : bk))) : 1.f;
         const float fa = integer ? __fmul_rn(__fmul_rn(rold, norm), decay) : decay;
         s.rowa[tid] = make_float4(fa, fa, kx, kx);
-        s.rowb[tid] = make_float4(qx, qx, integer ? 1.f : 0.f, 0.f);
+        if (MODE == kReadout)  // the readout's row decode table (kda_readout_rows)
+            s.rowb[tid] = make_float4(qx, integer ? -(8388608.f + float(qmax_i(bk))) : 0.f,
+                                      __uint_as_float(integer ? (1u << bk) - 1u : 0u), __int_as_float(s.offs[tid]));
+        else
+            s.rowb[tid] = make_float4(qx, qx, integer ? 1.f : 0.f, 0.f);
         s.colc[3][tid] = cold;
         if (MODE == kWriteback) s.colc[0][tid] = delta;
     }
