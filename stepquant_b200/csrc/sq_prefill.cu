@@ -15,7 +15,7 @@
 //
 // prep_kernel (one CTA per chunk and value head, all chunks in parallel)
 // computes everything that does not depend on S -- P, -W, U and the row
-// factors -- into a workspace record (mma.sync bf16 tiles, fp32 inverse);
+// factors -- into a workspace record (bf16 products on tcgen05, fp32 inverse);
 // state_kernel (one CTA per sequence and value head) walks the chunks in order
 // with the 128x128 state in tensor memory, on tcgen05 (see its comment).
 // Padded tokens of a last partial chunk have beta = 0 and log decay 0, so they
@@ -28,8 +28,6 @@ namespace {
 constexpr int PC = 64;    // chunk length
 constexpr int PK = 128;   // keys
 constexpr int PV = 128;   // values
-constexpr int kLd = 136;  // bf16 row stride of 128-wide tiles (272 B: ldmatrix rows hit distinct banks)
-constexpr int kLdP = 72;  // bf16 row stride of 64-wide tiles
 constexpr int kLdF = 68;  // fp32 row stride of 64x64 tiles
 
 using bf16 = __nv_bfloat16;
@@ -47,48 +45,8 @@ constexpr int kOffsetsBytes(int seqs) { return (4 * (seqs + 1) + 255) / 256 * 25
 
 __device__ __forceinline__ unsigned smem_addr(const void *p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
 
-__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], const void *p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_addr(p)));
-}
-__device__ __forceinline__ void ldsm4t(uint32_t (&r)[4], const void *p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_addr(p)));
-}
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 __device__ __forceinline__ void cp16(void *smem, const void *gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr(smem)), "l"(gmem));
-}
-
-// Fragment loads (lane l, i = l / 8, r = l % 8).
-// A tile 16x16 at (m0, k0) of a row-major [m][k] matrix.
-template <int LD>
-__device__ __forceinline__ void load_a(uint32_t (&a)[4], const bf16 (*m)[LD], int m0, int k0, int lane) {
-    const int i = lane >> 3, r = lane & 7;
-    ldsm4(a, &m[m0 + r + 8 * (i & 1)][k0 + 8 * (i >> 1)]);
-}
-// A tile 16x16 at (m0, k0) of A = X^T, X stored row-major [k][m].
-template <int LD>
-__device__ __forceinline__ void load_a_t(uint32_t (&a)[4], const bf16 (*x)[LD], int m0, int k0, int lane) {
-    const int i = lane >> 3, r = lane & 7;
-    ldsm4t(a, &x[k0 + r + 8 * (i >> 1)][m0 + 8 * (i & 1)]);
-}
-// B fragments of two n-tiles (n0, n0 + 8) at k0 from B^T stored row-major [n][k]:
-// b[0], b[1] for n-tile n0 and b[2], b[3] for n0 + 8.
-template <int LD>
-__device__ __forceinline__ void load_b_nk(uint32_t (&b)[4], const bf16 (*m)[LD], int n0, int k0, int lane) {
-    const int i = lane >> 3, r = lane & 7;
-    ldsm4(b, &m[n0 + r + 8 * (i >> 1)][k0 + 8 * (i & 1)]);
-}
-// The same from B stored row-major [k][n].
-template <int LD>
-__device__ __forceinline__ void load_b_kn(uint32_t (&b)[4], const bf16 (*m)[LD], int n0, int k0, int lane) {
-    const int i = lane >> 3, r = lane & 7;
-    ldsm4t(b, &m[k0 + r + 8 * (i & 1)][n0 + 8 * (i >> 1)]);
 }
 
 __device__ __forceinline__ uint32_t tf32_bits(float x) {
@@ -167,27 +125,6 @@ __global__ void __launch_bounds__(1024) offsets_kernel(sq_prefill_args a, int32_
     if (threadIdx.x == 0) offsets[a.num_seqs] = warp_total[31];
 }
 
-// ---------------------------------------------------------------------------
-// prep_kernel: one 256-thread CTA per (chunk, value head).
-// ---------------------------------------------------------------------------
-constexpr int kLdQ = 144;  // the q tile holds Tw and Tu (bf16 64x72 each) once q is no longer needed
-
-// 70 KB: three CTAs per SM.
-struct PrepSmem {
-    bf16 q[PC][kLdQ];   // raw q; then Tw (first half) and Tu (second half)
-    bf16 k[PC][kLd];
-    union {
-        float l[PC][kLdF];  // L below the diagonal; the block products X_rc above it (block (c, r))
-        bf16 v[PC][kLd];    // raw v, loaded once T is complete
-    } lv;
-    float t[PC][kLdF];  // T
-    float gam[PC];
-    float beta[PC];
-    float nq[PC];
-    float nk[PC];
-    float fw[PC];  // beta e^gam nk: column factors of Tw
-};
-
 // acc (a 16x16 block as two 16x8 tf32 accumulator tiles) += A[ar0.., ac0..] B[br0.., bc0..]
 // over a 16-deep k range (two m16n8k8 steps); fp32 operands rounded to tf32.
 __device__ __forceinline__ void mma_block16(float (&acc)[2][4], const float (*A)[kLdF], int ar0, int ac0,
@@ -215,291 +152,6 @@ __device__ __forceinline__ void store_block16(const float (&acc)[2][4], float (*
         dst[g8][col + 1] = acc[nt][1];
         dst[g8 + 8][col] = acc[nt][2];
         dst[g8 + 8][col + 1] = acc[nt][3];
-    }
-}
-
-__global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const int32_t *offsets,
-                                                      unsigned char *records) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    PrepSmem &s = *reinterpret_cast<PrepSmem *>(smem_raw);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g8 = lane >> 2, tig = lane & 3;
-    const int H = a.heads, head = blockIdx.y, chunk = blockIdx.x;
-    if (chunk >= offsets[a.num_seqs]) return;
-    int lo = 0, hi = a.num_seqs - 1;  // the sequence: largest n with offsets[n] <= chunk
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (offsets[mid] <= chunk) lo = mid;
-        else hi = mid - 1;
-    }
-    const int2 range = seq_range(a, lo);
-    const int t0 = range.x + (chunk - offsets[lo]) * PC, n = min(PC, range.y - t0);
-    const int qh = head / (H / a.qk_heads);
-    unsigned char *rec = records + (int64_t(chunk) * H + head) * kRec;
-
-    // ---- raw q, k rows of the chunk (zero rows past the end), gates
-    {
-        const bf16 *qg = static_cast<const bf16 *>(a.q), *kg = static_cast<const bf16 *>(a.k);
-        for (int idx = tid; idx < 2 * PC * 16; idx += 256) {
-            const int which = idx >> 10, row = (idx >> 4) & 63, piece = idx & 15;
-            bf16 *dst = (which == 0 ? s.q[row] : s.k[row]) + piece * 8;
-            if (row < n) {
-                const int64_t t = t0 + row;
-                const bf16 *src = which == 0 ? qg + t * a.q_stride + int64_t(qh) * PK : kg + t * a.k_stride + int64_t(qh) * PK;
-                cp16(dst, src + piece * 8);
-            } else {
-                *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
-            }
-        }
-        if (tid < PC) {
-            const bool live = tid < n;
-            const int64_t gi = (int64_t(t0) + tid) * H + head;
-            s.gam[tid] = live ? a.g[gi] : 0.f;
-            s.beta[tid] = live ? a.beta[gi] : 0.f;
-        }
-        asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::);
-        __syncthreads();
-    }
-    // ---- norms of the q and k rows (2 threads per row), cumulative log decay
-    {
-        const int row = (tid >> 1) & 63, half = tid & 1;
-        const bf16 *src = tid < 128 ? s.q[row] : s.k[row];
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint4 w = *reinterpret_cast<const uint4 *>(src + half * 64 + j * 8);
-            const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&w);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(h2[e]);
-                ss += f.x * f.x + f.y * f.y;
-            }
-        }
-        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-        const float nrm = a.normalize ? rsqrtf(ss + 1e-6f) : 1.f;
-        if (half == 0) {
-            if (tid < 128) s.nq[row] = nrm;
-            else s.nk[row] = nrm;
-        }
-    }
-    if (warp == 0) {
-        const float x0 = s.gam[2 * lane], x1 = s.gam[2 * lane + 1];
-        float run = x0 + x1;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, run, o);
-            if (lane >= o) run += y;
-        }
-        const float before = run - (x0 + x1);
-        __syncwarp();
-        s.gam[2 * lane] = before + x0;
-        s.gam[2 * lane + 1] = run;
-    }
-    __syncthreads();
-    if (tid < PC) s.fw[tid] = s.beta[tid] * expf(s.gam[tid]) * s.nk[tid];
-
-    // ---- G = K K^T, H = Q K^T (rows 16 (w / 2), columns 32 (w % 2) .. +31) -> L, P
-    {
-        const int r0 = 16 * (warp >> 1), c0 = 32 * (warp & 1);
-        float accG[4][4] = {}, accH[4][4] = {};
-#pragma unroll
-        for (int ks = 0; ks < PK / 16; ++ks) {
-            uint32_t ak[4], aq[4], b0[4], b1[4];
-            load_a<kLd>(ak, s.k, r0, 16 * ks, lane);
-            load_a<kLdQ>(aq, s.q, r0, 16 * ks, lane);
-            load_b_nk<kLd>(b0, s.k, c0, 16 * ks, lane);
-            load_b_nk<kLd>(b1, s.k, c0 + 16, 16 * ks, lane);
-            mma16816(accG[0], ak, b0[0], b0[1]);
-            mma16816(accG[1], ak, b0[2], b0[3]);
-            mma16816(accG[2], ak, b1[0], b1[1]);
-            mma16816(accG[3], ak, b1[2], b1[3]);
-            mma16816(accH[0], aq, b0[0], b0[1]);
-            mma16816(accH[1], aq, b0[2], b0[3]);
-            mma16816(accH[2], aq, b1[0], b1[1]);
-            mma16816(accH[3], aq, b1[2], b1[3]);
-        }
-        float gi[2], li[2], pi[2];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            const int i = r0 + g8 + 8 * hh;
-            gi[hh] = s.gam[i];
-            li[hh] = s.beta[i] * s.nk[i];
-            pi[hh] = s.nq[i] * a.scale;
-        }
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            const int j = c0 + 8 * nt + 2 * tig;
-            const float gj[2] = {s.gam[j], s.gam[j + 1]}, nkj[2] = {s.nk[j], s.nk[j + 1]};
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int i = r0 + g8 + 8 * hh;
-                float pv[2];
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int jj = j + e;
-                    const float dec = jj <= i ? __expf(gi[hh] - gj[e]) * nkj[e] : 0.f;
-                    s.lv.l[i][jj] = jj < i ? li[hh] * dec * accG[nt][2 * hh + e] : 0.f;
-                    pv[e] = pi[hh] * dec * accH[nt][2 * hh + e];
-                }
-                *reinterpret_cast<uint32_t *>(rec + kRecP + sw128(i, j, PC)) = pack_bf16(pv[0], pv[1]);
-            }
-        }
-    }
-    __syncthreads();
-
-    // ---- T = (I + L)^-1 in fp32: 16x16 diagonal blocks by substitution, then
-    // block rows r = 1..3 on tensor cores (tf32): T_rc = -T_rr (sum_m L_rm T_mc).
-    // Each block of Tw = T diag(beta e^gam nk) and Tu = T diag(beta) (bf16, in the
-    // dead q tile) is written as soon as the block of T is final.
-    bf16 (*Tw)[kLdP] = reinterpret_cast<bf16 (*)[kLdP]>(&s.q[0][0]);
-    bf16 (*Tu)[kLdP] = reinterpret_cast<bf16 (*)[kLdP]>(&s.q[0][0] + PC * kLdP);
-    if (warp < 4) {
-        if (lane < 16) {
-            const int b = 16 * warp, m = lane;
-            const float fw = s.fw[b + m], fb = s.beta[b + m];
-            float t[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                float val = i == m ? 1.f : 0.f;
-#pragma unroll
-                for (int j = 0; j < i; ++j) val -= s.lv.l[b + i][b + j] * t[j];
-                t[i] = val;
-                s.t[b + i][b + m] = val;
-                Tw[b + i][b + m] = __float2bfloat16_rn(val * fw);
-                Tu[b + i][b + m] = __float2bfloat16_rn(val * fb);
-            }
-        }
-    } else {
-        // zero the blocks of Tw and Tu above the diagonal
-        for (int e = tid - 128; e < 6 * 256; e += 128) {
-            const int blk = e >> 8, i = (e >> 4) & 15, m = e & 15;
-            const int r = blk < 3 ? 0 : blk < 5 ? 1 : 2;
-            const int c = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
-            Tw[16 * r + i][16 * c + m] = __float2bfloat16_rn(0.f);
-            Tu[16 * r + i][16 * c + m] = __float2bfloat16_rn(0.f);
-        }
-    }
-    __syncthreads();
-    // Blocks below the diagonal as a blocked inverse in two stages:
-    //   A: T10 = -T11 (L10 T00) (warp 0) and T32 = -T33 (L32 T22) (warp 1);
-    //   B: T[2:4, 0:2] = -T[2:4, 2:4] (L[2:4, 0:2] T[0:2, 0:2]), one block per warp.
-    // The block products X are kept in free blocks above L's diagonal.
-    {
-        float (*L)[kLdF] = s.lv.l;
-        float (*T)[kLdF] = s.t;
-        auto above = [&](int r, int c) { return reinterpret_cast<float (*)[kLdF]>(&L[16 * r][16 * c]); };
-        auto finish = [&](int r, int c, const float (&Y)[2][4]) {  // T_rc = -Y, with its Tw and Tu blocks
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int i = 16 * r + g8 + 8 * (e >> 1), j = 16 * c + 8 * nt + 2 * tig + (e & 1);
-                    const float tv = -Y[nt][e];
-                    T[i][j] = tv;
-                    Tw[i][j] = __float2bfloat16_rn(tv * s.fw[j]);
-                    Tu[i][j] = __float2bfloat16_rn(tv * s.beta[j]);
-                }
-            }
-        };
-        if (warp < 2) {
-            const int r = warp ? 3 : 1, c = r - 1;
-            float (*xb)[kLdF] = above(c, r);
-            float X[2][4] = {}, Y[2][4] = {};
-            mma_block16(X, L, 16 * r, 16 * c, T, 16 * c, 16 * c, g8, tig);
-            store_block16(X, xb, g8, tig);
-            __syncwarp();
-            mma_block16(Y, T, 16 * r, 16 * r, xb, 0, 0, g8, tig);
-            finish(r, c, Y);
-        }
-        __syncthreads();
-        if (warp < 4) {
-            const int i = 2 + (warp >> 1), j = warp & 1;
-            // X_mj = sum over m' = j..1 of L_{m m'} T_{m' j}, for m = 2 (and m = 3 in row 3)
-            float (*x2)[kLdF] = warp == 0 ? above(0, 1) : warp == 1 ? above(0, 2) : warp == 2 ? above(0, 3) : above(1, 3);
-            float (*x3)[kLdF] = warp == 2 ? above(1, 2) : above(2, 3);
-            float X[2][4] = {}, Y[2][4] = {};
-            for (int m = j; m < 2; ++m) mma_block16(X, L, 32, 16 * m, T, 16 * m, 16 * j, g8, tig);
-            store_block16(X, x2, g8, tig);
-            if (i == 3) {
-                float X3[2][4] = {};
-                for (int m = j; m < 2; ++m) mma_block16(X3, L, 48, 16 * m, T, 16 * m, 16 * j, g8, tig);
-                store_block16(X3, x3, g8, tig);
-            }
-            __syncwarp();
-            if (i == 2) {
-                mma_block16(Y, T, 32, 32, x2, 0, 0, g8, tig);  // T22 X_2j
-            } else {
-                mma_block16(Y, T, 48, 32, x2, 0, 0, g8, tig);  // T32 X_2j
-                mma_block16(Y, T, 48, 48, x3, 0, 0, g8, tig);  // + T33 X_3j
-            }
-            finish(i, j, Y);
-        }
-        __syncthreads();
-    }
-
-    // ---- raw v into the space of L (T is complete), while -W = -Tw K is formed
-    {
-        const bf16 *vg = static_cast<const bf16 *>(a.v);
-        for (int idx = tid; idx < PC * 16; idx += 256) {
-            const int row = idx >> 4, piece = idx & 15;
-            bf16 *dst = s.lv.v[row] + piece * 8;
-            if (row < n) cp16(dst, vg + (int64_t(t0) + row) * a.v_stride + int64_t(head) * PV + piece * 8);
-            else *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
-        }
-        asm volatile("cp.async.commit_group;\n" ::);
-    }
-    // Rows 16 (w % 4) and columns 64 (w / 4) .. +63 of -W, then of U.
-    const int wr0 = 16 * (warp & 3), wc0 = 64 * (warp >> 2);
-    {
-        float W[8][4] = {};
-#pragma unroll
-        for (int ks = 0; ks < PC / 16; ++ks) {
-            uint32_t aw[4];
-            load_a<kLdP>(aw, Tw, wr0, 16 * ks, lane);
-#pragma unroll
-            for (int np = 0; np < 4; ++np) {
-                uint32_t bk[4];
-                load_b_kn<kLd>(bk, s.k, wc0 + 16 * np, 16 * ks, lane);
-                mma16816(W[2 * np], aw, bk[0], bk[1]);
-                mma16816(W[2 * np + 1], aw, bk[2], bk[3]);
-            }
-        }
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            const int col = wc0 + 8 * nt + 2 * tig, i0 = wr0 + g8, i1 = i0 + 8;
-            *reinterpret_cast<uint32_t *>(rec + kRecW + sw128(i0, col, PC)) = pack_bf16(-W[nt][0], -W[nt][1]);
-            *reinterpret_cast<uint32_t *>(rec + kRecW + sw128(i1, col, PC)) = pack_bf16(-W[nt][2], -W[nt][3]);
-        }
-    }
-    asm volatile("cp.async.wait_group 0;\n" ::);
-    __syncthreads();
-    {
-        float U[8][4] = {};
-#pragma unroll
-        for (int ks = 0; ks < PC / 16; ++ks) {
-            uint32_t au[4];
-            load_a<kLdP>(au, Tu, wr0, 16 * ks, lane);
-#pragma unroll
-            for (int np = 0; np < 4; ++np) {
-                uint32_t bv[4];
-                load_b_kn<kLd>(bv, s.lv.v, wc0 + 16 * np, 16 * ks, lane);
-                mma16816(U[2 * np], au, bv[0], bv[1]);
-                mma16816(U[2 * np + 1], au, bv[2], bv[3]);
-            }
-        }
-        bf16 *urec = reinterpret_cast<bf16 *>(rec + kRecU);
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            const int col = wc0 + 8 * nt + 2 * tig, i0 = wr0 + g8, i1 = i0 + 8;
-            *reinterpret_cast<uint32_t *>(urec + i0 * PV + col) = pack_bf16(U[nt][0], U[nt][1]);
-            *reinterpret_cast<uint32_t *>(urec + i1 * PV + col) = pack_bf16(U[nt][2], U[nt][3]);
-        }
-    }
-    if (tid < PC) {
-        const float gC = s.gam[PC - 1];
-        reinterpret_cast<float *>(rec + kRecRo)[tid] = expf(s.gam[tid]) * s.nq[tid] * a.scale;
-        reinterpret_cast<float *>(rec + kRecRd)[tid] = expf(gC - s.gam[tid]) * s.nk[tid];
-        if (tid == 0) reinterpret_cast<float *>(rec + kRecDc)[0] = expf(gC);
     }
 }
 
@@ -640,6 +292,352 @@ __device__ __forceinline__ void tc_stage(const sq_prefill_args &a, TcStage &st, 
             *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// prep_kernel: one 256-thread CTA per (chunk, value head): the chunk's WY/UT
+// transform.  Its bf16 products run on tcgen05 with fp32 accumulators in
+// tensor memory (128 columns; three CTAs per SM):
+//   [K; Q] K^T -> columns [0, 64), lanes 0-63 = G = K K^T, lanes 64-127 = Q K^T
+//   W^T = K^T Tw^T -> columns [0, 64)      (lane = key, column = token)
+//   U^T = V^T Tu^T -> columns [64, 128)    (lane = value, column = token)
+// q and k are staged as one 128-row 128-byte-swizzled tile (k rows 0-63, q
+// rows 64-127): K-major as the A operand of [K; Q] K^T and as its B operand
+// (the first 64 rows), and, being [token][key] with keys contiguous, the same
+// bytes are the MN-major A operand K^T.  T = (I + L)^-1 stays in fp32 (16x16
+// blocks: substitution on the diagonal, tf32 mma.sync below it); Tw and Tu go
+// into the q rows of the tile once the Gram product has read them, raw v into
+// the space of L once T is complete.  Waits on the MMAs are bounded: a CTA
+// that gives up sets SQ_STATUS_TIMEOUT and leaves after freeing its columns.
+// ---------------------------------------------------------------------------
+constexpr int kPrepCols = 128;
+
+struct PrepSmem {
+    unsigned char qk[32768];  // SW128, 128 rows x 128 keys: k rows 0-63, q rows 64-127; then Tw, Tu
+    union {
+        float l[PC][kLdF];       // L below the diagonal; the block products X_rc above it (block (c, r))
+        unsigned char v[16384];  // raw v [t][v], SW128 (MN-major A operand of V^T), once T is complete
+    } lv;
+    float t[PC][kLdF];  // T
+    float gam[PC];
+    float beta[PC];
+    float nq[PC];
+    float nk[PC];
+    float fw[PC];  // beta e^gam nk: column factors of Tw
+    uint64_t bar;  // tcgen05.commit of the MMAs (two phases)
+    uint32_t tmem_slot;
+    int abort_flag;
+};
+constexpr int kPrepSmemBytes = int(sizeof(PrepSmem)) + 1024;  // + alignment of the swizzled tiles
+constexpr int kTwOff = 8192, kTuOff = 16384 + 8192;             // q rows of key atoms 0 and 1: 64x64 K-major tiles
+
+__device__ __forceinline__ uint32_t idesc_bf16_ab(int n, int a_mn, int b_mn) {
+    return idesc_bf16(n, b_mn) | (uint32_t(a_mn) << 15);
+}
+
+__global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const int32_t *offsets,
+                                                      unsigned char *records) {
+    extern __shared__ unsigned char smem_raw[];
+    PrepSmem &s = *reinterpret_cast<PrepSmem *>(smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g8 = lane >> 2, tig = lane & 3;
+    const int H = a.heads, head = blockIdx.y, chunk = blockIdx.x;
+    if (chunk >= offsets[a.num_seqs]) return;
+    int lo = 0, hi = a.num_seqs - 1;  // the sequence: largest n with offsets[n] <= chunk
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (offsets[mid] <= chunk) lo = mid;
+        else hi = mid - 1;
+    }
+    const int2 range = seq_range(a, lo);
+    const int t0 = range.x + (chunk - offsets[lo]) * PC, n = min(PC, range.y - t0);
+    const int qh = head / (H / a.qk_heads);
+    unsigned char *rec = records + (int64_t(chunk) * H + head) * kRec;
+    unsigned char *tw = s.qk + kTwOff, *tu = s.qk + kTuOff;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" :: "r"(smem_addr(&s.tmem_slot)), "r"(kPrepCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+    }
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" :: "r"(smem_addr(&s.bar)));
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        s.abort_flag = 0;
+    }
+    // ---- raw q, k rows of the chunk (zero rows past the end), gates
+    {
+        const bf16 *qg = static_cast<const bf16 *>(a.q), *kg = static_cast<const bf16 *>(a.k);
+        for (int idx = tid; idx < 2 * PC * 16; idx += 256) {
+            const int which = idx >> 10, row = (idx >> 4) & 63, piece = idx & 15;
+            unsigned char *dst = s.qk + sw128(which == 0 ? PC + row : row, 8 * piece, 2 * PC);
+            if (row < n) {
+                const int64_t t = t0 + row;
+                const bf16 *src = which == 0 ? qg + t * a.q_stride + int64_t(qh) * PK : kg + t * a.k_stride + int64_t(qh) * PK;
+                cp16(dst, src + piece * 8);
+            } else {
+                *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+        if (tid < PC) {
+            const bool live = tid < n;
+            const int64_t gi = (int64_t(t0) + tid) * H + head;
+            s.gam[tid] = live ? a.g[gi] : 0.f;
+            s.beta[tid] = live ? a.beta[gi] : 0.f;
+        }
+        asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+    }
+    proxy_fence();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s.tmem_slot;
+    const uint32_t tlane = uint32_t(32 * (warp & 3)) << 16;  // this warp's TMEM lane quarter
+    const int cq = warp >> 2;                                // and column half of each 64-column accumulator
+    // ---- [K; Q] K^T on the tensor cores while the norms and the decay scan run
+    if (tid == 0) {
+        const uint32_t qk = smem_addr(s.qk), id = idesc_bf16(PC, 0);
+#pragma unroll
+        for (int ks = 0; ks < PK / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+            umma(tmem, sdesc(qk + off, 16, 1024), sdesc(qk + off, 16, 1024), id, ks > 0);
+        }
+        umma_commit(&s.bar);
+    }
+    // norms of the q and k rows (2 threads per row), cumulative log decay
+    {
+        const int row = (tid >> 1) & 63, half = tid & 1;
+        const int r = tid < 128 ? PC + row : row;
+        const unsigned char *base = s.qk + half * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(base + ((j ^ (r & 7)) << 4));
+            const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&w);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(h2[e]);
+                ss += f.x * f.x + f.y * f.y;
+            }
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        const float nrm = a.normalize ? rsqrtf(ss + 1e-6f) : 1.f;
+        if (half == 0) {
+            if (tid < 128) s.nq[row] = nrm;
+            else s.nk[row] = nrm;
+        }
+    }
+    if (warp == 0) {
+        const float x0 = s.gam[2 * lane], x1 = s.gam[2 * lane + 1];
+        float run = x0 + x1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, run, o);
+            if (lane >= o) run += y;
+        }
+        const float before = run - (x0 + x1);
+        __syncwarp();
+        s.gam[2 * lane] = before + x0;
+        s.gam[2 * lane + 1] = run;
+    }
+    __syncthreads();
+    if (tid < PC) s.fw[tid] = s.beta[tid] * expf(s.gam[tid]) * s.nk[tid];
+    if (!bar_wait(&s.bar, 0)) s.abort_flag = 1;
+    tc_fence_after();
+    // ---- L (fp32, from the G lanes) and P (bf16 into the record, from the Q K^T lanes)
+    {
+        const int r = 32 * (warp & 3) + lane, c0 = 32 * cq;
+        float x[32];
+        tmem_ld32(tmem + tlane + c0, x);
+        const int i = r & 63;
+        const float gi = s.gam[i];
+        if (r < PC) {
+            const float li = s.beta[i] * s.nk[i];
+            float *lrow = &s.lv.l[i][c0];
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+                float4 o;
+                float *op = &o.x;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = c0 + 4 * j4 + e;
+                    const float dec = j <= i ? __expf(gi - s.gam[j]) * s.nk[j] : 0.f;
+                    op[e] = j < i ? li * dec * x[4 * j4 + e] : 0.f;
+                }
+                *reinterpret_cast<float4 *>(lrow + 4 * j4) = o;
+            }
+        } else {
+            const float pi = s.nq[i] * a.scale;
+#pragma unroll
+            for (int j8 = 0; j8 < 4; ++j8) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float pv[2];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int j = c0 + 8 * j8 + 2 * e + h;
+                        const float dec = j <= i ? __expf(gi - s.gam[j]) * s.nk[j] : 0.f;
+                        pv[h] = pi * dec * x[8 * j8 + 2 * e + h];
+                    }
+                    w[e] = pack_bf16(pv[0], pv[1]);
+                }
+                *reinterpret_cast<uint4 *>(rec + kRecP + sw128(i, c0 + 8 * j8, PC)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- T = (I + L)^-1 in fp32: 16x16 diagonal blocks by substitution, then
+    // the blocks below them on tensor cores (tf32).  Each block of
+    // Tw = T diag(beta e^gam nk) and Tu = T diag(beta) (bf16, K-major tiles in
+    // the q rows) is written as soon as the block of T is final.
+    auto put_t = [&](int i, int j, float tv) {
+        const uint32_t o = sw128(i, j, PC);
+        *reinterpret_cast<bf16 *>(tw + o) = __float2bfloat16_rn(tv * s.fw[j]);
+        *reinterpret_cast<bf16 *>(tu + o) = __float2bfloat16_rn(tv * s.beta[j]);
+    };
+    if (warp < 4) {
+        if (lane < 16) {
+            const int b = 16 * warp, m = lane;
+            float t[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                float val = i == m ? 1.f : 0.f;
+#pragma unroll
+                for (int j = 0; j < i; ++j) val -= s.lv.l[b + i][b + j] * t[j];
+                t[i] = val;
+                s.t[b + i][b + m] = val;
+                put_t(b + i, b + m, val);
+            }
+        }
+    } else {
+        // zero the blocks of Tw and Tu above the diagonal
+        for (int e = tid - 128; e < 6 * 256; e += 128) {
+            const int blk = e >> 8, i = (e >> 4) & 15, m = e & 15;
+            const int r = blk < 3 ? 0 : blk < 5 ? 1 : 2;
+            const int c = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
+            const uint32_t o = sw128(16 * r + i, 16 * c + m, PC);
+            *reinterpret_cast<bf16 *>(tw + o) = __float2bfloat16_rn(0.f);
+            *reinterpret_cast<bf16 *>(tu + o) = __float2bfloat16_rn(0.f);
+        }
+    }
+    __syncthreads();
+    // Blocks below the diagonal as a blocked inverse in two stages:
+    //   A: T10 = -T11 (L10 T00) (warp 0) and T32 = -T33 (L32 T22) (warp 1);
+    //   B: T[2:4, 0:2] = -T[2:4, 2:4] (L[2:4, 0:2] T[0:2, 0:2]), one block per warp.
+    // The block products X are kept in free blocks above L's diagonal.
+    {
+        float (*L)[kLdF] = s.lv.l;
+        float (*T)[kLdF] = s.t;
+        auto above = [&](int r, int c) { return reinterpret_cast<float (*)[kLdF]>(&L[16 * r][16 * c]); };
+        auto finish = [&](int r, int c, const float (&Y)[2][4]) {  // T_rc = -Y, with its Tw and Tu blocks
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int i = 16 * r + g8 + 8 * (e >> 1), j = 16 * c + 8 * nt + 2 * tig + (e & 1);
+                    const float tv = -Y[nt][e];
+                    T[i][j] = tv;
+                    put_t(i, j, tv);
+                }
+            }
+        };
+        if (warp < 2) {
+            const int r = warp ? 3 : 1, c = r - 1;
+            float (*xb)[kLdF] = above(c, r);
+            float X[2][4] = {}, Y[2][4] = {};
+            mma_block16(X, L, 16 * r, 16 * c, T, 16 * c, 16 * c, g8, tig);
+            store_block16(X, xb, g8, tig);
+            __syncwarp();
+            mma_block16(Y, T, 16 * r, 16 * r, xb, 0, 0, g8, tig);
+            finish(r, c, Y);
+        }
+        __syncthreads();
+        if (warp < 4) {
+            const int i = 2 + (warp >> 1), j = warp & 1;
+            // X_mj = sum over m' = j..1 of L_{m m'} T_{m' j}, for m = 2 (and m = 3 in row 3)
+            float (*x2)[kLdF] = warp == 0 ? above(0, 1) : warp == 1 ? above(0, 2) : warp == 2 ? above(0, 3) : above(1, 3);
+            float (*x3)[kLdF] = warp == 2 ? above(1, 2) : above(2, 3);
+            float X[2][4] = {}, Y[2][4] = {};
+            for (int m = j; m < 2; ++m) mma_block16(X, L, 32, 16 * m, T, 16 * m, 16 * j, g8, tig);
+            store_block16(X, x2, g8, tig);
+            if (i == 3) {
+                float X3[2][4] = {};
+                for (int m = j; m < 2; ++m) mma_block16(X3, L, 48, 16 * m, T, 16 * m, 16 * j, g8, tig);
+                store_block16(X3, x3, g8, tig);
+            }
+            __syncwarp();
+            if (i == 2) {
+                mma_block16(Y, T, 32, 32, x2, 0, 0, g8, tig);  // T22 X_2j
+            } else {
+                mma_block16(Y, T, 48, 32, x2, 0, 0, g8, tig);  // T32 X_2j
+                mma_block16(Y, T, 48, 48, x3, 0, 0, g8, tig);  // + T33 X_3j
+            }
+            finish(i, j, Y);
+        }
+        __syncthreads();
+    }
+
+    // ---- raw v into the space of L (T is complete) while -W^T = K^T Tw^T runs
+    {
+        const bf16 *vg = static_cast<const bf16 *>(a.v);
+        for (int idx = tid; idx < PC * 16; idx += 256) {
+            const int row = idx >> 4, piece = idx & 15;
+            unsigned char *dst = s.lv.v + sw128_mn(row, 8 * piece, PC);
+            if (row < n) cp16(dst, vg + (int64_t(t0) + row) * a.v_stride + int64_t(head) * PV + piece * 8);
+            else *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    }
+    proxy_fence();  // Tw and Tu (generic stores) before the MMAs read them
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const bool run = !s.abort_flag;
+    const uint32_t id_t = idesc_bf16_ab(PC, 1, 0);  // A MN-major (k or v as [token][key]), B K-major (Tw, Tu)
+    if (run && tid == 0) {
+        const uint32_t qk = smem_addr(s.qk), b = smem_addr(tw);
+#pragma unroll
+        for (int ks = 0; ks < PC / 16; ++ks)
+            umma(tmem, sdesc(qk + ks * 2048, 16384, 1024), sdesc(b + ks * 32, 16, 1024), id_t, ks > 0);
+    }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    proxy_fence();
+    __syncthreads();
+    if (run && tid == 0) {
+        const uint32_t v = smem_addr(s.lv.v), b = smem_addr(tu);
+#pragma unroll
+        for (int ks = 0; ks < PC / 16; ++ks)
+            umma(tmem + 64, sdesc(v + ks * 2048, 8192, 1024), sdesc(b + ks * 32, 16, 1024), id_t, ks > 0);
+        umma_commit(&s.bar);
+    }
+    bool ok = run;
+    if (run && !bar_wait(&s.bar, 1)) ok = false;
+    tc_fence_after();
+    // ---- -W (bf16, K-major tile) and U (bf16 row-major) into the record
+    if (ok) {
+        const int r = 32 * (warp & 3) + lane, c0 = 32 * cq;  // r: key (W) and value (U); columns: tokens
+        float x[32];
+        tmem_ld32(tmem + tlane + c0, x);
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+            *reinterpret_cast<bf16 *>(rec + kRecW + sw128(c0 + e, r, PC)) = __float2bfloat16_rn(-x[e]);
+        tmem_ld32(tmem + tlane + 64 + c0, x);
+        bf16 *urec = reinterpret_cast<bf16 *>(rec + kRecU);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) urec[(c0 + e) * PV + r] = __float2bfloat16_rn(x[e]);
+    }
+    if (tid < PC) {
+        const float gC = s.gam[PC - 1];
+        reinterpret_cast<float *>(rec + kRecRo)[tid] = expf(s.gam[tid]) * s.nq[tid] * a.scale;
+        reinterpret_cast<float *>(rec + kRecRd)[tid] = expf(gC - s.gam[tid]) * s.nk[tid];
+        if (tid == 0) reinterpret_cast<float *>(rec + kRecDc)[0] = expf(gC);
+    }
+    if (!ok && tid == 0 && a.status) atomicOr(a.status, SQ_STATUS_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" :: "r"(tmem), "r"(kPrepCols));
 }
 
 __global__ void __launch_bounds__(512, 1) state_kernel(sq_prefill_args a, const int32_t *offsets,
@@ -858,7 +856,7 @@ extern "C" int32_t sq_gdn_prefill(const sq_prefill_args *args, sq_stream_t strea
     int32_t *offsets = static_cast<int32_t *>(a.workspace);
     unsigned char *records = static_cast<unsigned char *>(a.workspace) + sq::kOffsetsBytes(a.num_seqs);
     sq::offsets_kernel<<<1, 1024, 0, s>>>(a, offsets);
-    const int prep_smem = int(sizeof(sq::PrepSmem)), state_smem = int(sizeof(sq::TcSmem)) + 1024;
+    const int prep_smem = sq::kPrepSmemBytes, state_smem = int(sizeof(sq::TcSmem)) + 1024;
     if (cudaFuncSetAttribute(sq::prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) != cudaSuccess ||
         cudaFuncSetAttribute(sq::state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, state_smem) != cudaSuccess)
         return SQ_ERR_CUDA;
