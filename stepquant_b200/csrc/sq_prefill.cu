@@ -42,6 +42,7 @@ constexpr int kRecRd = kRecRo + PC * 4;       // e^(gam_C - gam) nk  fp32 [64]
 constexpr int kRecDc = kRecRd + PC * 4;       // e^gam_C             fp32 (16 bytes)
 constexpr int kRec = (kRecDc + 16 + 255) / 256 * 256;
 constexpr int kOffsetsBytes(int seqs) { return (4 * (seqs + 1) + 255) / 256 * 256; }
+constexpr int64_t kChunkTabBytes(int64_t chunks) { return (8 * chunks + 255) / 256 * 256; }
 
 __device__ __forceinline__ unsigned smem_addr(const void *p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
 
@@ -87,8 +88,9 @@ __device__ __forceinline__ int2 seq_range(const sq_prefill_args &a, int n) {
     return make_int2(b, max(b, min(a.cu_seqlens[n + 1], a.tokens)));
 }
 
-// offsets[n] = number of chunks of the sequences before n (offsets[seqs] = all).
-__global__ void __launch_bounds__(1024) offsets_kernel(sq_prefill_args a, int32_t *offsets) {
+// offsets[n] = number of chunks of the sequences before n (offsets[seqs] = all),
+// and for every chunk its first token and length (chunk_tab).
+__global__ void __launch_bounds__(1024) offsets_kernel(sq_prefill_args a, int32_t *offsets, int2 *chunk_tab) {
     __shared__ int warp_total[32];
     const int per = (a.num_seqs + 1023) / 1024;
     const int first = threadIdx.x * per, last = min(a.num_seqs, first + per);
@@ -120,7 +122,7 @@ __global__ void __launch_bounds__(1024) offsets_kernel(sq_prefill_args a, int32_
     for (int n = first; n < last; ++n) {
         offsets[n] = before;
         const int2 r = seq_range(a, n);
-        before += (r.y - r.x + PC - 1) / PC;
+        for (int t = r.x; t < r.y; t += PC) chunk_tab[before++] = make_int2(t, min(PC, r.y - t));
     }
     if (threadIdx.x == 0) offsets[a.num_seqs] = warp_total[31];
 }
@@ -336,21 +338,18 @@ __device__ __forceinline__ uint32_t idesc_bf16_ab(int n, int a_mn, int b_mn) {
 }
 
 __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const int32_t *offsets,
-                                                      unsigned char *records) {
+                                                      const int2 *chunk_tab, unsigned char *records) {
     extern __shared__ unsigned char smem_raw[];
     PrepSmem &s = *reinterpret_cast<PrepSmem *>(smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g8 = lane >> 2, tig = lane & 3;
-    const int H = a.heads, head = blockIdx.y, chunk = blockIdx.x;
-    if (chunk >= offsets[a.num_seqs]) return;
-    int lo = 0, hi = a.num_seqs - 1;  // the sequence: largest n with offsets[n] <= chunk
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (offsets[mid] <= chunk) lo = mid;
-        else hi = mid - 1;
-    }
-    const int2 range = seq_range(a, lo);
-    const int t0 = range.x + (chunk - offsets[lo]) * PC, n = min(PC, range.y - t0);
+    // CTAs in (chunk, head) order: the value heads of one qk head are
+    // neighbours, so the second read of the chunk's q and k rows hits L2.
+    const int H = a.heads, chunk = blockIdx.x / H, head = blockIdx.x - chunk * H;
+    const int total = offsets[a.num_seqs];
+    const int2 ci = chunk_tab[chunk];  // read beside the total (entries past it are unset)
+    if (chunk >= total) return;
+    const int t0 = ci.x, n = ci.y;
     const int qh = head / (H / a.qk_heads);
     unsigned char *rec = records + (int64_t(chunk) * H + head) * kRec;
     unsigned char *tw = s.qk + kTwOff, *tu = s.qk + kTuOff;
@@ -443,45 +442,40 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     if (tid < PC) s.fw[tid] = s.beta[tid] * expf(s.gam[tid]) * s.nk[tid];
     if (!bar_wait(&s.bar, 0)) s.abort_flag = 1;
     tc_fence_after();
-    // ---- L (fp32, from the G lanes) and P (bf16 into the record, from the Q K^T lanes)
+    // ---- L (fp32, from the G lanes) and P (bf16 into the record, from the Q K^T lanes).
+    // A warp covers rows 32 (w % 2) .. +31 and columns 32 (w / 4) .. +31: the
+    // quarter above the diagonal (rows 0-31, columns 32-63) is zero in L and P.
     {
-        const int r = 32 * (warp & 3) + lane, c0 = 32 * cq;
+        const int r = 32 * (warp & 3) + lane, c0 = 32 * cq, i = r & 63;
+        const bool zero = c0 > (i | 31);  // warp-uniform
         float x[32];
-        tmem_ld32(tmem + tlane + c0, x);
-        const int i = r & 63;
+        if (!zero) tmem_ld32(tmem + tlane + c0, x);
         const float gi = s.gam[i];
+        const float fi = r < PC ? s.beta[i] * s.nk[i] : s.nq[i] * a.scale;
+        float y[32];  // L (j < i) or P (j <= i)
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 g4 = *reinterpret_cast<const float4 *>(&s.gam[c0 + 4 * j4]);
+            const float4 n4 = *reinterpret_cast<const float4 *>(&s.nk[c0 + 4 * j4]);
+            const float gj[4] = {g4.x, g4.y, g4.z, g4.w}, nkj[4] = {n4.x, n4.y, n4.z, n4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = c0 + 4 * j4 + e;
+                const bool keep = !zero && (r < PC ? j < i : j <= i);
+                y[4 * j4 + e] = keep ? fi * (__expf(gi - gj[e]) * nkj[e]) * x[4 * j4 + e] : 0.f;
+            }
+        }
         if (r < PC) {
-            const float li = s.beta[i] * s.nk[i];
             float *lrow = &s.lv.l[i][c0];
 #pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-                float4 o;
-                float *op = &o.x;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int j = c0 + 4 * j4 + e;
-                    const float dec = j <= i ? __expf(gi - s.gam[j]) * s.nk[j] : 0.f;
-                    op[e] = j < i ? li * dec * x[4 * j4 + e] : 0.f;
-                }
-                *reinterpret_cast<float4 *>(lrow + 4 * j4) = o;
-            }
+            for (int j4 = 0; j4 < 8; ++j4)
+                *reinterpret_cast<float4 *>(lrow + 4 * j4) = make_float4(y[4 * j4], y[4 * j4 + 1], y[4 * j4 + 2], y[4 * j4 + 3]);
         } else {
-            const float pi = s.nq[i] * a.scale;
 #pragma unroll
             for (int j8 = 0; j8 < 4; ++j8) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    float pv[2];
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int j = c0 + 8 * j8 + 2 * e + h;
-                        const float dec = j <= i ? __expf(gi - s.gam[j]) * s.nk[j] : 0.f;
-                        pv[h] = pi * dec * x[8 * j8 + 2 * e + h];
-                    }
-                    w[e] = pack_bf16(pv[0], pv[1]);
-                }
-                *reinterpret_cast<uint4 *>(rec + kRecP + sw128(i, c0 + 8 * j8, PC)) = make_uint4(w[0], w[1], w[2], w[3]);
+                const float *yy = y + 8 * j8;
+                *reinterpret_cast<uint4 *>(rec + kRecP + sw128(i, c0 + 8 * j8, PC)) =
+                    make_uint4(pack_bf16(yy[0], yy[1]), pack_bf16(yy[2], yy[3]), pack_bf16(yy[4], yy[5]), pack_bf16(yy[6], yy[7]));
             }
         }
     }
@@ -834,7 +828,8 @@ int64_t max_chunks(int64_t tokens, int64_t seqs) { return (tokens + PC - 1) / PC
 
 extern "C" int64_t sq_gdn_prefill_workspace_bytes(int32_t tokens, int32_t num_seqs, int32_t heads) {
     if (tokens < 0 || num_seqs < 0 || heads < 1) return -1;
-    return sq::kOffsetsBytes(num_seqs) + sq::max_chunks(tokens, num_seqs) * heads * int64_t(sq::kRec);
+    const int64_t chunks = sq::max_chunks(tokens, num_seqs);
+    return sq::kOffsetsBytes(num_seqs) + sq::kChunkTabBytes(chunks) + chunks * heads * int64_t(sq::kRec);
 }
 
 extern "C" int32_t sq_gdn_prefill(const sq_prefill_args *args, sq_stream_t stream) {
@@ -854,15 +849,17 @@ extern "C" int32_t sq_gdn_prefill(const sq_prefill_args *args, sq_stream_t strea
         return SQ_ERR_SHAPE;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     int32_t *offsets = static_cast<int32_t *>(a.workspace);
-    unsigned char *records = static_cast<unsigned char *>(a.workspace) + sq::kOffsetsBytes(a.num_seqs);
-    sq::offsets_kernel<<<1, 1024, 0, s>>>(a, offsets);
+    const int64_t chunks = sq::max_chunks(a.tokens, a.num_seqs);
+    if (chunks > 0x7fffffff) return SQ_ERR_SHAPE;
+    int2 *chunk_tab = reinterpret_cast<int2 *>(static_cast<unsigned char *>(a.workspace) + sq::kOffsetsBytes(a.num_seqs));
+    unsigned char *records = reinterpret_cast<unsigned char *>(chunk_tab) + sq::kChunkTabBytes(chunks);
+    sq::offsets_kernel<<<1, 1024, 0, s>>>(a, offsets, chunk_tab);
     const int prep_smem = sq::kPrepSmemBytes, state_smem = int(sizeof(sq::TcSmem)) + 1024;
     if (cudaFuncSetAttribute(sq::prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) != cudaSuccess ||
         cudaFuncSetAttribute(sq::state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, state_smem) != cudaSuccess)
         return SQ_ERR_CUDA;
-    const int64_t chunks = sq::max_chunks(a.tokens, a.num_seqs);
-    if (chunks > 0x7fffffff) return SQ_ERR_SHAPE;
-    if (chunks > 0) sq::prep_kernel<<<dim3(unsigned(chunks), unsigned(a.heads)), 256, prep_smem, s>>>(a, offsets, records);
+    if (chunks * a.heads > 0x7fffffff) return SQ_ERR_SHAPE;
+    if (chunks > 0) sq::prep_kernel<<<unsigned(chunks * a.heads), 256, prep_smem, s>>>(a, offsets, chunk_tab, records);
     sq::state_kernel<<<a.num_seqs * a.heads, 512, state_smem, s>>>(a, offsets, records);
     return cudaGetLastError() == cudaSuccess ? SQ_OK : SQ_ERR_CUDA;
 }
