@@ -483,37 +483,18 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     __syncthreads();
 
     // ---- T = (I + L)^-1 in fp32: 16x16 diagonal blocks by substitution, then
-    // the blocks below them on tensor cores (tf32).  Each block of
-    // Tw = T diag(beta e^gam nk) and Tu = T diag(beta) (bf16, K-major tiles in
-    // the q rows) is written as soon as the block of T is final.
-    auto put_t = [&](int i, int j, float tv) {
-        const uint32_t o = sw128(i, j, PC);
-        *reinterpret_cast<bf16 *>(tw + o) = __float2bfloat16_rn(tv * s.fw[j]);
-        *reinterpret_cast<bf16 *>(tu + o) = __float2bfloat16_rn(tv * s.beta[j]);
-    };
-    if (warp < 4) {
-        if (lane < 16) {
-            const int b = 16 * warp, m = lane;
-            float t[16];
+    // the blocks below them on tensor cores (tf32); then Tw = T diag(beta e^gam nk)
+    // and Tu = T diag(beta) in bf16 (K-major tiles in the q rows).
+    if (warp < 4 && lane < 16) {
+        const int b = 16 * warp, m = lane;
+        float t[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                float val = i == m ? 1.f : 0.f;
+        for (int i = 0; i < 16; ++i) {
+            float val = i == m ? 1.f : 0.f;
 #pragma unroll
-                for (int j = 0; j < i; ++j) val -= s.lv.l[b + i][b + j] * t[j];
-                t[i] = val;
-                s.t[b + i][b + m] = val;
-                put_t(b + i, b + m, val);
-            }
-        }
-    } else {
-        // zero the blocks of Tw and Tu above the diagonal
-        for (int e = tid - 128; e < 6 * 256; e += 128) {
-            const int blk = e >> 8, i = (e >> 4) & 15, m = e & 15;
-            const int r = blk < 3 ? 0 : blk < 5 ? 1 : 2;
-            const int c = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
-            const uint32_t o = sw128(16 * r + i, 16 * c + m, PC);
-            *reinterpret_cast<bf16 *>(tw + o) = __float2bfloat16_rn(0.f);
-            *reinterpret_cast<bf16 *>(tu + o) = __float2bfloat16_rn(0.f);
+            for (int j = 0; j < i; ++j) val -= s.lv.l[b + i][b + j] * t[j];
+            t[i] = val;
+            s.t[b + i][b + m] = val;
         }
     }
     __syncthreads();
@@ -531,9 +512,7 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int i = 16 * r + g8 + 8 * (e >> 1), j = 16 * c + 8 * nt + 2 * tig + (e & 1);
-                    const float tv = -Y[nt][e];
-                    T[i][j] = tv;
-                    put_t(i, j, tv);
+                    T[i][j] = -Y[nt][e];
                 }
             }
         };
@@ -571,6 +550,23 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
             finish(i, j, Y);
         }
         __syncthreads();
+    }
+
+    // Tw and Tu, eight columns per store (blocks above the diagonal are zero)
+    for (int idx = tid; idx < PC * 8; idx += 256) {
+        const int i = idx >> 3, j0 = 8 * (idx & 7);
+        uint4 w = make_uint4(0u, 0u, 0u, 0u), u = w;
+        if ((j0 >> 4) <= (i >> 4)) {
+            const float4 t0 = *reinterpret_cast<const float4 *>(&s.t[i][j0]), t1 = *reinterpret_cast<const float4 *>(&s.t[i][j0 + 4]);
+            const float4 f0 = *reinterpret_cast<const float4 *>(&s.fw[j0]), f1 = *reinterpret_cast<const float4 *>(&s.fw[j0 + 4]);
+            const float4 b0 = *reinterpret_cast<const float4 *>(&s.beta[j0]), b1 = *reinterpret_cast<const float4 *>(&s.beta[j0 + 4]);
+            w = make_uint4(pack_bf16(t0.x * f0.x, t0.y * f0.y), pack_bf16(t0.z * f0.z, t0.w * f0.w),
+                           pack_bf16(t1.x * f1.x, t1.y * f1.y), pack_bf16(t1.z * f1.z, t1.w * f1.w));
+            u = make_uint4(pack_bf16(t0.x * b0.x, t0.y * b0.y), pack_bf16(t0.z * b0.z, t0.w * b0.w),
+                           pack_bf16(t1.x * b1.x, t1.y * b1.y), pack_bf16(t1.z * b1.z, t1.w * b1.w));
+        }
+        *reinterpret_cast<uint4 *>(tw + sw128(i, j0, PC)) = w;
+        *reinterpret_cast<uint4 *>(tu + sw128(i, j0, PC)) = u;
     }
 
     // ---- raw v into the space of L (T is complete) while -W^T = K^T Tw^T runs
