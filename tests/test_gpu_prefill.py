@@ -67,6 +67,29 @@ def test_prefill_variable_lengths_gqa_against_oracle(decay_scale):
     assert torch.equal(final[1].cpu(), init[1])  # the empty sequence keeps its state
 
 
+def test_prefill_many_short_sequences():
+    """More sequences than the offsets kernel has threads (1,300 of 0-70 tokens,
+    many empty): every chunk finds its sequence and first token in the
+    per-chunk table, and empty sequences keep their initial state."""
+    from stepquant_b200.kernels.prefill import chunk_gated_delta_rule
+    gen = torch.Generator().manual_seed(11)
+    heads, qk, seqs = 2, 1, 1300
+    lengths = torch.randint(0, 4, (seqs,), generator=gen)
+    lengths[::97] = 70  # a few sequences longer than one chunk
+    cu = [0] + torch.cumsum(lengths, 0).tolist()
+    q, k, v, g, beta = _inputs(cu[-1], heads, qk, gen, 1.0)
+    init = torch.randn(seqs, heads, 128, 128, generator=gen) * 0.2
+    out, final = chunk_gated_delta_rule(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), initial_state=init.cuda(),
+                                        cu_seqlens=torch.tensor(cu, dtype=torch.int32).cuda())
+    o_ref, f_ref = O.prefill_sequential(q.float().numpy(), k.float().numpy(), v.float().numpy(), g.numpy(),
+                                        beta.numpy(), cu, init.numpy())
+    torch.cuda.synchronize()
+    assert _rel(final.cpu().numpy(), f_ref) < TOL
+    assert _rel(out.float().cpu().numpy(), o_ref) < TOL
+    empty = (lengths == 0).nonzero().flatten()
+    assert len(empty) > 0 and torch.equal(final[empty].cpu(), init[empty])
+
+
 def test_prefill_continuation_and_pool_extend():
     """A prompt split in two passes (state carried through the pool) equals one pass."""
     from stepquant_b200 import QuantizationPlan
