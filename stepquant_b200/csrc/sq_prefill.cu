@@ -444,38 +444,45 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     tc_fence_after();
     // ---- L (fp32, from the G lanes) and P (bf16 into the record, from the Q K^T lanes).
     // A warp covers rows 32 (w % 2) .. +31 and columns 32 (w / 4) .. +31: the
-    // quarter above the diagonal (rows 0-31, columns 32-63) is zero in L and P.
+    // quarter above the diagonal (rows 0-31, columns 32-63) is zero in P and
+    // never read in L (the inverse reads L below the diagonal only).
     {
-        const int r = 32 * (warp & 3) + lane, c0 = 32 * cq, i = r & 63;
-        const bool zero = c0 > (i | 31);  // warp-uniform
-        float x[32];
-        if (!zero) tmem_ld32(tmem + tlane + c0, x);
+        const int r = 32 * (warp & 3) + lane, i = r & 63;
+        const bool zero = 32 * cq > (i | 31);  // warp-uniform; L is not read there, P is written as zeros
         const float gi = s.gam[i];
         const float fi = r < PC ? s.beta[i] * s.nk[i] : s.nq[i] * a.scale;
-        float y[32];  // L (j < i) or P (j <= i)
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+            const int c0 = 32 * cq + 16 * half;
+            float x[16], y[16];  // y: L (j < i) or P (j <= i)
+            if (!zero) tmem_ld16(tmem + tlane + c0, x);
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-            const float4 g4 = *reinterpret_cast<const float4 *>(&s.gam[c0 + 4 * j4]);
-            const float4 n4 = *reinterpret_cast<const float4 *>(&s.nk[c0 + 4 * j4]);
-            const float gj[4] = {g4.x, g4.y, g4.z, g4.w}, nkj[4] = {n4.x, n4.y, n4.z, n4.w};
+            for (int j4 = 0; j4 < 4; ++j4) {
+                const float4 g4 = *reinterpret_cast<const float4 *>(&s.gam[c0 + 4 * j4]);
+                const float4 n4 = *reinterpret_cast<const float4 *>(&s.nk[c0 + 4 * j4]);
+                const float gj[4] = {g4.x, g4.y, g4.z, g4.w}, nkj[4] = {n4.x, n4.y, n4.z, n4.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = c0 + 4 * j4 + e;
-                const bool keep = !zero && (r < PC ? j < i : j <= i);
-                y[4 * j4 + e] = keep ? fi * (__expf(gi - gj[e]) * nkj[e]) * x[4 * j4 + e] : 0.f;
+                for (int e = 0; e < 4; ++e) {
+                    const int j = c0 + 4 * j4 + e;
+                    const bool keep = !zero && (r < PC ? j < i : j <= i);
+                    y[4 * j4 + e] = keep ? fi * (__expf(gi - gj[e]) * nkj[e]) * x[4 * j4 + e] : 0.f;
+                }
             }
-        }
-        if (r < PC) {
-            float *lrow = &s.lv.l[i][c0];
+            if (r < PC) {
+                if (!zero) {
+                    float *lrow = &s.lv.l[i][c0];
 #pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4)
-                *reinterpret_cast<float4 *>(lrow + 4 * j4) = make_float4(y[4 * j4], y[4 * j4 + 1], y[4 * j4 + 2], y[4 * j4 + 3]);
-        } else {
+                    for (int j4 = 0; j4 < 4; ++j4)
+                        *reinterpret_cast<float4 *>(lrow + 4 * j4) =
+                            make_float4(y[4 * j4], y[4 * j4 + 1], y[4 * j4 + 2], y[4 * j4 + 3]);
+                }
+            } else {
 #pragma unroll
-            for (int j8 = 0; j8 < 4; ++j8) {
-                const float *yy = y + 8 * j8;
-                *reinterpret_cast<uint4 *>(rec + kRecP + sw128(i, c0 + 8 * j8, PC)) =
-                    make_uint4(pack_bf16(yy[0], yy[1]), pack_bf16(yy[2], yy[3]), pack_bf16(yy[4], yy[5]), pack_bf16(yy[6], yy[7]));
+                for (int j8 = 0; j8 < 2; ++j8) {
+                    const float *yy = y + 8 * j8;
+                    *reinterpret_cast<uint4 *>(rec + kRecP + sw128(i, c0 + 8 * j8, PC)) =
+                        make_uint4(pack_bf16(yy[0], yy[1]), pack_bf16(yy[2], yy[3]), pack_bf16(yy[4], yy[5]), pack_bf16(yy[6], yy[7]));
+                }
             }
         }
     }
