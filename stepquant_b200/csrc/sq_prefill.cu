@@ -393,7 +393,9 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     const uint32_t tlane = uint32_t(32 * (warp & 3)) << 16;  // this warp's TMEM lane quarter
     const int cq = warp >> 2;                                // and column half of each 64-column accumulator
     // ---- [K; Q] K^T on the tensor cores while the norms and the decay scan run
-    if (tid == 0) {
+    // (issued from the last warp: warp 0 runs the scan)
+    constexpr int kIssuer = 224;
+    if (tid == kIssuer) {
         const uint32_t qk = smem_addr(s.qk), id = idesc_bf16(PC, 0);
 #pragma unroll
         for (int ks = 0; ks < PK / 16; ++ks) {
@@ -593,7 +595,7 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     tc_fence_after();
     const bool run = !s.abort_flag;
     const uint32_t id_t = idesc_bf16_ab(PC, 1, 0);  // A MN-major (k or v as [token][key]), B K-major (Tw, Tu)
-    if (run && tid == 0) {
+    if (run && tid == kIssuer) {
         const uint32_t qk = smem_addr(s.qk), b = smem_addr(tw);
 #pragma unroll
         for (int ks = 0; ks < PC / 16; ++ks)
@@ -602,7 +604,7 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     proxy_fence();
     __syncthreads();
-    if (run && tid == 0) {
+    if (run && tid == kIssuer) {
         const uint32_t v = smem_addr(s.lv.v), b = smem_addr(tu);
 #pragma unroll
         for (int ks = 0; ks < PC / 16; ++ks)
