@@ -343,15 +343,14 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     PrepSmem &s = *reinterpret_cast<PrepSmem *>(smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g8 = lane >> 2, tig = lane & 3;
-    // CTAs in (chunk, head) order: the value heads of one qk head are
-    // neighbours, so the second read of the chunk's q and k rows hits L2.
-    const int H = a.heads, chunk = blockIdx.x / H, head = blockIdx.x - chunk * H;
+    // One CTA per (chunk, qk head): q, k, their norms and [K; Q] K^T serve
+    // the qk head's R = H / HK value heads, which the CTA takes in turn.
+    const int H = a.heads, HK = a.qk_heads, R = H / HK;
+    const int chunk = blockIdx.x / HK, qh = blockIdx.x - chunk * HK;
     const int total = offsets[a.num_seqs];
     const int2 ci = chunk_tab[chunk];  // read beside the total (entries past it are unset)
     if (chunk >= total) return;
     const int t0 = ci.x, n = ci.y;
-    const int qh = head / (H / a.qk_heads);
-    unsigned char *rec = records + (int64_t(chunk) * H + head) * kRec;
     unsigned char *tw = s.qk + kTwOff, *tu = s.qk + kTuOff;
 
     if (warp == 0) {
@@ -379,7 +378,7 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
         }
         if (tid < PC) {
             const bool live = tid < n;
-            const int64_t gi = (int64_t(t0) + tid) * H + head;
+            const int64_t gi = (int64_t(t0) + tid) * H + qh * R;
             s.gam[tid] = live ? a.g[gi] : 0.f;
             s.beta[tid] = live ? a.beta[gi] : 0.f;
         }
@@ -427,6 +426,17 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
             else s.nk[row] = nrm;
         }
     }
+    uint32_t phase = 0;  // completed phases of s.bar: [K; Q] K^T, then W^T and U^T of each head
+#pragma unroll 1
+    for (int hr = 0; hr < R; ++hr) {
+    const int head = qh * R + hr;
+    unsigned char *rec = records + (int64_t(chunk) * H + head) * kRec;
+    float g_next = 0.f, b_next = 0.f;  // the next head's gates, loaded while this one is formed
+    if (hr + 1 < R && tid < n) {
+        const int64_t gi = (int64_t(t0) + tid) * H + head + 1;
+        g_next = a.g[gi];
+        b_next = a.beta[gi];
+    }
     if (warp == 0) {
         const float x0 = s.gam[2 * lane], x1 = s.gam[2 * lane + 1];
         float run = x0 + x1;
@@ -442,7 +452,10 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     }
     __syncthreads();
     if (tid < PC) s.fw[tid] = s.beta[tid] * expf(s.gam[tid]) * s.nk[tid];
-    if (!bar_wait(&s.bar, 0)) s.abort_flag = 1;
+    if (hr == 0) {
+        if (!bar_wait(&s.bar, 0)) s.abort_flag = 1;
+        phase = 1;
+    }
     tc_fence_after();
     // ---- L (fp32, from the G lanes) and P (bf16 into the record, from the Q K^T lanes).
     // A warp covers rows 32 (w % 2) .. +31 and columns 32 (w / 4) .. +31: the
@@ -595,15 +608,30 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     tc_fence_after();
     const bool run = !s.abort_flag;
     const uint32_t id_t = idesc_bf16_ab(PC, 1, 0);  // A MN-major (k or v as [token][key]), B K-major (Tw, Tu)
+    // W^T, then U^T, in columns [64, 128): [K; Q] K^T stays in [0, 64) for the next head.
     if (run && tid == kIssuer) {
         const uint32_t qk = smem_addr(s.qk), b = smem_addr(tw);
 #pragma unroll
         for (int ks = 0; ks < PC / 16; ++ks)
-            umma(tmem, sdesc(qk + ks * 2048, 16384, 1024), sdesc(b + ks * 32, 16, 1024), id_t, ks > 0);
+            umma(tmem + 64, sdesc(qk + ks * 2048, 16384, 1024), sdesc(b + ks * 32, 16, 1024), id_t, ks > 0);
+        umma_commit(&s.bar);
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     proxy_fence();
-    __syncthreads();
+    if (run && !bar_wait(&s.bar, phase & 1)) s.abort_flag = 1;
+    ++phase;
+    tc_fence_after();
+    const int r = 32 * (warp & 3) + lane, c0 = 32 * cq;  // r: key (W) and value (U); columns: tokens
+    if (run) {  // -W (bf16, K-major tile) into the record
+        float x[32];
+        tmem_ld32(tmem + tlane + 64 + c0, x);
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+            *reinterpret_cast<bf16 *>(rec + kRecW + sw128(c0 + e, r, PC)) = __float2bfloat16_rn(-x[e]);
+    }
+    tc_fence_before();
+    __syncthreads();  // W^T is read out; v (cp.async) is visible
+    tc_fence_after();
     if (run && tid == kIssuer) {
         const uint32_t v = smem_addr(s.lv.v), b = smem_addr(tu);
 #pragma unroll
@@ -611,17 +639,11 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
             umma(tmem + 64, sdesc(v + ks * 2048, 8192, 1024), sdesc(b + ks * 32, 16, 1024), id_t, ks > 0);
         umma_commit(&s.bar);
     }
-    bool ok = run;
-    if (run && !bar_wait(&s.bar, 1)) ok = false;
+    if (run && !bar_wait(&s.bar, phase & 1)) s.abort_flag = 1;
+    ++phase;
     tc_fence_after();
-    // ---- -W (bf16, K-major tile) and U (bf16 row-major) into the record
-    if (ok) {
-        const int r = 32 * (warp & 3) + lane, c0 = 32 * cq;  // r: key (W) and value (U); columns: tokens
+    if (run) {  // U (bf16 row-major) into the record
         float x[32];
-        tmem_ld32(tmem + tlane + c0, x);
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-            *reinterpret_cast<bf16 *>(rec + kRecW + sw128(c0 + e, r, PC)) = __float2bfloat16_rn(-x[e]);
         tmem_ld32(tmem + tlane + 64 + c0, x);
         bf16 *urec = reinterpret_cast<bf16 *>(rec + kRecU);
 #pragma unroll
@@ -633,7 +655,16 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
         reinterpret_cast<float *>(rec + kRecRd)[tid] = expf(gC - s.gam[tid]) * s.nk[tid];
         if (tid == 0) reinterpret_cast<float *>(rec + kRecDc)[0] = expf(gC);
     }
-    if (!ok && tid == 0 && a.status) atomicOr(a.status, SQ_STATUS_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();  // every read of this head's gates, L, T and tiles is done
+    tc_fence_after();
+    if (hr + 1 < R && tid < PC) {
+        s.gam[tid] = g_next;
+        s.beta[tid] = b_next;
+    }
+    __syncthreads();
+    }  // value heads of the group
+    if (s.abort_flag && tid == 0 && a.status) atomicOr(a.status, SQ_STATUS_TIMEOUT);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" :: "r"(tmem), "r"(kPrepCols));
@@ -863,8 +894,8 @@ extern "C" int32_t sq_gdn_prefill(const sq_prefill_args *args, sq_stream_t strea
     if (cudaFuncSetAttribute(sq::prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) != cudaSuccess ||
         cudaFuncSetAttribute(sq::state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, state_smem) != cudaSuccess)
         return SQ_ERR_CUDA;
-    if (chunks * a.heads > 0x7fffffff) return SQ_ERR_SHAPE;
-    if (chunks > 0) sq::prep_kernel<<<unsigned(chunks * a.heads), 256, prep_smem, s>>>(a, offsets, chunk_tab, records);
+    if (chunks * a.qk_heads > 0x7fffffff) return SQ_ERR_SHAPE;
+    if (chunks > 0) sq::prep_kernel<<<unsigned(chunks * a.qk_heads), 256, prep_smem, s>>>(a, offsets, chunk_tab, records);
     sq::state_kernel<<<a.num_seqs * a.heads, 512, state_smem, s>>>(a, offsets, records);
     return cudaGetLastError() == cudaSuccess ? SQ_OK : SQ_ERR_CUDA;
 }
