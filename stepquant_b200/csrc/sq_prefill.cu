@@ -431,12 +431,6 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     for (int hr = 0; hr < R; ++hr) {
     const int head = qh * R + hr;
     unsigned char *rec = records + (int64_t(chunk) * H + head) * kRec;
-    float g_next = 0.f, b_next = 0.f;  // the next head's gates, loaded while this one is formed
-    if (hr + 1 < R && tid < n) {
-        const int64_t gi = (int64_t(t0) + tid) * H + head + 1;
-        g_next = a.g[gi];
-        b_next = a.beta[gi];
-    }
     if (warp == 0) {
         const float x0 = s.gam[2 * lane], x1 = s.gam[2 * lane + 1];
         float run = x0 + x1;
@@ -607,6 +601,12 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     __syncthreads();
     tc_fence_after();
     const bool run = !s.abort_flag;
+    float g_next = 0.f, b_next = 0.f;  // the next head's gates, loaded while W and U are formed
+    if (hr + 1 < R && tid < n) {
+        const int64_t gi = (int64_t(t0) + tid) * H + head + 1;
+        g_next = a.g[gi];
+        b_next = a.beta[gi];
+    }
     const uint32_t id_t = idesc_bf16_ab(PC, 1, 0);  // A MN-major (k or v as [token][key]), B K-major (Tw, Tu)
     // W^T, then U^T, in columns [64, 128): [K; Q] K^T stays in [0, 64) for the next head.
     if (run && tid == kIssuer) {
@@ -623,11 +623,14 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     tc_fence_after();
     const int r = 32 * (warp & 3) + lane, c0 = 32 * cq;  // r: key (W) and value (U); columns: tokens
     if (run) {  // -W (bf16, K-major tile) into the record
-        float x[32];
-        tmem_ld32(tmem + tlane + 64 + c0, x);
+#pragma unroll 1
+        for (int h = 0; h < 32; h += 16) {
+            float x[16];
+            tmem_ld16(tmem + tlane + 64 + c0 + h, x);
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-            *reinterpret_cast<bf16 *>(rec + kRecW + sw128(c0 + e, r, PC)) = __float2bfloat16_rn(-x[e]);
+            for (int e = 0; e < 16; ++e)
+                *reinterpret_cast<bf16 *>(rec + kRecW + sw128(c0 + h + e, r, PC)) = __float2bfloat16_rn(-x[e]);
+        }
     }
     tc_fence_before();
     __syncthreads();  // W^T is read out; v (cp.async) is visible
@@ -643,11 +646,14 @@ __global__ void __launch_bounds__(256, 3) prep_kernel(sq_prefill_args a, const i
     ++phase;
     tc_fence_after();
     if (run) {  // U (bf16 row-major) into the record
-        float x[32];
-        tmem_ld32(tmem + tlane + 64 + c0, x);
         bf16 *urec = reinterpret_cast<bf16 *>(rec + kRecU);
+#pragma unroll 1
+        for (int h = 0; h < 32; h += 16) {
+            float x[16];
+            tmem_ld16(tmem + tlane + 64 + c0 + h, x);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) urec[(c0 + e) * PV + r] = __float2bfloat16_rn(x[e]);
+            for (int e = 0; e < 16; ++e) urec[(c0 + h + e) * PV + r] = __float2bfloat16_rn(x[e]);
+        }
     }
     if (tid < PC) {
         const float gC = s.gam[PC - 1];
