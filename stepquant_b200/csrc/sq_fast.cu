@@ -552,11 +552,10 @@ struct WorkItem {
     bool active;  // 0 < slot < num_slots
 };
 
-__device__ __forceinline__ WorkItem describe(const TileParams &p, const FastSmem &s, int item, long long slot) {
+__device__ __forceinline__ WorkItem describe(const TileParams &p, const FastSmem &s, int req, int head, long long slot) {
     WorkItem it;
-    const int H = p.plan.heads;
-    it.req = item / H;
-    it.head = item - it.req * H;
+    it.req = req;
+    it.head = head;
     it.slot = slot;
     it.width = s.head[it.head].width;
     it.fast = it.width == 4 || it.width == 6 || it.width == 8;
@@ -876,9 +875,14 @@ __global__ void __launch_bounds__(kThreads, 3) fast_kernel(TileParams p, int ite
         s.head[h] = hi;
     }
     if (tm_mode<MODE>() && c.warp == 0) tm_alloc(&s.tmem_slot, kTmCols);
+    // (request, head) of item = request * H + head, advanced by stride = sreq * H + shead
+    // each round without a division.
+    const int sreq = stride / H, shead = stride - sreq * H;
+    int req = item / H, head = item - req * H;
+    auto next_req = [&](int r, int h) { return r + sreq + (h + shead >= H); };
     if (c.tid == 0) {
-        cp_async8(&s.slot_ring[0], p.slots + item / H);
-        if (item + stride < items) cp_async8(&s.slot_ring[1], p.slots + (item + stride) / H);
+        cp_async8(&s.slot_ring[0], p.slots + req);
+        if (item + stride < items) cp_async8(&s.slot_ring[1], p.slots + next_req(req, head));
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -890,7 +894,7 @@ __global__ void __launch_bounds__(kThreads, 3) fast_kernel(TileParams p, int ite
     }
     long long slot = s.slot_ring[0];
     {
-        const WorkItem first = describe(p, s, item, slot);
+        const WorkItem first = describe(p, s, req, head, slot);
         if (first.fast && first.active) prefetch<MODE>(p, s, s.st[0], first, c.tid);
         cp_async_commit();
         cp_async_wait<0>();
@@ -903,14 +907,22 @@ __global__ void __launch_bounds__(kThreads, 3) fast_kernel(TileParams p, int ite
     for (; item < items; item += stride) {
         const int ring1 = ring == 2 ? 0 : ring + 1, ring2 = ring1 == 2 ? 0 : ring1 + 1;
         const int next_item = item + stride;
+        // (The writeback divides instead: it has no registers to spare for the carried pair.)
+        constexpr bool kCarry = MODE != kWriteback;
+        if (!kCarry) {
+            req = item / H;
+            head = item - req * H;
+        }
+        const int nreq = kCarry ? next_req(req, head) : next_item / H;
+        const int nhead = kCarry ? (head + shead >= H ? head + shead - H : head + shead) : next_item - nreq * H;
         if (next_item < items) {
-            const WorkItem nxt = describe(p, s, next_item, s.slot_ring[ring1]);
+            const WorkItem nxt = describe(p, s, nreq, nhead, s.slot_ring[ring1]);
             if (nxt.fast && nxt.active) prefetch<MODE>(p, s, s.st[buf ^ 1], nxt, c.tid);
             if (c.tid == 0 && next_item + stride < items)
-                cp_async8(&s.slot_ring[ring2], p.slots + (next_item + stride) / H);
+                cp_async8(&s.slot_ring[ring2], p.slots + next_req(nreq, nhead));
         }
         cp_async_commit();
-        const WorkItem cur = describe(p, s, item, slot);
+        const WorkItem cur = describe(p, s, req, head, slot);
         c.req = cur.req;
         c.head = cur.head;
         c.slot = cur.slot;
@@ -933,6 +945,8 @@ __global__ void __launch_bounds__(kThreads, 3) fast_kernel(TileParams p, int ite
         cp_async_wait<0>();  // the next item's data and the slot after it
         __syncthreads();     // ... visible to all; the stage buffer just read is free
         slot = s.slot_ring[ring1];
+        req = nreq;
+        head = nhead;
         buf ^= 1;
         ring = ring1;
     }
