@@ -593,9 +593,9 @@ __device__ __forceinline__ void prefetch(const TileParams &p, const FastSmem &s,
     } else {
         const sq_step_args &a = p.step;
         const int esize = a.io_dtype == SQ_F32 ? 4 : 2;
-        const int pieces = FK * esize / 16;
-        if (j >= 0 && j < 3 * pieces) {
-            const int which = j / pieces, piece = j - which * pieces;
+        const int pshift = esize == 4 ? 5 : 4;  // 16-byte pieces per row: FK * esize / 16
+        if (j >= 0 && j < (3 << pshift)) {
+            const int which = j >> pshift, piece = j & ((1 << pshift) - 1);
             const int qh = it.head / (P.heads / a.qk_heads);
             const unsigned char *base =
                 which == 0 ? static_cast<const unsigned char *>(a.q) + (int64_t(it.req) * a.q_stride + int64_t(qh) * FK) * esize
@@ -850,8 +850,10 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 // + head).  While one item is computed the next one's data is in flight into
 // the other stage buffer, and the slot of the item after that into a small
 // ring, so each item starts with its page, scales and inputs on chip.
+// The readout, launched without the requantization plane, fits four CTAs per
+// SM when it stays within 64 registers; the rest are bounded at three.
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 3) fast_kernel(TileParams p, int items) {
+__global__ void __launch_bounds__(kThreads, MODE == kReadout ? 4 : 3) fast_kernel(TileParams p, int items) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FastSmem &s = *reinterpret_cast<FastSmem *>(smem_raw);
     const sq_plan &P = p.plan;
