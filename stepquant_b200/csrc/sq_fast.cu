@@ -880,6 +880,7 @@ __global__ void __launch_bounds__(kThreads, MODE == kReadout ? 4 : 3) fast_kerne
     // (request, head) of item = request * H + head, advanced by stride = sreq * H + shead
     // each round without a division.
     const int sreq = stride / H, shead = stride - sreq * H;
+    const int hshift = (H & (H - 1)) == 0 ? __ffs(H) - 1 : -1;
     int req = item / H, head = item - req * H;
     auto next_req = [&](int r, int h) { return r + sreq + (h + shead >= H); };
     if (c.tid == 0) {
@@ -909,13 +910,14 @@ __global__ void __launch_bounds__(kThreads, MODE == kReadout ? 4 : 3) fast_kerne
     for (; item < items; item += stride) {
         const int ring1 = ring == 2 ? 0 : ring + 1, ring2 = ring1 == 2 ? 0 : ring1 + 1;
         const int next_item = item + stride;
-        // (The writeback divides instead: it has no registers to spare for the carried pair.)
+        // (The writeback splits the item index instead: it has no registers to
+        // spare for the carried pair; a shift when H is a power of two.)
         constexpr bool kCarry = MODE != kWriteback;
         if (!kCarry) {
-            req = item / H;
+            req = hshift >= 0 ? item >> hshift : item / H;
             head = item - req * H;
         }
-        const int nreq = kCarry ? next_req(req, head) : next_item / H;
+        const int nreq = kCarry ? next_req(req, head) : hshift >= 0 ? next_item >> hshift : next_item / H;
         const int nhead = kCarry ? (head + shead >= H ? head + shead - H : head + shead) : next_item - nreq * H;
         if (next_item < items) {
             const WorkItem nxt = describe(p, s, nreq, nhead, s.slot_ring[ring1]);
