@@ -296,11 +296,13 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float q
         for (int w = 0; w < 8; ++w) m = fmaxf(m, s.red[0][w][tid]);
         if (SLOW) {
             mx = m;
+            ratio = __fdiv_rn(mx, qmax);
         } else {
             const uint32_t bits = __float_as_uint(m);
             const float lo = bits > 2u ? __uint_as_float(bits - 2u) : 0.f;
             mx = __uint_as_float(bits + 2u);
-            settled = fp16_scale(__fdiv_rn(lo, qmax)) == fp16_scale(__fdiv_rn(mx, qmax));
+            ratio = __fdiv_rn(mx, qmax);
+            settled = fp16_scale(__fdiv_rn(lo, qmax)) == fp16_scale(ratio);
         }
     }
     if (!SLOW && !__syncthreads_and(settled)) {
@@ -310,10 +312,10 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float q
             mx = 0.f;
 #pragma unroll
             for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
+            ratio = __fdiv_rn(mx, qmax);
         }
     }
     if (tid < FV) {
-        ratio = __fdiv_rn(mx, qmax);
         c0 = fp16_scale(ratio);
         s.colc[1][tid] = c0;
         s.colc[2][tid] = __frcp_rn(c0);
@@ -464,8 +466,9 @@ __device__ __forceinline__ void unpack_rows_tm(const FastSmem &s, const FastStag
 // Row |x| partial of row k in torch's order: one thread's 4 columns l, l+32,
 // l+64, l+96 are one accumulator slot of the 8-lane, 4-way interleaved chain.
 __device__ __forceinline__ void row_partial(float *rowpart, int k, int lane, const float2 (&x)[2]) {
+    // (0 + |x0|) + |x1| + ... in torch's order; 0 + |x0| is |x0| exactly.
     rowpart[k * kRowPartStride + lane] =
-        __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.f, fabsf(x[0].x)), fabsf(x[0].y)), fabsf(x[1].x)), fabsf(x[1].y));
+        __fadd_rn(__fadd_rn(__fadd_rn(fabsf(x[0].x), fabsf(x[0].y)), fabsf(x[1].x)), fabsf(x[1].y));
 }
 
 // P1 + P2 of the writeback (delta, k and c * decay are known before the
@@ -824,7 +827,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
         if (half) {
             total = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(prefix, s0), s1), s2), s3);
             const float w = st.imp[k];
-            const float mean = __fdiv_rn(total, float(FV));
+            const float mean = __fmul_rn(total, 1.f / float(FV));  // FV is a power of two: the same rounding as total / FV
             const float rr = fp16_scale(__fsqrt_rn(__fdiv_rn(fmaxf(mean, 1e-20f), w)));
             const float rc = __frcp_rn(rr);
             const float w2 = __fmul_rn(w, w);
