@@ -34,6 +34,15 @@ int32_t check_plan(const sq_plan *p) {
     return SQ_OK;
 }
 
+}  // namespace
+
+namespace sq {
+// Plan validation for the other translation units of the library.
+int32_t validate_plan(const sq_plan *p) { return check_plan(p); }
+}  // namespace sq
+
+namespace {
+
 int32_t check_step(const sq_plan *p, const sq_step_args *a) {
     if (!a || !a->q || !a->k || !a->v || !a->g || !a->beta || !a->out) return SQ_ERR_ARGUMENT;
     if (a->io_dtype < SQ_F32 || a->io_dtype > SQ_F16 || a->gate_dtype < SQ_F32 || a->gate_dtype > SQ_F16)

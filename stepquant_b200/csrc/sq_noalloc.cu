@@ -13,7 +13,7 @@
 //  * the array holds kNoAllocScratchBytes (16 MiB); every GPU that loads the
 //    library keeps it until the process exits;
 //  * a call needs round_up(batch * 8, 256) + batch * sq_scratch_floats(plan) * 4
-//    bytes of it (48 KiB per request for 32 heads of K = V = 128, so up to 340
+//    bytes of it (48 KiB per request for 32 heads of K = V = 128, so up to 341
 //    such requests); larger calls return SQ_ERR_CAPACITY before any work;
 //  * every call shares the array and it keeps the last call's contents.  Nothing
 //    in it needs to start at zero: the writeback half reads only values the
@@ -29,6 +29,10 @@
 #include <mutex>
 
 #include "../../include/stepquant_b200.h"
+
+namespace sq {
+int32_t validate_plan(const sq_plan *p);  // sq_abi.cu
+}  // namespace sq
 
 namespace {
 
@@ -64,8 +68,9 @@ int32_t sq_step_async_noalloc(const sq_plan *plan, uint8_t *pages, int64_t num_s
                               int32_t batch, const sq_step_args *args, int32_t *status, sq_stream_t stream) {
     if (batch < 0) return SQ_ERR_ARGUMENT;
     if (batch == 0) return SQ_OK;
+    // The plan's own error code (argument, shape or unsupported), as sq_readout returns it.
+    if (int32_t e = sq::validate_plan(plan)) return e;
     const int64_t floats = sq_scratch_floats(plan);
-    if (floats < 0) return SQ_ERR_ARGUMENT;
     const int64_t slot_bytes = (int64_t(batch) * 8 + 255) / 256 * 256;
     const int64_t need = slot_bytes + int64_t(batch) * floats * 4;
     if (need > int64_t(kNoAllocScratchBytes)) return SQ_ERR_CAPACITY;

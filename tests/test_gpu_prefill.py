@@ -67,6 +67,29 @@ def test_prefill_variable_lengths_gqa_against_oracle(decay_scale):
     assert torch.equal(final[1].cpu(), init[1])  # the empty sequence keeps its state
 
 
+@pytest.mark.parametrize("decay_scale", [1.0, 0.01])
+def test_prefill_2048_token_prompts(decay_scale):
+    """BASELINE config 3's prompt length: two prompts of 2,048 tokens (32
+    chunks each, so the state pass runs its full chunk chain), GQA 4 / 2, from
+    zero states.  Final state and outputs within ``TOL`` of their largest
+    magnitude, and the bf16 outputs within 2e-2 absolute (the stated output
+    tolerance)."""
+    from stepquant_b200.kernels.prefill import chunk_gated_delta_rule
+    gen = torch.Generator().manual_seed(13)
+    heads, qk = 4, 2
+    cu = [0, 2048, 4096]
+    q, k, v, g, beta = _inputs(cu[-1], heads, qk, gen, decay_scale)
+    out, final = chunk_gated_delta_rule(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(),
+                                        cu_seqlens=torch.tensor(cu, dtype=torch.int32).cuda())
+    o_ref, f_ref = O.prefill_sequential(q.float().numpy(), k.float().numpy(), v.float().numpy(), g.numpy(),
+                                        beta.numpy(), cu)
+    torch.cuda.synchronize()
+    o = out.float().cpu().numpy()
+    assert _rel(final.cpu().numpy(), f_ref) < TOL
+    assert _rel(o, o_ref) < TOL
+    assert np.abs(o - o_ref).max() <= 2e-2
+
+
 def test_prefill_many_short_sequences():
     """More sequences than the offsets kernel has threads (1,300 of 0-70 tokens,
     many empty): every chunk finds its sequence and first token in the
