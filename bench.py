@@ -941,8 +941,8 @@ def main():
             else:
                 dominant, dom_bytes, dom_ms = "sq_readout", page_io // 2 + other_io, rd
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms else None
-        # dram read + write bytes per launch from one ncu capture of this workload
-        # (profiles/fast_kernel_gdn_b256.md); None for other shapes.
+        # DRAM read + write bytes of one launch at this workload, from an ncu capture made
+        # outside the bench (ncu cannot run inside a timed region); None for other shapes.
         ncu_traffic = {"sq_step (fused)": 160.3e6, "sq_writeback": 161.6e6, "sq_readout": 115.8e6}
         default_shape = (not kda, batch, heads, qk_heads, args.dim, world) == (True, 256, 32, 16, 128, 1)
         name = ("kda-decode-b%d-h%d-k128 (config 2)" if kda else "gdn-decode-b%d-h%d-k128 (config 1)") % (batch, heads)

@@ -56,8 +56,8 @@ enum sq_architecture { SQ_GDN = 0, SQ_KDA = 1 };
 
 /*
  * One layer's quantization plan and page layout (QuantizationPlan,
- * stepquant/quantization.py:46-65, plus the tables PackedStatePool builds in
- * stepquant/kernels/pool.py:101-108).  Device tables:
+ * stepquant/quantization.py:7-26, plus the tables PackedStatePool builds in
+ * stepquant/kernels/pool.py:85-91).  Device tables:
  *   bits     [heads*keys]        2, 4, 6, 8 or 16 (16 = fp16 pivot row)
  *   impact   [heads*keys]        row weights w > 0
  *   offsets  [heads*keys+heads]  code/pivot byte offset of each key row, then
@@ -89,7 +89,7 @@ typedef struct sq_plan {
 
 /*
  * Inputs of one decode step (PackedStatePool.step arguments,
- * stepquant/kernels/pool.py:215-230).
+ * stepquant/kernels/pool.py:200-215).
  *   q, k  [batch, qk_heads, keys] with request stride q_stride / k_stride
  *         (elements); head vectors contiguous.  Value head h reads qk head
  *         h / (heads / qk_heads).
@@ -130,10 +130,10 @@ int32_t sq_version(void);
 const char *sq_error_string(int32_t code);
 
 /*
- * Host: page layout tables of a plan (stepquant/kernels/pool.py:34-81,
+ * Host: page layout tables of a plan (stepquant/kernels/pool.py:19-66,
  * ``packed_layout``).  bits_host is [heads*keys] host memory; the outputs are
  * host arrays of heads*keys+heads, heads*keys and heads entries.  storage: 0 =
- * packed, 1 = byte carriers (layout only; byte-carrier kernels are not built).
+ * packed, 1 = byte carriers (one int8 level per value; every device entry point accepts both).
  */
 int32_t sq_packed_layout(int32_t architecture, int32_t heads, int32_t keys, int32_t values,
                          int32_t value_group_size, const int32_t *bits_host, int32_t storage,
@@ -142,8 +142,8 @@ int32_t sq_packed_layout(int32_t architecture, int32_t heads, int32_t keys, int3
 
 /*
  * Dense fp32 state [batch, heads, keys, values] -> pages[slots[i]]
- * (PackedStatePool.encode / _writeback, stepquant/kernels/pool.py:199-205,334-346;
- * quantizer = fit_state, stepquant/quantization.py:93-137).  Only code bytes,
+ * (PackedStatePool.encode / _writeback, stepquant/kernels/pool.py:184-190,319-331;
+ * quantizer = fit_state, stepquant/quantization.py:54-98).  Only code bytes,
  * pivots and scales are written; alignment padding keeps its contents.
  */
 int32_t sq_encode(const sq_plan *plan, const float *state, const int64_t *slots, int32_t batch,
@@ -151,7 +151,7 @@ int32_t sq_encode(const sq_plan *plan, const float *state, const int64_t *slots,
 
 /*
  * pages[slots[i]] -> dense fp32 [batch, heads, keys, values]
- * (PackedStatePool.decode, stepquant/kernels/pool.py:207-213; fused.py:19-59).
+ * (PackedStatePool.decode, stepquant/kernels/pool.py:192-198; fused.py:19-59).
  */
 int32_t sq_decode(const sq_plan *plan, const uint8_t *pages, int64_t num_slots, const int64_t *slots,
                   int32_t batch, float *state, int32_t *status, sq_stream_t stream);
@@ -159,7 +159,7 @@ int32_t sq_decode(const sq_plan *plan, const uint8_t *pages, int64_t num_slots, 
 /*
  * One synchronous decode step, fused: unpack, gated delta rule, readout,
  * requantize (fit_state), repack, in place on pages[slots[i]]
- * (PackedStatePool.step without a writeback stream, stepquant/kernels/pool.py:215-297,
+ * (PackedStatePool.step without a writeback stream, stepquant/kernels/pool.py:200-282,
  * whose math is core.delta_step + fit_state).  state_out (optional,
  * [batch, heads, keys, values] fp32) receives the updated state before
  * requantization.
@@ -173,7 +173,7 @@ int64_t sq_scratch_floats(const sq_plan *plan);
 
 /*
  * Foreground half of an asynchronous step (readout.py:8-121 / segment_read.py
- * launched from pool.py:265-286): unpack, gated delta rule and readout.  Writes
+ * launched from pool.py:239-258): unpack, gated delta rule and readout.  Writes
  * out, fp16 pivot rows in place, per-request scratch
  * ([batch, sq_scratch_floats] fp32) and stable_slots[i] = slots[i].
  */
@@ -182,7 +182,7 @@ int32_t sq_readout(const sq_plan *plan, uint8_t *pages, int64_t num_slots, const
                    int32_t *status, sq_stream_t stream);
 
 /*
- * Background half (PackedStatePool._finish_update, pool.py:314-331: rows.py +
+ * Background half (PackedStatePool._finish_update, pool.py:299-316: rows.py +
  * fit.py): rebuilds the updated state from the page and the scratch of
  * sq_readout, requantizes and repacks the integer rows of
  * pages[stable_slots[i]].  Produces the same bytes as sq_step.
@@ -192,7 +192,7 @@ int32_t sq_writeback(const sq_plan *plan, uint8_t *pages, int64_t num_slots,
                      float *state_out, int32_t *status, sq_stream_t stream);
 
 /*
- * fit_state on the device (stepquant/quantization.py:93-137).
+ * fit_state on the device (stepquant/quantization.py:54-98).
  *   x      [batch, heads, keys, values] fp32
  *   z      [batch, heads, keys, values] int16 integer levels (all rows)
  *   r      [batch, heads, keys] fp16 bits (uint16) row scales (all rows)
@@ -221,6 +221,21 @@ int32_t sq_step_async_noalloc(const sq_plan *plan, uint8_t *pages, int64_t num_s
 
 /* Size in bytes of the file-scope scratch array used by sq_step_async_noalloc. */
 int64_t sq_noalloc_scratch_bytes(void);
+
+/*
+ * Writeback stream with an SM budget (replaces the green-context stream that
+ * stepquant/kernels/resources.py:19-53 builds through the CUDA driver from
+ * Python).  A non-blocking stream of a green context that owns at least
+ * `sm_budget` SMs of `device` (the driver rounds up to its SM-group size);
+ * kernels launched on it run on those SMs only.  One context and stream per
+ * (device, budget), created on the first call and kept until the process
+ * exits.  Out (host): *stream, *actual_sms (SMs granted), *total_sms (the
+ * device's SMs, also set when the budget is rejected).  SQ_ERR_ARGUMENT for a
+ * budget outside 1..total_sms or a bad device; SQ_ERR_UNSUPPORTED when the
+ * driver has no green contexts; SQ_ERR_CUDA when the driver refuses.
+ */
+int32_t sq_budget_stream(int32_t device, int32_t sm_budget, sq_stream_t *stream, int32_t *actual_sms,
+                         int32_t *total_sms);
 
 /* packing.pack (stepquant/packing.py:6-14): codes int16 [n] -> little-endian bytes. */
 int32_t sq_pack(const int16_t *codes, int64_t n, int32_t bits, uint8_t *out, sq_stream_t stream);

@@ -6,19 +6,19 @@ product path (``stepquant_b200``) never imports it and has no CPU fallback.
 
 This is a numpy restatement of the reference STEPQuant torch path:
 
-* ``fit_state``       -> stepquant/quantization.py:93-137
-* ``codec_encode``    -> stepquant/quantization.py:148-165  (StateCodec.encode)
-* ``codec_decode``    -> stepquant/quantization.py:167-191  (StateCodec.decode)
+* ``fit_state``       -> stepquant/quantization.py:54-98
+* ``codec_encode``    -> stepquant/quantization.py:109-126  (StateCodec.encode)
+* ``codec_decode``    -> stepquant/quantization.py:128-152  (StateCodec.decode)
 * ``pack/unpack``     -> stepquant/packing.py:6-22
-* ``packed_layout``   -> stepquant/kernels/pool.py:34-81
+* ``packed_layout``   -> stepquant/kernels/pool.py:19-66
 * ``page_encode``     -> pool page image written by pool.encode
-                         (kernels/pool.py:199-205,334-346; fused.py:252-282 rows,
+                         (kernels/pool.py:184-190,319-331; fused.py:252-282 rows,
                          fused.py:63-127 columns/codes; bitpack.py:7-30 word order)
 * ``page_decode``     -> fused.py:19-59 (codec_kernel / _read)
 * ``delta_step``      -> stepquant/core.py:5-15
 * ``prepare_inputs``  -> fused.py:156-179 and readout.py:22-39 (q/k L2 norm,
                          scale, GQA head map, raw gate transform)
-* ``decode_step``     -> PackedStatePool.step + writeback (kernels/pool.py:215-331)
+* ``decode_step``     -> PackedStatePool.step + writeback (kernels/pool.py:200-316)
                          with the sync semantics of core.delta_step + fit_state.
 
 Bit-exactness.  ``fit_state`` in the reference sums in fp32 with torch's CPU
@@ -161,7 +161,7 @@ def torch_outer_sum(x):
 
 @dataclass
 class Plan:
-    """Mirror of QuantizationPlan (quantization.py:46-65) as numpy arrays."""
+    """Mirror of QuantizationPlan (quantization.py:7-26) as numpy arrays."""
     architecture: str
     bits: np.ndarray     # [H, K] int, 16 = fp16 pivot
     impact: np.ndarray   # [H, K] float32
@@ -183,12 +183,12 @@ class Plan:
 
 
 def fp16_scale(x):
-    """quantization.py:88-90: clamp to the fp16 range, round to fp16 (RNE)."""
+    """quantization.py:49-51: clamp to the fp16 range, round to fp16 (RNE)."""
     return np.clip(np.asarray(x, F32), F32(2.0 ** -24), F32(65504)).astype(np.float16).astype(F32)
 
 
 def fit_state(x, plan: Plan):
-    """quantization.py:93-137; returns z int16, r fp16, c fp16, r2 fp16|None, recon f32."""
+    """quantization.py:54-98; returns z int16, r fp16, c fp16, r2 fp16|None, recon f32."""
     x = np.asarray(x, F32)
     bits = plan.bits
     w = plan.impact[None, :, :, None]
@@ -271,7 +271,7 @@ def unpack(data, bits, count):
 
 
 def codec_encode(state, plan: Plan):
-    """StateCodec.encode (quantization.py:148-165) -> dict of numpy byte streams."""
+    """StateCodec.encode (quantization.py:109-126) -> dict of numpy byte streams."""
     state = np.asarray(state, F32)
     if tuple(state.shape[1:3]) != tuple(plan.bits.shape):
         raise ValueError("state/precision-map shape mismatch")
@@ -296,7 +296,7 @@ def codec_encode(state, plan: Plan):
 
 
 def codec_decode(packed, plan: Plan):
-    """StateCodec.decode (quantization.py:167-191)."""
+    """StateCodec.decode (quantization.py:128-152)."""
     batch, heads, keys, values = packed["shape"]
     flat_bits = plan.bits.reshape(-1)
     z = np.zeros((batch, heads * keys, values), F32)
@@ -330,7 +330,7 @@ def codec_decode(packed, plan: Plan):
 # ---------------------------------------------------------------------------
 
 def packed_layout(plan: Plan, value_dim, storage="packed"):
-    """kernels/pool.py:34-81: (offsets, rows, columns, page_bytes)."""
+    """kernels/pool.py:19-66: (offsets, rows, columns, page_bytes)."""
     if storage not in ("packed", "byte"):
         raise ValueError("state storage must be packed or byte")
     bits = plan.bits.tolist()
@@ -396,7 +396,7 @@ def page_store(page, plan: Plan, values, z, r, c, r2, pivots_f16):
     """Write one request's fitted state into its (packed) page image in place.
 
     Only the bytes the reference kernels store are written: code bits of
-    integer rows (bitpack.py:7-30, fit.py:405-436), fp16 pivots
+    integer rows (bitpack.py:7-30, fit.py:114-148), fp16 pivots
     (fused.py:272-273), r / GDN 2-bit group r (fused.py:274-282) and c
     (fused.py:127).  Alignment padding keeps its previous contents.
     """
@@ -454,7 +454,7 @@ def page_store_byte(page, plan: Plan, values, z, r, c, r2, pivots_f16):
     """Byte-carrier page image of one request (storage='byte'), in place.
 
     Integer rows keep their signed level as one int8 at code_base + k + v*K
-    (KDA: the level times 2^(8-b); fit.py:111-115, kernels/pool.py:37-44);
+    (KDA: the level times 2^(8-b); fit.py:111-115, kernels/pool.py:29-43);
     fp16 pivot rows are contiguous at their offset; r (GDN 2-bit: per value
     group) and c as in packed pages.
     """
@@ -485,7 +485,7 @@ def page_store_byte(page, plan: Plan, values, z, r, c, r2, pivots_f16):
 
 
 def page_encode(state, plan: Plan, pages=None, storage="packed"):
-    """pool.encode (kernels/pool.py:199-205,334-346): dense fp32 [B,H,K,V] -> pages [B,P].
+    """pool.encode (kernels/pool.py:184-190,319-331): dense fp32 [B,H,K,V] -> pages [B,P].
 
     ``pages`` supplies the prior page contents (kept in alignment padding);
     zero pages are used when it is None.  ``storage`` selects packed codes or
@@ -725,7 +725,7 @@ def prefill_sequential(q, k, v, g, beta, cu_seqlens, initial_state=None, scale=N
 # ---------------------------------------------------------------------------
 
 def format_spec(name):
-    """formats.py:28-41 get_format -> (kind, bits, group)."""
+    """formats.py:28-44 get_format -> (kind, bits, group)."""
     import re
     if name == "fp32":
         return "fp32", 32, 32
@@ -760,7 +760,7 @@ def format_layout(heads, keys, values, kind, bits, group):
 
 
 def group_fit(x, bits, group):
-    """formats.py:51-65 (symmetric groupwise absmax): codes, scale, zero, recon."""
+    """formats.py:51-66 (symmetric groupwise absmax): codes, scale, zero, recon."""
     x = np.asarray(x, F32)
     y = x.reshape(*x.shape[:-1], -1, group)
     limit = F32(2 ** (bits - 1) - 1)
@@ -771,7 +771,7 @@ def group_fit(x, bits, group):
 
 
 def dual_fit(x, bits, pivots=None):
-    """formats.py:68-82 (Q-Mamba DSQ dual axis): codes, r, c, zero, recon.
+    """formats.py:69-82 (Q-Mamba DSQ dual axis): codes, r, c, zero, recon.
     ``pivots`` (bool [H, K]) marks fp16 rows; the baseline pools have none."""
     x = np.asarray(x, F32)
     mask = np.ones(x.shape[1:3], bool)[None, :, :, None] if pivots is None else ~pivots[None, :, :, None]
@@ -792,7 +792,7 @@ def _put_codes(page, off, codes, bits):
 
 def format_page_encode(state, name, pages=None):
     """One page per request of a baseline-format pool (format_pool.py encode,
-    formats.py:8-81 store): codes bit-packed per row, scales as fp16."""
+    format_pool.py:64-75 store, formats.py:51-82): codes bit-packed per row, scales as fp16."""
     kind, bits, group = format_spec(name)
     state = np.asarray(state, F32)
     batch, heads, keys, values = state.shape
@@ -822,7 +822,7 @@ def format_page_encode(state, name, pages=None):
 
 
 def format_page_decode(pages, name, heads, keys, values):
-    """formats.py:15-45 read: symmetric (code - zero) * scale; DSQ (r c)(code - levels)."""
+    """format_pool.py:77-128 read, formats.py:51-82: symmetric (code - zero) * scale; DSQ (r c)(code - levels)."""
     kind, bits, group = format_spec(name)
     pages = np.asarray(pages, np.uint8)
     offsets, rows, columns, _ = format_layout(heads, keys, values, kind, bits, group)

@@ -62,6 +62,7 @@ _SIGNATURES = {
     "sq_fp32_step": (_i32, [_p, _i64, _i32, _i32, _i32, _i32, _p, _i32, _p, _p, _p]),
     "sq_step_async_noalloc": (_i32, [_p, _p, _i64, _p, _i32, _p, _p, _p]),
     "sq_noalloc_scratch_bytes": (_i64, []),
+    "sq_budget_stream": (_i32, [_i32, _i32, ctypes.POINTER(_p), ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "sq_selftest_fp16_division": (_i32, [_p, _p, _p, _i64, _p]),
     "sq_gdn_prefill": (_i32, [_p, _p]),
     "sq_gdn_prefill_workspace_bytes": (_i64, [_i32, _i32, _i32]),

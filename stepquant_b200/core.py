@@ -1,10 +1,10 @@
-"""Calibration statistics of the recurrent update (stepquant/core.py:18-41).
+"""Calibration statistics of the recurrent update (stepquant/core.py:18-39).
 
 ``row_impact`` -- the squared transported read [D (q - beta k (k^T q))]^2 of
 each key row (core.py:18-24); ``impact_factors`` -- the per-row weights
 w = exp(gamma/2 (log omega - mean log omega)) (core.py:27-29);
 ``lifetime_weight`` -- sum_{t < horizon} retention^(2t) as a stable geometric
-sum (core.py:32-41).  Host or device tensors alike.
+sum (core.py:32-39).  Host or device tensors alike.
 """
 import torch
 

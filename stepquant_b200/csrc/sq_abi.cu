@@ -1,6 +1,6 @@
 // extern "C" entry points of libstepquant_b200 (declared in include/stepquant_b200.h).
 // Host-side argument validation mirrors the reference's eager ValueErrors
-// (stepquant/kernels/pool.py:86-101,186-187,210-230; quantization.py:53-65)
+// (stepquant/kernels/pool.py:71-84,186-187,210-230; quantization.py:14-26)
 // and returns an sq_error code instead of raising.
 #include <cuda_runtime.h>
 

@@ -42,7 +42,7 @@ __device__ __forceinline__ void store_from_float(void *p, int dtype, int64_t i, 
 }
 
 // ---------------------------------------------------------------------------
-// fp16 scales (quantization.py:88-90): clamp to [2^-24, 65504], round to fp16.
+// fp16 scales (quantization.py:49-51): clamp to [2^-24, 65504], round to fp16.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float fp16_scale(float x) {
     x = fminf(fmaxf(x, 5.9604644775390625e-8f), 65504.0f);
@@ -148,8 +148,8 @@ __device__ __forceinline__ uint32_t read_code(const uint8_t *p, uint32_t bitpos,
 }
 
 // Byte offset of value v of the fp16 pivot row at `off`: packed pages keep the
-// row's values in tiles `stride` apart (pool.py:50-57); byte-carrier pages
-// store the row contiguously (pool.py:37-44).
+// row's values in tiles `stride` apart (pool.py:44-52); byte-carrier pages
+// store the row contiguously (pool.py:33-41).
 __device__ __forceinline__ int64_t pivot_at(int off, int v, int tile, int stride, bool bytes) {
     return bytes ? int64_t(off) + 2 * v : int64_t(off) + int64_t(v / tile) * stride + 2 * (v % tile);
 }

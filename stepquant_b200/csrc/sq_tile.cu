@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
     const int stride = P.offsets[H * K + head];
     const int coff = P.columns[head];
     const int tile = min(kda ? 4 : 16, V);
-    const bool bytes = P.storage == 1;  // byte carriers (pool.py:34-49): codes at code_base + k + v K
+    const bool bytes = P.storage == 1;  // byte carriers (pool.py:29-43): codes at code_base + k + v K
     const int fmt = P.storage >= 2 ? P.storage : 0;  // baseline formats: 2 symmetric groups, 3 dual axis (DSQ)
     const bool gdn2 = !kda && P.bits[head * K] == 2;
     if (MODE == kWriteback && coff < 0) return;  // all-pivot head: finished by sq_readout
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
     if (MODE == kEncode || MODE == kFit) {
         for (int e = tid; e < K * V; e += kThreads) s.xs[e] = p.dense_in[tile_index + e];
     } else if (fmt) {
-        // Baseline formats (formats.py:15-45 read): each row one little-endian
+        // Baseline formats (format_pool.py:77-128 read, formats.py:51-82): each row one little-endian
         // bitstream; symmetric (code - zero) * scale per value group, DSQ
         // (r c)(code - levels).  No pivot rows.
         const int G = P.value_group_size;
@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
         return;
     }
 
-    // ---- fit_state (quantization.py:93-137) ----------------------------------
+    // ---- fit_state (quantization.py:54-98) ----------------------------------
     // Row scales r = fp16(sqrt(max(mean|x|, 1e-20) / w)).
     for (int k = tid; k < K; k += kThreads) {
         const float *row = s.xs + k * V;

@@ -1,9 +1,10 @@
 """State-format registry (the reference's ``stepquant.formats`` API, formats.py:28-44,85-101).
 
 Formats are named records; ``stepquant4`` / ``stepquant6`` are the calibrated
-packed formats this package executes.  The paper baselines (fp32, sym_int*,
-dsq_*) keep their registry entries; of them only fp32 has a device path here
-(``sq_fp32_step``).
+packed formats (``PackedStatePool``).  The paper baselines run on the device
+too: fp32 through ``Fp32StatePool`` (``sq_fp32_step``), sym_int*_g128 and
+dsq_int* through ``FormatStatePool`` (the tile kernel with ``sq_plan.storage``
+2 and 3).
 """
 from dataclasses import asdict, dataclass
 import re

@@ -19,7 +19,7 @@ class Fp32StatePool:
         if plan.bits.device.type != "cuda":
             raise ValueError("state pool requires CUDA")
         if spec is not None and spec.kind != "fp32":
-            raise NotImplementedError(f"state format {spec.name} has no device pool in this build (fp32 only)")
+            raise NotImplementedError(f"Fp32StatePool holds fp32 states; {spec.name} pages are FormatStatePool's")
         self.plan = plan
         self.heads, self.keys = plan.bits.shape
         self.values = value_dim

@@ -1,7 +1,7 @@
 """Fixed-layout GPU pages, shared plan tables and request-slot operations.
 
 ``PackedStatePool`` is the drop-in for the reference's pool
-(stepquant/kernels/pool.py:84-380): same constructor, attributes, page byte
+(stepquant/kernels/pool.py:69-365): same constructor, attributes, page byte
 layout (``packed_layout``) and stream/event semantics.  The arithmetic runs
 in libstepquant_b200 (include/stepquant_b200.h):
 
@@ -29,7 +29,7 @@ def _capture_id(stream):
 
 
 def packed_layout(plan, value_dim, storage="packed"):
-    """Page byte layout (kernels/pool.py:34-81): (offsets, rows, columns, page_bytes).
+    """Page byte layout (kernels/pool.py:19-66): (offsets, rows, columns, page_bytes).
 
     offsets: code/pivot byte offset of each key row followed by each head's
     stride between value tiles; rows: fp16 row-scale offsets (-1 = pivot);
@@ -82,21 +82,27 @@ class PackedStatePool:
         self._init_writeback(writeback_stream, writeback_chunk)
         self._init_workspace(slots, writeback_workspace)
 
-    # -- writeback plumbing (pool.py:136-173) ---------------------------------
+    # -- writeback state ------------------------------------------------------
+    # ready: recorded on the writeback stream after an eager writeback;
+    # graph_ready: an external event every producer (eager or captured)
+    # records, the one a consumer captured into another graph can wait on;
+    # completion: the event the next consumer waits for (ready, graph_ready or
+    # a WritebackGraph's completion); ready_capture: the capture that recorded
+    # ready, if any.
     def _init_writeback(self, writeback_stream, writeback_chunk):
         if writeback_chunk < 0:
             raise ValueError("writeback chunk must be nonnegative")
-        self.writeback_chunk = writeback_chunk
         self.writeback_stream = writeback_stream
-        self.pending = False
-        self.captured_consumers = False
+        self.writeback_chunk = writeback_chunk
+        self.deferred = None
+        self.pending = self.captured_consumers = False
         self.consumer_dependencies = set()
         self.ready_capture = None
-        self.deferred = None
-        self.ready = torch.cuda.Event() if writeback_stream is not None else None
-        self.graph_ready = torch.cuda.Event(external=True) if writeback_stream is not None else None
+        asynchronous = writeback_stream is not None
+        self.ready = torch.cuda.Event() if asynchronous else None
+        self.graph_ready = torch.cuda.Event(external=True) if asynchronous else None
         self.completion = self.ready
-        if self.graph_ready is not None:
+        if asynchronous:
             self.graph_ready.record(torch.cuda.current_stream(self.device))
 
     def _init_workspace(self, slots, writeback_workspace):
@@ -105,7 +111,7 @@ class PackedStatePool:
             return
         # Writer inputs live outside any CUDA graph's private pool: a graph may
         # reuse a freed temporary for a later tensor and the next replay could
-        # overwrite it before a deferred writeback reads it (pool.py:156-158).
+        # overwrite it before a deferred writeback reads it (pool.py:141-143).
         floats = int(N.lib().sq_scratch_floats(self._dp.ref()))
         self.scratch = (torch.empty((slots, floats), device=self.device, dtype=torch.float32),
                         torch.empty(slots, device=self.device, dtype=torch.int64))
@@ -118,7 +124,7 @@ class PackedStatePool:
         return self.data.numel()
 
     def configure_writeback(self, stream, chunk):
-        """Bind a capture's writer without replacing state or scratch storage (pool.py:179-194)."""
+        """Bind a capture's writer without replacing state or scratch storage (pool.py:164-179)."""
         if self.writeback_stream is None or chunk < 0:
             raise ValueError("configuring writeback requires an asynchronous pool and nonnegative chunk")
         if torch.cuda.is_current_stream_capturing():
@@ -197,7 +203,7 @@ class PackedStatePool:
 
     def step(self, q, k, v, g, beta, slots, *, normalize=False, scale=1., a_log=None, dt_bias=None,
              state_out=None):
-        """One decode step for ``slots`` (pool.py:215-297); returns out [B, H, V] in q.dtype.
+        """One decode step for ``slots`` (pool.py:200-282); returns out [B, H, V] in q.dtype.
 
         ``state_out`` (optional fp32 [B, H, K, V]) receives the updated state
         before requantization (synchronous pools only).
@@ -244,23 +250,26 @@ class PackedStatePool:
         return out
 
     def _schedule_writeback(self, scratch, stable_slots):
+        """Requantize on the writeback stream now, or queue it in the active deferral."""
         if self.deferred is not None:
             self.deferred.append((self, scratch, stable_slots))
             return
-        self.writeback_stream.wait_stream(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(self.writeback_stream):
+        producer = torch.cuda.current_stream(self.device)
+        writer = self.writeback_stream
+        writer.wait_stream(producer)
+        with torch.cuda.stream(writer):
             self._finish_update(scratch, stable_slots)
-            self.graph_ready.record()
-            self.ready.record()
-        for tensor in (scratch, stable_slots):
-            tensor.record_stream(self.writeback_stream)
-        capturing = torch.cuda.is_current_stream_capturing()
-        self.ready_capture = _capture_id(torch.cuda.current_stream(self.device)) if capturing else None
-        self.completion = self.graph_ready if self.ready_capture is not None else self.ready
+            self.graph_ready.record(writer)
+            self.ready.record(writer)
+        scratch.record_stream(writer)
+        stable_slots.record_stream(writer)
+        capture = _capture_id(producer) if torch.cuda.is_current_stream_capturing() else None
+        self.ready_capture = capture
+        self.completion = self.ready if capture is None else self.graph_ready
         self.pending = True
 
     def _finish_update(self, scratch, stable_slots, state_out=None):
-        """Requantize and repack the pages of one chunk on the current stream (pool.py:314-331)."""
+        """Requantize and repack the pages of one chunk on the current stream (pool.py:299-316)."""
         batch = stable_slots.numel()
         if not batch:
             return
@@ -268,25 +277,29 @@ class PackedStatePool:
                                      batch, N.ptr(scratch), N.ptr(state_out), N.ptr(self.status),
                                      N.stream_handle()))
 
+    def _pending_events(self, stream):
+        """The events ``stream`` must wait on before touching the pages."""
+        if self.deferred is not None:  # inside a capture that defers this pool's writes
+            return () if self.deferred.joined else (self.graph_ready,)
+        if not self.pending:
+            return ()
+        if not torch.cuda.is_current_stream_capturing():
+            return (self.completion,)
+        if self.ready_capture == _capture_id(stream):
+            return (self.ready,)  # produced earlier in this same capture
+        # A consumer captured into a graph of its own: it waits on graph_ready,
+        # which every later producer records too.  An event of an earlier
+        # producer graph is kept alive, since graph nodes do not own events.
+        self.captured_consumers = True
+        if self.completion is self.ready or self.completion is self.graph_ready:
+            return (self.graph_ready,)
+        self.consumer_dependencies.add(self.completion)
+        return (self.completion, self.graph_ready)
+
     def wait(self):
-        """Order the current stream after pending writeback (pool.py:349-371)."""
+        """Order the current stream after pending writeback (reference pool.py:334-356)."""
         stream = torch.cuda.current_stream(self.device)
-        if getattr(self, "deferred", None) is not None:
-            if not self.deferred.joined:
-                stream.wait_event(self.graph_ready)
-        elif self.pending:
-            event = self.completion
-            if torch.cuda.is_current_stream_capturing():
-                # Internal events join only their own capture; earlier captures
-                # and eager submissions need external event nodes.
-                if self.ready_capture == _capture_id(stream):
-                    event = self.ready
-                else:
-                    self.captured_consumers = True
-                    if self.completion is not self.ready and self.completion is not self.graph_ready:
-                        self.consumer_dependencies.add(self.completion)
-                        stream.wait_event(self.completion)
-                    event = self.graph_ready
+        for event in self._pending_events(stream):
             stream.wait_event(event)
 
     def clear(self, slots):

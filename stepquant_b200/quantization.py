@@ -1,6 +1,6 @@
 """Quantization plan, packed codec and fit_state (the reference's ``stepquant.quantization``).
 
-``QuantizationPlan`` keeps the reference's validation (quantization.py:46-69).
+``QuantizationPlan`` keeps the reference's validation (quantization.py:7-30).
 ``fit_state`` and ``StateCodec`` run on the device through the C ABI
 (``sq_fit_state``, ``sq_pack``, ``sq_unpack``); they accept CUDA tensors only.
 """
@@ -100,7 +100,7 @@ def _device_plan(plan, values):
 
 
 def fit_state(x, plan):
-    """Integer levels, stored row/column factors and reconstruction (quantization.py:93-137).
+    """Integer levels, stored row/column factors and reconstruction (quantization.py:54-98).
 
     Returns (z int16 [B,H,K,V], r fp16 [B,H,K], c fp16 [B,H,V],
     r2 fp16 [B,H2,K,V/G] for GDN 2-bit heads or None, recon fp32 [B,H,K,V]).
@@ -126,7 +126,7 @@ def fit_state(x, plan):
 
 
 class StateCodec:
-    """Packed persistent storage of a whole state (quantization.py:140-191)."""
+    """Packed persistent storage of a whole state (quantization.py:101-152)."""
 
     def __init__(self, plan):
         self.plan = plan

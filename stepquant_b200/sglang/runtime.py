@@ -1,21 +1,29 @@
-"""SGLang 0.5.12 hooks: packed Mamba pool, GDN/KDA dispatch and the writeback schedule.
+"""SGLang 0.5.12 hooks: packed state pools, GDN/KDA kernel routing, writeback schedule.
 
-Mirrors stepquant/sglang/runtime.py with this package's pool.  SGLang's model,
-convolution cache, attention backend and scheduler stay native: the pool hooks
-replace the dense recurrent cache by one ``PackedStatePool`` per layer, the
-kernel hooks route decode (``kernel_decode`` / ``kernel_packed_decode``) and the
-end of prefill (``kernel_extend``) through it, and ``capture_graph`` captures
-the background writeback with ``defer_writeback`` / ``WritebackGraph``.
+The hook names, their signatures (``original, self, ...``: AROUND hooks of
+SGLang's HookRegistry), the SGLang attributes they touch and the environment
+variables are those of stepquant/sglang/runtime.py, so the plugin is a drop-in;
+the code below is organised around this package's pool.
 
-Settings come from the environment (as set by the reference's launcher):
-STEPQUANT_PLAN, STEPQUANT_STATE_FORMAT, STEPQUANT_ARCHITECTURE,
-STEPQUANT_ASYNC_WRITEBACK, STEPQUANT_WRITEBACK_SMS, STEPQUANT_WRITEBACK_CHUNK,
-STEPQUANT_STATE_STORAGE.
+* Settings: ``STEPQUANT_PLAN`` (calibration file), ``STEPQUANT_STATE_FORMAT``,
+  ``STEPQUANT_ARCHITECTURE``, ``STEPQUANT_ASYNC_WRITEBACK``,
+  ``STEPQUANT_WRITEBACK_SMS`` / ``_CHUNK`` and ``STEPQUANT_STATE_STORAGE``.
+* Pools: SGLang's Mamba pool keeps its convolution cache and allocators; its
+  dense recurrent ("temporal") cache is replaced by ``TemporalPages``, one
+  ``PackedStatePool`` (or baseline-format pool) per layer with ``size + 1``
+  slots (slot 0 is SGLang's padding sentinel).  Slot operations go to both.
+* Kernels: decode routes to ``PackedStatePool.step``; prefill of GDN layers
+  runs this package's chunked pass (``PackedStatePool.extend``), other layers
+  let SGLang's chunk kernel update the decoded dense state in place.
+* Graphs: each captured decode batch size defers its background writeback
+  (``defer_writeback(..., attention_windows=True, joined=True)``) and the
+  captured graph is returned wrapped in a ``WritebackGraph``.
 """
 import dataclasses
 import functools
 import inspect
 import logging
+import math
 import os
 import re
 import weakref
@@ -28,31 +36,46 @@ from ..kernels.pool import PackedStatePool
 from ..quantization import QuantizationPlan
 
 log = logging.getLogger(__name__)
-_temporal_pools = weakref.WeakSet()
-_writeback_profiles = {}
+_temporal_pools = weakref.WeakSet()   # every TemporalPages this process created
+_writeback_profiles = {}              # captured batch size -> writeback SMs and chunk
+
+
+# ---------------------------------------------------------------------------
+# settings and the calibration file
+# ---------------------------------------------------------------------------
+def _env(name, default=None):
+    return os.environ.get(name, default)
+
+
+def state_format():
+    return get_format(_env("STEPQUANT_STATE_FORMAT", "stepquant"))
+
+
+def _storage():
+    return _env("STEPQUANT_STATE_STORAGE", "packed")
 
 
 @functools.lru_cache(maxsize=1)
 def artifact():
-    """The calibration plan file (torch.load, format_version 2)."""
-    value = torch.load(os.environ["STEPQUANT_PLAN"], map_location="cpu", weights_only=True)
-    if value.get("format_version") != 2:
+    """The calibration plan file: ``torch.load(weights_only=True)``, format_version 2."""
+    loaded = torch.load(_env("STEPQUANT_PLAN"), map_location="cpu", weights_only=True)
+    if loaded.get("format_version") != 2:
         raise ValueError("unsupported STEPQuant plan format")
-    return value
-
-
-def state_format():
-    return get_format(os.environ.get("STEPQUANT_STATE_FORMAT", "stepquant"))
+    return loaded
 
 
 def writeback_settings(architecture, batch):
-    """Writeback (SMs, chunk) for a captured batch; 'auto' uses the STEPQuant@6 profile."""
+    """(writeback SMs, chunk) for ``batch``.  Under stepquant6 both default to
+    'auto' (the ``stepquant6_profile`` tier of the batch), otherwise to 32 SMs
+    and chunks of 64; the environment overrides either."""
     from ..kernels.profiles import stepquant6_profile
-    nominal_six = state_format().name == "stepquant6"
-    profile = stepquant6_profile(architecture, batch) if nominal_six else None
-    sms = os.environ.get("STEPQUANT_WRITEBACK_SMS", "auto" if nominal_six else "32")
-    chunk = os.environ.get("STEPQUANT_WRITEBACK_CHUNK", "auto" if nominal_six else "64")
-    return (profile.sms if sms == "auto" else int(sms), profile.chunk if chunk == "auto" else int(chunk))
+    tuned = state_format().name == "stepquant6"
+    profile = stepquant6_profile(architecture, batch) if tuned else None
+    resolved = []
+    for var, field, fallback in (("STEPQUANT_WRITEBACK_SMS", "sms", "32"), ("STEPQUANT_WRITEBACK_CHUNK", "chunk", "64")):
+        text = _env(var, "auto" if tuned else fallback)
+        resolved.append(getattr(profile, field) if text == "auto" else int(text))
+    return tuple(resolved)
 
 
 def tp_rank_world():
@@ -62,51 +85,70 @@ def tp_rank_world():
 
 
 def shard_plan(entry, heads, rank, world, cls=QuantizationPlan):
-    """This rank's value heads of a layer plan: bits/impact rows [rank*heads, (rank+1)*heads)."""
-    plan = cls(**{k: v for k, v in entry.items() if k in ("architecture", "bits", "impact", "value_group_size")})
-    if plan.bits.shape[0] != heads * world:
+    """This rank's value heads of one layer's plan entry (rows rank*heads .. +heads)."""
+    fields = ("architecture", "bits", "impact", "value_group_size")
+    whole = cls(**{key: entry[key] for key in fields if key in entry})
+    if whole.bits.shape[0] != heads * world:
         raise ValueError("calibration head count does not match tensor-parallel shard")
-    rows = slice(rank * heads, (rank + 1) * heads)
-    return cls(plan.architecture, plan.bits[rows].contiguous(), plan.impact[rows].contiguous(), plan.value_group_size)
+    lo, hi = rank * heads, (rank + 1) * heads
+    return cls(whole.architecture, whole.bits[lo:hi].contiguous(), whole.impact[lo:hi].contiguous(),
+               whole.value_group_size)
+
+
+def _plans_by_layer(art):
+    """Layer index -> plan entry, the index parsed from ``...layers.<i>....`` names."""
+    table = {}
+    for name, entry in art["plans"].items():
+        found = re.search(r"\.layers\.(\d+)\.", name)
+        if found is None:
+            raise ValueError(f"cannot map layer name {name}")
+        table[int(found.group(1))] = entry
+    return table
 
 
 def local_plans(layer_ids, heads, device, keys=128, rank=None, world=None):
-    """One plan per layer for this tensor-parallel rank (runtime.py:47-77)."""
-    if rank is None or world is None:
-        rank, world = tp_rank_world()
+    """One plan per layer in ``layer_ids`` for this tensor-parallel rank.
+
+    Uncalibrated formats get a uniform plan of their width; calibrated ones are
+    read from the plan file, which must carry the requested nominal width."""
     spec = state_format()
     if not spec.calibrated:
-        architecture = os.environ["STEPQUANT_ARCHITECTURE"]
-        return [FormatPlan(architecture, torch.full((heads, keys), spec.bits, dtype=torch.long),
-                           torch.ones(heads, keys)).to(device) for _ in layer_ids]
-    expected = artifact().get("state_format", "stepquant")
-    if spec.name in ("stepquant4", "stepquant6") and artifact().get("settings", {}).get("nominal_bits") != spec.bits:
+        width = torch.full((heads, keys), spec.bits, dtype=torch.long)
+        return [FormatPlan(os.environ["STEPQUANT_ARCHITECTURE"], width, torch.ones(heads, keys)).to(device)
+                for _ in layer_ids]
+    art = artifact()
+    if spec.name in ("stepquant4", "stepquant6") and art.get("settings", {}).get("nominal_bits") != spec.bits:
         raise ValueError("plan nominal bits do not match the requested STEPQuant format")
-    if expected != "stepquant":
-        raise ValueError(f"{expected} plan requires its matching --state-format")
-    mapping = {}
-    for name, entry in artifact()["plans"].items():
-        match = re.search(r"\.layers\.(\d+)\.", name)
-        if not match:
-            raise ValueError(f"cannot map layer name {name}")
-        mapping[int(match[1])] = entry
-    return [shard_plan(mapping[layer], heads, rank, world).to(device) for layer in layer_ids]
+    saved = art.get("state_format", "stepquant")
+    if saved != "stepquant":
+        raise ValueError(f"{saved} plan requires its matching --state-format")
+    if rank is None or world is None:
+        rank, world = tp_rank_world()
+    table = _plans_by_layer(art)
+    return [shard_plan(table[layer], heads, rank, world).to(device) for layer in layer_ids]
 
 
+# ---------------------------------------------------------------------------
+# the pools standing in for SGLang's dense temporal cache
+# ---------------------------------------------------------------------------
 class TemporalPages:
-    """Stands in for SGLang's dense temporal cache tensor: one pool per layer."""
+    """SGLang's temporal cache tensor, replaced by one pool per layer.
+
+    SGLang only indexes it by layer and asks for its byte size."""
+
+    dtype = torch.uint8
 
     def __init__(self, pages):
         self.pages = pages
         _temporal_pools.add(self)
 
-    def __getitem__(self, index):
-        if not isinstance(index, int):
-            raise NotImplementedError("use packed pool slot operations")
-        return self.pages[index]
+    def __getitem__(self, layer):
+        if isinstance(layer, int):
+            return self.pages[layer]
+        raise NotImplementedError("use packed pool slot operations")
 
     def numel(self):
-        return sum(p.nbytes for p in self.pages)
+        return sum(pool.nbytes for pool in self.pages)
 
     def element_size(self):
         return 1
@@ -115,199 +157,251 @@ class TemporalPages:
     def shape(self):
         return (self.numel(),)
 
-    dtype = torch.uint8
+
+def _async_pools():
+    """Pools of every live TemporalPages that write back on a side stream."""
+    return [pool for pages in tuple(_temporal_pools) for pool in pages.pages
+            if getattr(pool, "writeback_stream", None) is not None]
 
 
 def make_pool(plan, size, values, spec, stream, workspace, chunk, storage):
-    if spec.kind == "stepquant":
-        return PackedStatePool(plan, size + 1, values, writeback_stream=stream, writeback_workspace=workspace,
-                               writeback_chunk=chunk, storage=storage)
-    return FormatStatePool(plan, size + 1, values, spec, writeback_stream=stream)
+    if spec.kind != "stepquant":
+        return FormatStatePool(plan, size + 1, values, spec, writeback_stream=stream)
+    return PackedStatePool(plan, size + 1, values, writeback_stream=stream, writeback_workspace=workspace,
+                           writeback_chunk=chunk, storage=storage)
+
+
+def _writeback_stream(device, architecture, size):
+    """(stream or None, chunk) for a pool of ``size`` requests."""
+    sms, chunk = writeback_settings(architecture, min(512, max(1, size)))
+    if _env("STEPQUANT_ASYNC_WRITEBACK") != "1":
+        return None, chunk
+    from ..kernels.resources import writeback_resources
+    res = writeback_resources(device, sms)
+    log.warning("STEPQuant background SMs: requested=%d actual=%d total=%d",
+                res.requested_sms, res.actual_sms, res.total_sms)
+    os.environ["STEPQUANT_WRITEBACK_ACTUAL_SMS"] = str(res.actual_sms)
+    return res.stream, chunk
 
 
 def pool_init(original, self, **kwargs):
+    """MambaPool.__init__: SGLang builds everything but the dense temporal cache,
+    which becomes one packed pool per recurrent layer."""
     if kwargs.get("speculative_num_draft_tokens") is not None:
         raise ValueError("STEPQuant currently does not support speculative decoding")
     params = kwargs["cache_params"]
-    heads, values, keys = params.shape.temporal  # SGLang stores [H, V, K]
+    heads, values, keys = params.shape.temporal  # SGLang's order: [H, V, K]
     plans = local_plans(kwargs["mamba_layer_ids"], heads, kwargs["device"], keys)
-    if any(p.bits.shape[1] != keys for p in plans):
+    if any(plan.bits.shape[1] != keys for plan in plans):
         raise ValueError("calibration key dimension mismatch")
-    # SGLang initialises its convolution cache and allocators with an empty
-    # temporal shape, so the dense recurrent pool is never allocated.
-    tiny = dataclasses.replace(params, shape=dataclasses.replace(params.shape, temporal=(heads, 0, 0)))
-    original(self, **dict(kwargs, cache_params=tiny))
-    stream = None
-    architecture = plans[0].architecture if plans else os.environ.get("STEPQUANT_ARCHITECTURE", "gdn")
-    sms, chunk = writeback_settings(architecture, min(512, max(1, kwargs["size"])))
-    if os.environ.get("STEPQUANT_ASYNC_WRITEBACK") == "1":
-        from ..kernels.resources import writeback_resources
-        resources = writeback_resources(kwargs["device"], sms)
-        stream = resources.stream
-        log.warning("STEPQuant background SMs: requested=%d actual=%d total=%d",
-                    resources.requested_sms, resources.actual_sms, resources.total_sms)
-        os.environ["STEPQUANT_WRITEBACK_ACTUAL_SMS"] = str(resources.actual_sms)
-    spec = state_format()
-    storage = os.environ.get("STEPQUANT_STATE_STORAGE", "packed")
-    workspace = {}
-    pages = TemporalPages([make_pool(p, kwargs["size"], values, spec, stream, workspace, chunk, storage) for p in plans])
+    empty = dataclasses.replace(params.shape, temporal=(heads, 0, 0))
+    original(self, **{**kwargs, "cache_params": dataclasses.replace(params, shape=empty)})
+    size = kwargs["size"]
+    architecture = plans[0].architecture if plans else _env("STEPQUANT_ARCHITECTURE", "gdn")
+    stream, chunk = _writeback_stream(kwargs["device"], architecture, size)
+    spec, storage, workspace = state_format(), _storage(), {}
+    pages = TemporalPages([make_pool(plan, size, values, spec, stream, workspace, chunk, storage) for plan in plans])
     self.mamba_cache = dataclasses.replace(self.mamba_cache, temporal=pages)
     self.mem_usage = self.mamba_cache.mem_usage_bytes() / 1024 ** 3
-    dense = len(plans) * (kwargs["size"] + 1) * heads * values * keys * 4
-    log.warning("STEPQuant state pool (%s): %d bytes (FP32 %d bytes), %d layers, slots=%d",
-                storage, pages.numel(), dense, len(plans), kwargs["size"] + 1)
+    log.warning("STEPQuant state pool (%s): %d bytes (FP32 %d bytes), %d layers, slots=%d", storage,
+                pages.numel(), len(plans) * (size + 1) * heads * values * keys * 4, len(plans), size + 1)
+
+
+def _each_cache(self, on_conv, on_pool):
+    for conv in self.mamba_cache.conv:
+        on_conv(conv)
+    for pool in self.mamba_cache.temporal.pages:
+        on_pool(pool)
 
 
 def pool_alloc(original, self, need_size):
+    """Take ``need_size`` free slots and zero their convolution and packed state."""
     if need_size > len(self.free_slots):
         return None
-    slots = self.free_slots[:need_size]
-    self.free_slots = self.free_slots[need_size:]
-    for conv in self.mamba_cache.conv:
+    slots, self.free_slots = self.free_slots[:need_size], self.free_slots[need_size:]
+
+    def zero(conv):
         conv[:, slots] = 0
-    for p in self.mamba_cache.temporal.pages:
-        p.clear(slots)
+    _each_cache(self, zero, lambda pool: pool.clear(slots))
     return slots
 
 
 def pool_copy_from(original, self, src_index, dst_index):
-    for conv in self.mamba_cache.conv:
+    def copy(conv):
         conv[:, dst_index] = conv[:, src_index]
-    for p in self.mamba_cache.temporal.pages:
-        p.copy(src_index, dst_index)
+    _each_cache(self, copy, lambda pool: pool.copy(src_index, dst_index))
 
 
 def pool_get_cpu_copy(original, self, indices):
-    """Raw page bytes of the given slots (the page layout is the wire format)."""
+    """Host copies of the slots' convolution state and raw page bytes (the page
+    layout is the wire format)."""
     torch.cuda.synchronize()
-    return ([c[:, indices].cpu() for c in self.mamba_cache.conv],
-            [p.data[indices].cpu() for p in self.mamba_cache.temporal.pages])
+    convs, pages = [], []
+    _each_cache(self, lambda conv: convs.append(conv[:, indices].cpu()),
+                lambda pool: pages.append(pool.data[indices].cpu()))
+    return convs, pages
 
 
 def pool_load_cpu_copy(original, self, mamba_cache_cpu, indices):
-    convs, pages = mamba_cache_cpu
-    for dst, src in zip(self.mamba_cache.conv, convs):
-        dst[:, indices] = src.to(dst.device)
-    for dst, src in zip(self.mamba_cache.temporal.pages, pages):
-        dst.wait()
-        dst.data[indices] = src.to(dst.device)
+    convs, pages = (iter(part) for part in mamba_cache_cpu)
+
+    def load_conv(conv):
+        conv[:, indices] = next(convs).to(conv.device)
+
+    def load_pool(pool):
+        pool.wait()
+        pool.data[indices] = next(pages).to(pool.data.device)
+    _each_cache(self, load_conv, load_pool)
 
 
 def pool_get_contiguous_buf_infos(original, self):
     raise NotImplementedError("STEPQuant does not support disaggregated serving")
 
 
+# ---------------------------------------------------------------------------
+# kernels
+# ---------------------------------------------------------------------------
+def _packed(ssm_states):
+    return isinstance(ssm_states, PackedStatePool)
+
+
 def kernel_decode(original, self, q, k, v, a, b, *, A_log, dt_bias, ssm_states, cache_indices, query_start_loc,
                   **kwargs):
-    if not isinstance(ssm_states, PackedStatePool):
+    """TritonGDNKernel / TritonKDAKernel.decode: one packed step, [1, B, H, V]."""
+    if not _packed(ssm_states):
         return original(self, q, k, v, a, b, A_log=A_log, dt_bias=dt_bias, ssm_states=ssm_states,
                         cache_indices=cache_indices, query_start_loc=query_start_loc, **kwargs)
-    out = ssm_states.step(q, k, v, a, b, cache_indices, normalize=True, scale=ssm_states.keys ** -0.5,
-                          a_log=A_log, dt_bias=dt_bias)
-    return out.unsqueeze(0)
+    return ssm_states.step(q, k, v, a, b, cache_indices, normalize=True, scale=ssm_states.keys ** -0.5,
+                           a_log=A_log, dt_bias=dt_bias)[None]
 
 
 def kernel_packed_decode(original, self, mixed_qkv, a, b, *, A_log, dt_bias, scale, ssm_states, cache_indices,
                          num_v_heads, head_v_dim, **kwargs):
-    if not isinstance(ssm_states, PackedStatePool):
+    """TritonGDNKernel.packed_decode: q, k, v arrive concatenated in ``mixed_qkv``."""
+    if not _packed(ssm_states):
         return original(self, mixed_qkv, a, b, A_log=A_log, dt_bias=dt_bias, scale=scale, ssm_states=ssm_states,
                         cache_indices=cache_indices, num_v_heads=num_v_heads, head_v_dim=head_v_dim, **kwargs)
-    vdim = num_v_heads * head_v_dim
-    kdim = (mixed_qkv.shape[-1] - vdim) // 2
-    q, k, v = mixed_qkv.split([kdim, kdim, vdim], -1)
+    value_width = num_v_heads * head_v_dim
+    key_width = (mixed_qkv.shape[-1] - value_width) // 2
+    q, k, v = mixed_qkv.split([key_width, key_width, value_width], -1)
     return ssm_states.step(q, k, v, a, b, cache_indices, normalize=True, scale=scale, a_log=A_log,
-                           dt_bias=dt_bias).unsqueeze(0)
+                           dt_bias=dt_bias)[None]
 
 
 def kernel_extend(original, self, q, k, v, g, beta, *, ssm_states, cache_indices, query_start_loc, **kwargs):
-    """Prefill.  GDN pools with K = V = 128 run the chunked state pass of this
-    library (``PackedStatePool.extend``: decode, chunk pass with in-kernel q/k
-    L2 normalisation, encode).  Other packed pools decode the active pages, let
-    the original chunk kernel update the dense V-first state in place, and
-    encode the final state back into the pages (runtime.py:193-202)."""
-    if not isinstance(ssm_states, PackedStatePool):
+    """Prefill.  GDN pools with K = V = 128 run this package's chunked state
+    pass (``PackedStatePool.extend``: decode, chunk pass with in-kernel q/k
+    L2 normalisation, encode).  Other packed pools hand SGLang's chunk kernel
+    the decoded states, V-first as it keeps them, with the active requests
+    numbered 0..n-1, and encode what it leaves there."""
+    if not _packed(ssm_states):
         return original(self, q, k, v, g, beta, ssm_states=ssm_states, cache_indices=cache_indices,
                         query_start_loc=query_start_loc, **kwargs)
     if ssm_states.plan.architecture == "gdn" and ssm_states.keys == 128 and ssm_states.values == 128:
         return ssm_states.extend(q, k, v, g, beta, cache_indices, query_start_loc, normalize=True)
-    active = ssm_states.decode(cache_indices).transpose(-1, -2).contiguous()
-    indices = torch.arange(cache_indices.numel(), device=cache_indices.device, dtype=cache_indices.dtype)
-    output = original(self, q, k, v, g, beta, ssm_states=active, cache_indices=indices,
-                      query_start_loc=query_start_loc, **kwargs)
-    ssm_states.encode(active.transpose(-1, -2), cache_indices)
-    return output
+    dense = ssm_states.decode(cache_indices).transpose(-1, -2).contiguous()
+    local = torch.arange(cache_indices.numel(), device=cache_indices.device, dtype=cache_indices.dtype)
+    out = original(self, q, k, v, g, beta, ssm_states=dense, cache_indices=local, query_start_loc=query_start_loc,
+                   **kwargs)
+    ssm_states.encode(dense.transpose(-1, -2), cache_indices)
+    return out
 
 
 def attention_forward(original, self, *args, **kwargs):
+    """Decoder-layer forward: a writeback release gate before its attention work."""
     from ..kernels.writeback import attention_window
     attention_window()
     return original(self, *args, **kwargs)
 
 
-def capture_graph(original, self, bs, forward, stream_idx=None):
-    """Capture one decode batch size with deferred (joined) background writeback."""
-    from ..kernels.writeback import WritebackGraph, defer_writeback
-    if state_format().name == "stepquant6":
-        from ..kernels.resources import writeback_resources
-        pools = [pool for temporal in tuple(_temporal_pools) for pool in temporal.pages
-                 if getattr(pool, "writeback_stream", None) is not None]
-        resources = chunk = None
-        for pool in pools:
-            sms, chunk = writeback_settings(pool.plan.architecture, bs)
-            resources = writeback_resources(pool.device, sms)
-            pool.configure_writeback(resources.stream, chunk)
-        if pools:
-            _writeback_profiles[str(bs)] = dict(requested_sms=resources.requested_sms,
-                                                actual_sms=resources.actual_sms, chunk=chunk)
-            log.warning("STEPQuant6 capture: batch=%d background_sms=%d requested_sms=%d chunk=%d",
-                        bs, resources.actual_sms, resources.requested_sms, chunk)
-    tasks = []
+# ---------------------------------------------------------------------------
+# CUDA-graph capture
+# ---------------------------------------------------------------------------
+def _bind_capture_resources(bs):
+    """stepquant6: give every async pool the writeback stream and chunk of the batch's profile tier."""
+    from ..kernels.resources import writeback_resources
+    chosen = None
+    for pool in _async_pools():
+        sms, chunk = writeback_settings(pool.plan.architecture, bs)
+        res = writeback_resources(pool.device, sms)
+        pool.configure_writeback(res.stream, chunk)
+        chosen = (res, chunk)
+    if chosen is not None:
+        res, chunk = chosen
+        _writeback_profiles[str(bs)] = dict(requested_sms=res.requested_sms, actual_sms=res.actual_sms, chunk=chunk)
+        log.warning("STEPQuant6 capture: batch=%d background_sms=%d requested_sms=%d chunk=%d",
+                    bs, res.actual_sms, res.requested_sms, chunk)
 
-    @functools.wraps(forward)
-    def capture_forward(*args, **kwargs):
+
+class _DeferredForward:
+    """The forward SGLang captures, with the async pools' writeback deferred
+    into the same graph (joined); eager calls pass straight through."""
+
+    def __init__(self, forward):
+        self.forward = forward
+        self.chunks = []
+        functools.update_wrapper(self, forward)
+
+    def __call__(self, *args, **kwargs):
         if not torch.cuda.is_current_stream_capturing():
-            return forward(*args, **kwargs)
-        pools = [pool for temporal in tuple(_temporal_pools) for pool in temporal.pages
-                 if getattr(pool, "writeback_stream", None) is not None]
-        with defer_writeback(pools, attention_windows=True, joined=True) as captured:
-            result = forward(*args, **kwargs)
-        tasks.extend(captured)
+            return self.forward(*args, **kwargs)
+        from ..kernels.writeback import defer_writeback
+        with defer_writeback(_async_pools(), attention_windows=True, joined=True) as captured:
+            result = self.forward(*args, **kwargs)
+        self.chunks.extend(captured)
         return result
 
-    graph, output = original(self, bs, capture_forward, stream_idx)
-    return (WritebackGraph(graph, tasks, joined=True) if tasks else graph), output
+
+def capture_graph(original, self, bs, forward, stream_idx=None):
+    """CudaGraphRunner.capture_one_batch_size: the graph, wrapped in a joined
+    ``WritebackGraph`` when it captured writeback."""
+    from ..kernels.writeback import WritebackGraph
+    if state_format().name == "stepquant6":
+        _bind_capture_resources(bs)
+    deferred = _DeferredForward(forward)
+    graph, output = original(self, bs, deferred, stream_idx)
+    return (WritebackGraph(graph, deferred.chunks, joined=True) if deferred.chunks else graph), output
 
 
-def validate_runner(original, self, *args, **kwargs):
-    """Refuse server modes the packed pool does not support (runtime.py:271-294)."""
-    from .plugin import verify_hooks
-    verify_hooks()
-    server = inspect.signature(original).bind(self, *args, **kwargs).arguments["server_args"]
-    check_server_args(server)
-    return original(self, *args, **kwargs)
+# ---------------------------------------------------------------------------
+# server checks and pool sizing
+# ---------------------------------------------------------------------------
+_SERVER_RULES = (
+    (lambda s: not s.disable_radix_cache,
+     "STEPQuant requires --disable-radix-cache until prefix-state tracking is enabled"),
+    (lambda s: s.enable_mamba_extra_buffer(), "STEPQuant requires --mamba-scheduler-strategy no_buffer"),
+    (lambda s: getattr(s, "enable_memory_saver", False),
+     "STEPQuant does not yet support SGLang memory-saver pause/resume"),
+    (lambda s: getattr(s, "pp_size", 1) != 1 or getattr(s, "enable_dp_attention", False),
+     "STEPQuant currently supports ordinary tensor parallelism only"),
+    (lambda s: getattr(s, "speculative_algorithm", None), "STEPQuant does not support speculative decoding"),
+    (lambda s: getattr(s, "disaggregation_mode", "null") not in ("null", None),
+     "STEPQuant does not support disaggregated serving"),
+    (lambda s: any(getattr(s, key, None) not in (None, "triton") for key in
+                   ("linear_attn_backend", "linear_attn_decode_backend", "linear_attn_prefill_backend")),
+     "STEPQuant requires --linear-attn-backend triton"),
+)
 
 
 def check_server_args(server):
-    if not server.disable_radix_cache:
-        raise ValueError("STEPQuant requires --disable-radix-cache until prefix-state tracking is enabled")
-    if server.enable_mamba_extra_buffer():
-        raise ValueError("STEPQuant requires --mamba-scheduler-strategy no_buffer")
-    if getattr(server, "enable_memory_saver", False):
-        raise ValueError("STEPQuant does not yet support SGLang memory-saver pause/resume")
-    if getattr(server, "pp_size", 1) != 1 or getattr(server, "enable_dp_attention", False):
-        raise ValueError("STEPQuant currently supports ordinary tensor parallelism only")
-    if getattr(server, "speculative_algorithm", None):
-        raise ValueError("STEPQuant does not support speculative decoding")
-    if getattr(server, "disaggregation_mode", "null") not in ("null", None):
-        raise ValueError("STEPQuant does not support disaggregated serving")
-    if any(getattr(server, key, None) not in (None, "triton") for key in
-           ("linear_attn_backend", "linear_attn_decode_backend", "linear_attn_prefill_backend")):
-        raise ValueError("STEPQuant requires --linear-attn-backend triton")
+    """Raise ValueError for the first server mode the packed pool cannot serve."""
+    for refuses, message in _SERVER_RULES:
+        if refuses(server):
+            raise ValueError(message)
+
+
+def validate_runner(original, self, *args, **kwargs):
+    """ModelRunner.__init__: every hook installed, the server mode supported."""
+    from .plugin import verify_hooks
+    verify_hooks()
+    check_server_args(inspect.signature(original).bind(self, *args, **kwargs).arguments["server_args"])
+    return original(self, *args, **kwargs)
 
 
 def agree_min(count, group):
-    """Smallest slot count over the ranks of ``group`` (a gloo CPU group); the
-    mixed-precision page size differs per rank (runtime.py:310-317)."""
+    """Smallest slot count over the ranks of ``group`` (a CPU group): mixed
+    precision gives ranks different page sizes, but every rank must offer the
+    scheduler the same number of slots."""
     if group is None or torch.distributed.get_world_size(group) <= 1:
         return count
     shared = torch.tensor(count, dtype=torch.int64)
@@ -319,23 +413,24 @@ def page_bytes_per_slot(plans, values, storage="packed"):
     """Bytes of one request slot over all layers' pools."""
     from ..kernels.pool import packed_layout
     spec = state_format()
-    return sum((packed_layout(p, values, storage) if spec.kind == "stepquant" else format_layout(p, values, spec))[-1]
-               for p in plans)
+    if spec.kind == "stepquant":
+        return sum(packed_layout(plan, values, storage)[-1] for plan in plans)
+    return sum(format_layout(plan, values, spec)[-1] for plan in plans)
 
 
 def size_pool(original, self, total_rest_memory):
-    """Size SGLang's slot count by the packed page size instead of the dense state."""
+    """ModelRunnerKVCacheMixin.handle_max_mamba_cache: size the slot count by the
+    packed bytes of a request instead of SGLang's dense estimate, and return
+    the memory SGLang deducted for dense slots that the packed pool leaves free."""
     params = self.mambaish_config.mamba2_cache_params
     heads, values, keys = params.shape.temporal
-    plans = local_plans(params.layers, heads, "cpu", keys)
-    conv_bytes = sum(__import__("math").prod(shape) for shape in params.shape.conv) * params.dtype.conv.itemsize \
-        * len(params.layers)
-    compact = conv_bytes + page_bytes_per_slot(plans, values, os.environ.get("STEPQUANT_STATE_STORAGE", "packed"))
-    dense = params.mamba_cache_per_req
+    conv = sum(math.prod(shape) for shape in params.shape.conv) * params.dtype.conv.itemsize * len(params.layers)
+    slot_bytes = conv + page_bytes_per_slot(local_plans(params.layers, heads, "cpu", keys), values, _storage())
     server = self.server_args
-    if server.max_mamba_cache_size is None and not (server.disable_radix_cache and server.max_running_requests is not None):
-        state_budget = total_rest_memory * server.mamba_full_memory_ratio / (1 + server.mamba_full_memory_ratio)
-        count = max(0, int(state_budget * (1 << 30) // compact) - 1)
+    if server.max_mamba_cache_size is None and not (server.disable_radix_cache and
+                                                    server.max_running_requests is not None):
+        ratio = server.mamba_full_memory_ratio
+        count = max(0, int(total_rest_memory * ratio / (1 + ratio) * (1 << 30) // slot_bytes) - 1)
         from sglang.srt.distributed import get_tp_group
         group = get_tp_group()
         if group.world_size > 1:
@@ -344,6 +439,5 @@ def size_pool(original, self, total_rest_memory):
             raise ValueError("insufficient memory for a STEPQuant request slot")
         server.max_mamba_cache_size = count * (server.dp_size if server.enable_dp_attention else 1)
     result = original(self, total_rest_memory)
-    # Upstream deducted the dense estimate; account for the packed bytes instead
-    # (slot zero is the sentinel and is counted too).
-    return result + (server.max_mamba_cache_size * (dense - compact) - compact) / (1 << 30)
+    # The sentinel slot 0 is allocated too, so it is deducted once more.
+    return result + (server.max_mamba_cache_size * (params.mamba_cache_per_req - slot_bytes) - slot_bytes) / (1 << 30)

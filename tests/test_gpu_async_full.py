@@ -16,8 +16,8 @@ steps:
   and that state is within 1e-3 of the oracle's ``decode_step``; readouts
   within 2e-2 (bf16).
 
-Reference semantics: stepquant/kernels/pool.py:198-262 (``step`` and
-``_schedule_writeback``) and :264-279 (``_finish_update``).
+Reference semantics: stepquant/kernels/pool.py:200-297 (``step`` and
+``_schedule_writeback``) and :299-316 (``_finish_update``).
 """
 import numpy as np
 import pytest

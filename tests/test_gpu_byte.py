@@ -1,4 +1,4 @@
-"""Byte-carrier pages (PackedStatePool(storage='byte'), kernels/pool.py:34-49,
+"""Byte-carrier pages (PackedStatePool(storage='byte'), kernels/pool.py:29-43,
 fit.py:111-115, byte_codec.py:6-27) on the device against the oracle.
 
 * encode writes exactly the oracle's byte-carrier page image (GDN heads of

@@ -130,7 +130,7 @@ def test_profile_tiers_and_invalid_batches():
 
 @pytest.mark.parametrize("chunk", [32, 64, 128, 256, 512])
 def test_kda_release_keeps_forward_tail_bounded(monkeypatch, chunk):
-    # test_writeback_schedule.py:8-23: the release schedule never accumulates
+    # test_writeback_schedule.py:9-23: the release schedule never accumulates
     # writeback work across recurrent layers.
     from stepquant_b200.kernels.writeback import CapturedWrites
     monkeypatch.setattr(torch.cuda, "Event", lambda **kwargs: SimpleNamespace(record=lambda: None))

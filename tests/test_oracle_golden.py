@@ -50,7 +50,7 @@ def test_codec_streams_match_reference(case):
     assert _same_bits(enc["pivots"], d["pivots"])
     if "two_bit_rows" in d:
         assert _same_bits(enc["two_bit_rows"], d["two_bit_rows"])
-    # decode(encode(x)) is fit_state's reconstruction (test_core.py:46-64).
+    # decode(encode(x)) is fit_state's reconstruction (test_core.py:47-64).
     recon = O.fit_state(d["x"], plan)[-1]
     assert (O.codec_decode(enc, plan) == recon).all()
 
@@ -95,7 +95,7 @@ def test_six_bit_page_has_no_padding(arch):
 
 
 def test_half_aligned_mixed_kda_page():
-    # test_kernel_edges.py:10-32: mixed KDA pages may be only half-aligned.
+    # test_kernel_edges.py:12-34: mixed KDA pages may be only half-aligned.
     plan = O.Plan("kda", np.array([[2, 4, 8, 16]]), np.ones((1, 4), np.float32))
     for values in (4, 32):
         assert O.packed_layout(plan, values)[-1] % 4 == 2

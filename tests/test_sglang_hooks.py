@@ -5,7 +5,7 @@ from types import SimpleNamespace
 import pytest
 import torch
 
-from stepquant_b200.sglang import config, plugin, runtime
+from stepquant_b200.sglang import plugin, runtime
 
 
 def test_writeback_settings_resolve_env(monkeypatch):
@@ -27,14 +27,6 @@ def test_writeback_settings_resolve_env(monkeypatch):
     monkeypatch.delenv("STEPQUANT_WRITEBACK_SMS")
     monkeypatch.delenv("STEPQUANT_WRITEBACK_CHUNK")
     assert runtime.writeback_settings("gdn", 32) == (32, 64)
-
-
-def test_request_limits_and_graph_batches():
-    assert config.request_limit("long") == 64 and config.request_limit("short") == 256
-    assert config.graph_batches(100) == [1, 2, 4, 8, 16, 32, 64, 100]
-    for bad in (0, 513, True, 1.5):
-        with pytest.raises(ValueError):
-            config.request_limit("long", bad)
 
 
 def _artifact(heads_total=8, keys=16, nominal=6):
