@@ -32,6 +32,7 @@ path (StateCodec.decode -> delta_step -> StateCodec.encode, restated in numpy
 by the oracle) on the host cores instead.
 """
 import argparse
+import contextlib
 import ctypes
 import json
 import math
@@ -177,14 +178,22 @@ def algorithmic_bytes(pool_page_bytes, heads_local, qk_local, batch, dim, kda=Fa
 _cpu_state = {}
 
 
-def _cpu_init(seed, heads, qk_heads, dim, requests):
+def _cpu_init(seed, heads, qk_heads, dim, counts, counter, barrier):
+    """Worker set-up: this worker's share of the batch (``counts[i]`` requests
+    for the i-th worker to start)."""
     import numpy as np
     from oracle import stepquant_oracle as O
+    with counter.get_lock():
+        index = counter.value
+        counter.value += 1
+    requests = counts[index]
+    _cpu_state["barrier"] = barrier
     rng = np.random.default_rng(seed)
     widths = np.array(([4] * (heads // 4) + [6] * (heads - 2 * (heads // 4)) + [8] * (heads // 4)))
     rng.shuffle(widths)
     bits = np.repeat(widths[:, None], dim, 1)
     plan = O.Plan("gdn", bits, (rng.random((heads, dim)) + 0.5).astype(np.float32))
+    rng = np.random.default_rng(seed + 1000 + index)
     state = (rng.standard_normal((requests, heads, dim, dim)) * 0.1).astype(np.float32)
     packed = O.codec_encode(state, plan)
     q = rng.standard_normal((requests, qk_heads, dim)).astype(np.float32)
@@ -201,51 +210,58 @@ def _cpu_step(_):
     from oracle import stepquant_oracle as O
     s = _cpu_state
     q, k, v, a, b, a_log, dt_bias = s["inputs"]
-    plan = s["plan"]
-    state = O.codec_decode(s["packed"], plan)
-    qp, kp, g, beta = O.prepare_inputs(q, k, a, b, plan.bits.shape[0], kda=False, normalize=True,
-                                       scale=s["dim"] ** -0.5, a_log=a_log, dt_bias=dt_bias)
-    _, updated = O.delta_step(state, qp, kp, v, g, beta)
-    s["packed"] = O.codec_encode(updated, plan)
+    if q.shape[0]:
+        plan = s["plan"]
+        state = O.codec_decode(s["packed"], plan)
+        qp, kp, g, beta = O.prepare_inputs(q, k, a, b, plan.bits.shape[0], kda=False, normalize=True,
+                                           scale=s["dim"] ** -0.5, a_log=a_log, dt_bias=dt_bias)
+        _, updated = O.delta_step(state, qp, kp, v, g, beta)
+        s["packed"] = O.codec_encode(updated, plan)
+    # Every worker takes exactly one task per step: none returns before all have finished theirs.
+    s["barrier"].wait(timeout=600)
     return int(q.shape[0])
 
 
-def cpu_reference(args, heads, qk_heads, steps, warmup, budget_seconds):
-    """Time the CPU port with one spawned worker per host core; returns a dict."""
+def cpu_reference(args, heads, qk_heads, batch, steps, warmup, budget_seconds=None):
+    """Time the CPU port of the reference path on the host cores: each step is
+    the whole batch, its requests split over one spawned worker per core.
+    Stops early (after at least one timed step) once ``budget_seconds`` of
+    timed steps have run.  Returns a dict."""
     import multiprocessing as mp
-    cores = os.cpu_count() or 1
-    requests = 1
+    cores = max(1, min(os.cpu_count() or 1, batch))
+    counts = [batch // cores + (1 if i < batch % cores else 0) for i in range(cores)]
     ctx = mp.get_context("spawn")
-    with ctx.Pool(cores, initializer=_cpu_init, initargs=(args.seed, heads, qk_heads, args.dim, requests)) as pool:
-        for _ in range(max(1, warmup)):
-            pool.map(_cpu_step, range(cores))
-        times = []
-        t_end = time.perf_counter() + budget_seconds
+    # One thread per worker process (the workers already use every core).
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = "1"
+    initargs = (args.seed, heads, qk_heads, args.dim, counts, ctx.Value("i", 0), ctx.Barrier(cores))
+    with ctx.Pool(cores, initializer=_cpu_init, initargs=initargs) as pool:
+        for _ in range(warmup):
+            pool.map(_cpu_step, range(cores), chunksize=1)
+        times, done = [], 0
         for _ in range(steps):
             t0 = time.perf_counter()
-            done = sum(pool.map(_cpu_step, range(cores)))
+            done = sum(pool.map(_cpu_step, range(cores), chunksize=1))
             times.append(time.perf_counter() - t0)
-            if time.perf_counter() > t_end:
+            if budget_seconds is not None and sum(times) > budget_seconds:
                 break
-    per_step = statistics.median(times)
-    updates = done * heads / per_step
-    return {"value": updates, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{cores} workers x {requests} request x {heads} heads (K=V={args.dim}) per step, "
-                      f"{len(times)} steps, median step {per_step * 1e3:.1f} ms"}
+    per_step = sum(times) / len(times)
+    return {"value": done * heads / per_step, "unit": UNIT, "cores": cores, "kind": "port",
+            "steps": len(times), "ms_per_step": per_step * 1e3, "requests": done,
+            "sample": f"{len(times)} full steps of {done} requests x {heads} heads (K=V={args.dim}) on {cores} "
+                      f"worker processes, mean step {per_step * 1e3:.0f} ms"}
 
 
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    # The reference arm times config 1 (the default workload's shapes).
+    # The reference arm runs config 1 (the default workload's shapes), whole steps.
     batch = args.batch or 256
     qk_heads = args.qk_heads or args.heads // 2
-    res = cpu_reference(args, args.heads, qk_heads, args.steps, args.warmup, max(20.0, args.cpu_seconds * 3))
+    res = cpu_reference(args, args.heads, qk_heads, batch, args.steps, args.warmup)
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup,
-            # one full batch-step at the sampled rate
-            "ms_per_step": batch * args.heads / res["value"] * 1e3, "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "gdn-decode-b%d-h%d-k128 (config 1), CPU port of the reference torch path"
                                    % (batch, args.heads),
@@ -448,52 +464,51 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
             for t, o, nbytes in zip((x.q, x.k, x.v, x.a, x.b), offsets, sizes):
                 buf[o:o + nbytes].copy_(t.contiguous().view(-1).view(torch.uint8).cpu())
             pinned.append(buf)
-        # Two input buffers: step i + 1's inputs cross PCIe on a copy stream
-        # while step i runs, and each step's output goes back on another, as a
-        # serving loop pipelines them.  One graph per (slot group, buffer).
+        # Two input buffers.  Each step is one captured graph (writeback joined):
+        # on a copy stream it brings step i + 1's inputs from pinned host memory
+        # into the other buffer while the step runs, and on another it copies the
+        # step's output back to pinned host memory -- a serving loop's pipeline,
+        # with the host issuing one graph launch per step.
         nbuf = 2
         dev_bufs = [torch.empty(offsets[-1], dtype=torch.uint8, device=device) for _ in range(nbuf)]
         dev_ins = [tuple(buf[o:o + nbytes].view(dt).view(sh) for (sh, dt), o, nbytes in zip(fields, offsets, sizes))
                    for buf in dev_bufs]
         host_outs = [torch.empty(batch, heads_l, dim, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
-        keys = [(g, b) for g in range(len(groups)) for b in range(nbuf)]
-        e2e_graphs = {key: capture(lambda key=key: pool.step(*dev_ins[key[1]], groups[key[0]], **kw), joined=False)
-                      for key in keys}
         h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
-        copied = [torch.cuda.Event() for _ in range(nbuf)]
-        consumed = [torch.cuda.Event() for _ in range(nbuf)]
-        produced = {key: torch.cuda.Event() for key in keys}
-        fetched = {key: torch.cuda.Event() for key in keys}
+        e2e_period = math.lcm(period, nbuf)
 
-        def e2e_step(i):
-            b, key = i % nbuf, (i % len(groups), i % nbuf)
-            main = torch.cuda.current_stream()
-            with torch.cuda.stream(h2d):
-                h2d.wait_event(consumed[b])  # the step that last read this buffer has
-                dev_bufs[b].copy_(pinned[i % len(pinned)], non_blocking=True)
-                copied[b].record()
-            main.wait_event(copied[b])
-            main.wait_event(fetched[key])  # this graph's previous output is on the host
-            graph, out = e2e_graphs[key]
-            graph.replay()
-            consumed[b].record()
-            produced[key].record()
-            with torch.cuda.stream(d2h):
-                d2h.wait_event(produced[key])
-                host_outs[b].copy_(out, non_blocking=True)
-                fetched[key].record()
+        def e2e_graph(i):
+            b, nb = i % nbuf, (i + 1) % nbuf
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                main = torch.cuda.current_stream()
+                deferral = defer_writeback([pool], joined=True) if mode == "async" else contextlib.nullcontext()
+                with deferral as tasks:
+                    h2d.wait_stream(main)
+                    with torch.cuda.stream(h2d):
+                        dev_bufs[nb].copy_(pinned[(i + 1) % len(pinned)], non_blocking=True)
+                    out = pool.step(*dev_ins[b], groups[i % len(groups)], **kw)
+                    d2h.wait_stream(main)
+                    with torch.cuda.stream(d2h):
+                        host_outs[b].copy_(out, non_blocking=True)
+                main.wait_stream(h2d)
+                main.wait_stream(d2h)
+            return WritebackGraph(graph, tasks, joined=True) if mode == "async" else graph
 
+        e2e_graphs = [e2e_graph(i) for i in range(e2e_period)]
+        dev_bufs[0].copy_(pinned[0])  # the first step's inputs; every later step's come with the step before
         for i in range(warmup):
-            e2e_step(i)
+            e2e_graphs[i % e2e_period].replay()
         pool.wait()
-        torch.cuda.current_stream().wait_stream(d2h)
+        dev_bufs[0].copy_(pinned[0])
+        torch.cuda.synchronize()
         barrier()
         e0, e1 = _events()
         e0.record()
         for i in range(steps):
-            e2e_step(i)
+            e2e_graphs[i % e2e_period].replay()
         pool.wait()
-        torch.cuda.current_stream().wait_stream(d2h)
         e1.record()
         barrier()
         host_out = host_outs[0]
@@ -997,7 +1012,7 @@ def main():
         return
     cpu = None
     if not args.no_cpu_baseline and world == 1 and workload == "gdn-decode":
-        cpu = cpu_reference(args, heads, qk_heads, 100, 1, args.cpu_seconds)
+        cpu = cpu_reference(args, heads, qk_heads, batch, 100, 1, args.cpu_seconds)
     line["cpu_baseline"] = cpu
     emit(line)
 

@@ -185,7 +185,9 @@ int32_t sq_readout(const sq_plan *plan, uint8_t *pages, int64_t num_slots, const
  * Background half (PackedStatePool._finish_update, pool.py:299-316: rows.py +
  * fit.py): rebuilds the updated state from the page and the scratch of
  * sq_readout, requantizes and repacks the integer rows of
- * pages[stable_slots[i]].  Produces the same bytes as sq_step.
+ * pages[stable_slots[i]].  Produces the same bytes as sq_step.  state_out is
+ * reserved and must be NULL (sq_step's state_out exposes the pre-quantization
+ * state).
  */
 int32_t sq_writeback(const sq_plan *plan, uint8_t *pages, int64_t num_slots,
                      const int64_t *stable_slots, int32_t batch, const float *scratch,

@@ -100,14 +100,19 @@ int32_t run(int mode, sq::TileParams t, int32_t batch, cudaStream_t stream) {
         t.skip_fast = 1;
     } else if ((fast_mode || gdn_codec) && sq::fast_eligible(t.plan, t.pages)) {
         if (cudaError_t e = sq::launch_fast(mode, t, batch, stream)) return cuda_status(e);
+        sq::PivotHeads ph;
+        const bool pivots = sq::pivot_heads(t.plan, &ph);  // pivot heads run in launch_fast
         bool rest = true;
         if (t.plan.bits_host) {
             rest = false;
-            for (int h = 0; h < t.plan.heads; ++h)
-                rest = rest || !sq::fast_head(t.plan, t.plan.bits_host[h * t.plan.keys]);
+            for (int h = 0; h < t.plan.heads; ++h) {
+                const int width = t.plan.bits_host[h * t.plan.keys];
+                rest = rest || !(sq::fast_head(t.plan, width) || (pivots && width == 16));
+            }
         }
         if (!rest) return SQ_OK;
         t.skip_fast = 1;
+        t.skip_pivot = pivots ? 1 : 0;
     }
     return cuda_status(sq::launch_tile(mode, t, items, stream));
 }
@@ -263,11 +268,10 @@ int32_t sq_writeback(const sq_plan *plan, uint8_t *pages, int64_t num_slots, con
     if (int32_t e = check_plan(plan)) return e;
     if (batch < 0 || num_slots < 1) return SQ_ERR_ARGUMENT;
     if (batch == 0) return SQ_OK;
-    if (!stable_slots || !pages || !scratch) return SQ_ERR_ARGUMENT;
+    if (!stable_slots || !pages || !scratch || state_out) return SQ_ERR_ARGUMENT;  // state_out is reserved
     sq::TileParams t = base_params(plan, pages, num_slots, stable_slots, status);
     t.scratch = const_cast<float *>(scratch);
     t.scratch_stride = sq_scratch_floats(plan);
-    t.dense_out = state_out;
     return run(sq::kWriteback, t, batch, stream);
 }
 

@@ -76,7 +76,6 @@ struct FastSmem {
     float misc[64];
     HeadInfo head[kMaxHeads];
     long long slot_ring[3];  // slots of the current and next two items (cp.async)
-    int flags;
     uint32_t tmem_slot;      // tensor-memory base of the CTA's state columns
     // Last, so that the readout and decode, which requantize nothing, launch
     // without it (four CTAs per SM instead of three).
@@ -283,11 +282,9 @@ __device__ __forceinline__ void column_max(FastSmem &s, int warp, int lane, uint
 // interval it is c0 (every step is monotone).  Tiles with a column where the
 // two differ redo the maxima with exact divisions.
 template <bool SLOW>
-__device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float qmax) {
+__device__ __forceinline__ void fast_quantize_tail(FastSmem &s, const Ctx &c, float qmax) {
     const int warp = c.warp, lane = c.lane, tid = c.tid;
-    // P3: c0 = fp16(max_k |x / r| / qmax) (uniform width: one division per column).
-    column_max<SLOW, SLOW>(s, warp, lane, c.tm);
-    __syncthreads();
+    // P3 (continued): c0 = fp16(max_k |x / r| / qmax) from the warps' partial maxima.
     int safe = 1, settled = 1;
     float mx = 0.f, ratio = 0.f, c0 = 0.f;  // mx: the exact maximum or an upper bound of it
     if (tid < FV) {
@@ -298,31 +295,41 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float q
             mx = m;
             ratio = __fdiv_rn(mx, qmax);
         } else {
+            // qmax (7, 31 or 127) is an exact fp16 value: the corrected
+            // reciprocal division is the IEEE quotient (a subnormal quotient
+            // only arises below the 2^-24 clamp of fp16_scale).
+            const float rq = __frcp_rn(qmax);
             const uint32_t bits = __float_as_uint(m);
             const float lo = bits > 2u ? __uint_as_float(bits - 2u) : 0.f;
             mx = __uint_as_float(bits + 2u);
-            ratio = __fdiv_rn(mx, qmax);
-            settled = fp16_scale(__fdiv_rn(lo, qmax)) == fp16_scale(ratio);
+            ratio = div_fp16(mx, qmax, rq);
+            settled = fp16_scale(div_fp16(lo, qmax, rq)) == fp16_scale(ratio);
         }
-    }
-    if (!SLOW && !__syncthreads_and(settled)) {
-        column_max<false, true>(s, warp, lane, c.tm);
-        __syncthreads();
-        if (tid < FV) {
-            mx = 0.f;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
-            ratio = __fdiv_rn(mx, qmax);
-        }
-    }
-    if (tid < FV) {
         c0 = fp16_scale(ratio);
         s.colc[1][tid] = c0;
         s.colc[2][tid] = __frcp_rn(c0);
         // With c0 a normal, unclamped fp16 value every |x/r/c0| < qmax + 1/2.
         safe = (c0 >= 6.103515625e-05f) && (ratio <= 65504.f);
     }
-    const bool no_clamp = __syncthreads_and(safe);
+    // One barrier in the common case: every column settled and safe.
+    bool no_clamp = __syncthreads_and(settled && safe);
+    if (!no_clamp) {
+        if (!SLOW && !__syncthreads_and(settled)) {
+            column_max<false, true>(s, warp, lane, c.tm);
+            __syncthreads();
+            if (tid < FV) {
+                mx = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
+                ratio = __fdiv_rn(mx, qmax);
+                c0 = fp16_scale(ratio);
+                s.colc[1][tid] = c0;
+                s.colc[2][tid] = __frcp_rn(c0);
+                safe = (c0 >= 6.103515625e-05f) && (ratio <= 65504.f);
+            }
+        }
+        no_clamp = __syncthreads_and(safe);
+    }
     // P4: first levels, weighted least-squares numerator / denominator (16-row blocks).
     {
         float2 num[2], den[2];
@@ -347,31 +354,55 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float q
             den = __fadd_rn(den, s.red[1][w][tid]);
         }
         const float c1 = den > 0.f ? fp16_scale(__fdiv_rn(num, fmaxf(den, 1e-30f))) : s.colc[1][tid];
+        const float rc1 = __frcp_rn(c1);
         s.colc[1][tid] = c1;
-        s.colc[2][tid] = __frcp_rn(c1);
-        safe = (c1 >= 6.103515625e-05f) && (__fdiv_rn(mx, c1) < qmax + 0.5f);
+        s.colc[2][tid] = rc1;
+        // (an overflowing quotient reads as unsafe; an underflowing one is far below qmax)
+        safe = (c1 >= 6.103515625e-05f) && ((SLOW ? __fdiv_rn(mx, c1) : div_fp16(mx, c1, rc1)) < qmax + 0.5f);
     }
     const bool no_clamp5 = __syncthreads_and(safe);
     // P5: final levels -> one signed level byte per value in the plane.
     if (!SLOW && no_clamp5) final_levels<SLOW, false>(s, warp, lane, c.tm, qmax);
     else final_levels<SLOW, true>(s, warp, lane, c.tm, qmax);
-    __syncthreads();
+    // Every code byte of a row comes from the warp that owns the row, and that
+    // warp packs the row's chunks (fast_store).
+    __syncwarp();
+}
+
+// P3-P5.  `warp_slow`: a row of this warp has an |x| sum beyond 2^96 (or NaN),
+// so its partial maxima use IEEE divisions; the whole tile switches to IEEE
+// divisions when any warp is slow (the partial maxima of the other warps are
+// then taken again with IEEE divisions).  The barrier that completes the
+// partial maxima also combines the warps' flags.
+__device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float qmax, bool warp_slow) {
+    if (warp_slow) column_max<true, true>(s, c.warp, c.lane, c.tm);
+    else column_max<false, false>(s, c.warp, c.lane, c.tm);
+    if (__syncthreads_or(warp_slow)) {
+        if (!warp_slow) column_max<true, true>(s, c.warp, c.lane, c.tm);
+        __syncthreads();
+        fast_quantize_tail<true>(s, c, qmax);
+    } else {
+        fast_quantize_tail<false>(s, c, qmax);
+    }
 }
 
 // Pack the code plane into the page (2*BITS bytes per row-tile chunk) and store r and c.
+// Warp w packs the chunks of its own rows 16w..16w+15 (all eight value tiles),
+// four per lane, and stores their row scales; threads 128-255 store c.
 template <int BITS>
 __device__ __forceinline__ void fast_store(const TileParams &p, FastSmem &s, const Ctx &c) {
     const sq_plan &P = p.plan;
     uint8_t *dst = c.page + c.off_head;
-    for (int ch = c.tid; ch < kTiles * FK; ch += kThreads) {
-        const int t = ch / FK, k = ch % FK;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int i = c.lane + 32 * m, t = i >> 4, k = c.warp * 16 + (i & 15);
         store_chunk<BITS>(dst + t * W<BITS>::tile_bytes + k * W<BITS>::chunk, s.plane + t * (FK * 16 + kStagePad) + k * 16);
     }
-    if (c.tid < FK) {
-        reinterpret_cast<__half *>(c.page + P.rows[c.head * FK])[c.tid] = __float2half_rn(s.rowa[c.tid].x);
-    } else {
-        reinterpret_cast<__half *>(c.page + P.columns[c.head])[c.tid - FK] = __float2half_rn(s.colc[1][c.tid - FK]);
+    if (c.lane < 16) {
+        const int k = c.warp * 16 + c.lane;
+        reinterpret_cast<__half *>(c.page + P.rows[c.head * FK])[k] = __float2half_rn(s.rowa[k].x);
     }
+    if (c.tid >= FK) reinterpret_cast<__half *>(c.page + P.columns[c.head])[c.tid - FK] = __float2half_rn(s.colc[1][c.tid - FK]);
 }
 
 // Stage the head's code bytes (cp.async, 16-byte pieces, one padded region per value tile).
@@ -544,6 +575,85 @@ __device__ __forceinline__ void decode_rows(const FastStage &st, int warp, int l
         row[32] = x01.y;
         row[64] = x23.x;
         row[96] = x23.y;
+    }
+}
+
+// fp16 pivot heads (width 16): the page holds x.half() of every value in the
+// value-tile layout -- tile t (16 values) is 128 rows of 32 bytes -- and no
+// scales.  Lane l covers the four consecutive columns 4l..4l+3 (tile l / 4,
+// bytes 8 (l % 4) .. +7 of a row), warp w the rows 16w..16w+15; a pivot head
+// is read straight from global memory (it is not staged).
+__device__ __forceinline__ uint8_t *pivot_lane(uint8_t *head, int warp, int lane) {
+    return head + (lane >> 2) * (FK * 32) + (lane & 3) * 8 + warp * 16 * 32;
+}
+__device__ __forceinline__ void halves4(uint2 raw, float2 &lo, float2 &hi) {
+    lo = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+    hi = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+}
+
+// P1 of the step and readout for a pivot head: column partials of k_raw^T Y
+// and q_raw^T Y over the warp's 16 rows, in row order (as readout_rows).
+template <class Smem>
+__device__ __forceinline__ void pivot_rows(Smem &s, uint8_t *head, int warp, int lane) {
+    const uint8_t *src = pivot_lane(head, warp, lane);
+    float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
+#pragma unroll 4
+    for (int r = 0; r < 16; ++r) {
+        const int k = warp * 16 + r;
+        float2 y01, y23;
+        halves4(*reinterpret_cast<const uint2 *>(src + r * 32), y01, y23);
+        const float4 a = s.rowa[k], b = s.rowb[k];
+        kx01 = pfma2(hi2(a), y01, kx01);
+        kx23 = pfma2(hi2(a), y23, kx23);
+        qx01 = pfma2(lo2(b), y01, qx01);
+        qx23 = pfma2(lo2(b), y23, qx23);
+    }
+    *reinterpret_cast<float4 *>(&s.red[0][warp][4 * lane]) = make_float4(kx01.x, kx01.y, kx23.x, kx23.y);
+    *reinterpret_cast<float4 *>(&s.red[1][warp][4 * lane]) = make_float4(qx01.x, qx01.y, qx23.x, qx23.y);
+}
+
+// The pivot head's update in place: x' = Y (c decay) + k delta per value (the
+// same operations as the integer heads' update), stored as fp16; the fp32 x'
+// also to `dense` ([K, V] of this item) when given.
+template <class Smem>
+__device__ __forceinline__ void pivot_update(const Smem &s, uint8_t *head, int warp, int lane, float *dense) {
+    uint8_t *dst = pivot_lane(head, warp, lane);
+    const float4 d = *reinterpret_cast<const float4 *>(&s.colc[0][4 * lane]);
+    const float4 cd = *reinterpret_cast<const float4 *>(&s.colc[3][4 * lane]);
+    const float2 d01 = lo2(d), d23 = hi2(d), cd01 = lo2(cd), cd23 = hi2(cd);
+#pragma unroll 4
+    for (int r = 0; r < 16; ++r) {
+        const int k = warp * 16 + r;
+        float2 y01, y23;
+        uint2 *word = reinterpret_cast<uint2 *>(dst + r * 32);
+        halves4(*word, y01, y23);
+        const float2 kk = hi2(s.rowa[k]);
+        const float2 x01 = pfma2(kk, d01, pmul2(y01, cd01));
+        const float2 x23 = pfma2(kk, d23, pmul2(y23, cd23));
+        const __half2 h01 = __float22half2_rn(x01), h23 = __float22half2_rn(x23);
+        *word = make_uint2(*reinterpret_cast<const uint32_t *>(&h01), *reinterpret_cast<const uint32_t *>(&h23));
+        if (dense) *reinterpret_cast<float4 *>(dense + k * FV + 4 * lane) = make_float4(x01.x, x01.y, x23.x, x23.y);
+    }
+}
+
+// Encode / decode of a pivot head: dense fp32 rows <-> fp16 values.
+__device__ __forceinline__ void pivot_encode(const float *src, uint8_t *head, int warp, int lane) {
+    uint8_t *dst = pivot_lane(head, warp, lane);
+#pragma unroll 4
+    for (int r = 0; r < 16; ++r) {
+        const float4 x = *reinterpret_cast<const float4 *>(src + (warp * 16 + r) * FV + 4 * lane);
+        const __half2 h01 = __floats2half2_rn(x.x, x.y), h23 = __floats2half2_rn(x.z, x.w);
+        *reinterpret_cast<uint2 *>(dst + r * 32) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&h01), *reinterpret_cast<const uint32_t *>(&h23));
+    }
+}
+__device__ __forceinline__ void pivot_decode(uint8_t *head, float *dst, int warp, int lane) {
+    const uint8_t *src = pivot_lane(head, warp, lane);
+#pragma unroll 4
+    for (int r = 0; r < 16; ++r) {
+        float2 y01, y23;
+        halves4(*reinterpret_cast<const uint2 *>(src + r * 32), y01, y23);
+        *reinterpret_cast<float4 *>(dst + (warp * 16 + r) * FV + 4 * lane) = make_float4(y01.x, y01.y, y23.x, y23.y);
     }
 }
 
@@ -776,7 +886,9 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
     }
 
     // ---- P2: rank-1 update; row sums of |x| in torch order; new row scales ---
+    bool warp_slow;
     {
+        bool huge = false;
         float *rowpart = reinterpret_cast<float *>(s.plane);
         if (MODE == kStep) {
             const float2 d01 = make_float2(s.colc[0][lane], s.colc[0][lane + 32]);
@@ -807,8 +919,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
             }
         }
         tm_wait_st();
-        if (tid == 0) s.flags = 0;
-        __syncthreads();
+        __syncwarp();  // a warp's row partials are written and finished by that warp alone
         // Lanes j and j+16 finish row 16*warp + j: S_l = ((A_l + A_{l+8}) + A_{l+16}) + A_{l+24},
         // total = S_0 + S_1 + ... + S_7 in order.
         const int j = lane & 15, half = lane >> 4;
@@ -833,17 +944,13 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
             const float w2 = __fmul_rn(w, w);
             s.rowa[k] = make_float4(rr, rr, rc, rc);
             s.rowb[k] = make_float4(-rr, -rr, w2, w2);
-            if (!(total <= 7.922816251426434e28f)) atomicOr(&s.flags, 1);  // 2^96, or NaN
+            huge = !(total <= 7.922816251426434e28f);  // 2^96, or NaN
         }
+        // The warp's new row constants are read by the warp alone (its P3 - P5 rows).
+        __syncwarp();
+        warp_slow = __any_sync(0xffffffffu, huge);
     }
-    __syncthreads();
-    const float qmax = float((1 << (width - 1)) - 1);
-    if (s.flags) {
-        // Pathological magnitudes: IEEE divisions for the whole tile.
-        fast_quantize<true>(s, c, qmax);
-    } else {
-        fast_quantize<false>(s, c, qmax);
-    }
+    fast_quantize(s, c, float((1 << (width - 1)) - 1), warp_slow);
     if (width == 4) fast_store<4>(p, s, c);
     else if (width == 6) fast_store<6>(p, s, c);
     else fast_store<8>(p, s, c);
@@ -965,6 +1072,110 @@ __global__ void __launch_bounds__(kThreads, MODE == kReadout ? 4 : 3) fast_kerne
     }
 }
 
+// ---------------------------------------------------------------------------
+// fp16 pivot heads: one CTA per (request, pivot head).  Step and readout alike
+// read the head's values, form the column partials of k^T Y and q^T Y, the
+// gates and the readout (the operations of fast_body with unit row and column
+// scales), and write the updated values back as fp16 -- the reference's
+// readout stores pivot rows itself, so the writeback has nothing to do for
+// them.  Encode and decode convert between fp32 and fp16.
+// ---------------------------------------------------------------------------
+struct PivotSmem {
+    float4 rowa[FK];  // {1, 1, k, k}: raw k, then the normalised k
+    float4 rowb[FK];  // {q, q, -, -} raw q
+    float red[2][8][FV];
+    float colc[4][FV];  // [0] delta, [3] decay (c = 1)
+    float misc[64];
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) pivot_kernel(TileParams p, PivotHeads ph) {
+    __shared__ PivotSmem s;
+    const sq_plan &P = p.plan;
+    const int H = P.heads;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int req = blockIdx.x / ph.count, head = ph.ids[blockIdx.x % ph.count];
+    const int64_t item = int64_t(req) * H + head;
+    const long long slot = p.slots[req];
+    if (!(slot > 0 && slot < p.num_slots)) {
+        if (slot > 0 && tid == 0) flag(p.status, SQ_STATUS_SLOT_RANGE);
+        if ((MODE == kStep || MODE == kReadout) && tid < FV) store_from_float(p.step.out, p.step.io_dtype, item * FV + tid, 0.f);
+        if ((MODE == kStep || MODE == kDecode) && p.dense_out)
+            for (int e = tid; e < FK * FV; e += kThreads) p.dense_out[item * FK * FV + e] = 0.f;
+        return;
+    }
+    uint8_t *values = p.pages + slot * P.page_bytes + P.offsets[head * FK];
+    if (MODE == kEncode) {
+        pivot_encode(p.dense_in + item * FK * FV, values, warp, lane);
+        return;
+    }
+    if (MODE == kDecode) {
+        pivot_decode(values, p.dense_out + item * FK * FV, warp, lane);
+        return;
+    }
+    const sq_step_args &a = p.step;
+    float qraw = 0.f, kraw = 0.f, vin = 0.f, braw = 0.f, graw = 0.f;
+    if (tid < FK) {
+        const int qh = head / (H / a.qk_heads);
+        qraw = load_as_float(a.q, a.io_dtype, int64_t(req) * a.q_stride + int64_t(qh) * FK + tid);
+        kraw = load_as_float(a.k, a.io_dtype, int64_t(req) * a.k_stride + int64_t(qh) * FK + tid);
+        vin = load_as_float(a.v, a.io_dtype, int64_t(req) * a.v_stride + int64_t(head) * FV + tid);
+        braw = load_as_float(a.beta, a.gate_dtype, item);
+        graw = load_as_float(a.g, a.gate_dtype, item);
+        s.rowa[tid] = make_float4(1.f, 1.f, kraw, kraw);
+        s.rowb[tid] = make_float4(qraw, qraw, 0.f, 0.f);
+        float3 part = make_float3(__fmul_rn(qraw, qraw), __fmul_rn(kraw, kraw), __fmul_rn(qraw, kraw));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            part.x += __shfl_xor_sync(0xffffffffu, part.x, o);
+            part.y += __shfl_xor_sync(0xffffffffu, part.y, o);
+            part.z += __shfl_xor_sync(0xffffffffu, part.z, o);
+        }
+        if (lane == 0) *reinterpret_cast<float4 *>(&s.misc[4 * warp]) = make_float4(part.x, part.y, part.z, 0.f);
+    }
+    __syncthreads();
+    pivot_rows(s, values, warp, lane);
+    __syncthreads();
+    if (tid < FV) {
+        const float beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
+        float g = graw;
+        if (a.a_log) {
+            const float u = g + a.dt_bias[head];
+            g = -expf(a.a_log[head]) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
+        }
+        const float decay = expf(g);
+        float qq = 0.f, kk = 0.f, dot = 0.f;
+#pragma unroll
+        for (int w = 0; w < FK / 32; ++w) {
+            const float4 m = reinterpret_cast<const float4 *>(s.misc)[w];
+            qq += m.x;
+            kk += m.y;
+            dot += m.z;
+        }
+        const float qn = a.normalize ? __frsqrt_rn(qq + 1e-6f) : 1.f;
+        const float kn = a.normalize ? __frsqrt_rn(kk + 1e-6f) : 1.f;
+        const float qscale = __fmul_rn(qn, a.scale);
+        const float qk = __fmul_rn(__fmul_rn(__fmul_rn(dot, qn), kn), a.scale);
+        float ks = 0.f, qs = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            ks = __fadd_rn(ks, s.red[0][w][tid]);
+            qs = __fadd_rn(qs, s.red[1][w][tid]);
+        }
+        const float kS = __fmul_rn(__fmul_rn(ks, kn), decay);
+        const float qS = __fmul_rn(__fmul_rn(qs, qscale), decay);
+        const float delta = __fmul_rn(beta, __fsub_rn(vin, kS));
+        const float kx = __fmul_rn(kraw, kn);
+        s.colc[0][tid] = delta;
+        s.colc[3][tid] = decay;
+        s.rowa[tid].z = kx;
+        s.rowa[tid].w = kx;
+        store_from_float(a.out, a.io_dtype, item * FV + tid, __fmaf_rn(qk, delta, qS));
+    }
+    __syncthreads();
+    pivot_update(s, values, warp, lane, MODE == kStep && p.dense_out ? p.dense_out + item * FK * FV : nullptr);
+}
+
 // Resident CTAs per SM for each mode, and SMs, per device (set up on the first
 // launch on a device).
 constexpr int kMaxDevices = 64;
@@ -1070,14 +1281,38 @@ cudaError_t launch_fast(int mode, const TileParams &params, int batch, cudaStrea
         p.stage_gates = a.gate_dtype == SQ_F32 && (reinterpret_cast<uintptr_t>(a.g) & 3u) == 0 &&
                         (reinterpret_cast<uintptr_t>(a.beta) & 3u) == 0;
     }
+    cudaError_t err;
     switch (mode) {
-        case kStep: return launch_fast_mode<kStep>(p, items, stream);
-        case kReadout: return launch_fast_mode<kReadout>(p, items, stream);
-        case kWriteback: return launch_fast_mode<kWriteback>(p, items, stream);
-        case kEncode: return launch_fast_mode<kEncode>(p, items, stream);
-        case kDecode: return launch_fast_mode<kDecode>(p, items, stream);
+        case kStep: err = launch_fast_mode<kStep>(p, items, stream); break;
+        case kReadout: err = launch_fast_mode<kReadout>(p, items, stream); break;
+        case kWriteback: err = launch_fast_mode<kWriteback>(p, items, stream); break;
+        case kEncode: err = launch_fast_mode<kEncode>(p, items, stream); break;
+        case kDecode: err = launch_fast_mode<kDecode>(p, items, stream); break;
         default: return cudaErrorNotSupported;
     }
+    if (err != cudaSuccess || mode == kWriteback) return err;
+    PivotHeads ph;
+    if (!pivot_heads(p.plan, &ph) || ph.count == 0) return cudaSuccess;
+    const int grid = batch * ph.count;
+    switch (mode) {
+        case kStep: pivot_kernel<kStep><<<grid, kThreads, 0, stream>>>(p, ph); break;
+        case kReadout: pivot_kernel<kReadout><<<grid, kThreads, 0, stream>>>(p, ph); break;
+        case kEncode: pivot_kernel<kEncode><<<grid, kThreads, 0, stream>>>(p, ph); break;
+        default: pivot_kernel<kDecode><<<grid, kThreads, 0, stream>>>(p, ph); break;
+    }
+    return cudaGetLastError();
+}
+
+bool pivot_heads(const sq_plan &plan, PivotHeads *out) {
+    out->count = 0;
+    if (plan.architecture != SQ_GDN || plan.keys != FK || plan.values != FV || plan.storage != 0 || !plan.bits_host)
+        return false;
+    for (int h = 0; h < plan.heads; ++h) {
+        if (plan.bits_host[h * plan.keys] != 16) continue;
+        if (out->count == kMaxPivotHeads) return false;
+        out->ids[out->count++] = h;
+    }
+    return true;
 }
 
 

@@ -27,6 +27,7 @@ struct TileParams {
     float *fit_recon;
     int32_t *status;
     int skip_fast;  // tile kernel: leave heads that fast_head() accepts to the fast kernel
+    int skip_pivot;  // tile kernel: leave GDN fp16 pivot heads to the pivot kernel
     int stage_inputs;  // fast kernels: q/k/v (or writeback scratch) rows are 16-byte aligned -> cp.async staging
     int stage_gates;   // fast kernels: fp32 gates -> cp.async staging
 };
@@ -35,14 +36,24 @@ size_t tile_smem_bytes(int K, int V, int groups);
 cudaError_t launch_tile(int mode, const TileParams &p, int items, cudaStream_t stream);
 
 // Register-resident kernels for K = V = 128 GDN heads of width 4, 6 or 8
-// (sq_fast.cu) for the step, readout and writeback modes.  fast_eligible():
-// the plan's shape and the page alignment allow them; fast_head(): a head of
-// that width is handled by them (the tile kernel handles the others).
+// (sq_fast.cu) for the step, readout, writeback, encode and decode modes.
+// fast_eligible(): the plan's shape and the page alignment allow them;
+// fast_head(): a head of that width is handled by them.  launch_fast also
+// runs the fp16 pivot heads that pivot_heads() lists (a second kernel; none
+// in the writeback, whose pivot values the readout already wrote).  The tile
+// kernel handles the other heads (GDN 2-bit heads; pivot heads when the plan
+// has no host copy of its bits or more than kMaxPivotHeads of them).
 bool fast_eligible(const sq_plan &plan, const void *pages);
 __host__ __device__ inline bool fast_head(const sq_plan &plan, int width) {
     return plan.architecture == SQ_GDN && plan.keys == 128 && plan.values == 128 &&
            (width == 4 || width == 6 || width == 8);
 }
+constexpr int kMaxPivotHeads = 32;
+struct PivotHeads {
+    int count;
+    int ids[kMaxPivotHeads];
+};
+bool pivot_heads(const sq_plan &plan, PivotHeads *out);
 cudaError_t launch_fast(int mode, const TileParams &p, int batch, cudaStream_t stream);
 
 // Register-resident kernels for KDA heads with K = V = 128 (sq_fast_kda.cu):
@@ -59,7 +70,7 @@ cudaError_t launch_fast_kda(int mode, const TileParams &p, int batch, cudaStream
 // kernel, launched with skip_fast, leaves it)?
 __device__ inline bool fast_head_dev(const sq_plan &P, int head) {
     if (P.storage != 0) return false;
-    if (P.architecture == SQ_GDN) return fast_head(P, P.bits[head * P.keys]);
+    if (P.architecture == SQ_GDN) return fast_head(P, P.bits[head * P.keys]);  // (pivot heads: skip_pivot)
     return P.keys == 128 && P.values == 128 &&
            kda_head_fits(P.offsets[P.heads * P.keys + head], P.values, P.columns[head]);
 }

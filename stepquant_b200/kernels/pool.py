@@ -268,13 +268,13 @@ class PackedStatePool:
         self.completion = self.ready if capture is None else self.graph_ready
         self.pending = True
 
-    def _finish_update(self, scratch, stable_slots, state_out=None):
+    def _finish_update(self, scratch, stable_slots):
         """Requantize and repack the pages of one chunk on the current stream (pool.py:299-316)."""
         batch = stable_slots.numel()
         if not batch:
             return
         N.check(N.lib().sq_writeback(self._dp.ref(), N.ptr(self.data), self.data.shape[0], N.ptr(stable_slots),
-                                     batch, N.ptr(scratch), N.ptr(state_out), N.ptr(self.status),
+                                     batch, N.ptr(scratch), None, N.ptr(self.status),
                                      N.stream_handle()))
 
     def _pending_events(self, stream):

@@ -84,12 +84,15 @@ def _run(arch, plan, oplan, batch, heads, qk, seed, check):
             assert (got[s[i]] == expected[j]).all(), f"step {step}, request {i}: bytes differ from the oracle"
 
 
-def test_gdn_config1_async_full_size():
+@pytest.mark.parametrize("pivot_heads", [0, 1])
+def test_gdn_config1_async_full_size(pivot_heads):
     """B = 256, 32 value heads over 16 qk heads, widths {4, 6, 8} at 8/16/8
-    (seed 1): 8,192 items per launch, the power-of-two item split."""
+    (seed 1): 8,192 items per launch, the power-of-two item split.  With a
+    fp16 pivot head the readout updates that head's values in place and the
+    writeback leaves them."""
     from stepquant_b200 import synthetic as S
     gen = torch.Generator().manual_seed(1)
-    widths = S.gdn_widths(32, gen)
+    widths = S.gdn_widths(32, gen, pivot_heads=pivot_heads)
     bits = widths[:, None].expand(32, 128).clone()
     plan, oplan = _plan("gdn", bits, 1)
     _run("gdn", plan, oplan, 256, 32, 16, 1, [0, 1, 77, 200, 255])
