@@ -70,7 +70,8 @@ def parse_args():
     p.add_argument("--heads", type=int, default=32)
     p.add_argument("--qk-heads", type=int, default=0, help="default: heads / 2 (GDN), heads (KDA)")
     p.add_argument("--dim", type=int, default=128)
-    p.add_argument("--pivot-heads", type=int, default=0)
+    p.add_argument("--pivot-heads", type=int, default=1,
+                   help="GDN heads stored as fp16 pivots (1% of 32 heads rounds to 0; at least one exercises the fp16 path)")
     p.add_argument("--slot-groups", type=int, default=4)
     p.add_argument("--warm-steps", type=int, default=256)
     p.add_argument("--seed", type=int, default=1)

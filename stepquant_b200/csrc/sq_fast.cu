@@ -425,30 +425,45 @@ template <int BITS>
 __device__ __forceinline__ void readout_rows(FastSmem &s, const FastStage &st, int warp, int lane) {
     const int gq = lane & 3;
     const unsigned char *tile = st.codes + (lane >> 2) * (W<BITS>::tile_bytes + kStagePad);
-    constexpr uint32_t mask = (1u << BITS) - 1u;
-    constexpr float bias = -(8388608.f + float(W<BITS>::off));
-    const float2 nbias = make_float2(bias, bias);
+    constexpr float off = float(W<BITS>::off);
+    // Code i of the lane's four is taken with its bits in place, ORed into
+    // 2^23; level = f * 2^-(its bit position) - (2^(23 - position) + offset),
+    // exact (8-bit codes are moved to bit 0 by a byte permute; the fourth 6-bit
+    // code by a shift, its bits would reach the exponent field).
+    constexpr int p1 = BITS == 8 ? 0 : BITS, p2 = BITS == 8 ? 0 : 2 * BITS, p3 = BITS == 4 ? 12 : 0;
+    const float2 sc01 = make_float2(1.f, __uint_as_float(uint32_t(127 - p1) << 23));
+    const float2 sc23 = make_float2(__uint_as_float(uint32_t(127 - p2) << 23), __uint_as_float(uint32_t(127 - p3) << 23));
+    const float2 bi01 = make_float2(-(8388608.f + off), -(8388608.f * sc01.y + off));
+    const float2 bi23 = make_float2(-(8388608.f * sc23.x + off), -(8388608.f * sc23.y + off));
     float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
 #pragma unroll 4
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
         const unsigned char *chunk = tile + k * W<BITS>::chunk;
-        uint32_t v;
+        uint32_t f0, f1, f2, f3;
         if (BITS == 8) {
-            v = *reinterpret_cast<const uint32_t *>(chunk + 4 * gq);
+            const uint32_t v = *reinterpret_cast<const uint32_t *>(chunk + 4 * gq);
+            f0 = __byte_perm(v, 0x4B000000u, 0x7650);
+            f1 = __byte_perm(v, 0x4B000000u, 0x7651);
+            f2 = __byte_perm(v, 0x4B000000u, 0x7652);
+            f3 = __byte_perm(v, 0x4B000000u, 0x7653);
         } else if (BITS == 4) {
-            v = *reinterpret_cast<const uint16_t *>(chunk + 2 * gq);
+            const uint32_t v = *reinterpret_cast<const uint16_t *>(chunk + 2 * gq);
+            f0 = 0x4B000000u | (v & 0xFu);
+            f1 = 0x4B000000u | (v & 0xF0u);
+            f2 = 0x4B000000u | (v & 0xF00u);
+            f3 = 0x4B000000u | (v & 0xF000u);
         } else {  // 3 bytes at 3 gq: two words and a funnel shift (the second word may be the next chunk's)
             const uint32_t *words = reinterpret_cast<const uint32_t *>(chunk) + ((3 * gq) >> 2);
-            v = __funnelshift_r(words[0], words[1], (3 * gq & 3) * 8);
+            const uint32_t v = __funnelshift_r(words[0], words[1], (3 * gq & 3) * 8);
+            f0 = 0x4B000000u | (v & 0x3Fu);
+            f1 = 0x4B000000u | (v & 0xFC0u);
+            f2 = 0x4B000000u | (v & 0x3F000u);
+            f3 = 0x4B000000u | ((v >> 18) & 0x3Fu);
         }
         const float4 a = s.rowa[k], b = s.rowb[k];
-        const float2 f01 = make_float2(__uint_as_float(0x4B000000u | (v & mask)),
-                                       __uint_as_float(0x4B000000u | ((v >> BITS) & mask)));
-        const float2 f23 = make_float2(__uint_as_float(0x4B000000u | ((v >> (2 * BITS)) & mask)),
-                                       __uint_as_float(0x4B000000u | ((v >> (3 * BITS)) & mask)));
-        const float2 y01 = pmul2(__fadd2_rn(f01, nbias), lo2(a));  // exact level, then * r_old
-        const float2 y23 = pmul2(__fadd2_rn(f23, nbias), lo2(a));
+        const float2 y01 = pmul2(pfma2(make_float2(__uint_as_float(f0), __uint_as_float(f1)), sc01, bi01), lo2(a));
+        const float2 y23 = pmul2(pfma2(make_float2(__uint_as_float(f2), __uint_as_float(f3)), sc23, bi23), lo2(a));
         kx01 = pfma2(hi2(a), y01, kx01);
         kx23 = pfma2(hi2(a), y23, kx23);
         qx01 = pfma2(lo2(b), y01, qx01);
@@ -597,7 +612,7 @@ template <class Smem>
 __device__ __forceinline__ void pivot_rows(Smem &s, uint8_t *head, int warp, int lane) {
     const uint8_t *src = pivot_lane(head, warp, lane);
     float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
-#pragma unroll 4
+#pragma unroll
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
         float2 y01, y23;
@@ -621,7 +636,7 @@ __device__ __forceinline__ void pivot_update(const Smem &s, uint8_t *head, int w
     const float4 d = *reinterpret_cast<const float4 *>(&s.colc[0][4 * lane]);
     const float4 cd = *reinterpret_cast<const float4 *>(&s.colc[3][4 * lane]);
     const float2 d01 = lo2(d), d23 = hi2(d), cd01 = lo2(cd), cd23 = hi2(cd);
-#pragma unroll 4
+#pragma unroll
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
         float2 y01, y23;
@@ -639,7 +654,7 @@ __device__ __forceinline__ void pivot_update(const Smem &s, uint8_t *head, int w
 // Encode / decode of a pivot head: dense fp32 rows <-> fp16 values.
 __device__ __forceinline__ void pivot_encode(const float *src, uint8_t *head, int warp, int lane) {
     uint8_t *dst = pivot_lane(head, warp, lane);
-#pragma unroll 4
+#pragma unroll
     for (int r = 0; r < 16; ++r) {
         const float4 x = *reinterpret_cast<const float4 *>(src + (warp * 16 + r) * FV + 4 * lane);
         const __half2 h01 = __floats2half2_rn(x.x, x.y), h23 = __floats2half2_rn(x.z, x.w);
@@ -649,7 +664,7 @@ __device__ __forceinline__ void pivot_encode(const float *src, uint8_t *head, in
 }
 __device__ __forceinline__ void pivot_decode(uint8_t *head, float *dst, int warp, int lane) {
     const uint8_t *src = pivot_lane(head, warp, lane);
-#pragma unroll 4
+#pragma unroll
     for (int r = 0; r < 16; ++r) {
         float2 y01, y23;
         halves4(*reinterpret_cast<const uint2 *>(src + r * 32), y01, y23);
@@ -784,18 +799,17 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
             braw = p.stage_gates ? st.gate[0] : load_as_float(a.beta, a.gate_dtype, int64_t(c.req) * H + c.head);
             graw = p.stage_gates ? st.gate[1] : load_as_float(a.g, a.gate_dtype, int64_t(c.req) * H + c.head);
         }
-        // Per-warp sums of q^2, k^2 and q.k (combined after the next barrier).
-        float3 part = make_float3(__fmul_rn(qraw, qraw), __fmul_rn(kraw, kraw), __fmul_rn(qraw, kraw));
+        // Per-warp sums of q^2, k^2 and q.k over the warps holding q and k
+        // (threads 0..K-1), combined after the next barrier.
+        if (tid < FK) {
+            float3 part = make_float3(__fmul_rn(qraw, qraw), __fmul_rn(kraw, kraw), __fmul_rn(qraw, kraw));
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            part.x += __shfl_xor_sync(0xffffffffu, part.x, o);
-            part.y += __shfl_xor_sync(0xffffffffu, part.y, o);
-            part.z += __shfl_xor_sync(0xffffffffu, part.z, o);
-        }
-        if (lane == 0) {
-            s.misc[4 * warp] = part.x;
-            s.misc[4 * warp + 1] = part.y;
-            s.misc[4 * warp + 2] = part.z;
+            for (int o = 16; o > 0; o >>= 1) {
+                part.x += __shfl_xor_sync(0xffffffffu, part.x, o);
+                part.y += __shfl_xor_sync(0xffffffffu, part.y, o);
+                part.z += __shfl_xor_sync(0xffffffffu, part.z, o);
+            }
+            if (lane == 0) *reinterpret_cast<float4 *>(&s.misc[4 * warp]) = make_float4(part.x, part.y, part.z, 0.f);
         }
     }
     __syncthreads();
@@ -847,7 +861,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
             if (tid < FV) {
                 float qq = 0.f, kk = 0.f, dot = 0.f;
 #pragma unroll
-                for (int w = 0; w < kThreads / 32; ++w) {
+                for (int w = 0; w < FK / 32; ++w) {
                     const float4 m = reinterpret_cast<const float4 *>(s.misc)[w];
                     qq += m.x;
                     kk += m.y;
