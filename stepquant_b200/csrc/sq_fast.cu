@@ -1260,6 +1260,9 @@ cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream
         if (resident) resident->store(per_sm, std::memory_order_relaxed);
         if (device < kMaxDevices) g_sms[device].store(sms, std::memory_order_relaxed);
     }
+    // Every resident slot gets a CTA; CTA b takes items b, b + grid, ... so each
+    // SM's share of the items differs from the mean by less than one per CTA
+    // (the kernels are issue-bound per SM; fewer, evenly loaded CTAs were measured slower).
     const int grid = std::max(1, std::min(items, per_sm * stream_sms(stream, sms)));
     fast_kernel<MODE><<<grid, kThreads, smem, stream>>>(p, items);
     return cudaGetLastError();

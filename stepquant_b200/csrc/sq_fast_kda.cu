@@ -46,8 +46,8 @@ struct KdaSmem {
     uint32_t tmem_slot;  // tensor-memory base of the CTA's state columns
     // Last, so that the readout, which goes without it, launches without it.
     union alignas(16) {
-        __half plane[DK * DV];          // P0 -> P1 and P5 -> store: [k][l][i] = column l + 32 i
-        float rowpart[DK * kRowPart];   // P2 row partials
+        float rowpart[DK * kRowPart];    // P2 row partials
+        unsigned char code[DK * DV];     // P5 -> pack: the code of value v of row k at k * DV + v
     } u;
 };
 
@@ -58,31 +58,24 @@ constexpr uint32_t kTmCols = 128;
 
 __device__ __forceinline__ int qmax_i(int b) { return (1 << ((b > 8 ? 8 : b) - 1)) - 1; }
 
-// P0: unpack every (row, tile) chunk of the staged codes into the fp16 plane.
-__device__ __forceinline__ void kda_unpack(KdaSmem &s, int lead, int off0, int stride, int tid) {
-    for (int idx = tid; idx < DK * DTILES; idx += kThreads) {
-        const int k = idx >> 5, t = idx & 31;
-        const int b = s.bits[k];
-        const unsigned char *src = s.codes + lead + (s.offs[k] - off0) + t * stride;
-        __half h[4];
-        if (b == 16) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) h[j] = __ushort_as_half(uint16_t(src[2 * j] | (uint16_t(src[2 * j + 1]) << 8)));
-        } else {
-            uint32_t w = src[0];
-            if (b >= 4) w |= uint32_t(src[1]) << 8;
-            if (b >= 6) w |= uint32_t(src[2]) << 16;
-            if (b == 8) w |= uint32_t(src[3]) << 24;
-            const int off = qmax_i(b), mask = (1 << b) - 1;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) h[j] = __int2half_rn(int((w >> (j * b)) & uint32_t(mask)) - off);
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int v = 4 * t + j;
-            s.u.plane[k * DV + (v & 31) * 4 + (v >> 5)] = h[j];
-        }
-    }
+// Row decode of the step and writeback (P1 straight from the staged bytes).
+// Value v of row k (width b) sits in value tile v / 4 at bit (v % 4) b of the
+// tile's chunk, which starts at the row's offset plus (v / 4) * stride; a
+// thread's four values share v % 4 = lane % 4 and lie in tiles lane / 4 + 8 j.
+// For an integer row the two bytes from the code's first one hold it
+// (a 6-bit code can straddle a byte boundary; the second byte may be past the
+// row's chunk, inside the staged region); a pivot row's value is its fp16.
+struct KdaRowDecode {
+    int at;       // staged byte of the lane's code in tile lane / 4 (add 8 j stride for the others)
+    uint32_t sh;  // its bit shift inside those two bytes
+    uint32_t mask;  // (1 << b) - 1; 0 for a pivot row
+    float bias;   // -(2^23 + offset)
+};
+
+__device__ __forceinline__ float kda_staged_value(const unsigned char *codes, const KdaRowDecode &d, int j_off) {
+    if (d.mask == 0u) return __half2float(*reinterpret_cast<const __half *>(codes + d.at + j_off));
+    const uint32_t u = uint32_t(codes[d.at + j_off]) | (uint32_t(codes[d.at + j_off + 1]) << 8);
+    return __fadd_rn(__uint_as_float(0x4B000000u | ((u >> d.sh) & d.mask)), d.bias);
 }
 
 // P1 of the readout, which keeps no state: lane l covers the four consecutive
@@ -219,15 +212,18 @@ __device__ __forceinline__ void kda_first_levels(const KdaSmem &s, int warp, int
     tm_wait_st();
 }
 
-// P5 body: final levels (integer rows) or the fp16 values (pivot rows) -> plane.
+// P5 body: final levels of integer rows -> their code bytes in the byte plane
+// (code = level + offset: the low byte of RN(y + 1.5 2^23) plus the offset);
+// pivot rows -> their fp16 values straight into the staged region (the
+// lane's value of tile lane / 4 + 8 j at `pivot_at` + 8 j stride + the row's offset).
 template <bool SLOW, bool CLAMP>
-__device__ __forceinline__ void kda_final_levels(KdaSmem &s, int warp, int lane, uint32_t tm) {
+__device__ __forceinline__ void kda_final_levels(KdaSmem &s, int warp, int lane, uint32_t tm, int pivot_at, int j8) {
     const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
     const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
     const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
     const float2 r23 = make_float2(s.colc[2][lane + 64], s.colc[2][lane + 96]);
     const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
-    const float2 round = make_float2(kRound, kRound), nround = make_float2(-kRound, -kRound);
+    const float2 round = make_float2(kRound, kRound);
 #pragma unroll 1
     for (int g = 0; g < 4; ++g) {
         float2 X[4][2];
@@ -236,24 +232,24 @@ __device__ __forceinline__ void kda_final_levels(KdaSmem &s, int warp, int lane,
         for (int i = 0; i < 4; ++i) {
             const int k = warp * 16 + 4 * g + i;
             const float4 cc = s.rowc[k], d = s.rowd[k];
-            float2 o[2];
             if (d.w != 0.f) {
+                unsigned char *code = s.u.code + k * DV + lane;
+                const uint32_t off = uint32_t(d.z);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     float2 y = pmul2(divide2<SLOW>(X[i][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), hi2(cc));
                     if (CLAMP) y = clamp2(y, d.z);
-                    o[h] = __fadd2_rn(__fadd2_rn(y, round), nround);  // the integer level
+                    const float2 t = __fadd2_rn(y, round);  // low byte: the level (two's complement)
+                    code[64 * h] = static_cast<unsigned char>(__float_as_uint(t.x) + off);
+                    code[64 * h + 32] = static_cast<unsigned char>(__float_as_uint(t.y) + off);
                 }
             } else {
-                o[0] = X[i][0];
-                o[1] = X[i][1];
+                unsigned char *dst = s.codes + pivot_at + s.offs[k];
+                reinterpret_cast<__half *>(dst)[0] = __float2half_rn(X[i][0].x);
+                reinterpret_cast<__half *>(dst + j8)[0] = __float2half_rn(X[i][0].y);
+                reinterpret_cast<__half *>(dst + 2 * j8)[0] = __float2half_rn(X[i][1].x);
+                reinterpret_cast<__half *>(dst + 3 * j8)[0] = __float2half_rn(X[i][1].y);
             }
-            // interleaved [k][l][i]: i = 0..3 <-> columns l, l+32, l+64, l+96
-            const __half2 h01 = __floats2half2_rn(o[0].x, o[0].y), h23 = __floats2half2_rn(o[1].x, o[1].y);
-            uint2 out;
-            out.x = *reinterpret_cast<const uint32_t *>(&h01);
-            out.y = *reinterpret_cast<const uint32_t *>(&h23);
-            *reinterpret_cast<uint2 *>(&s.u.plane[k * DV + lane * 4]) = out;
         }
     }
 }
@@ -268,7 +264,7 @@ __device__ __forceinline__ void kda_final_levels(KdaSmem &s, int warp, int lane,
 // the bound of M and qmax_max the head's largest qmax.  The SLOW path (huge
 // or NaN rows) divides in IEEE arithmetic and always clamps.
 template <bool SLOW>
-__device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int tid, uint32_t tm) {
+__device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int tid, uint32_t tm, int pivot_at, int j8) {
     kda_column_max<SLOW, SLOW>(s, warp, lane, tm);
     __syncthreads();
     int settled = 1;
@@ -334,8 +330,8 @@ __device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int
     }
     const bool no_clamp5 = __syncthreads_and(safe);
     // P5: final levels (integer rows) or the fp16 values (pivot rows) -> plane.
-    if (!SLOW && no_clamp5) kda_final_levels<SLOW, false>(s, warp, lane, tm);
-    else kda_final_levels<SLOW, true>(s, warp, lane, tm);
+    if (!SLOW && no_clamp5) kda_final_levels<SLOW, false>(s, warp, lane, tm, pivot_at, j8);
+    else kda_final_levels<SLOW, true>(s, warp, lane, tm, pivot_at, j8);
     __syncthreads();
 }
 
@@ -459,12 +455,11 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         if (MODE == kReadout)  // the readout's row decode table (kda_readout_rows)
             s.rowb[tid] = make_float4(qx, integer ? -(8388608.f + float(qmax_i(bk))) : 0.f,
                                       __uint_as_float(integer ? (1u << bk) - 1u : 0u), __int_as_float(s.offs[tid]));
-        else
-            s.rowb[tid] = make_float4(qx, qx, integer ? 1.f : 0.f, 0.f);
+        else  // {q, -, integer row, width (decode)}
+            s.rowb[tid] = make_float4(qx, qx, integer ? 1.f : 0.f, __int_as_float(bk));
         s.colc[3][tid] = cold;
         if (MODE == kWriteback) s.colc[0][tid] = delta;
     }
-    if (MODE != kReadout) kda_unpack(s, lead, off0, stride, tid);
     __syncthreads();
 
     // ---- P1: dequantize and decay; column partials of k^T S and q^T S -------
@@ -474,6 +469,7 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         const float2 one = make_float2(1.f, 1.f);
         float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
         if (MODE == kReadout) kda_readout_rows(s, lead, off0, stride, warp, lane);
+        const int e = lane & 3, tile_at = (lane >> 2) * stride, j8 = 8 * stride;
 #pragma unroll 1
         for (int g = 0; g < (MODE == kReadout ? 0 : 4); ++g) {
             float2 X[4][2];
@@ -481,9 +477,16 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
             for (int i = 0; i < 4; ++i) {
                 const int k = warp * 16 + 4 * g + i;
                 const float4 a = s.rowa[k], b = s.rowb[k];
-                const uint2 raw = *reinterpret_cast<const uint2 *>(&s.u.plane[k * DV + lane * 4]);
-                const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
-                const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                KdaRowDecode d;
+                {
+                    const int bk = __float_as_int(b.w), pos = e * (bk & 15);
+                    d.at = lead - off0 + s.offs[k] + tile_at + (bk == 16 ? 2 * e : pos >> 3);
+                    d.sh = uint32_t(pos & 7);
+                    d.mask = bk == 16 ? 0u : (1u << bk) - 1u;
+                    d.bias = -(8388608.f + float(qmax_i(bk)));
+                }
+                const float2 v01 = make_float2(kda_staged_value(s.codes, d, 0), kda_staged_value(s.codes, d, j8));
+                const float2 v23 = make_float2(kda_staged_value(s.codes, d, 2 * j8), kda_staged_value(s.codes, d, 3 * j8));
                 const bool integer = b.z != 0.f;
                 const float2 m01 = integer ? c01 : one, m23 = integer ? c23 : one;
                 const float2 x01 = pmul2(pmul2(v01, lo2(a)), m01);
@@ -604,37 +607,28 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         }
     }
     __syncthreads();
-    if (s.flags) kda_quantize<true>(s, warp, lane, tid, tm);
-    else kda_quantize<false>(s, warp, lane, tid, tm);
+    {
+        const int pivot_at = lead - off0 + (lane >> 2) * stride + 2 * (lane & 3);
+        if (s.flags) kda_quantize<true>(s, warp, lane, tid, tm, pivot_at, 8 * stride);
+        else kda_quantize<false>(s, warp, lane, tid, tm, pivot_at, 8 * stride);
+    }
 
-    // ---- pack the codes and the pivot rows into the staged region ----------
+    // ---- pack the integer rows' codes into the staged region ----------------
+    // Chunk (k, t): the four code bytes of values 4t..4t+3 (one word of the
+    // byte plane), the code of value 4t + i moved to bit i b; b / 2 bytes.
     for (int idx = tid; idx < DK * DTILES; idx += kThreads) {
         const int k = idx >> 5, t = idx & 31;
         const int b = s.bits[k];
+        if (b == 16) continue;  // pivot values were stored in P5
         unsigned char *dst = s.codes + lead + (s.offs[k] - off0) + t * stride;
-        __half h[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int v = 4 * t + j;
-            h[j] = s.u.plane[k * DV + (v & 31) * 4 + (v >> 5)];
-        }
-        if (b == 16) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint16_t u = __half_as_ushort(h[j]);
-                dst[2 * j] = uint8_t(u);
-                dst[2 * j + 1] = uint8_t(u >> 8);
-            }
-        } else {
-            const int off = qmax_i(b);
-            uint32_t w = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) w |= uint32_t(__half2int_rn(h[j]) + off) << (j * b);
-            dst[0] = uint8_t(w);
-            if (b >= 4) dst[1] = uint8_t(w >> 8);
-            if (b >= 6) dst[2] = uint8_t(w >> 16);
-            if (b == 8) dst[3] = uint8_t(w >> 24);
-        }
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(&s.u.code[k * DV + 4 * t]);
+        const uint32_t m = (1u << b) - 1u;
+        const uint32_t packed = (w & m) | ((w >> (8 - b)) & (m << b)) | ((w >> (16 - 2 * b)) & (m << (2 * b))) |
+                                ((w >> (24 - 3 * b)) & (m << (3 * b)));
+        dst[0] = uint8_t(packed);
+        if (b >= 4) dst[1] = uint8_t(packed >> 8);
+        if (b >= 6) dst[2] = uint8_t(packed >> 16);
+        if (b == 8) dst[3] = uint8_t(packed >> 24);
     }
     __syncthreads();
     // ---- write the head's code region back: whole 16-byte pieces as vectors,
