@@ -449,6 +449,7 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
     del graphs
     pool.check_status()
     res["page_bytes"] = pool.page_bytes
+    res["pivot_heads_local"] = 0 if kda else int((bits[:, 0] == 16).sum())
     res["algorithmic"] = algorithmic_bytes(pool.page_bytes, heads_l, qk_l, batch, dim, kda)
 
     if e2e:
@@ -960,7 +961,7 @@ def main():
         # DRAM read + write bytes of one launch at this workload, from an ncu capture made
         # outside the bench (ncu cannot run inside a timed region); None for other shapes.
         ncu_traffic = {"sq_step (fused)": 160.3e6, "sq_writeback": 161.6e6, "sq_readout": 115.8e6}
-        default_shape = (not kda, batch, heads, qk_heads, args.dim, world) == (True, 256, 32, 16, 128, 1)
+        default_shape = (not kda, batch, heads, qk_heads, args.dim, world, args.pivot_heads) == (True, 256, 32, 16, 128, 1, 1)
         name = ("kda-decode-b%d-h%d-k128 (config 2)" if kda else "gdn-decode-b%d-h%d-k128 (config 1)") % (batch, heads)
         plan_desc = ("stepquant4 reference-legal twin: row widths {2,4,6} at 30/50/20, 2% fp16 pivot rows" if kda else
                      "stepquant6 synthetic, widths {4,6,8} 25/50/25, pivot heads %d" % args.pivot_heads)
@@ -981,7 +982,8 @@ def main():
                          "algorithmic_bytes_per_launch": dom_bytes},
             "e2e": {"value": units / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"]},
-            "gpu_launches": args.steps * (2 if args.mode == "async" else 1),
+            # readout (or fused step), writeback, and the pivot-head kernel when this rank has pivot heads
+            "gpu_launches": args.steps * ((2 if args.mode == "async" else 1) + (1 if res["pivot_heads_local"] else 0)),
         })
     line["clocks"] = clocks.summary()
 
@@ -1004,6 +1006,15 @@ def main():
             "hbm_frac": (r3["bytes"] / (pk / 1e3) / 1e9 / peak_hbm) if pk else None,
             "tensor_tflops": r3["flops"] / (pk / 1e3) / 1e12 if pk else None,
             "tensor_frac": (r3["flops"] / (pk / 1e3) / 1e12 / peak_tf) if pk else None, "peak_source": peak_tf_kind}
+        r4 = measure_stack(args, 512, 32, 16, 5, 2, 1, 0, device, barrier)
+        fam, ms4 = r4["kernel_ms"], r4["elapsed_ms"] / 5
+        sec["gdn-stack-l%d-b512-h32-hidden%d (config 4)" % (args.layers, args.hidden)] = {
+            "value": 512 * 5 / (r4["elapsed_ms"] / 1e3), "unit": "tokens/s", "ms_per_step": ms4,
+            "e2e": 512 * 5 / (r4["e2e_ms"] / 1e3), "kernel_ms_per_step": fam,
+            "state_update_share": (fam["state_readout"] + fam["state_writeback"]) / ms4, "steps": 5,
+            "finite": r4["finite"],
+            "note": "%d GDN layers, prompt %d tokens then decode; one CUDA graph per decode token (writeback joined), "
+                    "1 GPU (the all-gather is the identity)" % (args.layers, args.prompt)}
         line["secondary"] = sec
 
     if world > 1:

@@ -161,11 +161,20 @@ def torch_outer_sum(x):
 
 @dataclass
 class Plan:
-    """Mirror of QuantizationPlan (quantization.py:7-26) as numpy arrays."""
+    """Mirror of QuantizationPlan (quantization.py:7-26) as numpy arrays.
+
+    ``extended_widths`` admits 3- and 5-bit rows: this build's labelled
+    extension (the reference rejects them, quantization.py:19-20).  fit_state
+    is the reference's formula unchanged at those widths (qmax 2^(b-1) - 1,
+    KDA norm 2^(8-b)); codes pack as the reference packs every width (code i
+    at bit i b), and a page row's tile chunk takes ceil(tile b / 8) bytes
+    (KDA tiles of 4 values: 2 bytes at 3 bits, 3 at 5 bits, tail bits zero).
+    """
     architecture: str
     bits: np.ndarray     # [H, K] int, 16 = fp16 pivot
     impact: np.ndarray   # [H, K] float32
     value_group_size: int = 32
+    extended_widths: bool = False
 
     def __post_init__(self):
         self.bits = np.asarray(self.bits).astype(np.int64)
@@ -174,7 +183,8 @@ class Plan:
             raise ValueError("architecture must be gdn or kda")
         if self.bits.ndim != 2 or self.bits.shape != self.impact.shape:
             raise ValueError("bits and impact must have shape [heads, key_dim]")
-        if not np.isin(self.bits, [2, 4, 6, 8, 16]).all():
+        allowed = [2, 3, 4, 5, 6, 8, 16] if self.extended_widths else [2, 4, 6, 8, 16]
+        if not np.isin(self.bits, allowed).all():
             raise ValueError("precision must be 2, 4, 6, 8 or 16")
         if self.architecture == "gdn" and not (self.bits == self.bits[:, :1]).all():
             raise ValueError("GDN allocation is per whole head")
@@ -249,9 +259,20 @@ def fit_state(x, plan: Plan):
 # packing and the StateCodec byte streams
 # ---------------------------------------------------------------------------
 
-def pack(codes, bits):
-    """packing.py:6-14: little-endian, n = 8/gcd(b,8) codes per n*b/8 bytes."""
-    if bits not in (2, 4, 6, 8):
+def widths(plan):
+    """The integer code widths a plan may hold."""
+    return (2, 3, 4, 5, 6, 8) if getattr(plan, "extended_widths", False) else (2, 4, 6, 8)
+
+
+def chunk_bytes(tile, bits):
+    """Bytes of one row's value-tile chunk (tile * bits / 8 at the reference's widths)."""
+    return (tile * bits + 7) // 8
+
+
+def pack(codes, bits, extended=False):
+    """packing.py:6-14: little-endian, n = 8/gcd(b,8) codes per n*b/8 bytes
+    (``extended``: also 3 and 5 bits, 8 codes per 3 or 5 bytes)."""
+    if bits not in ((2, 3, 4, 5, 6, 8) if extended else (2, 4, 6, 8)):
         raise ValueError("supported code widths: 2, 4, 6, 8")
     flat = np.asarray(codes).reshape(-1).astype(np.int64)
     n = 8 // math.gcd(bits, 8)
@@ -280,14 +301,14 @@ def codec_encode(state, plan: Plan):
     flat_bits = plan.bits.reshape(-1)
     z = z.reshape(batch, heads * keys, values).astype(np.int64)
     codes = {}
-    for b in (2, 4, 6, 8):
+    for b in widths(plan):
         idx = np.nonzero(flat_bits == b)[0]
         sel = z[:, idx]
         if b == 2 and plan.architecture == "gdn":
             sel = (sel + 3) // 2
         else:
             sel = sel + (2 ** (b - 1) - 1)
-        codes[b] = pack(sel, b)
+        codes[b] = pack(sel, b, extended=True)
     integer_rows = np.nonzero(flat_bits != 16)[0]
     integer_heads = np.nonzero((plan.bits != 16).any(-1))[0]
     pivots = state.reshape(batch, heads * keys, values)[:, np.nonzero(flat_bits == 16)[0]].astype(np.float16)
@@ -300,7 +321,7 @@ def codec_decode(packed, plan: Plan):
     batch, heads, keys, values = packed["shape"]
     flat_bits = plan.bits.reshape(-1)
     z = np.zeros((batch, heads * keys, values), F32)
-    for b in (2, 4, 6, 8):
+    for b in widths(plan):
         idx = np.nonzero(flat_bits == b)[0]
         codes = unpack(packed["codes"][b], b, batch * idx.size * values).reshape(batch, -1, values).astype(F32)
         if b == 2 and plan.architecture == "gdn":
@@ -360,7 +381,7 @@ def packed_layout(plan: Plan, value_dim, storage="packed"):
                 if b == 16:
                     local = (local + 1) // 2 * 2
                 offsets.append(cursor + local)
-                local += tile * b // 8
+                local += chunk_bytes(tile, b)
             stride = (local + 1) // 2 * 2
             strides.append(stride)
             cursor += stride * (value_dim // tile)
@@ -435,7 +456,7 @@ def page_store(page, plan: Plan, values, z, r, c, r2, pivots_f16):
                 word = 0
                 for u, code in enumerate(codes):
                     word |= int(code) << (u * b)
-                nbytes = tile * b // 8
+                nbytes = chunk_bytes(tile, b)
                 page[base:base + nbytes] = np.frombuffer(word.to_bytes(nbytes, "little"), np.uint8)
             if b != 16:
                 if b == 2 and plan.architecture == "gdn":
@@ -574,7 +595,7 @@ def page_decode(pages, plan: Plan, values, storage="packed"):
                         row_vals[t * tile:(t + 1) * tile] = np.frombuffer(
                             page[base:base + 2 * tile].tobytes(), np.float16).astype(F32)
                         continue
-                    nbytes = tile * b // 8
+                    nbytes = chunk_bytes(tile, b)
                     word = int.from_bytes(page[base:base + nbytes].tobytes(), "little")
                     codes = np.array([(word >> (u * b)) & ((1 << b) - 1) for u in range(tile)], np.int64)
                     if b == 2 and plan.architecture == "gdn":

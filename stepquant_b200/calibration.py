@@ -141,7 +141,9 @@ class _Layer:
         bits = widths.reshape(self.unit_shape)
         if architecture == "gdn":  # one width per head, repeated over its key rows
             bits = bits[:, None].expand(self.impact.shape).clone()
-        return asdict(QuantizationPlan(architecture, bits.cpu(), self.impact.cpu(), self.group))
+        entry = asdict(QuantizationPlan(architecture, bits.cpu(), self.impact.cpu(), self.group))
+        entry.pop("extended_widths")  # the reference's plan record: architecture, bits, impact, group size
+        return entry
 
 
 def _pivot_mask(architecture, cost, fp_cost, candidates, nominal_budget, count):

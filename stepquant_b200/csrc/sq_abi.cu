@@ -78,7 +78,7 @@ bool kda_head_fast_host(const int32_t *bits, int keys, int values) {
     for (int k = 0; k < keys; ++k) {
         if (bits[k] == 16) local = (local + 1) / 2 * 2;
         else any_int = true;
-        local += 4 * bits[k] / 8;
+        local += (4 * bits[k] + 7) / 8;
     }
     return sq::kda_head_fits((local + 1) / 2 * 2, values, any_int ? 0 : -1);
 }
@@ -145,7 +145,7 @@ int32_t sq_packed_layout(int32_t architecture, int32_t heads, int32_t keys, int3
     const bool kda = architecture == SQ_KDA;
     for (int i = 0; i < heads * keys; ++i) {
         const int b = bits[i];
-        if (b != 2 && b != 4 && b != 6 && b != 8 && b != 16) return SQ_ERR_ARGUMENT;
+        if (b != 2 && b != 3 && b != 4 && b != 5 && b != 6 && b != 8 && b != 16) return SQ_ERR_ARGUMENT;
     }
     auto head_has_int = [&](int h) {
         for (int k = 0; k < keys; ++k)
@@ -180,7 +180,7 @@ int32_t sq_packed_layout(int32_t architecture, int32_t heads, int32_t keys, int3
                 const int b = bits[h * keys + k];
                 if (b == 16) local = (local + 1) / 2 * 2;
                 offsets_out[n++] = int32_t(cursor + local);
-                local += tile * b / 8;
+                local += (tile * b + 7) / 8;  // 3/5 bits (extension): a KDA chunk rounds up to whole bytes
             }
             const int64_t stride = (local + 1) / 2 * 2;
             strides[h] = stride;
@@ -292,19 +292,19 @@ int32_t sq_fit_state(const sq_plan *plan, const float *x, int32_t batch, int16_t
 }
 
 int32_t sq_pack(const int16_t *codes, int64_t n, int32_t bits, uint8_t *out, sq_stream_t stream) {
-    if (bits != 2 && bits != 4 && bits != 6 && bits != 8) return SQ_ERR_ARGUMENT;
+    if (bits < 2 || bits > 8 || bits == 7) return SQ_ERR_ARGUMENT;
     if (n < 0 || (n > 0 && (!codes || !out))) return SQ_ERR_ARGUMENT;
     return cuda_status(sq::launch_pack(codes, n, bits, out, stream));
 }
 
 int64_t sq_packed_bytes(int64_t n, int32_t bits) {
-    if (bits != 2 && bits != 4 && bits != 6 && bits != 8) return -1;
+    if (bits < 2 || bits > 8 || bits == 7) return -1;
     if (n < 0) return -1;
     return sq::packed_bytes(n, bits);
 }
 
 int32_t sq_unpack(const uint8_t *data, int64_t count, int32_t bits, int16_t *out, sq_stream_t stream) {
-    if (bits != 2 && bits != 4 && bits != 6 && bits != 8) return SQ_ERR_ARGUMENT;
+    if (bits < 2 || bits > 8 || bits == 7) return SQ_ERR_ARGUMENT;
     if (count < 0 || (count > 0 && (!data || !out))) return SQ_ERR_ARGUMENT;
     return cuda_status(sq::launch_unpack(data, count, bits, out, stream));
 }

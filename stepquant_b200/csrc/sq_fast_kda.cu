@@ -625,10 +625,10 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         const uint32_t m = (1u << b) - 1u;
         const uint32_t packed = (w & m) | ((w >> (8 - b)) & (m << b)) | ((w >> (16 - 2 * b)) & (m << (2 * b))) |
                                 ((w >> (24 - 3 * b)) & (m << (3 * b)));
-        dst[0] = uint8_t(packed);
-        if (b >= 4) dst[1] = uint8_t(packed >> 8);
-        if (b >= 6) dst[2] = uint8_t(packed >> 16);
-        if (b == 8) dst[3] = uint8_t(packed >> 24);
+        dst[0] = uint8_t(packed);  // ceil(4 b / 8) bytes (3/5-bit rows of the extension end in zero bits)
+        if (b >= 3) dst[1] = uint8_t(packed >> 8);
+        if (b >= 5) dst[2] = uint8_t(packed >> 16);
+        if (b >= 7) dst[3] = uint8_t(packed >> 24);
     }
     __syncthreads();
     // ---- write the head's code region back: whole 16-byte pieces as vectors,

@@ -128,6 +128,7 @@ __device__ void format_store(int fmt, int G, uint8_t *page, Smem &s, int K, int 
                 nbits -= 8;
             }
         }
+        if (nbits > 0) dst[w] = uint8_t(acc & 0xffu);  // 3/5-bit KDA chunks: zero tail bits
     }
 }
 
@@ -490,6 +491,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
                 nbits -= 8;
             }
         }
+        if (nbits > 0) dst[w] = uint8_t(acc & 0xffu);  // 3/5-bit KDA chunks: zero tail bits
     }
     for (int k = tid; k < K; k += kThreads) {
         if (s.rbits[k] == 16) continue;

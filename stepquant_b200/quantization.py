@@ -12,19 +12,35 @@ from . import _native as N
 from .packing import pack, unpack
 
 
+REFERENCE_WIDTHS = (2, 4, 6, 8)
+EXTENDED_WIDTHS = (2, 3, 4, 5, 6, 8)
+
+
 @dataclass
 class QuantizationPlan:
+    """A layer's per-row code widths (16: fp16 pivot) and impact factors.
+
+    ``extended_widths=True`` also admits 3- and 5-bit rows, an extension of
+    this package (the reference accepts 2, 4, 6, 8 and 16 only).  fit_state
+    treats them with the reference's width-generic formula (qmax 2^(b-1) - 1,
+    KDA norm 2^(8-b)); codes pack like every other width, and a page row's
+    value-tile chunk takes ceil(tile b / 8) bytes (KDA: 2 bytes at 3 bits, 3
+    at 5 bits, the tail bits zero).  Plans without the flag keep the
+    reference's validation and page layout exactly.
+    """
     architecture: str
     bits: torch.Tensor    # [H, K], 16 denotes fp16 pivots
     impact: torch.Tensor  # [H, K], normalized row weights w
     value_group_size: int = 32
+    extended_widths: bool = False
 
     def __post_init__(self):
         if self.architecture not in ("gdn", "kda"):
             raise ValueError("architecture must be gdn or kda")
         if self.bits.ndim != 2 or self.bits.shape != self.impact.shape:
             raise ValueError("bits and impact must have shape [heads, key_dim]")
-        if not torch.isin(self.bits, torch.tensor([2, 4, 6, 8, 16], device=self.bits.device)).all():
+        allowed = (*EXTENDED_WIDTHS, 16) if self.extended_widths else (*REFERENCE_WIDTHS, 16)
+        if not torch.isin(self.bits, torch.tensor(allowed, device=self.bits.device)).all():
             raise ValueError("precision must be 2, 4, 6, 8 or 16")
         if self.architecture == "gdn" and not (self.bits == self.bits[:, :1]).all():
             raise ValueError("GDN allocation is per whole head")
@@ -35,7 +51,12 @@ class QuantizationPlan:
 
     def to(self, device):
         return QuantizationPlan(self.architecture, self.bits.to(device), self.impact.to(device),
-                                self.value_group_size)
+                                self.value_group_size, self.extended_widths)
+
+    @property
+    def widths(self):
+        """The integer code widths this plan may hold."""
+        return EXTENDED_WIDTHS if self.extended_widths else REFERENCE_WIDTHS
 
 
 @dataclass
@@ -131,7 +152,8 @@ class StateCodec:
     def __init__(self, plan):
         self.plan = plan
         flat = plan.bits.flatten()
-        self.indices = {b: (flat == b).nonzero().flatten() for b in (2, 4, 6, 8, 16)}
+        self.widths = getattr(plan, "widths", REFERENCE_WIDTHS)
+        self.indices = {b: (flat == b).nonzero().flatten() for b in (*self.widths, 16)}
         self.integer_rows = (flat != 16).nonzero().flatten()
         self.integer_heads = (plan.bits != 16).any(-1).nonzero().flatten()
         self.two_heads = (plan.bits[:, 0] == 2).nonzero().flatten() if plan.architecture == "gdn" else None
@@ -143,13 +165,13 @@ class StateCodec:
         batch, heads, keys, values = state.shape
         z = z.reshape(batch, heads * keys, values)
         packed = {}
-        for bits in (2, 4, 6, 8):
+        for bits in self.widths:
             codes = z[:, self.indices[bits]]
             if bits == 2 and self.plan.architecture == "gdn":
                 codes = torch.div(codes + 3, 2, rounding_mode="floor")
             else:
                 codes = codes + (2 ** (bits - 1) - 1)
-            packed[bits] = pack(codes.to(torch.int16), bits)
+            packed[bits] = pack(codes.to(torch.int16), bits, extended=True)
         pivots = state.reshape(batch, heads * keys, values)[:, self.indices[16]].half()
         return PackedState(packed, r.reshape(batch, -1)[:, self.integer_rows], c[:, self.integer_heads],
                            pivots, r2, tuple(state.shape))
@@ -159,9 +181,10 @@ class StateCodec:
         device = packed.rows.device
         N.require_cuda(packed.rows)
         z = torch.zeros((batch, heads * keys, values), device=device)
-        for bits in (2, 4, 6, 8):
+        for bits in self.widths:
             idx = self.indices[bits]
-            codes = unpack(packed.codes[bits], bits, batch * idx.numel() * values).reshape(batch, -1, values).float()
+            codes = unpack(packed.codes[bits], bits, batch * idx.numel() * values,
+                           extended=True).reshape(batch, -1, values).float()
             if bits == 2 and self.plan.architecture == "gdn":
                 codes = 2 * codes - 3
             else:

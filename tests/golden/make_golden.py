@@ -32,6 +32,13 @@ Files written next to this script:
                         ``group_fit``, dsq_int* ``dual_fit``) on seeded states,
                         and ``kernels.format_pool.format_layout`` tables.
 
+* ``widths_ext.npz`` -- ``stepquant.quantization.fit_state`` at 3- and 5-bit
+                        rows (this build's width extension; the reference's
+                        QuantizationPlan rejects those widths, so the plan
+                        object is built without its validation and fit_state,
+                        whose formula is width-generic, runs unchanged).
+
+``--extension-only`` rewrites ``widths_ext.npz`` alone;
 ``--prefill-only`` rewrites ``prefill.npz`` alone; ``--calibration-only``
 rewrites ``calibration.npz`` alone; ``--formats-only`` rewrites
 ``formats.npz`` alone.
@@ -207,14 +214,51 @@ def format_vectors(get_format, group_fit, dual_fit, format_layout):
     return out
 
 
+def extension_cases():
+    """(name, arch, bits[H,K], group, batch, values, scale, seed) with 3/5-bit rows."""
+    gen = torch.Generator().manual_seed(50)
+    kda = torch.tensor([3, 4, 6])[torch.multinomial(torch.tensor([0.3, 0.5, 0.2]), 2 * 128, True, generator=gen)]
+    kda = kda.reshape(2, 128)
+    kda[torch.rand(2, 128, generator=gen) < 0.02] = 16
+    return [
+        ("gdn_w35_k32", "gdn", _bits_mixed("gdn", [3, 5, 4, 6, 8, 16], 32), 32, 2, 32, 1.0, 51),
+        ("gdn_w35_k128", "gdn", _bits_mixed("gdn", [3, 5, 6], 128), 32, 1, 128, 0.1, 52),
+        ("kda_w346_k128", "kda", kda, 32, 1, 128, 0.1, 53),
+        ("kda_w35_k16", "kda", torch.tensor([[3, 5, 16, 4] * 4, [5, 3, 8, 2] * 4]), 32, 3, 8, 1.0, 54),
+    ]
+
+
+def extension_vectors(QuantizationPlan, fit_state):
+    out = {}
+    for name, arch, bits, group, batch, values, scale, seed in extension_cases():
+        torch.manual_seed(seed)
+        heads, keys = bits.shape
+        impact = torch.rand(heads, keys) + 0.25
+        plan = object.__new__(QuantizationPlan)  # no width validation: 3/5 bits are this build's extension
+        plan.architecture, plan.bits, plan.impact, plan.value_group_size = arch, bits, impact, group
+        x = torch.randn(batch, heads, keys, values) * scale
+        z, r, c, r2, recon = fit_state(x, plan)
+        out.update({f"{name}_arch": np.array(arch), f"{name}_bits": bits.numpy().astype(np.int8),
+                    f"{name}_impact": impact.numpy(), f"{name}_group": np.array(group), f"{name}_x": x.numpy(),
+                    f"{name}_z": z.numpy().astype(np.int8), f"{name}_r": r.numpy(), f"{name}_c": c.numpy()})
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path of the STEPQuant checkout")
     parser.add_argument("--prefill-only", action="store_true")
     parser.add_argument("--calibration-only", action="store_true")
     parser.add_argument("--formats-only", action="store_true")
+    parser.add_argument("--extension-only", action="store_true")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
+    if args.extension_only:
+        from stepquant.quantization import QuantizationPlan, fit_state
+        torch.set_num_threads(1)
+        np.savez_compressed(os.path.join(HERE, "widths_ext.npz"), **extension_vectors(QuantizationPlan, fit_state))
+        print("extension vectors written to", HERE)
+        return
     if args.formats_only:
         from stepquant.formats import get_format, group_fit, dual_fit
         from stepquant.kernels.format_pool import format_layout

@@ -46,10 +46,19 @@ def test_layout_rejects_bad_storage_and_widths():
     plan = QuantizationPlan("gdn", torch.full((1, 4), 6), torch.ones(1, 4))
     with pytest.raises(ValueError):
         packed_layout(plan, 8, "nibble")
-    bits = (ctypes.c_int32 * 4)(6, 6, 5, 6)
+    bits = (ctypes.c_int32 * 4)(6, 6, 7, 6)
     out = (ctypes.c_int32 * 8)()
     page = ctypes.c_int64()
     assert N.lib().sq_packed_layout(0, 1, 4, 8, 32, bits, 0, out, out, out, ctypes.byref(page)) == N.SQ_ERR_ARGUMENT
+    # 3 and 5 bits are the width extension: the C layout takes them, a plan only with extended_widths.
+    bits = (ctypes.c_int32 * 4)(5, 5, 5, 5)
+    assert N.lib().sq_packed_layout(0, 1, 4, 8, 32, bits, 0, out, out, out, ctypes.byref(page)) == N.SQ_OK
+    with pytest.raises(ValueError):
+        QuantizationPlan("gdn", torch.full((1, 4), 5), torch.ones(1, 4))
+    ext = QuantizationPlan("kda", torch.tensor([[3, 5, 16, 4]]), torch.ones(1, 4), extended_widths=True)
+    from oracle import stepquant_oracle as O
+    assert packed_layout(ext, 8) == O.packed_layout(O.Plan("kda", ext.bits.numpy(), ext.impact.numpy(),
+                                                           extended_widths=True), 8)
 
 
 def test_device_entry_points_reject_bad_arguments_before_launch():
@@ -64,7 +73,7 @@ def test_device_entry_points_reject_bad_arguments_before_launch():
     plan = N.SqPlan(0, 4, 128, 128, 32, 0, 1000, fake, fake, fake, fake, fake)
     args = N.SqStepArgs(16, 16, 16, 0, 0, 0, 3, 0, 16, 16, 0, 0, None, None, 1.0, 0, 16)
     assert N.lib().sq_step(ctypes.byref(plan), fake, 4, fake, 1, ctypes.byref(args), None, None, None) == N.SQ_ERR_SHAPE
-    assert N.lib().sq_pack(fake, 4, 5, fake, None) == N.SQ_ERR_ARGUMENT
+    assert N.lib().sq_pack(fake, 4, 7, fake, None) == N.SQ_ERR_ARGUMENT
     # Page storage codes: 0 packed, 1 byte carriers, 2 / 3 baseline formats; others are rejected.
     for storage, code in ((4, N.SQ_ERR_ARGUMENT), (-1, N.SQ_ERR_ARGUMENT), (3, N.SQ_ERR_SHAPE)):
         plan = N.SqPlan(0, 2, 96, 128, 32, storage, 1000, fake, fake, fake, fake, fake)

@@ -210,3 +210,43 @@ def test_baseline_formats_match_reference(name):
     pages = O.format_page_encode(x, name)
     assert pages.shape == (x.shape[0], total)
     np.testing.assert_array_equal(O.format_page_decode(pages, name, heads, keys, values), d[f"{name}_recon"])
+
+
+def _extension_cases():
+    d = load_golden("widths_ext.npz")
+    return sorted({k.rsplit("_", 1)[0] for k in d.files if k.endswith("_arch")})
+
+
+@pytest.mark.parametrize("case", _extension_cases())
+def test_extended_widths_fit_state_matches_reference_formula(case):
+    """3- and 5-bit rows (this build's extension): the oracle's fit_state equals
+    the reference's own fit_state run on a plan built without its width
+    validation (tests/golden/make_golden.py --extension-only)."""
+    d = load_golden("widths_ext.npz")
+    plan = O.Plan(str(d[f"{case}_arch"]), d[f"{case}_bits"].astype(np.int64), d[f"{case}_impact"],
+                  int(d[f"{case}_group"]), extended_widths=True)
+    z, r, c, r2, recon = O.fit_state(d[f"{case}_x"], plan)
+    assert (z == d[f"{case}_z"]).all()
+    assert _same_bits(r, d[f"{case}_r"]) and _same_bits(c, d[f"{case}_c"])
+    # decode(encode(x)) through the extended codec and page image is the reconstruction.
+    enc = O.codec_encode(d[f"{case}_x"], plan)
+    assert (O.codec_decode(enc, plan) == recon).all()
+    pages = O.page_encode(d[f"{case}_x"], plan)
+    assert (O.page_decode(pages, plan, d[f"{case}_x"].shape[-1]) == recon).all()
+
+
+def test_extended_widths_are_opt_in():
+    bits = np.full((2, 8), 3)
+    with pytest.raises(ValueError):
+        O.Plan("kda", bits, np.ones((2, 8), np.float32))
+    with pytest.raises(ValueError):
+        O.pack(np.zeros(8, np.int64), 3)
+    for b in (3, 5):
+        codes = np.random.default_rng(b).integers(0, 2 ** b, 37)
+        data = O.pack(codes, b, extended=True)
+        assert data.size == (37 + 7) // 8 * b
+        assert (O.unpack(data, b, 37) == codes).all()
+    # KDA value tiles of 4: a 3-bit row takes 2 bytes per tile, a 5-bit row 3.
+    plan = O.Plan("kda", np.array([[3, 5, 16, 4]]), np.ones((1, 4), np.float32), extended_widths=True)
+    offsets, rows, columns, total = O.packed_layout(plan, 8)
+    assert offsets[:4] == [0, 2, 6, 14] and offsets[4] == 16  # the pivot row: 4 fp16 values per tile
