@@ -64,6 +64,9 @@ def parse_args():
     p.add_argument("--mode", choices=("async", "sync"), default="async")
     p.add_argument("--workload", choices=("gdn-decode", "kda-decode", "gdn-prefill", "gdn-stack"), default="gdn-decode",
                    help="config 1 (default), config 2, config 3 or config 4")
+    p.add_argument("--kda-widths", default="2,4,6",
+                   help="KDA row widths at 30/50/20 (kda-decode): 2,4,6 is the reference-legal twin of config 2's "
+                        "3,4,6, which needs the 3/5-bit width extension")
     p.add_argument("--batch", type=int, default=0,
                    help="default: 256 (config 1), 512 (config 2), 32 (config 3), 512 (config 4)")
     p.add_argument("--tokens", type=int, default=2048, help="prompt length (gdn-prefill)")
@@ -345,7 +348,7 @@ def kernel_times(pool, inputs, groups, kw, mode, launches=8, reps=4):
 
 
 def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world, rank, device, barrier,
-                   mode="async", e2e=True, clocks=None, warm_steps=256, slot_groups=4, seed=1):
+                   mode="async", e2e=True, clocks=None, warm_steps=256, slot_groups=4, seed=1, kda_widths=(2, 4, 6)):
     """Decode steps of one layer (GDN config 1 or KDA config 2); returns the measured quantities."""
     import torch
     from stepquant_b200 import _native as N
@@ -359,7 +362,7 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
     gen = torch.Generator(device=device).manual_seed(seed * 1000 + rank)
     cpu_gen = torch.Generator().manual_seed(seed)
     if kda:
-        bits = S.kda_widths(heads_total, dim, cpu_gen)[rank * heads_l:(rank + 1) * heads_l]
+        bits = S.kda_widths(heads_total, dim, cpu_gen, choices=tuple(kda_widths))[rank * heads_l:(rank + 1) * heads_l]
     else:
         widths = S.gdn_widths(heads_total, cpu_gen, args.pivot_heads)[rank * heads_l:(rank + 1) * heads_l]
         bits = widths[:, None].expand(heads_l, dim).clone()
@@ -382,7 +385,8 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
         q, k, g, beta = S.prepared(inp, heads_l, dim, kda, a_log, dt_bias)
         omega += S.row_impact(q, k, g, beta).double().sum(0)
     impact = S.impact_factors(omega / (warm_steps * requests))
-    plan = QuantizationPlan("kda" if kda else "gdn", bits.to(device), impact.to(device))
+    extended = bool(kda and any(w in (3, 5) for w in kda_widths))  # the 3/5-bit width extension
+    plan = QuantizationPlan("kda" if kda else "gdn", bits.to(device), impact.to(device), extended_widths=extended)
 
     stream = torch.cuda.Stream(device) if mode == "async" else None
     # One writeback launch per step (no chunking), as the eager path does.
@@ -943,7 +947,8 @@ def main():
     else:
         res = measure_decode(args, kda, batch, heads, qk_heads, args.steps, args.warmup, world, rank, device, barrier,
                              mode=args.mode, e2e=True, clocks=clocks, warm_steps=args.warm_steps,
-                             slot_groups=args.slot_groups, seed=2 if kda else args.seed)
+                             slot_groups=args.slot_groups, seed=2 if kda else args.seed,
+                             kda_widths=tuple(int(w) for w in args.kda_widths.split(",")))
         elapsed_ms, e2e_ms = max_over_ranks(res["elapsed_ms"], res["e2e_ms"])
         page_io, other_io = res["algorithmic"]
         job_page_bytes, step_bytes = (int(x) for x in sum_over_ranks(res["page_bytes"], page_io + other_io))
@@ -960,10 +965,13 @@ def main():
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms else None
         # DRAM read + write bytes of one launch at this workload, from an ncu capture made
         # outside the bench (ncu cannot run inside a timed region); None for other shapes.
-        ncu_traffic = {"sq_step (fused)": 160.3e6, "sq_writeback": 161.6e6, "sq_readout": 115.8e6}
+        ncu_traffic = {"sq_writeback": 156.6e6, "sq_readout": 114.1e6}
         default_shape = (not kda, batch, heads, qk_heads, args.dim, world, args.pivot_heads) == (True, 256, 32, 16, 128, 1, 1)
         name = ("kda-decode-b%d-h%d-k128 (config 2)" if kda else "gdn-decode-b%d-h%d-k128 (config 1)") % (batch, heads)
-        plan_desc = ("stepquant4 reference-legal twin: row widths {2,4,6} at 30/50/20, 2% fp16 pivot rows" if kda else
+        kw_desc = "{%s}" % args.kda_widths
+        plan_desc = (("stepquant4 reference-legal twin: " if args.kda_widths == "2,4,6" else
+                      "config 2's plan (3/5-bit width extension): ") + "row widths %s at 30/50/20, 2%% fp16 pivot rows"
+                     % kw_desc if kda else
                      "stepquant6 synthetic, widths {4,6,8} 25/50/25, pivot heads %d" % args.pivot_heads)
         line.update({
             "value": units / (elapsed_ms / 1e3), "ms_per_step": elapsed_ms / args.steps,
@@ -994,8 +1002,16 @@ def main():
                             warm_steps=64, slot_groups=2, seed=2)
         sec["kda-decode-b512-h32-k128 (config 2)"] = {
             "value": 512 * 32 * 5 / (r2["elapsed_ms"] / 1e3), "unit": UNIT, "ms_per_step": r2["elapsed_ms"] / 5,
-            "kernel_ms": r2["kernel_ms"], "steps": 5, "mode": "async",
-            "note": "register-resident KDA kernels; 64 warm-up steps, 2 slot groups"}
+            "kernel_ms": r2["kernel_ms"], "steps": 5, "mode": "async", "page_bytes_per_request": r2["page_bytes"],
+            "note": "reference-legal twin plan: row widths {2,4,6} at 30/50/20, 2% fp16 pivot rows; "
+                    "64 warm-up steps, 2 slot groups"}
+        r2x = measure_decode(args, True, 512, 32, 32, 5, 3, 1, 0, device, barrier, mode="async", e2e=False,
+                             warm_steps=64, slot_groups=2, seed=2, kda_widths=(3, 4, 6))
+        sec["kda-decode-b512-h32-k128-w346 (config 2, width extension)"] = {
+            "value": 512 * 32 * 5 / (r2x["elapsed_ms"] / 1e3), "unit": UNIT, "ms_per_step": r2x["elapsed_ms"] / 5,
+            "kernel_ms": r2x["kernel_ms"], "steps": 5, "mode": "async", "page_bytes_per_request": r2x["page_bytes"],
+            "note": "config 2's own plan: row widths {3,4,6} at 30/50/20, 2% fp16 pivot rows (3-bit rows are this "
+                    "build's extension; the reference rejects them)"}
         r3 = measure_prefill(args, 32, 2048, 32, 16, 5, 2, 1, 0, device, barrier, e2e=False)
         peak_tf, peak_tf_kind = measured_peak("bf16_tflops")
         peak_hbm, _ = measured_peak("hbm_gbs")

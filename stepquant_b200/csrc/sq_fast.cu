@@ -606,17 +606,20 @@ __device__ __forceinline__ void halves4(uint2 raw, float2 &lo, float2 &hi) {
     hi = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
 }
 
-// P1 of the step and readout for a pivot head: column partials of k_raw^T Y
-// and q_raw^T Y over the warp's 16 rows, in row order (as readout_rows).
+// The pivot head's two passes on the warp's 16 rows, held in registers (the
+// pivot kernel loads them once, ahead of its inputs): the column partials of
+// k_raw^T Y and q_raw^T Y over the rows in order (as readout_rows), then the
+// update in place, x' = Y (c decay) + k delta per value (the same operations
+// as the integer heads' update) stored as fp16, the fp32 x' also to `dense`
+// ([K, V] of this item) when given.
 template <class Smem>
-__device__ __forceinline__ void pivot_rows(Smem &s, uint8_t *head, int warp, int lane) {
-    const uint8_t *src = pivot_lane(head, warp, lane);
+__device__ __forceinline__ void pivot_rows_held(Smem &s, const uint2 (&raw)[16], int warp, int lane) {
     float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
         float2 y01, y23;
-        halves4(*reinterpret_cast<const uint2 *>(src + r * 32), y01, y23);
+        halves4(raw[r], y01, y23);
         const float4 a = s.rowa[k], b = s.rowb[k];
         kx01 = pfma2(hi2(a), y01, kx01);
         kx23 = pfma2(hi2(a), y23, kx23);
@@ -627,11 +630,9 @@ __device__ __forceinline__ void pivot_rows(Smem &s, uint8_t *head, int warp, int
     *reinterpret_cast<float4 *>(&s.red[1][warp][4 * lane]) = make_float4(qx01.x, qx01.y, qx23.x, qx23.y);
 }
 
-// The pivot head's update in place: x' = Y (c decay) + k delta per value (the
-// same operations as the integer heads' update), stored as fp16; the fp32 x'
-// also to `dense` ([K, V] of this item) when given.
 template <class Smem>
-__device__ __forceinline__ void pivot_update(const Smem &s, uint8_t *head, int warp, int lane, float *dense) {
+__device__ __forceinline__ void pivot_update_held(const Smem &s, const uint2 (&raw)[16], uint8_t *head, int warp,
+                                                  int lane, float *dense) {
     uint8_t *dst = pivot_lane(head, warp, lane);
     const float4 d = *reinterpret_cast<const float4 *>(&s.colc[0][4 * lane]);
     const float4 cd = *reinterpret_cast<const float4 *>(&s.colc[3][4 * lane]);
@@ -640,13 +641,13 @@ __device__ __forceinline__ void pivot_update(const Smem &s, uint8_t *head, int w
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
         float2 y01, y23;
-        uint2 *word = reinterpret_cast<uint2 *>(dst + r * 32);
-        halves4(*word, y01, y23);
+        halves4(raw[r], y01, y23);
         const float2 kk = hi2(s.rowa[k]);
         const float2 x01 = pfma2(kk, d01, pmul2(y01, cd01));
         const float2 x23 = pfma2(kk, d23, pmul2(y23, cd23));
         const __half2 h01 = __float22half2_rn(x01), h23 = __float22half2_rn(x23);
-        *word = make_uint2(*reinterpret_cast<const uint32_t *>(&h01), *reinterpret_cast<const uint32_t *>(&h23));
+        *reinterpret_cast<uint2 *>(dst + r * 32) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&h01), *reinterpret_cast<const uint32_t *>(&h23));
         if (dense) *reinterpret_cast<float4 *>(dense + k * FV + 4 * lane) = make_float4(x01.x, x01.y, x23.x, x23.y);
     }
 }
@@ -1127,6 +1128,13 @@ __global__ void __launch_bounds__(kThreads) pivot_kernel(TileParams p, PivotHead
         pivot_decode(values, p.dense_out + item * FK * FV, warp, lane);
         return;
     }
+    // The warp's rows first: their loads overlap the input loads and norms below.
+    uint2 raw[16];
+    {
+        const uint8_t *src = pivot_lane(values, warp, lane);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) raw[r] = *reinterpret_cast<const uint2 *>(src + r * 32);
+    }
     const sq_step_args &a = p.step;
     float qraw = 0.f, kraw = 0.f, vin = 0.f, braw = 0.f, graw = 0.f;
     if (tid < FK) {
@@ -1148,7 +1156,7 @@ __global__ void __launch_bounds__(kThreads) pivot_kernel(TileParams p, PivotHead
         if (lane == 0) *reinterpret_cast<float4 *>(&s.misc[4 * warp]) = make_float4(part.x, part.y, part.z, 0.f);
     }
     __syncthreads();
-    pivot_rows(s, values, warp, lane);
+    pivot_rows_held(s, raw, warp, lane);
     __syncthreads();
     if (tid < FV) {
         const float beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
@@ -1187,7 +1195,7 @@ __global__ void __launch_bounds__(kThreads) pivot_kernel(TileParams p, PivotHead
         store_from_float(a.out, a.io_dtype, item * FV + tid, __fmaf_rn(qk, delta, qS));
     }
     __syncthreads();
-    pivot_update(s, values, warp, lane, MODE == kStep && p.dense_out ? p.dense_out + item * FK * FV : nullptr);
+    pivot_update_held(s, raw, values, warp, lane, MODE == kStep && p.dense_out ? p.dense_out + item * FK * FV : nullptr);
 }
 
 // Resident CTAs per SM for each mode, and SMs, per device (set up on the first
