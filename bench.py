@@ -965,7 +965,7 @@ def main():
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms else None
         # DRAM read + write bytes of one launch at this workload, from an ncu capture made
         # outside the bench (ncu cannot run inside a timed region); None for other shapes.
-        ncu_traffic = {"sq_writeback": 156.6e6, "sq_readout": 114.1e6}
+        ncu_traffic = {"sq_step (fused)": 153.8e6, "sq_writeback": 156.6e6, "sq_readout": 114.1e6}
         default_shape = (not kda, batch, heads, qk_heads, args.dim, world, args.pivot_heads) == (True, 256, 32, 16, 128, 1, 1)
         name = ("kda-decode-b%d-h%d-k128 (config 2)" if kda else "gdn-decode-b%d-h%d-k128 (config 1)") % (batch, heads)
         kw_desc = "{%s}" % args.kda_widths
