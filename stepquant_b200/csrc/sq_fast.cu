@@ -796,9 +796,19 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
             s.rowa[tid] = make_float4(ro, ro, kraw, kraw);
             s.rowb[tid] = make_float4(qraw, qraw, 0.f, 0.f);
         }
-        if (tid < FV) {  // only the value-column threads finish the readout
+        if (tid == kThreads - 32) {
+            // The item's two gates, once, by a thread of the last warp (idle
+            // here): beta = sigmoid(b), decay = exp(-exp(A_log) softplus(a + dt_bias)).
             braw = p.stage_gates ? st.gate[0] : load_as_float(a.beta, a.gate_dtype, int64_t(c.req) * H + c.head);
             graw = p.stage_gates ? st.gate[1] : load_as_float(a.g, a.gate_dtype, int64_t(c.req) * H + c.head);
+            const float beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
+            float g = graw;
+            if (a.a_log) {
+                const float u = g + s.head[c.head].dt_bias;
+                g = -expf(s.head[c.head].a_log) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
+            }
+            s.misc[32] = beta;
+            s.misc[33] = expf(g);
         }
         // Per-warp sums of q^2, k^2 and q.k over the warps holding q and k
         // (threads 0..K-1), combined after the next barrier.
@@ -844,22 +854,10 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
         }
         {
             const sq_step_args &a = p.step;
-            // Gates, norms and the column results: the four warps of the value
-            // columns only (the gates are independent of the unpack above).
-            float beta = 0.f, decay = 0.f;
-            if (tid < FV) {
-                const float alog = s.head[c.head].a_log;
-                const float bias = s.head[c.head].dt_bias;
-                beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
-                float g = graw;
-                if (a.a_log) {
-                    const float u = g + bias;
-                    g = -expf(alog) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
-                }
-                decay = expf(g);
-            }
+            // Norms and the column results: the four warps of the value columns.
             __syncthreads();
             if (tid < FV) {
+                const float beta = s.misc[32], decay = s.misc[33];
                 float qq = 0.f, kk = 0.f, dot = 0.f;
 #pragma unroll
                 for (int w = 0; w < FK / 32; ++w) {
