@@ -60,7 +60,9 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--impl", choices=("stepquant_b200", "reference"), default="stepquant_b200")
+    p.add_argument("--impl", choices=("stepquant_b200", "reference", "reference-gpu"), default="stepquant_b200",
+                   help="reference: the CPU port of the reference path; reference-gpu: the reference's own "
+                        "Triton/Gluon pool from baseline/_ref beside this library's, config 1, one GPU")
     p.add_argument("--mode", choices=("async", "sync"), default="async")
     p.add_argument("--workload", choices=("gdn-decode", "kda-decode", "gdn-prefill", "gdn-stack"), default="gdn-decode",
                    help="config 1 (default), config 2, config 3 or config 4")
@@ -272,6 +274,140 @@ def reference_arm(args):
                        "batch": batch, "heads": args.heads, "qk_heads": qk_heads, "dim": args.dim},
             "cpu_baseline": res, "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0}}
+    emit(line)
+
+
+def reference_gpu_arm(args):
+    """The reference's own GPU path beside this library's on one B200.
+
+    The unmodified reference package, installed into ``baseline/_ref`` (pip
+    ``--target``; it is not part of this repository), runs config 1 through its
+    public ``PackedStatePool`` (Triton/Gluon kernels, asynchronous writeback),
+    timed the way its ``benchmarks/bench_formats.py`` times it: ``step();
+    wait()`` captured in a CUDA graph (one per slot group and input set) and
+    replayed between CUDA events.  This library's pool runs the identical plan,
+    states, inputs and graph structure in the same process.  After encoding and
+    after one step from the same pages the two pools' bytes and outputs are
+    compared.  Rank 0 only; prints one JSON line.
+    """
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    path = os.path.join(ROOT, "baseline", "_ref")
+    base = {"impl": "reference-gpu", "metric": METRIC, "unit": UNIT}
+    if not os.path.isdir(os.path.join(path, "stepquant")):
+        emit(dict(base, unavailable="the reference package is not installed in baseline/_ref"))
+        return
+    import torch
+    sys.path.insert(0, path)
+    try:
+        from stepquant.kernels.pool import PackedStatePool as RefPool
+        from stepquant.quantization import QuantizationPlan as RefPlan
+    except Exception as exc:  # an import failure of the reference is its result here
+        emit(dict(base, unavailable="reference import failed: %s: %s" % (type(exc).__name__, exc)))
+        return
+    from stepquant_b200 import synthetic as S
+    from stepquant_b200.kernels.pool import PackedStatePool
+    from stepquant_b200.quantization import QuantizationPlan
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    batch, heads, dim = args.batch or 256, args.heads, args.dim
+    qk = args.qk_heads or heads // 2
+    groups_n = args.slot_groups
+    cpu_gen = torch.Generator().manual_seed(args.seed)
+    widths = S.gdn_widths(heads, cpu_gen, args.pivot_heads)
+    bits = widths[:, None].expand(heads, dim).contiguous()
+    impact = torch.rand(heads, dim, generator=cpu_gen) + 0.5
+    gen = torch.Generator(device=device).manual_seed(args.seed)
+    a_log, dt_bias = S.gate_parameters(heads, dim, False, gen, device)
+    kw = dict(normalize=True, scale=dim ** -0.5, a_log=a_log, dt_bias=dt_bias)
+    slots_total = batch * groups_n + 1
+    groups = [torch.arange(1 + g * batch, 1 + (g + 1) * batch, device=device) for g in range(groups_n)]
+    inputs = [S.draw_inputs(batch, heads, qk, dim, dim, False, gen, device) for _ in range(2)]
+    state = torch.randn(batch * groups_n, heads, dim, dim, generator=gen, device=device) * 0.1
+
+    def make(kind):
+        stream = torch.cuda.Stream(device)
+        if kind == "reference":
+            return RefPool(RefPlan("gdn", bits.to(device), impact.to(device)), slots_total, dim,
+                           writeback_stream=stream)
+        return PackedStatePool(QuantizationPlan("gdn", bits.to(device), impact.to(device)), slots_total, dim,
+                               writeback_stream=stream)
+
+    def run(pool, i):
+        x = inputs[i % len(inputs)]
+        out = pool.step(x.q, x.k, x.v, x.a, x.b, groups[i % groups_n], **kw)
+        pool.wait()
+        return out
+
+    def timed(pool, clocks=None):
+        for i in range(args.warmup):
+            run(pool, i)
+        torch.cuda.synchronize()
+        period = math.lcm(len(inputs), groups_n)
+        graphs = []
+        for j in range(period):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                run(pool, j)
+            graphs.append(graph)
+        for i in range(args.warmup):
+            graphs[i % period].replay()
+        torch.cuda.synchronize()
+        start, end = _events()
+        if clocks:
+            clocks.start()
+        start.record()
+        for i in range(args.steps):
+            graphs[i % period].replay()
+        end.record()
+        torch.cuda.synchronize()
+        if clocks:
+            clocks.stop()
+        del graphs
+        return start.elapsed_time(end) / args.steps
+
+    ours, theirs = make("this"), make("reference")
+    for pool in (ours, theirs):
+        pool.encode(state, torch.arange(1, slots_total, device=device))
+    torch.cuda.synchronize()
+    del state
+    # One step from the same pages: compare the pools' bytes and outputs.
+    same_layout = ours.data.shape == theirs.data.shape
+    enc_equal = float((ours.data == theirs.data).float().mean()) if same_layout else None
+    out_ours, out_theirs = run(ours, 0), run(theirs, 0)
+    torch.cuda.synchronize()
+    rows = groups[0]
+    step_equal = float((ours.data[rows] == theirs.data[rows]).float().mean()) if same_layout else None
+    out_diff = float((out_ours.float() - out_theirs.float()).abs().max())
+    # The parity step advanced group 0 in both pools alike; the timed runs continue from there.
+    clocks = ClockSampler(0)
+    try:
+        ref_ms = timed(theirs, clocks)
+    except Exception as exc:
+        emit(dict(base, unavailable="reference step failed: %s: %s" % (type(exc).__name__, exc)))
+        return
+    our_ms = timed(ours)
+    updates = batch * heads
+    import triton
+    line = dict(base, value=updates / (ref_ms / 1e3), n_gpus=1, steps=args.steps, warmup=args.warmup,
+                ms_per_step=ref_ms, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="f32",
+                data="synthetic",
+                config={"workload": "gdn-decode-b%d-h%d-k128 (config 1), reference Triton/Gluon PackedStatePool"
+                                    % (batch, heads), "batch": batch, "heads": heads, "qk_heads": qk, "dim": dim,
+                        "plan": "widths {4,6,8} 25/50/25, pivot heads %d, impact uniform [0.5, 1.5)"
+                                % args.pivot_heads,
+                        "writeback": "async (reference default chunk 64)",
+                        "timing": "step(); wait() in one CUDA graph per step, CUDA events",
+                        "l2": "slots rotate over %d groups (%.0f MB of pages)"
+                              % (groups_n, slots_total * theirs.page_bytes / 1e6)},
+                triton=triton.__version__, clocks=clocks.summary(),
+                this_build={"value": updates / (our_ms / 1e3), "ms_per_step": our_ms,
+                            "speedup_over_reference": ref_ms / our_ms},
+                parity={"page_bytes_equal_after_encode": enc_equal, "page_bytes_equal_after_step": step_equal,
+                        "out_max_abs_diff": out_diff, "page_bytes": theirs.page_bytes,
+                        "page_bytes_this_build": ours.page_bytes})
     emit(line)
 
 
@@ -827,6 +963,9 @@ def main():
     if args.impl == "reference":
         reference_arm(args)
         return
+    if args.impl == "reference-gpu":
+        reference_gpu_arm(args)
+        return
     import torch
     import torch.distributed as dist
 
@@ -995,42 +1134,49 @@ def main():
         })
     line["clocks"] = clocks.summary()
 
-    # Short measurements of the other configurations (single GPU, default run only).
-    if world == 1 and workload == "gdn-decode" and not args.no_secondary:
+    # Short measurements of the other configurations (default workload only), on
+    # the same ranks: value heads sharded as in config 1, times max over ranks.
+    if workload == "gdn-decode" and not args.no_secondary:
         sec = {}
-        r2 = measure_decode(args, True, 512, 32, 32, 5, 3, 1, 0, device, barrier, mode="async", e2e=False,
-                            warm_steps=64, slot_groups=2, seed=2)
-        sec["kda-decode-b512-h32-k128 (config 2)"] = {
-            "value": 512 * 32 * 5 / (r2["elapsed_ms"] / 1e3), "unit": UNIT, "ms_per_step": r2["elapsed_ms"] / 5,
-            "kernel_ms": r2["kernel_ms"], "steps": 5, "mode": "async", "page_bytes_per_request": r2["page_bytes"],
-            "note": "reference-legal twin plan: row widths {2,4,6} at 30/50/20, 2% fp16 pivot rows; "
-                    "64 warm-up steps, 2 slot groups"}
-        r2x = measure_decode(args, True, 512, 32, 32, 5, 3, 1, 0, device, barrier, mode="async", e2e=False,
-                             warm_steps=64, slot_groups=2, seed=2, kda_widths=(3, 4, 6))
-        sec["kda-decode-b512-h32-k128-w346 (config 2, width extension)"] = {
-            "value": 512 * 32 * 5 / (r2x["elapsed_ms"] / 1e3), "unit": UNIT, "ms_per_step": r2x["elapsed_ms"] / 5,
-            "kernel_ms": r2x["kernel_ms"], "steps": 5, "mode": "async", "page_bytes_per_request": r2x["page_bytes"],
-            "note": "config 2's own plan: row widths {3,4,6} at 30/50/20, 2% fp16 pivot rows (3-bit rows are this "
-                    "build's extension; the reference rejects them)"}
-        r3 = measure_prefill(args, 32, 2048, 32, 16, 5, 2, 1, 0, device, barrier, e2e=False)
+        for widths, key, note in (
+                ((2, 4, 6), "kda-decode-b512-h32-k128 (config 2)",
+                 "reference-legal twin plan: row widths {2,4,6} at 30/50/20, 2% fp16 pivot rows; "
+                 "64 warm-up steps, 2 slot groups"),
+                ((3, 4, 6), "kda-decode-b512-h32-k128-w346 (config 2, width extension)",
+                 "config 2's own plan: row widths {3,4,6} at 30/50/20, 2% fp16 pivot rows (3-bit rows are this "
+                 "build's extension; the reference rejects them)")):
+            r2 = measure_decode(args, True, 512, 32, 32, 5, 3, world, rank, device, barrier, mode="async", e2e=False,
+                                warm_steps=64, slot_groups=2, seed=2, kda_widths=widths)
+            (ms2,) = max_over_ranks(r2["elapsed_ms"])
+            (pb2,) = sum_over_ranks(r2["page_bytes"])
+            sec[key] = {"value": 512 * 32 * 5 / (ms2 / 1e3), "unit": UNIT, "ms_per_step": ms2 / 5,
+                        "kernel_ms": r2["kernel_ms"], "steps": 5, "mode": "async",
+                        "page_bytes_per_request": int(pb2), "note": note}
+        r3 = measure_prefill(args, 32, 2048, 32, 16, 5, 2, world, rank, device, barrier, e2e=False)
+        (ms3,) = max_over_ranks(r3["elapsed_ms"])
+        flops3, bytes3 = sum_over_ranks(r3["flops"], r3["bytes"])
         peak_tf, peak_tf_kind = measured_peak("bf16_tflops")
         peak_hbm, _ = measured_peak("hbm_gbs")
         pk = sum(r3["kernel_ms"].values())
         sec["gdn-prefill-b32-t2048-h32-k128 (config 3)"] = {
-            "value": 32 * 2048 * 5 / (r3["elapsed_ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r3["elapsed_ms"] / 5,
+            "value": 32 * 2048 * 5 / (ms3 / 1e3), "unit": "tokens/s", "ms_per_step": ms3 / 5,
             "kernel_ms": r3["kernel_ms"], "steps": 5,
-            "hbm_frac": (r3["bytes"] / (pk / 1e3) / 1e9 / peak_hbm) if pk else None,
-            "tensor_tflops": r3["flops"] / (pk / 1e3) / 1e12 if pk else None,
-            "tensor_frac": (r3["flops"] / (pk / 1e3) / 1e12 / peak_tf) if pk else None, "peak_source": peak_tf_kind}
-        r4 = measure_stack(args, 512, 32, 16, 5, 2, 1, 0, device, barrier)
-        fam, ms4 = r4["kernel_ms"], r4["elapsed_ms"] / 5
+            "hbm_frac": (bytes3 / world / (pk / 1e3) / 1e9 / peak_hbm) if pk else None,
+            "tensor_tflops": flops3 / world / (pk / 1e3) / 1e12 if pk else None,
+            "tensor_frac": (flops3 / world / (pk / 1e3) / 1e12 / peak_tf) if pk else None,
+            "peak_source": peak_tf_kind}
+        r4 = measure_stack(args, 512, 32, 16, 5, 2, world, rank, device, barrier)
+        ms4_all, e2e4 = max_over_ranks(r4["elapsed_ms"], r4["e2e_ms"])
+        fam, ms4 = r4["kernel_ms"], ms4_all / 5
         sec["gdn-stack-l%d-b512-h32-hidden%d (config 4)" % (args.layers, args.hidden)] = {
-            "value": 512 * 5 / (r4["elapsed_ms"] / 1e3), "unit": "tokens/s", "ms_per_step": ms4,
-            "e2e": 512 * 5 / (r4["e2e_ms"] / 1e3), "kernel_ms_per_step": fam,
+            "value": 512 * 5 / (ms4_all / 1e3), "unit": "tokens/s", "ms_per_step": ms4,
+            "e2e": 512 * 5 / (e2e4 / 1e3), "kernel_ms_per_step": fam,
             "state_update_share": (fam["state_readout"] + fam["state_writeback"]) / ms4, "steps": 5,
             "finite": r4["finite"],
             "note": "%d GDN layers, prompt %d tokens then decode; one CUDA graph per decode token (writeback joined), "
-                    "1 GPU (the all-gather is the identity)" % (args.layers, args.prompt)}
+                    "%s" % (args.layers, args.prompt,
+                            "1 GPU (the all-gather is the identity)" if world == 1 else
+                            "tp%d: NCCL all-gather of each layer's readout inside the graph" % world)}
         line["secondary"] = sec
 
     if world > 1:

@@ -1,14 +1,16 @@
 // Register-resident decode kernels for GDN heads with K = V = 128 and a code
 // width of 4, 6 or 8 bits (the served shape of Qwen-Next-style layers).
 //
-// Persistent 256-thread CTAs, three per SM, each walking (request, value head)
-// items; the next item's page bytes and inputs are prefetched (cp.async) into
-// a second stage buffer while the current item is computed.  Warp w owns
-// key rows 16w..16w+15 and lane l owns value columns l, l+32, l+64, l+96, so
-// each thread owns 64 state elements for the whole step; the step, writeback
-// and encode keep them in the thread's tensor-memory lane between phases and
-// bring 16 at a time into registers (80 registers a thread).  That mapping
-// makes both ordered sums of fit_state local:
+// One persistent CTA per SM made of four 256-thread item groups; a group
+// works one (request, value head) item at a time and takes the next of its
+// SM's items from a shared counter, so the groups of an SM finish together.
+// The next item's page bytes and inputs are prefetched (cp.async) while the
+// current item is computed.  Within a group warp w owns key rows 16w..16w+15
+// and lane l owns value columns l, l+32, l+64, l+96, so each thread owns 64
+// state elements for the whole step; the step, writeback and encode keep them
+// in the thread's tensor-memory lane between phases and bring 16 at a time
+// into registers (64 registers a thread).  That mapping makes both ordered
+// sums of fit_state local:
 //  * torch sums a row of 128 values as 8 lanes (column % 8), each lane a 4-way
 //    interleaved chain over vectors; the chain of lane (column % 8) over the
 //    columns l + 32 i is exactly what thread l holds -- only the last two
@@ -67,8 +69,18 @@ struct HeadInfo {
     float a_log, dt_bias;
 };
 
+// Readout and decode: the second stage buffer (the next item's data lands
+// there while the current item is computed).  Step, writeback and encode: the
+// row partials, then the new code bytes; these modes keep one stage buffer and
+// refill it as soon as the current item's staged data has been consumed.
+union FastTail {
+    FastStage st1;
+    unsigned char plane[kPlaneBytes];
+};
+
+// One item group's shared memory (a CTA holds kGroups of them).
 struct FastSmem {
-    FastStage st[2];
+    FastStage st0;
     float red[2][8][FV];               // per-warp column partials
     float4 rowa[FK];                   // per-row constants, duplicated pairs:
     float4 rowb[FK];                   //   P1: {r_old, r_old, k, k} {q, q, -, -}; P3-P5: {r, r, 1/r, 1/r} {-r, -r, w2, w2}
@@ -76,17 +88,42 @@ struct FastSmem {
     float misc[64];
     HeadInfo head[kMaxHeads];
     long long slot_ring[3];  // slots of the current and next two items (cp.async)
-    uint32_t tmem_slot;      // tensor-memory base of the CTA's state columns
-    // Last, so that the readout and decode, which requantize nothing, launch
-    // without it (four CTAs per SM instead of three).
-    alignas(16) unsigned char plane[kPlaneBytes];  // row partials, then new code bytes
+    int item_ring[3];        // the items themselves
+    uint32_t tmem_slot;      // (group 0) tensor-memory base of the CTA's columns
+    alignas(16) FastTail tail;
+    __device__ FastStage &stage(int b) { return b ? tail.st1 : st0; }
 };
 
+// A CTA is one SM's worth of item groups: kGroups groups of 256 threads, each
+// working one (request, head) item at a time with its own shared memory and
+// named barrier, taking the SM's items one by one from a shared counter.
+constexpr int kGroups = 4;
+struct FastCta {
+    FastSmem grp[kGroups];
+    int next;  // the SM's next untaken item
+};
+
+// Barriers of one item group (ids 1..kGroups; 0 is the CTA's __syncthreads).
+__device__ __forceinline__ void group_sync(int bar) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(bar), "n"(kThreads) : "memory");
+}
+__device__ __forceinline__ bool group_and(int bar, bool pred) {
+    uint32_t r;
+    asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+                 : "=r"(r) : "r"(uint32_t(pred)), "r"(bar), "n"(kThreads) : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ bool group_or(int bar, bool pred) {
+    uint32_t r;
+    asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+                 : "=r"(r) : "r"(uint32_t(pred)), "r"(bar), "n"(kThreads) : "memory");
+    return r != 0;
+}
+
 // Step, writeback and encode keep each thread's 64 state values in tensor
-// memory between phases (128 columns per CTA: warps w and w + 4 share a lane
-// quarter, each with 64 columns), so a thread holds only 16 of them in
-// registers at a time and three CTAs fit on an SM.
-constexpr uint32_t kTmCols = 128;
+// memory between phases (128 columns per item group: warps w and w + 4 share
+// a lane quarter, each with 64 columns), so a thread holds only 16 of them in
+// registers at a time; the four groups of a CTA take the SM's 512 columns.
 template <int MODE>
 __host__ __device__ constexpr bool tm_mode() { return MODE == kStep || MODE == kWriteback || MODE == kEncode; }
 
@@ -152,7 +189,7 @@ __device__ __forceinline__ void store_chunk(uint8_t *dst, const unsigned char *p
 }
 
 struct Ctx {
-    int req, head, warp, lane, tid;
+    int req, head, warp, lane, tid, bar;  // bar: the item group's barrier
     int64_t slot;
     uint8_t *page;
     int off_head;
@@ -212,7 +249,7 @@ __device__ __forceinline__ void final_levels(FastSmem &s, int warp, int lane, ui
     const float2 n01 = make_float2(-c01.x, -c01.y), n23 = make_float2(-c23.x, -c23.y);
     const float2 round = make_float2(kRound, kRound);
     const int t0 = lane >> 4, u = lane & 15;
-    unsigned char *plane = s.plane + t0 * (FK * 16 + kStagePad) + u + warp * 16 * 16;
+    unsigned char *plane = s.tail.plane + t0 * (FK * 16 + kStagePad) + u + warp * 16 * 16;
 #pragma unroll 1
     for (int g = 0; g < 4; ++g) {
         float2 X[4][2];
@@ -312,11 +349,11 @@ __device__ __forceinline__ void fast_quantize_tail(FastSmem &s, const Ctx &c, fl
         safe = (c0 >= 6.103515625e-05f) && (ratio <= 65504.f);
     }
     // One barrier in the common case: every column settled and safe.
-    bool no_clamp = __syncthreads_and(settled && safe);
+    bool no_clamp = group_and(c.bar, settled && safe);
     if (!no_clamp) {
-        if (!SLOW && !__syncthreads_and(settled)) {
+        if (!SLOW && !group_and(c.bar, settled)) {
             column_max<false, true>(s, warp, lane, c.tm);
-            __syncthreads();
+            group_sync(c.bar);
             if (tid < FV) {
                 mx = 0.f;
 #pragma unroll
@@ -328,7 +365,7 @@ __device__ __forceinline__ void fast_quantize_tail(FastSmem &s, const Ctx &c, fl
                 safe = (c0 >= 6.103515625e-05f) && (ratio <= 65504.f);
             }
         }
-        no_clamp = __syncthreads_and(safe);
+        no_clamp = group_and(c.bar, safe);
     }
     // P4: first levels, weighted least-squares numerator / denominator (16-row blocks).
     {
@@ -344,7 +381,7 @@ __device__ __forceinline__ void fast_quantize_tail(FastSmem &s, const Ctx &c, fl
         s.red[1][warp][lane + 64] = den[1].x;
         s.red[1][warp][lane + 96] = den[1].y;
     }
-    __syncthreads();
+    group_sync(c.bar);
     safe = 1;
     if (tid < FV) {
         float num = 0.f, den = 0.f;
@@ -360,7 +397,7 @@ __device__ __forceinline__ void fast_quantize_tail(FastSmem &s, const Ctx &c, fl
         // (an overflowing quotient reads as unsafe; an underflowing one is far below qmax)
         safe = (c1 >= 6.103515625e-05f) && ((SLOW ? __fdiv_rn(mx, c1) : div_fp16(mx, c1, rc1)) < qmax + 0.5f);
     }
-    const bool no_clamp5 = __syncthreads_and(safe);
+    const bool no_clamp5 = group_and(c.bar, safe);
     // P5: final levels -> one signed level byte per value in the plane.
     if (!SLOW && no_clamp5) final_levels<SLOW, false>(s, warp, lane, c.tm, qmax);
     else final_levels<SLOW, true>(s, warp, lane, c.tm, qmax);
@@ -374,12 +411,17 @@ __device__ __forceinline__ void fast_quantize_tail(FastSmem &s, const Ctx &c, fl
 // divisions when any warp is slow (the partial maxima of the other warps are
 // then taken again with IEEE divisions).  The barrier that completes the
 // partial maxima also combines the warps' flags.
-__device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float qmax, bool warp_slow) {
+// `consumed` runs right after that barrier, when every thread of the group is
+// past its last read of the item's stage buffer.
+template <class Consumed>
+__device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float qmax, bool warp_slow, Consumed &&consumed) {
     if (warp_slow) column_max<true, true>(s, c.warp, c.lane, c.tm);
     else column_max<false, false>(s, c.warp, c.lane, c.tm);
-    if (__syncthreads_or(warp_slow)) {
+    const bool slow = group_or(c.bar, warp_slow);
+    consumed();
+    if (slow) {
         if (!warp_slow) column_max<true, true>(s, c.warp, c.lane, c.tm);
-        __syncthreads();
+        group_sync(c.bar);
         fast_quantize_tail<true>(s, c, qmax);
     } else {
         fast_quantize_tail<false>(s, c, qmax);
@@ -390,19 +432,19 @@ __device__ __forceinline__ void fast_quantize(FastSmem &s, const Ctx &c, float q
 // Warp w packs the chunks of its own rows 16w..16w+15 (all eight value tiles),
 // four per lane, and stores their row scales; threads 128-255 store c.
 template <int BITS>
-__device__ __forceinline__ void fast_store(const TileParams &p, FastSmem &s, const Ctx &c) {
-    const sq_plan &P = p.plan;
+__device__ __forceinline__ void fast_store(FastSmem &s, const Ctx &c) {
     uint8_t *dst = c.page + c.off_head;
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
         const int i = c.lane + 32 * m, t = i >> 4, k = c.warp * 16 + (i & 15);
-        store_chunk<BITS>(dst + t * W<BITS>::tile_bytes + k * W<BITS>::chunk, s.plane + t * (FK * 16 + kStagePad) + k * 16);
+        store_chunk<BITS>(dst + t * W<BITS>::tile_bytes + k * W<BITS>::chunk, s.tail.plane + t * (FK * 16 + kStagePad) + k * 16);
     }
+    const HeadInfo &hi = s.head[c.head];
     if (c.lane < 16) {
         const int k = c.warp * 16 + c.lane;
-        reinterpret_cast<__half *>(c.page + P.rows[c.head * FK])[k] = __float2half_rn(s.rowa[k].x);
+        reinterpret_cast<__half *>(c.page + hi.rows)[k] = __float2half_rn(s.rowa[k].x);
     }
-    if (c.tid >= FK) reinterpret_cast<__half *>(c.page + P.columns[c.head])[c.tid - FK] = __float2half_rn(s.colc[1][c.tid - FK]);
+    if (c.tid >= FK) reinterpret_cast<__half *>(c.page + hi.columns)[c.tid - FK] = __float2half_rn(s.colc[1][c.tid - FK]);
 }
 
 // Stage the head's code bytes (cp.async, 16-byte pieces, one padded region per value tile).
@@ -529,7 +571,7 @@ __device__ __forceinline__ void unpack_update_tm(FastSmem &s, const FastStage &s
     const float2 d23 = make_float2(s.colc[0][lane + 64], s.colc[0][lane + 96]);
     const float2 cd01 = make_float2(s.colc[3][lane], s.colc[3][lane + 32]);
     const float2 cd23 = make_float2(s.colc[3][lane + 64], s.colc[3][lane + 96]);
-    float *rowpart = reinterpret_cast<float *>(s.plane);
+    float *rowpart = reinterpret_cast<float *>(s.tail.plane);
 #pragma unroll 1
     for (int g = 0; g < 4; ++g) {
         float2 X[4][2];
@@ -551,7 +593,7 @@ __device__ __forceinline__ void unpack_update_tm(FastSmem &s, const FastStage &s
 
 // P1 + P2 of the encode: the dense state rows, row partials, to tensor memory.
 __device__ __forceinline__ void load_rows_tm(FastSmem &s, const float *src, int warp, int lane, uint32_t tm) {
-    float *rowpart = reinterpret_cast<float *>(s.plane);
+    float *rowpart = reinterpret_cast<float *>(s.tail.plane);
 #pragma unroll 1
     for (int g = 0; g < 4; ++g) {
         float2 X[4][2];
@@ -746,8 +788,9 @@ __device__ __forceinline__ void prefetch(const TileParams &p, const FastSmem &s,
 // update and the quantizer are one copy shared by every width, so CTAs of
 // different widths resident on one SM run the same instructions.
 // ---------------------------------------------------------------------------
-template <int MODE>
-__device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st, const Ctx &c, int width) {
+template <int MODE, class Consumed>
+__device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st, const Ctx &c, int width,
+                          Consumed &&consumed) {
     const sq_plan &P = p.plan;
     const int H = P.heads;
     const int warp = c.warp, lane = c.lane, tid = c.tid;
@@ -823,7 +866,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
             if (lane == 0) *reinterpret_cast<float4 *>(&s.misc[4 * warp]) = make_float4(part.x, part.y, part.z, 0.f);
         }
     }
-    __syncthreads();
+    group_sync(c.bar);
 
     // ---- P1: unpack; column partials of k_raw^T Y and q_raw^T Y ---------------
     // (Encode and writeback fold P2's work into this pass.)
@@ -855,7 +898,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
         {
             const sq_step_args &a = p.step;
             // Norms and the column results: the four warps of the value columns.
-            __syncthreads();
+            group_sync(c.bar);
             if (tid < FV) {
                 const float beta = s.misc[32], decay = s.misc[33];
                 float qq = 0.f, kk = 0.f, dot = 0.f;
@@ -894,7 +937,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
                 }
             }
             if (MODE == kReadout) return;
-            __syncthreads();
+            group_sync(c.bar);
         }
     }
 
@@ -902,7 +945,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
     bool warp_slow;
     {
         bool huge = false;
-        float *rowpart = reinterpret_cast<float *>(s.plane);
+        float *rowpart = reinterpret_cast<float *>(s.tail.plane);
         if (MODE == kStep) {
             const float2 d01 = make_float2(s.colc[0][lane], s.colc[0][lane + 32]);
             const float2 d23 = make_float2(s.colc[0][lane + 64], s.colc[0][lane + 96]);
@@ -963,31 +1006,38 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
         __syncwarp();
         warp_slow = __any_sync(0xffffffffu, huge);
     }
-    fast_quantize(s, c, float((1 << (width - 1)) - 1), warp_slow);
-    if (width == 4) fast_store<4>(p, s, c);
-    else if (width == 6) fast_store<6>(p, s, c);
-    else fast_store<8>(p, s, c);
+    fast_quantize(s, c, float((1 << (width - 1)) - 1), warp_slow, consumed);
+    if (width == 4) fast_store<4>(s, c);
+    else if (width == 6) fast_store<6>(s, c);
+    else fast_store<8>(s, c);
 }
 
-// Persistent loop: CTA b takes items b, b + gridDim.x, ... (item = request * H
-// + head).  While one item is computed the next one's data is in flight into
-// the other stage buffer, and the slot of the item after that into a small
-// ring, so each item starts with its page, scales and inputs on chip.
-// The readout, launched without the requantization plane, fits four CTAs per
-// SM when it stays within 64 registers; the rest are bounded at three.
+// Persistent kernel, one CTA per SM: CTA b owns the contiguous item range
+// [b * items / grid, (b + 1) * items / grid) (item = request * H + head) and
+// its kGroups item groups take the range's items one at a time from a shared
+// counter, so a group that runs ahead takes more items and the groups of an SM
+// finish together.  Each group keeps the next item's data in flight while it
+// computes the current one, and the slot of the item after that in a small
+// ring, so each item starts with its page, scales and inputs on chip.  The
+// readout and decode keep two stage buffers and issue the next item's copies
+// first; the step, writeback and encode keep one (the other's space holds their
+// row partials and code bytes) and refill it once the item's staged data is
+// consumed, before the quantizer's column passes.  64 registers a thread.
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, MODE == kReadout ? 4 : 3) fast_kernel(TileParams p, int items) {
+__global__ void __launch_bounds__(kGroups * kThreads, 1) fast_kernel(TileParams p, int items) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    FastSmem &s = *reinterpret_cast<FastSmem *>(smem_raw);
+    FastCta &cta = *reinterpret_cast<FastCta *>(smem_raw);
+    const int group = threadIdx.x / kThreads;
+    FastSmem &s = cta.grp[group];
     const sq_plan &P = p.plan;
     const int H = P.heads;
     Ctx c;
-    c.tid = threadIdx.x;
+    c.tid = threadIdx.x % kThreads;
     c.warp = c.tid >> 5;
     c.lane = c.tid & 31;
-    int item = blockIdx.x;
-    if (item >= items) return;
-    const int stride = gridDim.x;
+    c.bar = 1 + group;
+    const int lo = int(int64_t(blockIdx.x) * items / gridDim.x);
+    const int hi = int(int64_t(blockIdx.x + 1) * items / gridDim.x);
     for (int h = c.tid; h < H; h += kThreads) {
         HeadInfo hi;
         hi.width = P.bits[h * FK];
@@ -999,16 +1049,18 @@ __global__ void __launch_bounds__(kThreads, MODE == kReadout ? 4 : 3) fast_kerne
         hi.dt_bias = gates ? p.step.dt_bias[h] : 0.f;
         s.head[h] = hi;
     }
-    if (tm_mode<MODE>() && c.warp == 0) tm_alloc(&s.tmem_slot, kTmCols);
-    // (request, head) of item = request * H + head, advanced by stride = sreq * H + shead
-    // each round without a division.
-    const int sreq = stride / H, shead = stride - sreq * H;
+    if (threadIdx.x == 0) cta.next = lo + 2 * kGroups;
+    if (tm_mode<MODE>() && threadIdx.x < 32) tm_alloc(&cta.grp[0].tmem_slot, 512);
     const int hshift = (H & (H - 1)) == 0 ? __ffs(H) - 1 : -1;
-    int req = item / H, head = item - req * H;
-    auto next_req = [&](int r, int h) { return r + sreq + (h + shead >= H); };
+    auto request_of = [&](int it) { return hshift >= 0 ? it >> hshift : it / H; };
+    // The group's first two items are lo + group and lo + kGroups + group; the
+    // rest come from the counter.
     if (c.tid == 0) {
-        cp_async8(&s.slot_ring[0], p.slots + req);
-        if (item + stride < items) cp_async8(&s.slot_ring[1], p.slots + next_req(req, head));
+        const int i0 = lo + group, i1 = lo + kGroups + group;
+        s.item_ring[0] = i0;
+        s.item_ring[1] = i1;
+        if (i0 < hi) cp_async8(&s.slot_ring[0], p.slots + request_of(i0));
+        if (i1 < hi) cp_async8(&s.slot_ring[1], p.slots + request_of(i1));
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -1016,49 +1068,57 @@ __global__ void __launch_bounds__(kThreads, MODE == kReadout ? 4 : 3) fast_kerne
     __syncthreads();
     if (tm_mode<MODE>()) {
         tm_fence_after();
-        c.tm = s.tmem_slot + (uint32_t(32 * (c.warp & 3)) << 16) + uint32_t(64 * (c.warp >> 2));
+        c.tm = cta.grp[0].tmem_slot + (uint32_t(32 * (c.warp & 3)) << 16) + uint32_t(128 * group + 64 * (c.warp >> 2));
     }
+    int item = s.item_ring[0];
     long long slot = s.slot_ring[0];
-    {
-        const WorkItem first = describe(p, s, req, head, slot);
-        if (first.fast && first.active) prefetch<MODE>(p, s, s.st[0], first, c.tid);
-        cp_async_commit();
-        cp_async_wait<0>();
-        __syncthreads();
+    if (item < hi) {
+        const int req = request_of(item);
+        const WorkItem first = describe(p, s, req, item - req * H, slot);
+        if (first.fast && first.active) prefetch<MODE>(p, s, s.st0, first, c.tid);
     }
-    // Invariant at the top of round r: the current item's data is in s.st[buf],
-    // and the next item's slot is in slot_ring[(r + 1) % 3].  Round r fills
-    // entry (r + 2) % 3, last read before the barrier that ended round r - 1.
+    cp_async_commit();
+    cp_async_wait<0>();
+    group_sync(c.bar);
+    // Invariant at the top of round r: the current item's data is in
+    // s.stage(buf), and the next item and its slot are in item_ring and
+    // slot_ring[(r + 1) % 3].  Round r fills entry (r + 2) % 3, last read
+    // before the barrier that ended round r - 1.
+    constexpr bool kOneStage = tm_mode<MODE>();
     int buf = 0, ring = 0;  // ring = r % 3
-    for (; item < items; item += stride) {
+    while (item < hi) {
         const int ring1 = ring == 2 ? 0 : ring + 1, ring2 = ring1 == 2 ? 0 : ring1 + 1;
-        const int next_item = item + stride;
-        // (The writeback splits the item index instead: it has no registers to
-        // spare for the carried pair; a shift when H is a power of two.)
-        constexpr bool kCarry = MODE != kWriteback;
-        if (!kCarry) {
-            req = hshift >= 0 ? item >> hshift : item / H;
-            head = item - req * H;
-        }
-        const int nreq = kCarry ? next_req(req, head) : hshift >= 0 ? next_item >> hshift : next_item / H;
-        const int nhead = kCarry ? (head + shead >= H ? head + shead - H : head + shead) : next_item - nreq * H;
-        if (next_item < items) {
-            const WorkItem nxt = describe(p, s, nreq, nhead, s.slot_ring[ring1]);
-            if (nxt.fast && nxt.active) prefetch<MODE>(p, s, s.st[buf ^ 1], nxt, c.tid);
-            if (c.tid == 0 && next_item + stride < items)
-                cp_async8(&s.slot_ring[ring2], p.slots + next_req(nreq, nhead));
-        }
-        cp_async_commit();
-        const WorkItem cur = describe(p, s, req, head, slot);
+        const int next_item = s.item_ring[ring1];
+        auto issue_next = [&]() {
+            if (next_item < hi) {
+                const int nreq = request_of(next_item);
+                const WorkItem nxt = describe(p, s, nreq, next_item - nreq * H, s.slot_ring[ring1]);
+                if (nxt.fast && nxt.active) prefetch<MODE>(p, s, s.stage(kOneStage ? 0 : buf ^ 1), nxt, c.tid);
+                if (c.tid == 0) {
+                    const int after = atomicAdd(&cta.next, 1);
+                    s.item_ring[ring2] = after;
+                    if (after < hi) cp_async8(&s.slot_ring[ring2], p.slots + request_of(after));
+                }
+            } else if (c.tid == 0) {
+                s.item_ring[ring2] = hi;
+            }
+            cp_async_commit();
+        };
+        if (!kOneStage) issue_next();
+        const int req = request_of(item);
+        const WorkItem cur = describe(p, s, req, item - req * H, slot);
         c.req = cur.req;
         c.head = cur.head;
         c.slot = cur.slot;
         if (MODE == kReadout && c.head == 0 && c.tid == 0) p.stable_slots[c.req] = c.slot;
+        const bool body = cur.fast && cur.active;
+        if (kOneStage && !body) issue_next();
         if (cur.fast) {
             if (cur.active) {
                 c.page = p.pages + c.slot * P.page_bytes;
                 c.off_head = s.head[c.head].off_head;
-                fast_body<MODE>(p, s, s.st[buf], c, cur.width);
+                if constexpr (kOneStage) fast_body<MODE>(p, s, s.st0, c, cur.width, issue_next);
+                else fast_body<MODE>(p, s, s.stage(buf), c, cur.width, [] {});
             } else {
                 if (cur.slot > 0 && c.tid == 0) flag(p.status, SQ_STATUS_SLOT_RANGE);
                 if ((MODE == kStep || MODE == kReadout) && c.tid < FV)
@@ -1070,18 +1130,17 @@ __global__ void __launch_bounds__(kThreads, MODE == kReadout ? 4 : 3) fast_kerne
             }
         }
         cp_async_wait<0>();  // the next item's data and the slot after it
-        __syncthreads();     // ... visible to all; the stage buffer just read is free
+        group_sync(c.bar);   // ... visible to the group; the stage buffer just read is free
         slot = s.slot_ring[ring1];
-        req = nreq;
-        head = nhead;
-        buf ^= 1;
+        item = next_item;
+        if (!kOneStage) buf ^= 1;
         ring = ring1;
     }
     if (tm_mode<MODE>()) {
         tm_fence_before();
         __syncthreads();
         tm_fence_after();
-        if (c.warp == 0) tm_dealloc(s.tmem_slot, kTmCols);
+        if (threadIdx.x < 32) tm_dealloc(cta.grp[0].tmem_slot, 512);
     }
 }
 
@@ -1199,7 +1258,7 @@ __global__ void __launch_bounds__(kThreads) pivot_kernel(TileParams p, PivotHead
 // Resident CTAs per SM for each mode, and SMs, per device (set up on the first
 // launch on a device).
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_resident[kFit + 1][kMaxDevices];  // indexed by Mode
+std::atomic<int> g_ready[kFit + 1][kMaxDevices];  // kernel attributes set, indexed by Mode
 std::atomic<int> g_sms[kMaxDevices];
 
 // SMs the kernels of `stream` run on: its green context's SM partition (a
@@ -1232,45 +1291,23 @@ int stream_sms(cudaStream_t stream, int device_sms) {
 
 template <int MODE>
 cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream) {
-    const int smem = MODE == kReadout || MODE == kDecode ? int(offsetof(FastSmem, plane)) : int(sizeof(FastSmem));
+    constexpr int smem = int(sizeof(FastCta));
     int device = 0;
     cudaError_t err = cudaGetDevice(&device);
     if (err != cudaSuccess) return err;
-    std::atomic<int> *resident = device < kMaxDevices ? &g_resident[MODE][device] : nullptr;
-    int per_sm = resident ? resident->load(std::memory_order_relaxed) : 0;
+    std::atomic<int> *ready = device < kMaxDevices ? &g_ready[MODE][device] : nullptr;
     int sms = device < kMaxDevices ? g_sms[device].load(std::memory_order_relaxed) : 0;
-    if (per_sm == 0 || sms == 0) {
+    if (!ready || !ready->load(std::memory_order_relaxed) || sms == 0) {
         err = cudaFuncSetAttribute(fast_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (err != cudaSuccess) return err;
         if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return err;
-        if (tm_mode<MODE>()) {
-            // The occupancy query reports one CTA per SM for a kernel that
-            // allocates tensor memory; resident CTAs are bounded here by
-            // registers, shared memory, threads and the 512 columns.
-            cudaFuncAttributes fa;
-            int regs_sm = 0, smem_sm = 0, threads_sm = 0, reserved = 0;
-            if ((err = cudaFuncGetAttributes(&fa, fast_kernel<MODE>)) != cudaSuccess) return err;
-            if ((err = cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, device)) != cudaSuccess ||
-                (err = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device)) != cudaSuccess ||
-                (err = cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, device)) != cudaSuccess ||
-                (err = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, device)) != cudaSuccess)
-                return err;
-            const int regs_cta = ((fa.numRegs * 32 + 255) / 256 * 256) * (kThreads / 32);
-            per_sm = std::min({regs_sm / std::max(1, regs_cta), smem_sm / (smem + int(fa.sharedSizeBytes) + reserved),
-                               threads_sm / kThreads, int(512 / kTmCols)});
-        } else if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fast_kernel<MODE>, kThreads, smem)) !=
-                   cudaSuccess) {
-            return err;
-        }
-        per_sm = std::max(1, per_sm);
-        if (resident) resident->store(per_sm, std::memory_order_relaxed);
+        if (ready) ready->store(1, std::memory_order_relaxed);
         if (device < kMaxDevices) g_sms[device].store(sms, std::memory_order_relaxed);
     }
-    // Every resident slot gets a CTA; CTA b takes items b, b + grid, ... so each
-    // SM's share of the items differs from the mean by less than one per CTA
-    // (the kernels are issue-bound per SM; fewer, evenly loaded CTAs were measured slower).
-    const int grid = std::max(1, std::min(items, per_sm * stream_sms(stream, sms)));
-    fast_kernel<MODE><<<grid, kThreads, smem, stream>>>(p, items);
+    // One CTA per SM of the stream (its green context's SMs, if it has one),
+    // each with a contiguous share of the items.
+    const int grid = std::max(1, std::min(items, stream_sms(stream, sms)));
+    fast_kernel<MODE><<<grid, kGroups * kThreads, smem, stream>>>(p, items);
     return cudaGetLastError();
 }
 
