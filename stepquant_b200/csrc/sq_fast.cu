@@ -1,7 +1,7 @@
 // Register-resident decode kernels for GDN heads with K = V = 128 and a code
 // width of 4, 6 or 8 bits (the served shape of Qwen-Next-style layers).
 //
-// One persistent CTA per SM made of four 256-thread item groups; a group
+// One persistent CTA per SM made of 256-thread item groups; a group
 // works one (request, value head) item at a time and takes the next of its
 // SM's items from a shared counter, so the groups of an SM finish together.
 // The next item's page bytes and inputs are prefetched (cp.async) while the
@@ -9,7 +9,7 @@
 // and lane l owns value columns l, l+32, l+64, l+96, so each thread owns 64
 // state elements for the whole step; the step, writeback and encode keep them
 // in the thread's tensor-memory lane between phases and bring 16 at a time
-// into registers (64 registers a thread).  That mapping makes both ordered
+// into registers.  That mapping makes both ordered
 // sums of fit_state local:
 //  * torch sums a row of 128 values as 8 lanes (column % 8), each lane a 4-way
 //    interleaved chain over vectors; the chain of lane (column % 8) over the
@@ -94,16 +94,19 @@ struct FastSmem {
     __device__ FastStage &stage(int b) { return b ? tail.st1 : st0; }
 };
 
-// A CTA is one SM's worth of item groups: kGroups groups of 256 threads, each
+// A CTA is one SM's worth of item groups: G groups of 256 threads, each
 // working one (request, head) item at a time with its own shared memory and
 // named barrier, taking the SM's items one by one from a shared counter.
-constexpr int kGroups = 4;
+// Four groups at 64 registers a thread for the readout and decode; three at
+// 80 for the modes that requantize (their quantizer keeps 16 state values,
+// the column constants and the sums live at once).
+template <int G>
 struct FastCta {
-    FastSmem grp[kGroups];
+    FastSmem grp[G];
     int next;  // the SM's next untaken item
 };
 
-// Barriers of one item group (ids 1..kGroups; 0 is the CTA's __syncthreads).
+// Barriers of one item group (ids 1..G; 0 is the CTA's __syncthreads).
 __device__ __forceinline__ void group_sync(int bar) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(bar), "n"(kThreads) : "memory");
 }
@@ -126,6 +129,8 @@ __device__ __forceinline__ bool group_or(int bar, bool pred) {
 // registers at a time; the four groups of a CTA take the SM's 512 columns.
 template <int MODE>
 __host__ __device__ constexpr bool tm_mode() { return MODE == kStep || MODE == kWriteback || MODE == kEncode; }
+template <int MODE>
+__host__ __device__ constexpr int groups_of() { return tm_mode<MODE>() ? 3 : 4; }
 
 // Bits of the code of value-lane u in row k of value tile t, read from the
 // staged page, ORed into the float 2^23: with the lane's conversion constants
@@ -1014,7 +1019,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 
 // Persistent kernel, one CTA per SM: CTA b owns the contiguous item range
 // [b * items / grid, (b + 1) * items / grid) (item = request * H + head) and
-// its kGroups item groups take the range's items one at a time from a shared
+// its item groups take the range's items one at a time from a shared
 // counter, so a group that runs ahead takes more items and the groups of an SM
 // finish together.  Each group keeps the next item's data in flight while it
 // computes the current one, and the slot of the item after that in a small
@@ -1022,11 +1027,12 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 // readout and decode keep two stage buffers and issue the next item's copies
 // first; the step, writeback and encode keep one (the other's space holds their
 // row partials and code bytes) and refill it once the item's staged data is
-// consumed, before the quantizer's column passes.  64 registers a thread.
+// consumed, before the quantizer's column passes.
 template <int MODE>
-__global__ void __launch_bounds__(kGroups * kThreads, 1) fast_kernel(TileParams p, int items) {
+__global__ void __launch_bounds__(groups_of<MODE>() * kThreads, 1) fast_kernel(TileParams p, int items) {
+    constexpr int kGroups = groups_of<MODE>();
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    FastCta &cta = *reinterpret_cast<FastCta *>(smem_raw);
+    FastCta<kGroups> &cta = *reinterpret_cast<FastCta<kGroups> *>(smem_raw);
     const int group = threadIdx.x / kThreads;
     FastSmem &s = cta.grp[group];
     const sq_plan &P = p.plan;
@@ -1291,7 +1297,8 @@ int stream_sms(cudaStream_t stream, int device_sms) {
 
 template <int MODE>
 cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream) {
-    constexpr int smem = int(sizeof(FastCta));
+    constexpr int kGroups = groups_of<MODE>();
+    constexpr int smem = int(sizeof(FastCta<kGroups>));
     int device = 0;
     cudaError_t err = cudaGetDevice(&device);
     if (err != cudaSuccess) return err;
