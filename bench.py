@@ -77,6 +77,8 @@ def parse_args():
     p.add_argument("--dim", type=int, default=128)
     p.add_argument("--pivot-heads", type=int, default=1,
                    help="GDN heads stored as fp16 pivots (1% of 32 heads rounds to 0; at least one exercises the fp16 path)")
+    p.add_argument("--two-bit-heads", type=int, default=0,
+                   help="GDN heads stored at 2 bits with value-group row scales (a stepquant4-style plan; 0 in config 1)")
     p.add_argument("--slot-groups", type=int, default=4)
     p.add_argument("--warm-steps", type=int, default=256)
     p.add_argument("--seed", type=int, default=1)
@@ -327,8 +329,8 @@ def reference_gpu_arm(args):
     inputs = [S.draw_inputs(batch, heads, qk, dim, dim, False, gen, device) for _ in range(2)]
     state = torch.randn(batch * groups_n, heads, dim, dim, generator=gen, device=device) * 0.1
 
-    def make(kind):
-        stream = torch.cuda.Stream(device)
+    def make(kind, asynchronous=True):
+        stream = torch.cuda.Stream(device) if asynchronous else None
         if kind == "reference":
             return RefPool(RefPlan("gdn", bits.to(device), impact.to(device)), slots_total, dim,
                            writeback_stream=stream)
@@ -365,8 +367,18 @@ def reference_gpu_arm(args):
         torch.cuda.synchronize()
         if clocks:
             clocks.stop()
+        # Device time per step by kernel (torch profiler over one replay of each graph).
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for graph in graphs:
+                graph.replay()
+            torch.cuda.synchronize()
+        kernels = {}
+        for ev in prof.key_averages():
+            if ev.device_type == torch.autograd.DeviceType.CUDA:
+                kernels[ev.key[:60]] = kernels.get(ev.key[:60], 0.0) + ev.device_time_total / period
         del graphs
-        return start.elapsed_time(end) / args.steps
+        return start.elapsed_time(end) / args.steps, {k: round(v, 1) for k, v in sorted(kernels.items(), key=lambda kv: -kv[1])}
 
     ours, theirs = make("this"), make("reference")
     for pool in (ours, theirs):
@@ -384,11 +396,22 @@ def reference_gpu_arm(args):
     # The parity step advanced group 0 in both pools alike; the timed runs continue from there.
     clocks = ClockSampler(0)
     try:
-        ref_ms = timed(theirs, clocks)
+        ref_ms, ref_kernels = timed(theirs, clocks)
     except Exception as exc:
         emit(dict(base, unavailable="reference step failed: %s: %s" % (type(exc).__name__, exc)))
         return
-    our_ms = timed(ours)
+    our_ms, our_kernels = timed(ours)
+    page_bytes, page_bytes_ours = theirs.page_bytes, ours.page_bytes
+    del ours, theirs
+    # The same comparison without a writeback stream (the fused / synchronous step of each).
+    sync = {}
+    for kind in ("reference", "this"):
+        pool = make(kind, asynchronous=False)
+        pool.encode(torch.randn(batch * groups_n, heads, dim, dim, generator=gen, device=device) * 0.1,
+                    torch.arange(1, slots_total, device=device))
+        ms, kernels = timed(pool)
+        sync[kind] = {"ms_per_step": ms, "kernel_us_per_step": kernels}
+        del pool
     updates = batch * heads
     import triton
     line = dict(base, value=updates / (ref_ms / 1e3), n_gpus=1, steps=args.steps, warmup=args.warmup,
@@ -401,13 +424,19 @@ def reference_gpu_arm(args):
                         "writeback": "async (reference default chunk 64)",
                         "timing": "step(); wait() in one CUDA graph per step, CUDA events",
                         "l2": "slots rotate over %d groups (%.0f MB of pages)"
-                              % (groups_n, slots_total * theirs.page_bytes / 1e6)},
+                              % (groups_n, slots_total * page_bytes / 1e6)},
                 triton=triton.__version__, clocks=clocks.summary(),
+                kernel_us_per_step=ref_kernels,
                 this_build={"value": updates / (our_ms / 1e3), "ms_per_step": our_ms,
-                            "speedup_over_reference": ref_ms / our_ms},
+                            "speedup_over_reference": ref_ms / our_ms, "kernel_us_per_step": our_kernels},
+                synchronous={"reference_ms_per_step": sync["reference"]["ms_per_step"],
+                             "this_build_ms_per_step": sync["this"]["ms_per_step"],
+                             "speedup_over_reference": sync["reference"]["ms_per_step"] / sync["this"]["ms_per_step"],
+                             "reference_kernel_us_per_step": sync["reference"]["kernel_us_per_step"],
+                             "this_build_kernel_us_per_step": sync["this"]["kernel_us_per_step"]},
                 parity={"page_bytes_equal_after_encode": enc_equal, "page_bytes_equal_after_step": step_equal,
-                        "out_max_abs_diff": out_diff, "page_bytes": theirs.page_bytes,
-                        "page_bytes_this_build": ours.page_bytes})
+                        "out_max_abs_diff": out_diff, "page_bytes": page_bytes,
+                        "page_bytes_this_build": page_bytes_ours})
     emit(line)
 
 
@@ -500,7 +529,7 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
     if kda:
         bits = S.kda_widths(heads_total, dim, cpu_gen, choices=tuple(kda_widths))[rank * heads_l:(rank + 1) * heads_l]
     else:
-        widths = S.gdn_widths(heads_total, cpu_gen, args.pivot_heads)[rank * heads_l:(rank + 1) * heads_l]
+        widths = S.gdn_widths(heads_total, cpu_gen, args.pivot_heads, args.two_bit_heads)[rank * heads_l:(rank + 1) * heads_l]
         bits = widths[:, None].expand(heads_l, dim).clone()
     a_log, dt_bias = S.gate_parameters(heads_l, dim, kda, gen, device)
     requests = batch * slot_groups
@@ -590,6 +619,7 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
     pool.check_status()
     res["page_bytes"] = pool.page_bytes
     res["pivot_heads_local"] = 0 if kda else int((bits[:, 0] == 16).sum())
+    res["two_bit_heads_local"] = 0 if kda else int((bits[:, 0] == 2).sum())
     res["algorithmic"] = algorithmic_bytes(pool.page_bytes, heads_l, qk_l, batch, dim, kda)
 
     if e2e:
@@ -1104,14 +1134,16 @@ def main():
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms else None
         # DRAM read + write bytes of one launch at this workload, from an ncu capture made
         # outside the bench (ncu cannot run inside a timed region); None for other shapes.
-        ncu_traffic = {"sq_step (fused)": 153.8e6, "sq_writeback": 156.6e6, "sq_readout": 114.1e6}
-        default_shape = (not kda, batch, heads, qk_heads, args.dim, world, args.pivot_heads) == (True, 256, 32, 16, 128, 1, 1)
+        ncu_traffic = {"sq_step (fused)": 153.8e6, "sq_writeback": 159.9e6, "sq_readout": 113.5e6}
+        default_shape = (not kda, batch, heads, qk_heads, args.dim, world, args.pivot_heads, args.two_bit_heads) == \
+            (True, 256, 32, 16, 128, 1, 1, 0)
         name = ("kda-decode-b%d-h%d-k128 (config 2)" if kda else "gdn-decode-b%d-h%d-k128 (config 1)") % (batch, heads)
         kw_desc = "{%s}" % args.kda_widths
         plan_desc = (("stepquant4 reference-legal twin: " if args.kda_widths == "2,4,6" else
                       "config 2's plan (3/5-bit width extension): ") + "row widths %s at 30/50/20, 2%% fp16 pivot rows"
                      % kw_desc if kda else
-                     "stepquant6 synthetic, widths {4,6,8} 25/50/25, pivot heads %d" % args.pivot_heads)
+                     "stepquant6 synthetic, widths {4,6,8} 25/50/25, pivot heads %d" % args.pivot_heads +
+                     (", 2-bit heads %d" % args.two_bit_heads if args.two_bit_heads else ""))
         line.update({
             "value": units / (elapsed_ms / 1e3), "ms_per_step": elapsed_ms / args.steps,
             "config": {"workload": name, "batch": batch, "heads": heads, "qk_heads": qk_heads, "dim": args.dim,
@@ -1129,8 +1161,9 @@ def main():
                          "algorithmic_bytes_per_launch": dom_bytes},
             "e2e": {"value": units / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"]},
-            # readout (or fused step), writeback, and the pivot-head kernel when this rank has pivot heads
-            "gpu_launches": args.steps * ((2 if args.mode == "async" else 1) + (1 if res["pivot_heads_local"] else 0)),
+            # readout (or fused step), writeback; the pivot-head readout; the 2-bit heads' readout and writeback
+            "gpu_launches": args.steps * ((2 if args.mode == "async" else 1) + (1 if res["pivot_heads_local"] else 0) +
+                                          ((2 if args.mode == "async" else 1) if res["two_bit_heads_local"] else 0)),
         })
     line["clocks"] = clocks.summary()
 

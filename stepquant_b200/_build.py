@@ -16,7 +16,7 @@ LIBDIR = os.path.join(PACKAGE, "_lib")
 LIBRARY = os.path.join(LIBDIR, "libstepquant_b200.so")
 HEADER = os.path.join(ROOT, "include", "stepquant_b200.h")
 SOURCES = ["sq_abi.cu", "sq_tile.cu", "sq_fast.cu", "sq_pack.cu", "sq_fp32.cu", "sq_noalloc.cu", "sq_prefill.cu",
-           "sq_fast_kda.cu", "sq_streams.cu"]
+           "sq_fast_kda.cu", "sq_streams.cu", "sq_fast_two.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -101,18 +101,21 @@ int32_t run(int mode, sq::TileParams t, int32_t batch, cudaStream_t stream) {
     } else if ((fast_mode || gdn_codec) && sq::fast_eligible(t.plan, t.pages)) {
         if (cudaError_t e = sq::launch_fast(mode, t, batch, stream)) return cuda_status(e);
         sq::PivotHeads ph;
-        const bool pivots = sq::pivot_heads(t.plan, &ph);  // pivot heads run in launch_fast
+        sq::TwoHeads th;
+        const bool pivots = sq::pivot_heads(t.plan, &ph);  // pivot and 2-bit heads run in launch_fast
+        const bool twos = sq::two_heads(t.plan, &th);
         bool rest = true;
         if (t.plan.bits_host) {
             rest = false;
             for (int h = 0; h < t.plan.heads; ++h) {
                 const int width = t.plan.bits_host[h * t.plan.keys];
-                rest = rest || !(sq::fast_head(t.plan, width) || (pivots && width == 16));
+                rest = rest || !(sq::fast_head(t.plan, width) || (pivots && width == 16) || (twos && width == 2));
             }
         }
         if (!rest) return SQ_OK;
         t.skip_fast = 1;
         t.skip_pivot = pivots ? 1 : 0;
+        t.skip_two = twos ? 1 : 0;
     }
     return cuda_status(sq::launch_tile(mode, t, items, stream));
 }

@@ -1357,7 +1357,11 @@ cudaError_t launch_fast(int mode, const TileParams &params, int batch, cudaStrea
         case kDecode: err = launch_fast_mode<kDecode>(p, items, stream); break;
         default: return cudaErrorNotSupported;
     }
-    if (err != cudaSuccess || mode == kWriteback) return err;
+    if (err != cudaSuccess) return err;
+    TwoHeads th;
+    if (two_heads(p.plan, &th) && th.count > 0 && (err = launch_two(mode, p, th, batch, stream)) != cudaSuccess)
+        return err;
+    if (mode == kWriteback) return cudaSuccess;
     PivotHeads ph;
     if (!pivot_heads(p.plan, &ph) || ph.count == 0) return cudaSuccess;
     const int grid = batch * ph.count;

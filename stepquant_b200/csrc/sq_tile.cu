@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(kThreads) tile_kernel(TileParams p) {
     if (MODE == kReadout && head == 0 && tid == 0) p.stable_slots[req] = slot;
     if (p.skip_fast && fast_head_dev(P, head)) return;
     if (p.skip_pivot && P.bits[head * P.keys] == 16) return;
+    if (p.skip_two && P.bits[head * P.keys] == 2) return;
     bool active = slot > 0;
     if (active && MODE != kFit && slot >= p.num_slots) {
         if (head == 0 && tid == 0) flag(p.status, SQ_STATUS_SLOT_RANGE);

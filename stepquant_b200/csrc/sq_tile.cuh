@@ -28,6 +28,7 @@ struct TileParams {
     int32_t *status;
     int skip_fast;  // tile kernel: leave heads that fast_head() accepts to the fast kernel
     int skip_pivot;  // tile kernel: leave GDN fp16 pivot heads to the pivot kernel
+    int skip_two;    // tile kernel: leave GDN 2-bit heads to the 2-bit kernel
     int stage_inputs;  // fast kernels: q/k/v (or writeback scratch) rows are 16-byte aligned -> cp.async staging
     int stage_gates;   // fast kernels: fp32 gates -> cp.async staging
 };
@@ -40,9 +41,10 @@ cudaError_t launch_tile(int mode, const TileParams &p, int items, cudaStream_t s
 // fast_eligible(): the plan's shape and the page alignment allow them;
 // fast_head(): a head of that width is handled by them.  launch_fast also
 // runs the fp16 pivot heads that pivot_heads() lists (a second kernel; none
-// in the writeback, whose pivot values the readout already wrote).  The tile
-// kernel handles the other heads (GDN 2-bit heads; pivot heads when the plan
-// has no host copy of its bits or more than kMaxPivotHeads of them).
+// in the writeback, whose pivot values the readout already wrote) and the
+// 2-bit heads that two_heads() lists.  The tile kernel handles the other heads
+// (pivot or 2-bit heads when the plan has no host copy of its bits or more than
+// 32 of them; 2-bit heads with value groups other than 32).
 bool fast_eligible(const sq_plan &plan, const void *pages);
 __host__ __device__ inline bool fast_head(const sq_plan &plan, int width) {
     return plan.architecture == SQ_GDN && plan.keys == 128 && plan.values == 128 &&
@@ -55,6 +57,18 @@ struct PivotHeads {
 };
 bool pivot_heads(const sq_plan &plan, PivotHeads *out);
 cudaError_t launch_fast(int mode, const TileParams &p, int batch, cudaStream_t stream);
+
+// GDN 2-bit heads (value groups of 32, K = V = 128) on their own kernel
+// (sq_fast_two.cu), one CTA per (request, head), every mode; launch_fast runs
+// it for the heads that two_heads() lists (none without a host copy of the
+// bits or with more than kMaxTwoHeads of them: the tile kernel takes them).
+constexpr int kMaxTwoHeads = 32;
+struct TwoHeads {
+    int count;
+    int ids[kMaxTwoHeads];
+};
+bool two_heads(const sq_plan &plan, TwoHeads *out);
+cudaError_t launch_two(int mode, const TileParams &p, const TwoHeads &th, int batch, cudaStream_t stream);
 
 // Register-resident kernels for KDA heads with K = V = 128 (sq_fast_kda.cu):
 // a head qualifies when it has integer rows and its code region (stride x

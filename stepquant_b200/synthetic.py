@@ -62,14 +62,17 @@ def prepared(inputs, heads, keys, kda, a_log, dt_bias):
 
 
 
-def gdn_widths(heads, generator, pivot_heads=0):
-    """Per-head widths {4, 6, 8} at 25/50/25, permuted; the first ``pivot_heads`` of the permutation become fp16."""
+def gdn_widths(heads, generator, pivot_heads=0, two_bit_heads=0):
+    """Per-head widths {4, 6, 8} at 25/50/25, permuted; the first ``pivot_heads`` of the permutation become fp16,
+    the next ``two_bit_heads`` 2-bit (value groups of 32)."""
     counts = [heads // 4, heads - 2 * (heads // 4), heads // 4]
     widths = [4] * counts[0] + [6] * counts[1] + [8] * counts[2]
     perm = torch.randperm(heads, generator=generator).tolist()
     widths = [widths[i] for i in perm]
     for i in range(pivot_heads):
         widths[i] = 16
+    for i in range(pivot_heads, pivot_heads + two_bit_heads):
+        widths[i] = 2
     return torch.tensor(widths)
 
 
