@@ -318,7 +318,7 @@ def reference_gpu_arm(args):
     qk = args.qk_heads or heads // 2
     groups_n = args.slot_groups
     cpu_gen = torch.Generator().manual_seed(args.seed)
-    widths = S.gdn_widths(heads, cpu_gen, args.pivot_heads)
+    widths = S.gdn_widths(heads, cpu_gen, args.pivot_heads, args.two_bit_heads)
     bits = widths[:, None].expand(heads, dim).contiguous()
     impact = torch.rand(heads, dim, generator=cpu_gen) + 0.5
     gen = torch.Generator(device=device).manual_seed(args.seed)
@@ -419,8 +419,8 @@ def reference_gpu_arm(args):
                 data="synthetic",
                 config={"workload": "gdn-decode-b%d-h%d-k128 (config 1), reference Triton/Gluon PackedStatePool"
                                     % (batch, heads), "batch": batch, "heads": heads, "qk_heads": qk, "dim": dim,
-                        "plan": "widths {4,6,8} 25/50/25, pivot heads %d, impact uniform [0.5, 1.5)"
-                                % args.pivot_heads,
+                        "plan": "widths {4,6,8} 25/50/25, pivot heads %d, 2-bit heads %d, impact uniform [0.5, 1.5)"
+                                % (args.pivot_heads, args.two_bit_heads),
                         "writeback": "async (reference default chunk 64)",
                         "timing": "step(); wait() in one CUDA graph per step, CUDA events",
                         "l2": "slots rotate over %d groups (%.0f MB of pages)"

@@ -38,6 +38,7 @@ struct TwoSmem {
     float red[2][8][TV];        // per-warp column partials
     float colc[4][TV];          // [0] delta, [1] c, [2] 1/c, [3] c_old * decay (c_old in decode)
     float misc[64];
+    float gsum[TK][4];          // the rows' group |x| sums (P2)
     unsigned char plane[8][TK * 16 + 16];  // final codes (0..3), value tile t, row k, position u
     uint32_t tmem_slot;
 };
@@ -93,59 +94,94 @@ struct TwoCtx {
     uint32_t tm;
 };
 
-// P2 finish for row k: the four group scales from the group sums, into rowa
-// (scales) and rowb (reciprocals) by lanes 0, 8, 16, 24.  Returns true for a
-// huge or NaN group sum at this lane.
-__device__ __forceinline__ bool two_row_scales(TwoSmem &s, int k, const float (&x)[4], int lane, float w) {
-    const float total = group_abs_sum(x, lane);
+// P2 finish of a warp's 16 rows: the 64 group scales from the group sums in
+// s.gsum, two per lane (row 16 w + lane / 2, groups 2 (lane % 2) and the next),
+// into rowa (scales) and rowb (reciprocals).  Returns true for a huge or NaN
+// group sum among the lane's two.
+__device__ __forceinline__ bool two_row_scales(TwoSmem &s, int warp, int lane) {
+    const int k = warp * 16 + (lane >> 1), m0 = 2 * (lane & 1);
+    const float w = s.w2[k];
     bool huge = false;
-    if ((lane & 7) == 0) {
-        const int m = lane >> 3;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const float total = s.gsum[k][m0 + j];
         const float mean = __fmul_rn(total, 1.f / float(kGroup));  // a power of two: the rounding of total / 32
         const float rr = fp16_scale(__fsqrt_rn(__fdiv_rn(fmaxf(mean, 1e-20f), w)));
-        reinterpret_cast<float *>(&s.rowa[k])[m] = rr;
-        reinterpret_cast<float *>(&s.rowb[k])[m] = __frcp_rn(rr);
-        huge = !(total <= 7.922816251426434e28f);  // 2^96, or NaN
+        reinterpret_cast<float *>(&s.rowa[k])[m0 + j] = rr;
+        reinterpret_cast<float *>(&s.rowb[k])[m0 + j] = __frcp_rn(rr);
+        huge = huge || !(total <= 7.922816251426434e28f);  // 2^96, or NaN
     }
     return huge;
 }
 
+// P3 partial: the warp's column maxima of |x / r| -> s.red[0].  EXACT divides
+// (corrected reciprocal, or IEEE on the SLOW path); otherwise the product
+// x * RN(1/r), within one float step of the quotient, bounds the maximum.
+template <bool SLOW, bool EXACT>
+__device__ __forceinline__ void two_column_max(TwoSmem &s, const TwoCtx &c) {
+    const int warp = c.warp, lane = c.lane;
+    float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        float2 X[4][2];
+        tm_ld16(c.tm + 16 * g, X);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int k = warp * 16 + 4 * g + i;
+            const float4 a = s.rowa[k], b = s.rowb[k];
+            const float2 s01 = EXACT ? divide2<SLOW>(X[i][0], lo2(a), lo2(b), make_float2(-a.x, -a.y)) : pmul2(X[i][0], lo2(b));
+            const float2 s23 = EXACT ? divide2<SLOW>(X[i][1], hi2(a), hi2(b), make_float2(-a.z, -a.w)) : pmul2(X[i][1], hi2(b));
+            m0 = fmaxf(m0, fabsf(s01.x));
+            m1 = fmaxf(m1, fabsf(s01.y));
+            m2 = fmaxf(m2, fabsf(s23.x));
+            m3 = fmaxf(m3, fabsf(s23.y));
+        }
+    }
+    s.red[0][warp][lane] = m0;
+    s.red[0][warp][lane + 32] = m1;
+    s.red[0][warp][lane + 64] = m2;
+    s.red[0][warp][lane + 96] = m3;
+}
+
 // P3-P5 on the thread's values (x on entry in tensor memory; x / r on exit).
+// c0 = fp16(RN(M / 3)) needs M only up to its fp16 rounding: the maximum M' of
+// the products lies within one float step of M (two are allowed for), and
+// when fp16(RN(. / 3)) is the same at both ends of that interval it is c0;
+// otherwise the tile redoes the maxima with exact divisions.
 template <bool SLOW>
 __device__ __forceinline__ void two_quantize(TwoSmem &s, const TwoCtx &c) {
     const int warp = c.warp, lane = c.lane, tid = c.tid;
-    // P3: column max of |x / r|.
-    {
-        float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
-#pragma unroll 1
-        for (int g = 0; g < 4; ++g) {
-            float2 X[4][2];
-            tm_ld16(c.tm + 16 * g, X);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int k = warp * 16 + 4 * g + i;
-                const float4 a = s.rowa[k], b = s.rowb[k];
-                const float2 s01 = divide2<SLOW>(X[i][0], lo2(a), lo2(b), make_float2(-a.x, -a.y));
-                const float2 s23 = divide2<SLOW>(X[i][1], hi2(a), hi2(b), make_float2(-a.z, -a.w));
-                m0 = fmaxf(m0, fabsf(s01.x));
-                m1 = fmaxf(m1, fabsf(s01.y));
-                m2 = fmaxf(m2, fabsf(s23.x));
-                m3 = fmaxf(m3, fabsf(s23.y));
-            }
-        }
-        s.red[0][warp][lane] = m0;
-        s.red[0][warp][lane + 32] = m1;
-        s.red[0][warp][lane + 64] = m2;
-        s.red[0][warp][lane + 96] = m3;
-    }
+    two_column_max<SLOW, SLOW>(s, c);
     __syncthreads();
+    int settled = 1;
     if (tid < TV) {
-        float mx = 0.f;
+        float m = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
-        const float c0 = fp16_scale(SLOW ? __fdiv_rn(mx, 3.f) : div_fp16(mx, 3.f, __frcp_rn(3.f)));
+        for (int w = 0; w < 8; ++w) m = fmaxf(m, s.red[0][w][tid]);
+        const float r3 = __frcp_rn(3.f);
+        float c0;
+        if (SLOW) {
+            c0 = fp16_scale(__fdiv_rn(m, 3.f));
+        } else {
+            const uint32_t bits = __float_as_uint(m);
+            const float lo = bits > 2u ? __uint_as_float(bits - 2u) : 0.f;
+            c0 = fp16_scale(div_fp16(__uint_as_float(bits + 2u), 3.f, r3));
+            settled = fp16_scale(div_fp16(lo, 3.f, r3)) == c0;
+        }
         s.colc[1][tid] = c0;
         s.colc[2][tid] = __frcp_rn(c0);
+    }
+    if (!SLOW && !__syncthreads_and(settled)) {
+        two_column_max<false, true>(s, c);
+        __syncthreads();
+        if (tid < TV) {
+            float mx = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) mx = fmaxf(mx, s.red[0][w][tid]);
+            const float c0 = fp16_scale(div_fp16(mx, 3.f, __frcp_rn(3.f)));
+            s.colc[1][tid] = c0;
+            s.colc[2][tid] = __frcp_rn(c0);
+        }
     }
     __syncthreads();
     // P4: first levels and the weighted least-squares sums.
@@ -502,15 +538,16 @@ __global__ void __launch_bounds__(kThreads) two_kernel(TileParams p, TwoHeads th
                 }
             }
             tm_st16(c.tm + 16 * g, X);
-            __syncwarp();  // every lane of the warp is done with the rows' old constants
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const int k = warp * 16 + 4 * g + i;
-                huge = two_row_scales(s, k, nr[i], lane, s.w2[k]) || huge;
+                const float total = group_abs_sum(nr[i], lane);
+                if ((lane & 7) == 0) s.gsum[warp * 16 + 4 * g + i][lane >> 3] = total;
             }
         }
         tm_wait_st();
-        __syncwarp();
+        __syncwarp();  // the warp's group sums are in place and its lanes are done with the old row constants
+        huge = two_row_scales(s, warp, lane);
+        __syncwarp();  // ... and with the unsquared weights
         if (lane < 16) {
             const int k = warp * 16 + lane;
             const float w = s.w2[k];
