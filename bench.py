@@ -314,27 +314,35 @@ def reference_gpu_arm(args):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    batch, heads, dim = args.batch or 256, args.heads, args.dim
-    qk = args.qk_heads or heads // 2
-    groups_n = args.slot_groups
-    cpu_gen = torch.Generator().manual_seed(args.seed)
-    widths = S.gdn_widths(heads, cpu_gen, args.pivot_heads, args.two_bit_heads)
-    bits = widths[:, None].expand(heads, dim).contiguous()
+    kda = args.workload == "kda-decode"
+    arch = "kda" if kda else "gdn"
+    batch, heads, dim = args.batch or (512 if kda else 256), args.heads, args.dim
+    qk = args.qk_heads or (heads if kda else heads // 2)
+    groups_n = 2 if kda else args.slot_groups
+    cpu_gen = torch.Generator().manual_seed(2 if kda else args.seed)
+    if kda:  # config 2's reference-legal twin plan: row widths {2,4,6} at 30/50/20, 2 % fp16 pivot rows
+        bits = S.kda_widths(heads, dim, cpu_gen, choices=(2, 4, 6))
+        plan_desc = "row widths {2,4,6} 30/50/20, 2% fp16 pivot rows, impact uniform [0.5, 1.5)"
+    else:
+        widths = S.gdn_widths(heads, cpu_gen, args.pivot_heads, args.two_bit_heads)
+        bits = widths[:, None].expand(heads, dim).contiguous()
+        plan_desc = ("widths {4,6,8} 25/50/25, pivot heads %d, 2-bit heads %d, impact uniform [0.5, 1.5)"
+                     % (args.pivot_heads, args.two_bit_heads))
     impact = torch.rand(heads, dim, generator=cpu_gen) + 0.5
     gen = torch.Generator(device=device).manual_seed(args.seed)
-    a_log, dt_bias = S.gate_parameters(heads, dim, False, gen, device)
+    a_log, dt_bias = S.gate_parameters(heads, dim, kda, gen, device)
     kw = dict(normalize=True, scale=dim ** -0.5, a_log=a_log, dt_bias=dt_bias)
     slots_total = batch * groups_n + 1
     groups = [torch.arange(1 + g * batch, 1 + (g + 1) * batch, device=device) for g in range(groups_n)]
-    inputs = [S.draw_inputs(batch, heads, qk, dim, dim, False, gen, device) for _ in range(2)]
+    inputs = [S.draw_inputs(batch, heads, qk, dim, dim, kda, gen, device) for _ in range(2)]
     state = torch.randn(batch * groups_n, heads, dim, dim, generator=gen, device=device) * 0.1
 
     def make(kind, asynchronous=True):
         stream = torch.cuda.Stream(device) if asynchronous else None
         if kind == "reference":
-            return RefPool(RefPlan("gdn", bits.to(device), impact.to(device)), slots_total, dim,
+            return RefPool(RefPlan(arch, bits.to(device), impact.to(device)), slots_total, dim,
                            writeback_stream=stream)
-        return PackedStatePool(QuantizationPlan("gdn", bits.to(device), impact.to(device)), slots_total, dim,
+        return PackedStatePool(QuantizationPlan(arch, bits.to(device), impact.to(device)), slots_total, dim,
                                writeback_stream=stream)
 
     def run(pool, i):
@@ -417,10 +425,9 @@ def reference_gpu_arm(args):
     line = dict(base, value=updates / (ref_ms / 1e3), n_gpus=1, steps=args.steps, warmup=args.warmup,
                 ms_per_step=ref_ms, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="f32",
                 data="synthetic",
-                config={"workload": "gdn-decode-b%d-h%d-k128 (config 1), reference Triton/Gluon PackedStatePool"
-                                    % (batch, heads), "batch": batch, "heads": heads, "qk_heads": qk, "dim": dim,
-                        "plan": "widths {4,6,8} 25/50/25, pivot heads %d, 2-bit heads %d, impact uniform [0.5, 1.5)"
-                                % (args.pivot_heads, args.two_bit_heads),
+                config={"workload": "%s-decode-b%d-h%d-k128 (config %d), reference Triton/Gluon PackedStatePool"
+                                    % (arch, batch, heads, 2 if kda else 1), "batch": batch, "heads": heads,
+                        "qk_heads": qk, "dim": dim, "plan": plan_desc,
                         "writeback": "async (reference default chunk 64)",
                         "timing": "step(); wait() in one CUDA graph per step, CUDA events",
                         "l2": "slots rotate over %d groups (%.0f MB of pages)"
