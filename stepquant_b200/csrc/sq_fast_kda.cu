@@ -43,6 +43,7 @@ struct KdaSmem {
     float misc[64];
     int flags;
     int qmax_max;        // largest qmax of the head's integer rows
+    int rho_bits;        // max over columns of RN(M' / c1) (float bits; P5 clamps)
     uint32_t tmem_slot;  // tensor-memory base of the CTA's state columns
     // Last, so that the readout, which goes without it, launches without it.
     union alignas(16) {
@@ -216,8 +217,12 @@ __device__ __forceinline__ void kda_first_levels(const KdaSmem &s, int warp, int
 // (code = level + offset: the low byte of RN(y + 1.5 2^23) plus the offset);
 // pivot rows -> their fp16 values straight into the staged region (the
 // lane's value of tile lane / 4 + 8 j at `pivot_at` + 8 j stride + the row's offset).
+// CLAMP: rows whose qmax times `rho` (the largest RN(M'/c1) of the tile's
+// columns) can exceed qmax + 1/2 clamp their levels; the others cannot reach
+// the clamp (|y| <= qmax M / c1 for a row with that qmax).
 template <bool SLOW, bool CLAMP>
-__device__ __forceinline__ void kda_final_levels(KdaSmem &s, int warp, int lane, uint32_t tm, int pivot_at, int j8) {
+__device__ __forceinline__ void kda_final_levels(KdaSmem &s, int warp, int lane, uint32_t tm, int pivot_at, int j8,
+                                                 float rho) {
     const float2 c01 = make_float2(s.colc[1][lane], s.colc[1][lane + 32]);
     const float2 c23 = make_float2(s.colc[1][lane + 64], s.colc[1][lane + 96]);
     const float2 r01 = make_float2(s.colc[2][lane], s.colc[2][lane + 32]);
@@ -235,10 +240,11 @@ __device__ __forceinline__ void kda_final_levels(KdaSmem &s, int warp, int lane,
             if (d.w != 0.f) {
                 unsigned char *code = s.u.code + k * DV + lane;
                 const uint32_t off = uint32_t(d.z);
+                const bool clamp = CLAMP && (SLOW || !(__fmul_rn(rho, d.z) <= d.z + 0.49f));  // warp-uniform (row k)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     float2 y = pmul2(divide2<SLOW>(X[i][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), hi2(cc));
-                    if (CLAMP) y = clamp2(y, d.z);
+                    if (clamp) y = clamp2(y, d.z);
                     const float2 t = __fadd2_rn(y, round);  // low byte: the level (two's complement)
                     code[64 * h] = static_cast<unsigned char>(__float_as_uint(t.x) + off);
                     code[64 * h + 32] = static_cast<unsigned char>(__float_as_uint(t.y) + off);
@@ -292,6 +298,7 @@ __device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int
         }
     }
     int safe = 1;
+    if (tid == 0) s.rho_bits = 0;
     if (tid < DV) {
         const float c0 = fp16_scale(mx);
         s.colc[1][tid] = c0;
@@ -326,12 +333,15 @@ __device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int
         s.colc[1][tid] = c1;
         s.colc[2][tid] = __frcp_rn(c1);
         const float qm = float(s.qmax_max);
-        safe = (c1 >= 6.103515625e-05f) && (__fmul_rn(__fdiv_rn(mx, c1), qm) <= qm + 0.49f);
+        const float rho = c1 >= 6.103515625e-05f ? __fdiv_rn(mx, c1) : __int_as_float(0x7f800000);
+        atomicMax(&s.rho_bits, __float_as_int(rho));  // non-negative floats order as their bits (NaN above all)
+        safe = (c1 >= 6.103515625e-05f) && (__fmul_rn(rho, qm) <= qm + 0.49f);
     }
     const bool no_clamp5 = __syncthreads_and(safe);
     // P5: final levels (integer rows) or the fp16 values (pivot rows) -> plane.
-    if (!SLOW && no_clamp5) kda_final_levels<SLOW, false>(s, warp, lane, tm, pivot_at, j8);
-    else kda_final_levels<SLOW, true>(s, warp, lane, tm, pivot_at, j8);
+    const float rho = __int_as_float(s.rho_bits);
+    if (!SLOW && no_clamp5) kda_final_levels<SLOW, false>(s, warp, lane, tm, pivot_at, j8, rho);
+    else kda_final_levels<SLOW, true>(s, warp, lane, tm, pivot_at, j8, rho);
     __syncthreads();
 }
 
