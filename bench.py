@@ -696,8 +696,10 @@ def measure_decode(args, kda, batch, heads_total, qk_total, steps, warmup, world
 
 
 def measure_prefill(args, batch, tokens, heads_total, qk_total, steps, warmup, world, rank, device, barrier,
-                    e2e=True, clocks=None, seed=3):
-    """Chunked prefill of ``batch`` prompts of ``tokens`` tokens to their first packed states (config 3)."""
+                    e2e=True, clocks=None, seed=3, kda=False):
+    """Prefill of ``batch`` prompts of ``tokens`` tokens to their first packed
+    states: GDN chunked (config 3), or with ``kda`` the KDA recurrent pass
+    (per-key-channel decay) on a {2,4,6} KDA plan of the same shape."""
     import torch
     from torch.profiler import ProfilerActivity, profile
     from stepquant_b200 import synthetic as S
@@ -708,9 +710,13 @@ def measure_prefill(args, batch, tokens, heads_total, qk_total, steps, warmup, w
     heads_l, qk_l = heads_total // world, qk_total // world
     gen = torch.Generator(device=device).manual_seed(seed * 1000 + rank)
     cpu_gen = torch.Generator().manual_seed(seed)
-    widths = S.gdn_widths(heads_total, cpu_gen)[rank * heads_l:(rank + 1) * heads_l]
-    plan = QuantizationPlan("gdn", widths[:, None].expand(heads_l, dim).clone().to(device),
-                            (torch.rand(heads_l, dim, generator=cpu_gen) + 0.5).to(device))
+    if kda:
+        bits = S.kda_widths(heads_total, dim, cpu_gen, choices=(2, 4, 6))[rank * heads_l:(rank + 1) * heads_l]
+        plan = QuantizationPlan("kda", bits.to(device), (torch.rand(heads_l, dim, generator=cpu_gen) + 0.5).to(device))
+    else:
+        widths = S.gdn_widths(heads_total, cpu_gen)[rank * heads_l:(rank + 1) * heads_l]
+        plan = QuantizationPlan("gdn", widths[:, None].expand(heads_l, dim).clone().to(device),
+                                (torch.rand(heads_l, dim, generator=cpu_gen) + 0.5).to(device))
     pool = PackedStatePool(plan, batch + 1, dim)
     slots = torch.arange(1, batch + 1, device=device)
     total = batch * tokens
@@ -718,7 +724,9 @@ def measure_prefill(args, batch, tokens, heads_total, qk_total, steps, warmup, w
     k = torch.randn(1, total, qk_l, dim, device=device, generator=gen).bfloat16()
     v = torch.randn(1, total, heads_l, dim, device=device, generator=gen).bfloat16()
     a_log, _ = S.gate_parameters(heads_l, dim, False, gen, device)
-    g = -a_log.exp() * torch.nn.functional.softplus(torch.randn(1, total, heads_l, device=device, generator=gen))
+    g_shape = (1, total, heads_l, dim) if kda else (1, total, heads_l)
+    g = -(a_log.exp()[:, None] if kda else a_log.exp()) * torch.nn.functional.softplus(
+        torch.randn(*g_shape, device=device, generator=gen))
     beta = torch.randn(1, total, heads_l, device=device, generator=gen).sigmoid()
     cu = torch.arange(0, total + 1, tokens, device=device, dtype=torch.int32)
 
@@ -748,15 +756,20 @@ def measure_prefill(args, batch, tokens, heads_total, qk_total, steps, warmup, w
     kernels = {}
     for ev in prof.key_averages():
         name = ev.key
-        for short in ("prep_kernel", "state_kernel", "offsets_kernel", "tile_kernel", "fast_kernel"):
+        for short in ("prep_kernel", "state_kernel", "offsets_kernel", "kda_prefill_kernel", "tile_kernel",
+                      "fast_kernel", "kda_kernel"):
             if short in name:
                 kernels[short] = kernels.get(short, 0.0) + ev.device_time_total / 1e3
     res["kernel_ms"] = kernels
     chunk_heads = batch * ((tokens + 63) // 64) * heads_l
     c, kk, vv = 64, dim, dim
-    res["flops"] = chunk_heads * 2 * (3 * c * c * kk + 2 * c * kk * vv + c * kk * vv + c * c * vv)
+    if kda:  # per token and head: the decay product, two column sums and the rank-1 update (7 K V flops)
+        res["flops"] = total * heads_l * 7 * kk * vv
+    else:
+        res["flops"] = chunk_heads * 2 * (3 * c * c * kk + 2 * c * kk * vv + c * kk * vv + c * c * vv)
     # Bytes the path must move: bf16 q, k, v in, fp32 g and beta in, bf16 outputs, the packed first states.
-    res["bytes"] = total * ((2 * qk_l * dim + 2 * heads_l * dim) * 2 + 2 * heads_l * 4) + batch * pool.page_bytes
+    g_bytes = heads_l * (dim if kda else 1) * 4
+    res["bytes"] = total * ((2 * qk_l * dim + 2 * heads_l * dim) * 2 + g_bytes + heads_l * 4) + batch * pool.page_bytes
 
     if e2e:
         pin = [x.cpu().pin_memory() for x in (q, k, v, g, beta)]
@@ -1168,8 +1181,8 @@ def main():
                          "algorithmic_bytes_per_launch": dom_bytes},
             "e2e": {"value": units / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"]},
-            # readout (or fused step), writeback; the pivot-head readout; the 2-bit heads' readout and writeback
-            "gpu_launches": args.steps * ((2 if args.mode == "async" else 1) + (1 if res["pivot_heads_local"] else 0) +
+            # readout (or fused step; pivot heads are its items) and writeback; the 2-bit heads' readout and writeback
+            "gpu_launches": args.steps * ((2 if args.mode == "async" else 1) +
                                           ((2 if args.mode == "async" else 1) if res["two_bit_heads_local"] else 0)),
         })
     line["clocks"] = clocks.summary()
@@ -1205,6 +1218,20 @@ def main():
             "tensor_tflops": flops3 / world / (pk / 1e3) / 1e12 if pk else None,
             "tensor_frac": (flops3 / world / (pk / 1e3) / 1e12 / peak_tf) if pk else None,
             "peak_source": peak_tf_kind}
+        r5 = measure_prefill(args, 32, 2048, 32, 32, 3, 1, world, rank, device, barrier, e2e=False, kda=True)
+        (ms5,) = max_over_ranks(r5["elapsed_ms"])
+        (flops5,) = sum_over_ranks(r5["flops"])
+        pk5 = sum(r5["kernel_ms"].values())
+        # fp32 FMA pipe, nominal: 148 SMs x 128 lanes x 2 flops x 1.965 GHz
+        fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        kp5 = r5["kernel_ms"].get("kda_prefill_kernel", 0.0)
+        sec["kda-prefill-b32-t2048-h32-k128"] = {
+            "value": 32 * 2048 * 3 / (ms5 / 1e3), "unit": "tokens/s", "ms_per_step": ms5 / 3,
+            "kernel_ms": r5["kernel_ms"], "steps": 3,
+            "fp32_tflops": flops5 / world / (kp5 / 1e3) / 1e12 if kp5 else None,
+            "fp32_frac_of_nominal": flops5 / world / (kp5 / 1e3) / 1e12 / fp32_peak if kp5 else None,
+            "note": "KDA prefill to the first packed states ({2,4,6} KDA plan, H = HK = 32): decode, the recurrent "
+                    "fp32 state pass (kda_prefill_kernel, 7 K V flops per token and head), encode"}
         r4 = measure_stack(args, 512, 32, 16, 5, 2, world, rank, device, barrier)
         ms4_all, e2e4 = max_over_ranks(r4["elapsed_ms"], r4["e2e_ms"])
         fam, ms4 = r4["kernel_ms"], ms4_all / 5

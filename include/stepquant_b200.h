@@ -313,6 +313,20 @@ int64_t sq_gdn_prefill_workspace_bytes(int32_t tokens, int32_t num_seqs, int32_t
 int32_t sq_gdn_prefill(const sq_prefill_args *args, sq_stream_t stream);
 
 /*
+ * KDA prefill: the same state pass for layers with a per-key-channel decay
+ * (Kimi-Delta-Attention).  It replaces the SGLang KDA chunk kernel that the
+ * same hook (stepquant/sglang/runtime.py:193-202) calls; the recurrence is
+ * core.delta_step (stepquant/core.py:5-15) with log_decay [heads, keys].
+ * Arguments as for sq_gdn_prefill except
+ *   g      [tokens, heads, keys] fp32 log decay per key channel, 16-byte
+ *          aligned base
+ *   workspace, workspace_bytes, status: unused (may be NULL / 0)
+ * The pass keeps each (sequence, head) state in fp32 registers and walks the
+ * tokens in order (fp32 arithmetic throughout); keys = values = 128 only.
+ */
+int32_t sq_kda_prefill(const sq_prefill_args *args, sq_stream_t stream);
+
+/*
  * Self-test of the division used by the register-resident decode kernels: for
  * i < n, out[i] = a[i] / b[i] computed with a correctly rounded reciprocal of
  * the fp16 value b[i] (given as its bits) and one Markstein correction.  It

@@ -16,7 +16,7 @@ LIBDIR = os.path.join(PACKAGE, "_lib")
 LIBRARY = os.path.join(LIBDIR, "libstepquant_b200.so")
 HEADER = os.path.join(ROOT, "include", "stepquant_b200.h")
 SOURCES = ["sq_abi.cu", "sq_tile.cu", "sq_fast.cu", "sq_pack.cu", "sq_fp32.cu", "sq_noalloc.cu", "sq_prefill.cu",
-           "sq_fast_kda.cu", "sq_streams.cu", "sq_fast_two.cu"]
+           "sq_fast_kda.cu", "sq_streams.cu", "sq_fast_two.cu", "sq_prefill_kda.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -26,8 +26,8 @@ NVCC_FLAGS = [
 ]
 # The quantizer must not contract a*b+c into FMAs (bit-exactness with the
 # reference fit_state; intended FMAs are written as fmaf()).  The chunked
-# prefill is toleranced and is built with contraction.
-CONTRACT = {"sq_prefill.cu"}
+# prefill passes are toleranced and are built with contraction.
+CONTRACT = {"sq_prefill.cu", "sq_prefill_kda.cu"}
 
 
 def _nvcc():

@@ -66,6 +66,7 @@ _SIGNATURES = {
     "sq_selftest_fp16_division": (_i32, [_p, _p, _p, _i64, _p]),
     "sq_gdn_prefill": (_i32, [_p, _p]),
     "sq_gdn_prefill_workspace_bytes": (_i64, [_i32, _i32, _i32]),
+    "sq_kda_prefill": (_i32, [_p, _p]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

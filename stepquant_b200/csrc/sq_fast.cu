@@ -662,14 +662,22 @@ __device__ __forceinline__ void halves4(uint2 raw, float2 &lo, float2 &hi) {
 // `dense` ([K, V] of this item) when given.  Each lane rewrites the 8 bytes it
 // read; the second read hits L2.  As in the reference (its readout stores
 // pivot rows itself, readout.py:118-121), the writeback skips pivot heads.
+// (AHEAD: every row load in flight at once -- the readout, whose registers
+// allow it; the fused step issues them four at a time.)
+template <bool AHEAD>
 __device__ __forceinline__ void pivot_pass1(FastSmem &s, const uint8_t *head, int warp, int lane) {
     const uint8_t *src = pivot_lane(const_cast<uint8_t *>(head), warp, lane);
     float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
-#pragma unroll 4
+    constexpr int kAhead = AHEAD ? 16 : 4;
+    uint2 raw[16];
+#pragma unroll
+    for (int r = 0; r < kAhead; ++r) raw[r] = *reinterpret_cast<const uint2 *>(src + r * 32);
+#pragma unroll
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
         float2 y01, y23;
-        halves4(*reinterpret_cast<const uint2 *>(src + r * 32), y01, y23);
+        if (r + kAhead < 16) raw[r + kAhead] = *reinterpret_cast<const uint2 *>(src + (r + kAhead) * 32);
+        halves4(raw[r], y01, y23);
         const float4 a = s.rowa[k], b = s.rowb[k];
         kx01 = pfma2(hi2(a), y01, kx01);
         kx23 = pfma2(hi2(a), y23, kx23);
@@ -891,7 +899,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
         else unpack_update_tm<8>(s, st, warp, lane, c.tm);
     } else {
         if (width == 16) {
-            pivot_pass1(s, c.page + c.off_head, warp, lane);
+            pivot_pass1<MODE == kReadout>(s, c.page + c.off_head, warp, lane);
         } else if (MODE == kReadout) {
             if (width == 4) readout_rows<4>(s, st, warp, lane);
             else if (width == 6) readout_rows<6>(s, st, warp, lane);

@@ -1,22 +1,24 @@
 // Register-resident decode kernels for KDA heads with K = V = 128 (the served
 // shape of Kimi-Linear-style layers): per key row a code width of 2, 4, 6 or
-// 8 bits or an fp16 pivot row, per-channel decay, value tile 4.
+// 8 bits (3 and 5 with the width extension) or an fp16 pivot row, per-channel
+// decay, value tile 4.
 //
-// One 256-thread CTA per (request, value head), two CTAs per SM.  The head's
-// code bytes are staged by cp.async; a cooperative pass (P0) unpacks every
-// (row, value tile) chunk into a dense fp16 plane (levels of integer rows,
-// values of pivot rows) laid out so that thread (w, l) reads its four columns
-// l, l+32, l+64, l+96 of a row with one 8-byte load.  From there the mapping
-// is the one of the GDN kernels (warp w owns rows 16w..16w+15, both torch sum
-// orders thread-local): P1 dequantizes and decays (x = level * r_old *
-// 2^(8-b) * decay_k * c, pivot rows value * decay_k) and forms the column
-// partials of k^T S and q^T S, P2 applies the rank-1 update and the row |x|
-// sums, P3-P5 evaluate fit_state for KDA rows (limit = qmax 2^(8-b), y =
-// x / r / c / 2^(8-b), pivot rows excluded from c and the least squares), and a
-// cooperative pass packs the codes.  Divisions by fp16 scales and by the row
-// limits (64, 112, 124, 127: at most 7 significant bits) use the corrected
-// reciprocal of the GDN kernels, exact for such divisors; division by
-// 2^(8-b) is an exact multiplication.
+// One 256-thread CTA per (request, value head), three per SM (four for the
+// readout).  The head's code bytes are staged by cp.async from a 16-byte
+// cover.  Warp w owns rows 16w..16w+15 and thread (w, l) the columns l, l+32,
+// l+64, l+96 of each (both torch sum orders thread-local): P1 decodes each
+// value straight from the staged bytes, dequantizes and decays it (x = level *
+// r_old * 2^(8-b) * decay_k * c, pivot rows value * decay_k) and forms the
+// column partials of k^T S and q^T S, P2 applies the rank-1 update and the row
+// |x| sums, P3-P5 evaluate fit_state for KDA rows (limit = qmax 2^(8-b),
+// y = x / r / c / 2^(8-b), pivot rows excluded from c and the least squares),
+// and a cooperative pass packs the codes into the staged region, which is
+// written back whole.  P3-P5 divide by rn = r 2^(8-b) instead of r and then
+// by c: RN(x / rn) = RN(x / r) 2^(b-8) exactly (a power-of-two scaling of a
+// normal float; a quotient small enough to be subnormal has level 0 either
+// way), so y needs no separate scaling.  Divisions by fp16 scales (and their
+// power-of-two multiples) and by qmax (1..127: at most 7 significant bits) use
+// the corrected reciprocal of the GDN kernels, exact for such divisors.
 #include "sq_fast.cuh"
 
 namespace sq {
@@ -35,10 +37,10 @@ struct KdaSmem {
     int rows[DK];
     float imp[DK];
     float red[2][8][DV];
-    float4 rowa[DK];  // P1: {fa, fa, k, k}          P3-P5: {r, r, 1/r, 1/r}
-    float4 rowb[DK];  // P1: {q, q, isint, -}        P3-P5: {-r, -r, w2, w2}
-    float4 rowc[DK];  // P3-P5: {rn, rn, 2^(b-8), 2^(b-8)}   rn = r 2^(8-b)
-    float4 rowd[DK];  // P3-P5: {limit, 1/limit, qmax, isint}
+    float4 rowa[DK];  // P1: {fa, fa, k, k}          P3-P5: {rn, rn, 1/rn, 1/rn}   rn = r 2^(8-b)
+    float4 rowb[DK];  // P1: {q, q, isint, -}        P3-P5: {-rn, -rn, w2, w2}
+    float4 rowd[DK];  // P3-P5: {-, 1/qmax (0: pivot row), qmax, isint}
+    float rscale[DK]; // P3-: r (the fp16 row scale the page stores; 1 for pivot rows)
     float colc[4][DV];
     float misc[64];
     int flags;
@@ -131,9 +133,11 @@ __device__ __forceinline__ void kda_readout_rows(KdaSmem &s, int lead, int off0,
 }
 
 // P3 partial: per column, the maximum over the warp's integer rows of
-// |x / r| / limit -> s.red[0].  EXACT divides (corrected reciprocals, IEEE on
-// the SLOW path); otherwise |x| * RN(1/r) * RN(1/limit), whose relative
-// distance from the exact value is below 6 * 2^-24 (six float steps), bounds it.
+// |x / r| / limit = |x / rn| / qmax -> s.red[0].  EXACT divides (corrected
+// reciprocals, IEEE on the SLOW path); otherwise |x| * RN(1/rn) * RN(1/qmax),
+// whose relative distance from the exact value is below 6 * 2^-24 (six float
+// steps), bounds it.  (A maximum in the subnormal range gives c0 = fp16's
+// smallest scale whatever its value.)
 template <bool SLOW, bool EXACT>
 __device__ __forceinline__ void kda_column_max(KdaSmem &s, int warp, int lane, uint32_t tm) {
     float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
@@ -148,20 +152,22 @@ __device__ __forceinline__ void kda_column_max(KdaSmem &s, int warp, int lane, u
             const float keep = d.w;
             float2 t01, t23;
             if (EXACT) {
-                const float2 lim = make_float2(d.x, d.x), rl = make_float2(d.y, d.y), nl = make_float2(-d.x, -d.x);
+                const float2 qm = make_float2(d.z, d.z), rq = make_float2(d.y, d.y), nq = make_float2(-d.z, -d.z);
                 const float2 s01 = divide2<SLOW>(X[i][0], lo2(a), hi2(a), lo2(b));
                 const float2 s23 = divide2<SLOW>(X[i][1], lo2(a), hi2(a), lo2(b));
-                t01 = divide2<SLOW>(make_float2(fabsf(s01.x), fabsf(s01.y)), lim, rl, nl);
-                t23 = divide2<SLOW>(make_float2(fabsf(s23.x), fabsf(s23.y)), lim, rl, nl);
+                t01 = divide2<SLOW>(make_float2(fabsf(s01.x), fabsf(s01.y)), qm, rq, nq);
+                t23 = divide2<SLOW>(make_float2(fabsf(s23.x), fabsf(s23.y)), qm, rq, nq);
             } else {
                 const float2 rl = make_float2(d.y, d.y);
                 t01 = pmul2(pmul2(make_float2(fabsf(X[i][0].x), fabsf(X[i][0].y)), hi2(a)), rl);
                 t23 = pmul2(pmul2(make_float2(fabsf(X[i][1].x), fabsf(X[i][1].y)), hi2(a)), rl);
             }
-            m0 = fmaxf(m0, t01.x * keep);
-            m1 = fmaxf(m1, t01.y * keep);
-            m2 = fmaxf(m2, t23.x * keep);
-            m3 = fmaxf(m3, t23.y * keep);
+            // (pivot rows: 1/qmax is 0 in the row table, so the products and
+            // the corrected-reciprocal quotients are 0; IEEE quotients are masked)
+            m0 = fmaxf(m0, SLOW ? t01.x * keep : t01.x);
+            m1 = fmaxf(m1, SLOW ? t01.y * keep : t01.y);
+            m2 = fmaxf(m2, SLOW ? t23.x * keep : t23.x);
+            m3 = fmaxf(m3, SLOW ? t23.y * keep : t23.y);
         }
     }
     s.red[0][warp][lane] = m0;
@@ -171,7 +177,7 @@ __device__ __forceinline__ void kda_column_max(KdaSmem &s, int warp, int lane, u
 }
 
 // P4 body: first levels and the weighted least-squares sums; the thread's
-// values go from x to x / r (integer rows) in tensor memory.
+// values go from x to x / rn in tensor memory (rn = 1 for pivot rows).
 template <bool SLOW, bool CLAMP>
 __device__ __forceinline__ void kda_first_levels(const KdaSmem &s, int warp, int lane, uint32_t tm, float2 (&num)[2],
                                                  float2 (&den)[2]) {
@@ -189,23 +195,23 @@ __device__ __forceinline__ void kda_first_levels(const KdaSmem &s, int warp, int
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int k = warp * 16 + 4 * g + i;
-            const float4 a = s.rowa[k], b = s.rowb[k], cc = s.rowc[k], d = s.rowd[k];
-            const float2 rn = lo2(cc), inv = hi2(cc), w2 = hi2(b);
+            const float4 a = s.rowa[k], b = s.rowb[k], d = s.rowd[k];
+            const float2 rn = lo2(a), w2 = hi2(b);
             const float q = d.z;
             const bool integer = d.w != 0.f;
             const float2 nrk = pmul2(rn, nround);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const float2 x = X[i][h];
-                const float2 sn = divide2<SLOW>(x, lo2(a), hi2(a), lo2(b));
-                float2 y = pmul2(divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), inv);
+                const float2 sn = divide2<SLOW>(x, rn, hi2(a), lo2(b));
+                float2 y = divide2<SLOW>(sn, h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
                 // Pivot rows (weight 0 in the sums) are always clamped: their
                 // unbounded levels could overflow v * v and turn 0 * inf into NaN.
                 if (CLAMP || !integer) y = clamp2(y, q);
                 const float2 v = pfma2(rn, __fadd2_rn(y, round), nrk);
                 num[h] = __fadd2_rn(num[h], product_term(pmul2(w2, v), x));
                 den[h] = __fadd2_rn(den[h], product_term(w2, pmul2(v, v)));
-                if (integer) X[i][h] = sn;
+                X[i][h] = sn;  // (pivot rows: rn = 1, so sn is x exactly)
             }
         }
         tm_st16(tm + 16 * g, X);
@@ -236,14 +242,14 @@ __device__ __forceinline__ void kda_final_levels(KdaSmem &s, int warp, int lane,
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int k = warp * 16 + 4 * g + i;
-            const float4 cc = s.rowc[k], d = s.rowd[k];
+            const float4 d = s.rowd[k];
             if (d.w != 0.f) {
                 unsigned char *code = s.u.code + k * DV + lane;
                 const uint32_t off = uint32_t(d.z);
                 const bool clamp = CLAMP && (SLOW || !(__fmul_rn(rho, d.z) <= d.z + 0.49f));  // warp-uniform (row k)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    float2 y = pmul2(divide2<SLOW>(X[i][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01), hi2(cc));
+                    float2 y = divide2<SLOW>(X[i][h], h ? c23 : c01, h ? r23 : r01, h ? n23 : n01);
                     if (clamp) y = clamp2(y, d.z);
                     const float2 t = __fadd2_rn(y, round);  // low byte: the level (two's complement)
                     code[64 * h] = static_cast<unsigned char>(__float_as_uint(t.x) + off);
@@ -602,16 +608,16 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
             const float mean = __fdiv_rn(total, float(DV));
             float rr = fp16_scale(__fsqrt_rn(__fdiv_rn(fmaxf(mean, 1e-20f), w)));
             if (!integer) rr = 1.f;
-            const float rc = __frcp_rn(rr);
             const float w2 = integer ? __fmul_rn(w, w) : 0.f;
             const int bb = b > 8 ? 8 : b;
             const float norm = float(1 << (8 - bb)), inv = __uint_as_float(uint32_t(127 - 8 + bb) << 23);
+            // rn = r 2^(8-b) and RN(1/rn) = RN(1/r) 2^(b-8): exact power-of-two scalings
+            const float rn = __fmul_rn(rr, norm), rcn = __fmul_rn(__frcp_rn(rr), inv);
             const float qm = float(qmax_i(b));
-            const float lim = __fmul_rn(qm, norm);
-            s.rowa[k] = make_float4(rr, rr, rc, rc);
-            s.rowb[k] = make_float4(-rr, -rr, w2, w2);
-            s.rowc[k] = make_float4(__fmul_rn(rr, norm), __fmul_rn(rr, norm), inv, inv);
-            s.rowd[k] = make_float4(lim, __frcp_rn(lim), qm, integer ? 1.f : 0.f);
+            s.rowa[k] = make_float4(rn, rn, rcn, rcn);
+            s.rowb[k] = make_float4(-rn, -rn, w2, w2);
+            s.rowd[k] = make_float4(0.f, integer ? __frcp_rn(qm) : 0.f, qm, integer ? 1.f : 0.f);
+            s.rscale[k] = rr;
             if (integer) atomicMax(&s.qmax_max, qmax_i(b));
             if (integer && !(total <= 7.922816251426434e28f)) atomicOr(&s.flags, 1);  // 2^96, or NaN
         }
@@ -658,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         }
     }
     if (tid < DK) {
-        if (s.rows[tid] >= 0) put_half(page, s.rows[tid], s.rowa[tid].x);
+        if (s.rows[tid] >= 0) put_half(page, s.rows[tid], s.rscale[tid]);
     } else {
         put_half(page, coff + 2 * (tid - DK), s.colc[1][tid - DK]);
     }

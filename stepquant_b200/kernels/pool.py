@@ -165,19 +165,19 @@ class PackedStatePool:
         return state
 
     def extend(self, q, k, v, g, beta, slots, query_start_loc, *, normalize=True, scale=None):
-        """Prefill ``slots``: decode their states, run the chunked GDN pass over
+        """Prefill ``slots``: decode their states, run the prefill pass over
         each request's tokens (request i owns tokens query_start_loc[i] ..
         query_start_loc[i + 1]) and encode the final states back -- the
         decode -> chunk kernel -> encode sequence of the reference hook
-        (stepquant/sglang/runtime.py:193-202).  g is the log decay and beta the
-        activated gate, per token and value head.  Returns the outputs shaped
-        like ``v`` (bf16)."""
-        if self.plan.architecture != "gdn":
-            raise NotImplementedError("the chunked prefill is built for GDN layers")
-        from .prefill import chunk_gated_delta_rule
+        (stepquant/sglang/runtime.py:193-202).  g is the log decay (GDN: per
+        token and value head; KDA: per token, value head and key channel) and
+        beta the activated gate, per token and value head.  Returns the
+        outputs shaped like ``v`` (bf16)."""
+        from .prefill import chunk_gated_delta_rule, chunk_kda
         active = self.decode(slots)
-        out, final = chunk_gated_delta_rule(q, k, v, g, beta, scale=scale, initial_state=active,
-                                            use_qk_l2norm_in_kernel=normalize, cu_seqlens=query_start_loc)
+        run = chunk_kda if self.plan.architecture == "kda" else chunk_gated_delta_rule
+        out, final = run(q, k, v, g, beta, scale=scale, initial_state=active, use_qk_l2norm_in_kernel=normalize,
+                         cu_seqlens=query_start_loc)
         self.encode(final, slots)
         return out
 

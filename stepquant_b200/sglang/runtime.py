@@ -12,9 +12,10 @@ the code below is organised around this package's pool.
   dense recurrent ("temporal") cache is replaced by ``TemporalPages``, one
   ``PackedStatePool`` (or baseline-format pool) per layer with ``size + 1``
   slots (slot 0 is SGLang's padding sentinel).  Slot operations go to both.
-* Kernels: decode routes to ``PackedStatePool.step``; prefill of GDN layers
-  runs this package's chunked pass (``PackedStatePool.extend``), other layers
-  let SGLang's chunk kernel update the decoded dense state in place.
+* Kernels: decode routes to ``PackedStatePool.step``; prefill of GDN and KDA
+  layers with K = V = 128 runs this package's state pass
+  (``PackedStatePool.extend``), other layers let SGLang's chunk kernel update
+  the decoded dense state in place.
 * Graphs: each captured decode batch size defers its background writeback
   (``defer_writeback(..., attention_windows=True, joined=True)``) and the
   captured graph is returned wrapped in a ``WritebackGraph``.
@@ -289,15 +290,17 @@ def kernel_packed_decode(original, self, mixed_qkv, a, b, *, A_log, dt_bias, sca
 
 
 def kernel_extend(original, self, q, k, v, g, beta, *, ssm_states, cache_indices, query_start_loc, **kwargs):
-    """Prefill.  GDN pools with K = V = 128 run this package's chunked state
-    pass (``PackedStatePool.extend``: decode, chunk pass with in-kernel q/k
-    L2 normalisation, encode).  Other packed pools hand SGLang's chunk kernel
-    the decoded states, V-first as it keeps them, with the active requests
+    """Prefill.  Pools with K = V = 128 run this package's state pass
+    (``PackedStatePool.extend``: decode, the GDN chunk pass or the KDA
+    recurrent pass with in-kernel q/k L2 normalisation, encode); g is the
+    kernel's log decay as the layer hands it over ([.., T, H] for GDN,
+    [.., T, H, K] for KDA).  Other packed pools hand SGLang's chunk kernel the
+    decoded states, V-first as it keeps them, with the active requests
     numbered 0..n-1, and encode what it leaves there."""
     if not _packed(ssm_states):
         return original(self, q, k, v, g, beta, ssm_states=ssm_states, cache_indices=cache_indices,
                         query_start_loc=query_start_loc, **kwargs)
-    if ssm_states.plan.architecture == "gdn" and ssm_states.keys == 128 and ssm_states.values == 128:
+    if ssm_states.keys == 128 and ssm_states.values == 128:
         return ssm_states.extend(q, k, v, g, beta, cache_indices, query_start_loc, normalize=True)
     dense = ssm_states.decode(cache_indices).transpose(-1, -2).contiguous()
     local = torch.arange(cache_indices.numel(), device=cache_indices.device, dtype=cache_indices.dtype)
