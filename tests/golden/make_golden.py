@@ -20,7 +20,9 @@ Files written next to this script:
                         decode inputs, the updated state and its fitted codes.
 * ``prefill.npz``    -- ``stepquant.adapters.RecurrentKernel`` (the token-by-
                         token prefill recurrence) on bf16-valued q/k/v with
-                        in-kernel L2 normalisation: outputs and final states.
+                        in-kernel L2 normalisation: outputs and final states;
+                        cases a, b GDN (decay per head), c, d KDA (decay per
+                        key channel).
 
 * ``calibration.npz`` -- ``stepquant.calibration``: the statistics a seeded
                         run of ``LayerStatistics.observe`` exports (two GDN
@@ -117,6 +119,23 @@ def prefill_cases(RecurrentKernel):
         beta = torch.randn(1, tokens, heads, generator=gen).sigmoid()
         state = torch.randn(1, heads, keys, values, generator=gen) * 0.1 if initial else None
         o, final = RecurrentKernel("gdn")(q, k, v, g, beta, initial_state=state, output_final_state=True,
+                                          use_qk_l2norm_in_kernel=True)
+        out.update({f"{name}_{n}": t.numpy() for n, t in dict(q=q, k=k, v=v, g=g, beta=beta, out=o, final=final).items()})
+        if initial:
+            out[f"{name}_initial"] = state.numpy()
+    # KDA (per-key-channel decay, the Kimi gate -exp(A_log) softplus(.) per
+    # channel): the same recurrence with g [1, T, H, K]; GQA-free, 2 heads.
+    gen = torch.Generator().manual_seed(4)
+    for name, tokens, initial in (("c", 150, True), ("d", 64, False)):
+        heads, keys, values = 2, 128, 128
+        q = torch.randn(1, tokens, heads, keys, generator=gen).bfloat16().float()
+        k = torch.randn(1, tokens, heads, keys, generator=gen).bfloat16().float()
+        v = torch.randn(1, tokens, heads, values, generator=gen).bfloat16().float()
+        a_log = torch.rand(heads, 1, generator=gen) * math.log(16)
+        g = -a_log.exp() * torch.nn.functional.softplus(torch.randn(1, tokens, heads, keys, generator=gen))
+        beta = torch.randn(1, tokens, heads, generator=gen).sigmoid()
+        state = torch.randn(1, heads, keys, values, generator=gen) * 0.1 if initial else None
+        o, final = RecurrentKernel("kda")(q, k, v, g, beta, initial_state=state, output_final_state=True,
                                           use_qk_l2norm_in_kernel=True)
         out.update({f"{name}_{n}": t.numpy() for n, t in dict(q=q, k=k, v=v, g=g, beta=beta, out=o, final=final).items()})
         if initial:

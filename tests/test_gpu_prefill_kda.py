@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 import torch
 
+from conftest import load_golden
 from oracle import stepquant_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -41,6 +42,22 @@ def _check(out, final, q, k, v, g, beta, cu, init=None):
     torch.cuda.synchronize()
     assert _rel(final.cpu().numpy(), f_ref) < TOL_STATE
     assert _rel(out.float().cpu().numpy(), o_ref) < TOL_OUT
+
+
+@pytest.mark.parametrize("case", ["c", "d"])
+def test_kda_prefill_matches_reference_recurrent_kernel(case):
+    """Golden vectors of the reference's adapters.RecurrentKernel("kda") (150
+    tokens from an initial state, 64 from zero)."""
+    from stepquant_b200.kernels.prefill import chunk_kda
+    d = load_golden("prefill.npz")
+    q, k, v, g, beta = (torch.from_numpy(d[f"{case}_{n}"]).cuda() for n in ("q", "k", "v", "g", "beta"))
+    init = torch.from_numpy(d[f"{case}_initial"]).cuda() if f"{case}_initial" in d else None
+    out, final = chunk_kda(q.bfloat16(), k.bfloat16(), v.bfloat16(), g, beta, initial_state=init,
+                           use_qk_l2norm_in_kernel=True)
+    torch.cuda.synchronize()
+    assert out.shape == v.shape and out.dtype == torch.bfloat16
+    assert _rel(final.cpu().numpy(), d[f"{case}_final"]) < TOL_STATE
+    assert _rel(out.float().cpu().numpy(), d[f"{case}_out"]) < TOL_OUT
 
 
 @pytest.mark.parametrize("decay_scale", [1.0, 0.01])

@@ -153,9 +153,10 @@ def test_zero_state_encodes_finite():
         assert np.isfinite(dec).all() and np.abs(dec).max() < 1e-10
 
 
-@pytest.mark.parametrize("case", ["a", "b"])
+@pytest.mark.parametrize("case", ["a", "b", "c", "d"])
 def test_prefill_oracle_matches_reference_recurrent_kernel(case):
-    """oracle.prefill_sequential vs stepquant.adapters.RecurrentKernel (150 / 64 tokens)."""
+    """oracle.prefill_sequential vs stepquant.adapters.RecurrentKernel (150 / 64
+    tokens; a, b GDN with a decay per head, c, d KDA with one per key channel)."""
     d = load_golden("prefill.npz")
     q, k, v, g, beta = (d[f"{case}_{n}"][0] for n in ("q", "k", "v", "g", "beta"))
     init = d[f"{case}_initial"] if f"{case}_initial" in d else None
