@@ -23,7 +23,8 @@ per GPU at N = 1, larger than the 126 MB L2), so each step reads pages that are
 not L2-resident.
 
 Other workloads: ``--workload kda-decode`` (config 2), ``gdn-prefill``
-(config 3: chunked prefill to the first packed state) and ``gdn-stack``
+(config 3: chunked prefill to the first packed state), ``kda-prefill`` (the
+same for KDA layers, recurrent fp32 pass) and ``gdn-stack``
 (config 4: 48 GDN layers decoding through one CUDA graph per token, value heads
 tensor-parallel with an NCCL all-gather of each layer's readout).
 
@@ -64,7 +65,8 @@ def parse_args():
                    help="reference: the CPU port of the reference path; reference-gpu: the reference's own "
                         "Triton/Gluon pool from baseline/_ref beside this library's, config 1, one GPU")
     p.add_argument("--mode", choices=("async", "sync"), default="async")
-    p.add_argument("--workload", choices=("gdn-decode", "kda-decode", "gdn-prefill", "gdn-stack"), default="gdn-decode",
+    p.add_argument("--workload", choices=("gdn-decode", "kda-decode", "gdn-prefill", "kda-prefill", "gdn-stack"),
+                   default="gdn-decode",
                    help="config 1 (default), config 2, config 3 or config 4")
     p.add_argument("--kda-widths", default="2,4,6",
                    help="KDA row widths at 30/50/20 (kda-decode): 2,4,6 is the reference-legal twin of config 2's "
@@ -753,14 +755,17 @@ def measure_prefill(args, batch, tokens, heads_total, qk_total, steps, warmup, w
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         one_step()
         torch.cuda.synchronize()
-    kernels = {}
+    kernels, launches = {}, 0
     for ev in prof.key_averages():
         name = ev.key
+        if "sq::" in name and ev.device_time_total > 0:
+            launches += ev.count
         for short in ("prep_kernel", "state_kernel", "offsets_kernel", "kda_prefill_kernel", "tile_kernel",
                       "fast_kernel", "kda_kernel"):
             if short in name:
                 kernels[short] = kernels.get(short, 0.0) + ev.device_time_total / 1e3
     res["kernel_ms"] = kernels
+    res["sq_launches"] = launches
     chunk_heads = batch * ((tokens + 63) // 64) * heads_l
     c, kk, vv = 64, dim, dim
     if kda:  # per token and head: the decay product, two column sums and the rank-1 update (7 K V flops)
@@ -1049,10 +1054,10 @@ def main():
 
     workload = args.workload
     kda = workload == "kda-decode"
-    batch = args.batch if args.batch else (512 if kda or workload == "gdn-stack" else 32 if workload == "gdn-prefill"
-                                           else 256)
+    batch = args.batch if args.batch else (512 if kda or workload == "gdn-stack" else
+                                           32 if workload in ("gdn-prefill", "kda-prefill") else 256)
     heads = args.heads
-    qk_heads = args.qk_heads if args.qk_heads else (heads if kda else heads // 2)
+    qk_heads = args.qk_heads if args.qk_heads else (heads if kda or workload == "kda-prefill" else heads // 2)
     if heads % world or qk_heads % world:
         raise SystemExit("heads must divide evenly over ranks")
     clocks = ClockSampler(local)
@@ -1132,6 +1137,34 @@ def main():
             "e2e": {"value": units / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"]},
             "gpu_launches": args.steps * 5,
+        })
+    elif workload == "kda-prefill":
+        res = measure_prefill(args, batch, args.tokens, heads, qk_heads, args.steps, args.warmup, world, rank, device,
+                              barrier, e2e=True, clocks=clocks, kda=True)
+        elapsed_ms, e2e_ms = max_over_ranks(res["elapsed_ms"], res["e2e_ms"])
+        (flops,) = sum_over_ranks(res["flops"])
+        units = batch * args.tokens * args.steps
+        kern = res["kernel_ms"]
+        kp = kern.get("kda_prefill_kernel", 0.0)
+        # The recurrent pass runs on the FP32 pipe (packed FMUL2 / FFMA2); its
+        # roofline is the nominal fp32 rate, 148 SMs x 128 lanes x 2 flops x 1.965 GHz.
+        peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        achieved = flops / world / (kp / 1e3) / 1e12 if kp else None
+        line.update({
+            "metric": "prefill tokens/s", "unit": "tokens/s", "value": units / (elapsed_ms / 1e3),
+            "ms_per_step": elapsed_ms / args.steps, "dtype": "f32",
+            "config": {"workload": "kda-prefill-b%d-t%d-h%d-k128" % (batch, args.tokens, heads),
+                       "batch": batch, "tokens": args.tokens, "heads": heads, "qk_heads": qk_heads,
+                       "plan": "{2,4,6} KDA rows, 2% fp16 pivot rows (first packed state)",
+                       "parallelism": f"tp{world} (value heads)", "l2": "inputs > L2"},
+            "kernel_ms": kern,
+            "roofline": {"kernel": "kda_prefill_kernel", "bound": "fp32", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak if achieved else None, "traffic": None,
+                         "peak_source": "nominal fp32 FMA rate (no measured figure for the FP32 pipe)",
+                         "algorithmic_flops_per_launch": flops / world},
+            "e2e": {"value": units / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": res["h2d"],
+                    "d2h_bytes_per_step": res["d2h"]},
+            "gpu_launches": res["sq_launches"] * args.steps,
         })
     else:
         res = measure_decode(args, kda, batch, heads, qk_heads, args.steps, args.warmup, world, rank, device, barrier,

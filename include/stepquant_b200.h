@@ -320,6 +320,7 @@ int32_t sq_gdn_prefill(const sq_prefill_args *args, sq_stream_t stream);
  * Arguments as for sq_gdn_prefill except
  *   g      [tokens, heads, keys] fp32 log decay per key channel, 16-byte
  *          aligned base
+ *   initial_state, final_state: 16-byte aligned
  *   workspace, workspace_bytes, status: unused (may be NULL / 0)
  * The pass keeps each (sequence, head) state in fp32 registers and walks the
  * tokens in order (fp32 arithmetic throughout); keys = values = 128 only.

@@ -7,18 +7,24 @@
 // shape [H, K]:
 //     S <- diag(e^g) S;  d = beta (v - S^T k);  S <- S + k d^T;  o = S^T q.
 //
-// One 256-thread CTA per (sequence, value head), two per SM.  Thread t keeps
-// columns c and c + 64 (c = t / 4) of the fp32 state, rows 32 (t % 4) ..
-// 32 (t % 4) + 31, in registers for the whole prompt: the state is read once
-// and written once, and the per-token column sums S^T k and S^T q are the
-// thread's 32-row partials plus those of the three other lanes of its
-// quad (two shuffles each, no barrier).  o = S_dec^T q + (q . k) d, with
-// S_dec the decayed state, so one pass over the state forms both sums.
-// Tokens are taken in blocks of 16: the next block's q, k, v and g rows are
-// staged by cp.async while the current block runs, and a short prologue per
-// block normalises q and k, forms e^g, beta and q . k in shared memory.
-// Arithmetic is fp32 (products in packed f32x2 form), so the result matches
-// the fp32 recurrence up to summation order.
+// One 256-thread CTA per (sequence, value head), two per SM, the fp32 state
+// in registers for the whole prompt (read once, written once).  Lane l of
+// warp w holds rows 8 (l % 16) .. 8 (l % 16) + 7 of the eight columns
+// 16 w + 8 (l / 16) .. + 7: the sixteen lanes of a half-warp share a column
+// group and cover all 128 rows.  Per token a lane reads its 8 rows of e^g, k
+// and q (six 16-byte shared loads; the 8-row chunks are 12 floats apart, so
+// the eight chunks a quarter-warp reads fill the 32 banks once), forms the
+// 16 partial column sums (k and q for 8 columns) over its rows, and the
+// half-warp reduces them by recursive halving (15 shuffles, each lane ends
+// with one total), the k lanes form d = beta (v - S^T k), the q lanes
+// o = S^T q + (q . k) d, and d reaches every lane of the group (8 shuffles)
+// for the rank-1 update.  Shared-memory traffic per token and warp is about
+// a third of a layout in which lanes hold long row ranges of few columns.
+// Tokens are staged in blocks of 16: the next block's q, k, v and g rows
+// arrive by cp.async while the current block runs, and a prologue per block
+// normalises q and k and forms e^g, beta and q . k in shared memory.
+// Arithmetic is fp32 (products in packed f32x2 form over row pairs), so the
+// result matches the fp32 recurrence up to rounding order.
 #include <cuda_runtime.h>
 
 #include "sq_fast.cuh"
@@ -31,10 +37,9 @@ constexpr int KV = 128;           // values
 constexpr int KTB = 16;           // tokens per staged block
 constexpr int kKpThreads = 256;
 constexpr int kPieces = 16 + 16 + 16 + 32;  // 16-byte pieces of one token: q, k, v (bf16), g (fp32)
-// Prepared rows keep the four 32-key quarters 36 floats apart, so that the
-// four lanes of a quad (one quarter each) read distinct banks.
-constexpr int kRowPad = 4 * 36;
-__device__ __forceinline__ int kq_at(int key) { return (key >> 5) * 36 + (key & 31); }
+constexpr int kChunk = 12;                  // floats per 8-key chunk of a prepared row (8 + 4 pad)
+constexpr int kRowPad = 16 * kChunk;
+__device__ __forceinline__ int kq_at(int key) { return (key >> 3) * kChunk + (key & 7); }
 
 struct KdaPrefillRaw {
     __nv_bfloat16 q[KTB][KK];
@@ -49,7 +54,7 @@ struct KdaPrefillSmem {
     float kn[KTB][kRowPad];  // k / |k|
     float e[KTB][kRowPad];   // e^g
     float beta[KTB];
-    float qk[KTB];      // (q / |q| * scale) . (k / |k|)
+    float qk[KTB];           // (q / |q| * scale) . (k / |k|)
 };
 
 __device__ __forceinline__ int2 kda_seq_range(const sq_prefill_args &a, int n) {
@@ -84,9 +89,9 @@ __device__ __forceinline__ void kda_stage(KdaPrefillRaw &r, const sq_prefill_arg
     asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
 
-// Per-block prologue: thread (j, part) = (tid / 16, tid % 16) covers elements
-// 8 part .. 8 part + 7 of token j; the squared norms and q . k are summed over
-// the token's 16 lanes by shuffles.
+// Per-block prologue: thread (j, part) = (tid / 16, tid % 16) covers keys
+// 8 part .. 8 part + 7 of token j (one prepared chunk); the squared norms and
+// q . k are summed over the token's 16 lanes by shuffles.
 __device__ __forceinline__ void kda_prepare(KdaPrefillSmem &s, const KdaPrefillRaw &r, const sq_prefill_args &a,
                                             int t0, int n, int head, int tid) {
     const int j = tid >> 4, part = tid & 15;
@@ -145,56 +150,73 @@ __device__ __forceinline__ void kda_prepare(KdaPrefillSmem &s, const KdaPrefillR
 __device__ __forceinline__ float2 lo_pair(float4 v) { return make_float2(v.x, v.y); }
 __device__ __forceinline__ float2 hi_pair(float4 v) { return make_float2(v.z, v.w); }
 
-// Tokens of one staged block.  S0 / S1: columns c / c + 64, element i holding
-// rows 32 qd + 2 i and 32 qd + 2 i + 1.
+// Tokens of one staged block.  S[p][c]: rows 8 (lane % 16) + 2 p and + 1 of
+// column col0 + c, col0 = 16 warp + 8 (lane / 16).
 __device__ __forceinline__ void kda_block(const KdaPrefillSmem &s, const KdaPrefillRaw &r, const sq_prefill_args &a,
-                                          int t0, int n, int head, int qd, int c, float2 (&S0)[16], float2 (&S1)[16]) {
+                                          int t0, int n, int head, int lane, int col0, float2 (&S)[4][8]) {
     __nv_bfloat16 *out = static_cast<__nv_bfloat16 *>(a.out);
+    const int c16 = lane & 15, src0 = lane & 16;
+    const int col = col0 + (c16 >> 1);  // the column of this lane's total
+    const bool is_q = (c16 & 1) != 0;   // totals: k sums on even lanes, q sums on odd lanes
 #pragma unroll 1
     for (int j = 0; j < n; ++j) {
-        const float4 *e4 = reinterpret_cast<const float4 *>(&s.e[j][36 * qd]);
-        const float4 *k4 = reinterpret_cast<const float4 *>(&s.kn[j][36 * qd]);
-        const float4 *q4 = reinterpret_cast<const float4 *>(&s.qn[j][36 * qd]);
-        float2 ak0 = make_float2(0.f, 0.f), aq0 = ak0, ak1 = ak0, aq1 = ak0;
+        const float4 *e4 = reinterpret_cast<const float4 *>(&s.e[j][kChunk * c16]);
+        const float4 *k4 = reinterpret_cast<const float4 *>(&s.kn[j][kChunk * c16]);
+        const float4 *q4 = reinterpret_cast<const float4 *>(&s.qn[j][kChunk * c16]);
+        const float4 ea = e4[0], eb = e4[1], ka = k4[0], kb = k4[1], qa = q4[0], qb = q4[1];
+        const float2 E[4] = {lo_pair(ea), hi_pair(ea), lo_pair(eb), hi_pair(eb)};
+        const float2 K[4] = {lo_pair(ka), hi_pair(ka), lo_pair(kb), hi_pair(kb)};
+        const float2 Q[4] = {lo_pair(qa), hi_pair(qa), lo_pair(qb), hi_pair(qb)};
+        float sums[16];  // 2 c: the lane's part of (S^T k)_c, 2 c + 1: of (S^T q)_c, after the decay
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 ev = e4[i], kv = k4[i], qv = q4[i];
-            S0[2 * i] = pmul2(S0[2 * i], lo_pair(ev));
-            S0[2 * i + 1] = pmul2(S0[2 * i + 1], hi_pair(ev));
-            S1[2 * i] = pmul2(S1[2 * i], lo_pair(ev));
-            S1[2 * i + 1] = pmul2(S1[2 * i + 1], hi_pair(ev));
-            ak0 = pfma2(lo_pair(kv), S0[2 * i], ak0);
-            ak0 = pfma2(hi_pair(kv), S0[2 * i + 1], ak0);
-            aq0 = pfma2(lo_pair(qv), S0[2 * i], aq0);
-            aq0 = pfma2(hi_pair(qv), S0[2 * i + 1], aq0);
-            ak1 = pfma2(lo_pair(kv), S1[2 * i], ak1);
-            ak1 = pfma2(hi_pair(kv), S1[2 * i + 1], ak1);
-            aq1 = pfma2(lo_pair(qv), S1[2 * i], aq1);
-            aq1 = pfma2(hi_pair(qv), S1[2 * i + 1], aq1);
-        }
-        float ks0 = ak0.x + ak0.y, qs0 = aq0.x + aq0.y, ks1 = ak1.x + ak1.y, qs1 = aq1.x + aq1.y;
+        for (int c = 0; c < 8; ++c) {
+            float2 ak = make_float2(0.f, 0.f), aq = ak;
 #pragma unroll
-        for (int o = 1; o < 4; o <<= 1) {  // the quad's four row ranges
-            ks0 += __shfl_xor_sync(0xffffffffu, ks0, o);
-            qs0 += __shfl_xor_sync(0xffffffffu, qs0, o);
-            ks1 += __shfl_xor_sync(0xffffffffu, ks1, o);
-            qs1 += __shfl_xor_sync(0xffffffffu, qs1, o);
+            for (int p = 0; p < 4; ++p) {
+                S[p][c] = pmul2(S[p][c], E[p]);
+                ak = pfma2(K[p], S[p][c], ak);
+                aq = pfma2(Q[p], S[p][c], aq);
+            }
+            sums[2 * c] = ak.x + ak.y;
+            sums[2 * c + 1] = aq.x + aq.y;
         }
-        const float b = s.beta[j], qk = s.qk[j];
-        const float d0 = b * (__bfloat162float(r.v[j][c]) - ks0);
-        const float d1 = b * (__bfloat162float(r.v[j][c + 64]) - ks1);
-        const float2 dd0 = make_float2(d0, d0), dd1 = make_float2(d1, d1);
+        // Recursive halving over the half-warp: at mask m a lane keeps the
+        // upper half of its values when (lane & m), adds the partner's copy of
+        // that half and passes on the other; lane c16 ends with total c16.
+        float h8[8], h4[4], h2[2];
+        {
+            const bool up = (c16 & 8) != 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 kv = k4[i];
-            S0[2 * i] = pfma2(lo_pair(kv), dd0, S0[2 * i]);
-            S0[2 * i + 1] = pfma2(hi_pair(kv), dd0, S0[2 * i + 1]);
-            S1[2 * i] = pfma2(lo_pair(kv), dd1, S1[2 * i]);
-            S1[2 * i + 1] = pfma2(hi_pair(kv), dd1, S1[2 * i + 1]);
+            for (int i = 0; i < 8; ++i)
+                h8[i] = (up ? sums[i + 8] : sums[i]) + __shfl_xor_sync(0xffffffffu, up ? sums[i] : sums[i + 8], 8);
         }
-        const int64_t row = (int64_t(t0 + j) * a.heads + head) * KV;
-        if (qd == 0) out[row + c] = __float2bfloat16_rn(qs0 + qk * d0);
-        if (qd == 1) out[row + c + 64] = __float2bfloat16_rn(qs1 + qk * d1);
+        {
+            const bool up = (c16 & 4) != 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                h4[i] = (up ? h8[i + 4] : h8[i]) + __shfl_xor_sync(0xffffffffu, up ? h8[i] : h8[i + 4], 4);
+        }
+        {
+            const bool up = (c16 & 2) != 0;
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+                h2[i] = (up ? h4[i + 2] : h4[i]) + __shfl_xor_sync(0xffffffffu, up ? h4[i] : h4[i + 2], 2);
+        }
+        const float total = (is_q ? h2[1] : h2[0]) + __shfl_xor_sync(0xffffffffu, is_q ? h2[0] : h2[1], 1);
+        // k lanes: d = beta (v - S^T k); q lanes take it from their k lane and store o.
+        float d = s.beta[j] * (__bfloat162float(r.v[j][col]) - total);
+        const float dk = __shfl_xor_sync(0xffffffffu, d, 1);
+        if (is_q) {
+            d = dk;
+            out[(int64_t(t0 + j) * a.heads + head) * KV + col] = __float2bfloat16_rn(total + s.qk[j] * d);
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float dc = __shfl_sync(0xffffffffu, d, src0 + 2 * c);
+            const float2 dd = make_float2(dc, dc);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) S[p][c] = pfma2(K[p], dd, S[p][c]);
+        }
     }
 }
 
@@ -203,24 +225,35 @@ __global__ void __launch_bounds__(kKpThreads, 2) kda_prefill_kernel(sq_prefill_a
     KdaPrefillSmem &s = *reinterpret_cast<KdaPrefillSmem *>(smem_raw);
     const int seq = blockIdx.x / a.heads, head = blockIdx.x - seq * a.heads;
     const int qh = head / (a.heads / a.qk_heads);
-    const int tid = threadIdx.x, qd = tid & 3, c = tid >> 2;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int row0 = 8 * (lane & 15), col0 = 16 * warp + 8 * (lane >> 4);
     const int2 range = kda_seq_range(a, seq);
     const int64_t base = (int64_t(seq) * a.heads + head) * KK * KV;
     const int blocks = (range.y - range.x + KTB - 1) / KTB;
     if (blocks > 0) kda_stage(s.raw[0], a, range.x, min(KTB, range.y - range.x), head, qh, tid);
 
-    float2 S0[16], S1[16];
+    float2 S[4][8];
     if (a.initial_state) {
         const float *init = a.initial_state + base;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int r = 32 * qd + 2 * i;
-            S0[i] = make_float2(init[r * KV + c], init[(r + 1) * KV + c]);
-            S1[i] = make_float2(init[r * KV + c + 64], init[(r + 1) * KV + c + 64]);
+        for (int p = 0; p < 4; ++p) {
+            const float *r0 = init + (row0 + 2 * p) * KV + col0, *r1 = r0 + KV;
+            const float4 a0 = *reinterpret_cast<const float4 *>(r0), a1 = *reinterpret_cast<const float4 *>(r0 + 4);
+            const float4 b0 = *reinterpret_cast<const float4 *>(r1), b1 = *reinterpret_cast<const float4 *>(r1 + 4);
+            S[p][0] = make_float2(a0.x, b0.x);
+            S[p][1] = make_float2(a0.y, b0.y);
+            S[p][2] = make_float2(a0.z, b0.z);
+            S[p][3] = make_float2(a0.w, b0.w);
+            S[p][4] = make_float2(a1.x, b1.x);
+            S[p][5] = make_float2(a1.y, b1.y);
+            S[p][6] = make_float2(a1.z, b1.z);
+            S[p][7] = make_float2(a1.w, b1.w);
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) S0[i] = S1[i] = make_float2(0.f, 0.f);
+        for (int p = 0; p < 4; ++p)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) S[p][c] = make_float2(0.f, 0.f);
     }
 
 #pragma unroll 1
@@ -235,18 +268,18 @@ __global__ void __launch_bounds__(kKpThreads, 2) kda_prefill_kernel(sq_prefill_a
         __syncthreads();  // block b staged for every thread
         kda_prepare(s, s.raw[b & 1], a, t0, n, head, tid);
         __syncthreads();
-        kda_block(s, s.raw[b & 1], a, t0, n, head, qd, c, S0, S1);
+        kda_block(s, s.raw[b & 1], a, t0, n, head, lane, col0, S);
         __syncthreads();  // prepared rows and raw[b & 1] are free again
     }
 
     float *fin = a.final_state + base;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int r = 32 * qd + 2 * i;
-        fin[r * KV + c] = S0[i].x;
-        fin[(r + 1) * KV + c] = S0[i].y;
-        fin[r * KV + c + 64] = S1[i].x;
-        fin[(r + 1) * KV + c + 64] = S1[i].y;
+    for (int p = 0; p < 4; ++p) {
+        float *r0 = fin + (row0 + 2 * p) * KV + col0, *r1 = r0 + KV;
+        *reinterpret_cast<float4 *>(r0) = make_float4(S[p][0].x, S[p][1].x, S[p][2].x, S[p][3].x);
+        *reinterpret_cast<float4 *>(r0 + 4) = make_float4(S[p][4].x, S[p][5].x, S[p][6].x, S[p][7].x);
+        *reinterpret_cast<float4 *>(r1) = make_float4(S[p][0].y, S[p][1].y, S[p][2].y, S[p][3].y);
+        *reinterpret_cast<float4 *>(r1 + 4) = make_float4(S[p][4].y, S[p][5].y, S[p][6].y, S[p][7].y);
     }
 }
 
@@ -268,8 +301,8 @@ extern "C" int32_t sq_kda_prefill(const sq_prefill_args *args, sq_stream_t strea
     if (a.q_stride < 0 || a.k_stride < 0 || a.v_stride < 0) return SQ_ERR_SHAPE;
     if (!sq::kda_aligned_rows(a.q, a.q_stride) || !sq::kda_aligned_rows(a.k, a.k_stride) ||
         !sq::kda_aligned_rows(a.v, a.v_stride) || (reinterpret_cast<uintptr_t>(a.g) & 15u) ||
-        (reinterpret_cast<uintptr_t>(a.out) & 1u) || (reinterpret_cast<uintptr_t>(a.final_state) & 3u) ||
-        (reinterpret_cast<uintptr_t>(a.initial_state) & 3u))
+        (reinterpret_cast<uintptr_t>(a.out) & 1u) || (reinterpret_cast<uintptr_t>(a.final_state) & 15u) ||
+        (reinterpret_cast<uintptr_t>(a.initial_state) & 15u))
         return SQ_ERR_SHAPE;
     if (int64_t(a.num_seqs) * a.heads > 0x7fffffff) return SQ_ERR_SHAPE;
     const int smem = int(sizeof(sq::KdaPrefillSmem));

@@ -35,11 +35,12 @@ def test_packed_decode_hook_equals_pool_step():
 
 
 def test_extend_hook_round_trips_pages_through_native_kernel():
-    """KDA pools: the original chunk kernel runs on the decoded V-first state."""
+    """Pools the native passes do not cover (here KDA with K = V = 64): the
+    original chunk kernel runs on the decoded V-first state."""
     from stepquant_b200.kernels.pool import PackedStatePool
     from stepquant_b200.sglang import runtime
     torch.manual_seed(1)
-    heads, keys, batch = 4, 128, 3
+    heads, keys, batch = 4, 64, 3
     plan = _plan(heads, keys, "kda")
     pool = PackedStatePool(plan, batch + 1, keys)
     slots = torch.tensor([2, 3, 1], device="cuda")
@@ -83,6 +84,32 @@ def test_extend_hook_runs_native_gdn_prefill():
                                 query_start_loc=cu)
     ref = pools[1].extend(q, k, v, g, beta, slots, cu)
     assert out.shape == (1, 90, heads, keys)
+    assert torch.equal(out, ref) and torch.equal(pools[0].data, pools[1].data)
+
+
+def test_extend_hook_runs_native_kda_prefill():
+    """KDA pools with K = V = 128: the hook is PackedStatePool.extend (decode,
+    the recurrent KDA pass with g per key channel, encode)."""
+    from stepquant_b200.kernels.pool import PackedStatePool
+    from stepquant_b200.sglang import runtime
+    torch.manual_seed(4)
+    heads, keys = 4, 128
+    plan = _plan(heads, keys, "kda")
+    pools = [PackedStatePool(plan, 5, keys) for _ in range(2)]
+    slots = torch.tensor([2, 4], device="cuda")
+    cu = torch.tensor([0, 33, 80], device="cuda", dtype=torch.int32)
+    q, k = (torch.randn(1, 80, heads, keys, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    v = torch.randn(1, 80, heads, keys, device="cuda", dtype=torch.bfloat16)
+    g = -torch.rand(1, 80, heads, keys, device="cuda")
+    beta = torch.rand(1, 80, heads, device="cuda")
+
+    def original(*args, **kwargs):
+        raise AssertionError("KDA prefill at K = V = 128 must not call the original kernel")
+
+    out = runtime.kernel_extend(original, None, q, k, v, g, beta, ssm_states=pools[0], cache_indices=slots,
+                                query_start_loc=cu)
+    ref = pools[1].extend(q, k, v, g, beta, slots, cu)
+    assert out.shape == (1, 80, heads, keys)
     assert torch.equal(out, ref) and torch.equal(pools[0].data, pools[1].data)
 
 
