@@ -41,6 +41,8 @@ struct KdaSmem {
     float4 rowb[DK];  // P1: {q, q, isint, -}        P3-P5: {-rn, -rn, w2, w2}
     float4 rowd[DK];  // P3-P5: {-, 1/qmax (0: pivot row), qmax, isint}
     float rscale[DK]; // P3-: r (the fp16 row scale the page stores; 1 for pivot rows)
+    int4 rowdec[DK];  // P1 (step, writeback): {staged byte of the row's chunk in tile 0, bits per code
+                      //   (16: fp16 row), code mask (0: fp16 row), level bias -(2^23 + offset) as float bits}
     float colc[4][DV];
     float misc[64];
     int flags;
@@ -471,8 +473,11 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
         if (MODE == kReadout)  // the readout's row decode table (kda_readout_rows)
             s.rowb[tid] = make_float4(qx, integer ? -(8388608.f + float(qmax_i(bk))) : 0.f,
                                       __uint_as_float(integer ? (1u << bk) - 1u : 0u), __int_as_float(s.offs[tid]));
-        else  // {q, -, integer row, width (decode)}
+        else  // {q, -, integer row, width}
             s.rowb[tid] = make_float4(qx, qx, integer ? 1.f : 0.f, __int_as_float(bk));
+        if (MODE != kReadout)
+            s.rowdec[tid] = make_int4(lead - off0 + s.offs[tid], integer ? bk : 16, integer ? int((1u << bk) - 1u) : 0,
+                                      __float_as_int(-(8388608.f + float(qmax_i(bk)))));
         s.colc[3][tid] = cold;
         if (MODE == kWriteback) s.colc[0][tid] = delta;
     }
@@ -495,15 +500,16 @@ __global__ void __launch_bounds__(kThreads, 3) kda_kernel(TileParams p) {
                 const float4 a = s.rowa[k], b = s.rowb[k];
                 KdaRowDecode d;
                 {
-                    const int bk = __float_as_int(b.w), pos = e * (bk & 15);
-                    d.at = lead - off0 + s.offs[k] + tile_at + (bk == 16 ? 2 * e : pos >> 3);
+                    const int4 rd = s.rowdec[k];
+                    const int pos = e * rd.y;  // fp16 rows: 16 e, i.e. byte 2 e, shift 0
+                    d.at = rd.x + tile_at + (pos >> 3);
                     d.sh = uint32_t(pos & 7);
-                    d.mask = bk == 16 ? 0u : (1u << bk) - 1u;
-                    d.bias = -(8388608.f + float(qmax_i(bk)));
+                    d.mask = uint32_t(rd.z);
+                    d.bias = __int_as_float(rd.w);
                 }
                 const float2 v01 = make_float2(kda_staged_value(s.codes, d, 0), kda_staged_value(s.codes, d, j8));
                 const float2 v23 = make_float2(kda_staged_value(s.codes, d, 2 * j8), kda_staged_value(s.codes, d, 3 * j8));
-                const bool integer = b.z != 0.f;
+                const bool integer = d.mask != 0u;
                 const float2 m01 = integer ? c01 : one, m23 = integer ? c23 : one;
                 const float2 x01 = pmul2(pmul2(v01, lo2(a)), m01);
                 const float2 x23 = pmul2(pmul2(v23, lo2(a)), m23);

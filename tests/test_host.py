@@ -168,3 +168,23 @@ def test_captured_writes_reject_double_layer_write(monkeypatch):
     assert [len(t.tensors[0]) for t in tasks] + [len(p[1][0]) for p in tasks.pending] == [3, 3, 1] or len(tasks) + len(tasks.pending) == 3
     with pytest.raises(ValueError):
         tasks.append((pool, torch.arange(7)))
+
+
+def test_prefill_arguments_are_checked_before_any_launch():
+    """chunk_gated_delta_rule / chunk_kda reject bad shapes and CPU tensors on
+    the host (ValueError / NotImplementedError), with no CPU fallback."""
+    from stepquant_b200.kernels.prefill import chunk_gated_delta_rule, chunk_kda
+    q = torch.randn(10, 2, 128, dtype=torch.bfloat16)
+    v3 = torch.randn(10, 3, 128, dtype=torch.bfloat16)
+    v2 = torch.randn(10, 2, 128, dtype=torch.bfloat16)
+    beta = torch.rand(10, 2)
+    for run in (chunk_gated_delta_rule, chunk_kda):
+        with pytest.raises(ValueError):
+            run(q, q, v3, beta, beta)  # 3 value heads over 2 qk heads
+        small = torch.randn(10, 2, 64, dtype=torch.bfloat16)
+        with pytest.raises(NotImplementedError):
+            run(small, small, small, beta, beta)
+    with pytest.raises(ValueError):
+        chunk_gated_delta_rule(q, q, v2, beta, beta)  # CPU tensors
+    with pytest.raises(ValueError):
+        chunk_kda(q, q, v2, torch.zeros(10, 2, 128), beta)  # CPU tensors
