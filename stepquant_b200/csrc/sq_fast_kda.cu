@@ -354,7 +354,7 @@ __device__ __forceinline__ void kda_quantize(KdaSmem &s, int warp, int lane, int
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, MODE == kReadout ? 5 : 3) kda_kernel(TileParams p) {
+__global__ void __launch_bounds__(kThreads, MODE == kReadout ? 6 : 3) kda_kernel(TileParams p) {
     constexpr bool kTm = MODE == kStep || MODE == kWriteback;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     KdaSmem &s = *reinterpret_cast<KdaSmem *>(smem_raw);
