@@ -3,8 +3,9 @@
 // 8 bits (3 and 5 with the width extension) or an fp16 pivot row, per-channel
 // decay, value tile 4.
 //
-// One 256-thread CTA per (request, value head), three per SM (four for the
-// readout).  The head's code bytes are staged by cp.async from a 16-byte
+// One 256-thread CTA per (request, value head), three per SM (six for the
+// readout, which holds no state in tensor memory and launches without the
+// code plane).  The head's code bytes are staged by cp.async from a 16-byte
 // cover.  Warp w owns rows 16w..16w+15 and thread (w, l) the columns l, l+32,
 // l+64, l+96 of each (both torch sum orders thread-local): P1 decodes each
 // value straight from the staged bytes, dequantizes and decays it (x = level *
