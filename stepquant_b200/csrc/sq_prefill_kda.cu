@@ -9,17 +9,16 @@
 //
 // One 256-thread CTA per (sequence, value head), two per SM, the fp32 state
 // in registers for the whole prompt (read once, written once).  Lane l of
-// warp w holds rows 8 (l % 16) .. 8 (l % 16) + 7 of the eight columns
-// 16 w + 8 (l / 16) .. + 7: the sixteen lanes of a half-warp share a column
-// group and cover all 128 rows.  Per token a lane reads its 8 rows of e^g, k
-// and q (six 16-byte shared loads; the 8-row chunks are 12 floats apart, so
-// the eight chunks a quarter-warp reads fill the 32 banks once), forms the
-// 16 partial column sums (k and q for 8 columns) over its rows, and the
-// half-warp reduces them by recursive halving (15 shuffles, each lane ends
+// warp w holds rows 16 (l % 8) .. 16 (l % 8) + 15 of the four columns
+// 16 w + 4 (l / 8) .. + 3: the eight lanes of a quarter-warp share a column
+// group and cover all 128 rows.  Per token a lane reads its 16 rows of e^g, k
+// and q (twelve 16-byte shared loads; the 16-row chunks are 20 floats apart,
+// so the eight chunks a quarter-warp reads fill the 32 banks once), forms the
+// 8 partial column sums (k and q for 4 columns) over its rows, and the
+// column group reduces them by recursive halving (7 shuffles, each lane ends
 // with one total), the k lanes form d = beta (v - S^T k), the q lanes
-// o = S^T q + (q . k) d, and d reaches every lane of the group (8 shuffles)
-// for the rank-1 update.  Shared-memory traffic per token and warp is about
-// a third of a layout in which lanes hold long row ranges of few columns.
+// o = S^T q + (q . k) d, and d reaches every lane of the group (4 shuffles)
+// for the rank-1 update.
 // Tokens are staged in blocks of 16: the next block's q, k, v and g rows
 // arrive by cp.async while the current block runs, and a prologue per block
 // normalises q and k and forms e^g, beta and q . k in shared memory.
@@ -37,9 +36,9 @@ constexpr int KV = 128;           // values
 constexpr int KTB = 16;           // tokens per staged block
 constexpr int kKpThreads = 256;
 constexpr int kPieces = 16 + 16 + 16 + 32;  // 16-byte pieces of one token: q, k, v (bf16), g (fp32)
-constexpr int kChunk = 12;                  // floats per 8-key chunk of a prepared row (8 + 4 pad)
-constexpr int kRowPad = 16 * kChunk;
-__device__ __forceinline__ int kq_at(int key) { return (key >> 3) * kChunk + (key & 7); }
+constexpr int kChunk = 20;                  // floats per 16-key chunk of a prepared row (16 + 4 pad)
+constexpr int kRowPad = 8 * kChunk;
+__device__ __forceinline__ int kq_at(int key) { return (key >> 4) * kChunk + (key & 15); }
 
 struct KdaPrefillRaw {
     __nv_bfloat16 q[KTB][KK];
@@ -150,54 +149,64 @@ __device__ __forceinline__ void kda_prepare(KdaPrefillSmem &s, const KdaPrefillR
 __device__ __forceinline__ float2 lo_pair(float4 v) { return make_float2(v.x, v.y); }
 __device__ __forceinline__ float2 hi_pair(float4 v) { return make_float2(v.z, v.w); }
 
-// Tokens of one staged block.  S[p][c]: rows 8 (lane % 16) + 2 p and + 1 of
-// column col0 + c, col0 = 16 warp + 8 (lane / 16).
+// Tokens of one staged block.  S[p][c]: rows 16 (lane % 8) + 2 p and + 1 of
+// column col0 + c, col0 = 16 warp + 4 (lane / 8).
 __device__ __forceinline__ void kda_block(const KdaPrefillSmem &s, const KdaPrefillRaw &r, const sq_prefill_args &a,
-                                          int t0, int n, int head, int lane, int col0, float2 (&S)[4][8]) {
+                                          int t0, int n, int head, int lane, int col0, float2 (&S)[8][4]) {
     __nv_bfloat16 *out = static_cast<__nv_bfloat16 *>(a.out);
-    const int c16 = lane & 15, src0 = lane & 16;
-    const int col = col0 + (c16 >> 1);  // the column of this lane's total
-    const bool is_q = (c16 & 1) != 0;   // totals: k sums on even lanes, q sums on odd lanes
+    const int c8 = lane & 7, src0 = lane & 24;
+    const int col = col0 + (c8 >> 1);  // the column of this lane's total
+    const bool is_q = (c8 & 1) != 0;   // totals: k sums on even lanes, q sums on odd lanes
 #pragma unroll 1
     for (int j = 0; j < n; ++j) {
-        const float4 *e4 = reinterpret_cast<const float4 *>(&s.e[j][kChunk * c16]);
-        const float4 *k4 = reinterpret_cast<const float4 *>(&s.kn[j][kChunk * c16]);
-        const float4 *q4 = reinterpret_cast<const float4 *>(&s.qn[j][kChunk * c16]);
-        const float4 ea = e4[0], eb = e4[1], ka = k4[0], kb = k4[1], qa = q4[0], qb = q4[1];
-        const float2 E[4] = {lo_pair(ea), hi_pair(ea), lo_pair(eb), hi_pair(eb)};
-        const float2 K[4] = {lo_pair(ka), hi_pair(ka), lo_pair(kb), hi_pair(kb)};
-        const float2 Q[4] = {lo_pair(qa), hi_pair(qa), lo_pair(qb), hi_pair(qb)};
-        float sums[16];  // 2 c: the lane's part of (S^T k)_c, 2 c + 1: of (S^T q)_c, after the decay
+        const float4 *e4 = reinterpret_cast<const float4 *>(&s.e[j][kChunk * c8]);
+        const float4 *k4 = reinterpret_cast<const float4 *>(&s.kn[j][kChunk * c8]);
+        const float4 *q4 = reinterpret_cast<const float4 *>(&s.qn[j][kChunk * c8]);
+        float2 K[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            float2 ak = make_float2(0.f, 0.f), aq = ak;
+        for (int h = 0; h < 4; ++h) {
+            const float4 kv = k4[h];
+            K[2 * h] = lo_pair(kv);
+            K[2 * h + 1] = hi_pair(kv);
+        }
+        float sums[8];  // 2 c: the lane's part of (S^T k)_c, 2 c + 1: of (S^T q)_c, after the decay
+        {
+            float2 ak[4], aq[4];
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                S[p][c] = pmul2(S[p][c], E[p]);
-                ak = pfma2(K[p], S[p][c], ak);
-                aq = pfma2(Q[p], S[p][c], aq);
+            for (int c = 0; c < 4; ++c) ak[c] = aq[c] = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const float4 ev = e4[h], qv = q4[h];
+                const float2 E0 = lo_pair(ev), E1 = hi_pair(ev), Q0 = lo_pair(qv), Q1 = hi_pair(qv);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    S[2 * h][c] = pmul2(S[2 * h][c], E0);
+                    S[2 * h + 1][c] = pmul2(S[2 * h + 1][c], E1);
+                    ak[c] = pfma2(K[2 * h], S[2 * h][c], ak[c]);
+                    aq[c] = pfma2(Q0, S[2 * h][c], aq[c]);
+                    ak[c] = pfma2(K[2 * h + 1], S[2 * h + 1][c], ak[c]);
+                    aq[c] = pfma2(Q1, S[2 * h + 1][c], aq[c]);
+                }
             }
-            sums[2 * c] = ak.x + ak.y;
-            sums[2 * c + 1] = aq.x + aq.y;
-        }
-        // Recursive halving over the half-warp: at mask m a lane keeps the
-        // upper half of its values when (lane & m), adds the partner's copy of
-        // that half and passes on the other; lane c16 ends with total c16.
-        float h8[8], h4[4], h2[2];
-        {
-            const bool up = (c16 & 8) != 0;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                h8[i] = (up ? sums[i + 8] : sums[i]) + __shfl_xor_sync(0xffffffffu, up ? sums[i] : sums[i + 8], 8);
+            for (int c = 0; c < 4; ++c) {
+                sums[2 * c] = ak[c].x + ak[c].y;
+                sums[2 * c + 1] = aq[c].x + aq[c].y;
+            }
         }
+        // Recursive halving over the 8 lanes of the column group: at mask m a
+        // lane keeps the upper half of its values when (lane & m), adds the
+        // partner's copy of that half and passes on the other; lane c8 ends
+        // with total c8.
+        float h4[4], h2[2];
         {
-            const bool up = (c16 & 4) != 0;
+            const bool up = (c8 & 4) != 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                h4[i] = (up ? h8[i + 4] : h8[i]) + __shfl_xor_sync(0xffffffffu, up ? h8[i] : h8[i + 4], 4);
+                h4[i] = (up ? sums[i + 4] : sums[i]) + __shfl_xor_sync(0xffffffffu, up ? sums[i] : sums[i + 4], 4);
         }
         {
-            const bool up = (c16 & 2) != 0;
+            const bool up = (c8 & 2) != 0;
 #pragma unroll
             for (int i = 0; i < 2; ++i)
                 h2[i] = (up ? h4[i + 2] : h4[i]) + __shfl_xor_sync(0xffffffffu, up ? h4[i] : h4[i + 2], 2);
@@ -211,11 +220,11 @@ __device__ __forceinline__ void kda_block(const KdaPrefillSmem &s, const KdaPref
             out[(int64_t(t0 + j) * a.heads + head) * KV + col] = __float2bfloat16_rn(total + s.qk[j] * d);
         }
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < 4; ++c) {
             const float dc = __shfl_sync(0xffffffffu, d, src0 + 2 * c);
             const float2 dd = make_float2(dc, dc);
 #pragma unroll
-            for (int p = 0; p < 4; ++p) S[p][c] = pfma2(K[p], dd, S[p][c]);
+            for (int p = 0; p < 8; ++p) S[p][c] = pfma2(K[p], dd, S[p][c]);
         }
     }
 }
@@ -226,34 +235,29 @@ __global__ void __launch_bounds__(kKpThreads, 2) kda_prefill_kernel(sq_prefill_a
     const int seq = blockIdx.x / a.heads, head = blockIdx.x - seq * a.heads;
     const int qh = head / (a.heads / a.qk_heads);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int row0 = 8 * (lane & 15), col0 = 16 * warp + 8 * (lane >> 4);
+    const int row0 = 16 * (lane & 7), col0 = 16 * warp + 4 * (lane >> 3);
     const int2 range = kda_seq_range(a, seq);
     const int64_t base = (int64_t(seq) * a.heads + head) * KK * KV;
     const int blocks = (range.y - range.x + KTB - 1) / KTB;
     if (blocks > 0) kda_stage(s.raw[0], a, range.x, min(KTB, range.y - range.x), head, qh, tid);
 
-    float2 S[4][8];
+    float2 S[8][4];
     if (a.initial_state) {
         const float *init = a.initial_state + base;
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            const float *r0 = init + (row0 + 2 * p) * KV + col0, *r1 = r0 + KV;
-            const float4 a0 = *reinterpret_cast<const float4 *>(r0), a1 = *reinterpret_cast<const float4 *>(r0 + 4);
-            const float4 b0 = *reinterpret_cast<const float4 *>(r1), b1 = *reinterpret_cast<const float4 *>(r1 + 4);
-            S[p][0] = make_float2(a0.x, b0.x);
-            S[p][1] = make_float2(a0.y, b0.y);
-            S[p][2] = make_float2(a0.z, b0.z);
-            S[p][3] = make_float2(a0.w, b0.w);
-            S[p][4] = make_float2(a1.x, b1.x);
-            S[p][5] = make_float2(a1.y, b1.y);
-            S[p][6] = make_float2(a1.z, b1.z);
-            S[p][7] = make_float2(a1.w, b1.w);
+        for (int p = 0; p < 8; ++p) {
+            const float4 r0 = *reinterpret_cast<const float4 *>(init + (row0 + 2 * p) * KV + col0);
+            const float4 r1 = *reinterpret_cast<const float4 *>(init + (row0 + 2 * p + 1) * KV + col0);
+            S[p][0] = make_float2(r0.x, r1.x);
+            S[p][1] = make_float2(r0.y, r1.y);
+            S[p][2] = make_float2(r0.z, r1.z);
+            S[p][3] = make_float2(r0.w, r1.w);
         }
     } else {
 #pragma unroll
-        for (int p = 0; p < 4; ++p)
+        for (int p = 0; p < 8; ++p)
 #pragma unroll
-            for (int c = 0; c < 8; ++c) S[p][c] = make_float2(0.f, 0.f);
+            for (int c = 0; c < 4; ++c) S[p][c] = make_float2(0.f, 0.f);
     }
 
 #pragma unroll 1
@@ -274,12 +278,10 @@ __global__ void __launch_bounds__(kKpThreads, 2) kda_prefill_kernel(sq_prefill_a
 
     float *fin = a.final_state + base;
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-        float *r0 = fin + (row0 + 2 * p) * KV + col0, *r1 = r0 + KV;
-        *reinterpret_cast<float4 *>(r0) = make_float4(S[p][0].x, S[p][1].x, S[p][2].x, S[p][3].x);
-        *reinterpret_cast<float4 *>(r0 + 4) = make_float4(S[p][4].x, S[p][5].x, S[p][6].x, S[p][7].x);
-        *reinterpret_cast<float4 *>(r1) = make_float4(S[p][0].y, S[p][1].y, S[p][2].y, S[p][3].y);
-        *reinterpret_cast<float4 *>(r1 + 4) = make_float4(S[p][4].y, S[p][5].y, S[p][6].y, S[p][7].y);
+    for (int p = 0; p < 8; ++p) {
+        *reinterpret_cast<float4 *>(fin + (row0 + 2 * p) * KV + col0) = make_float4(S[p][0].x, S[p][1].x, S[p][2].x, S[p][3].x);
+        *reinterpret_cast<float4 *>(fin + (row0 + 2 * p + 1) * KV + col0) =
+            make_float4(S[p][0].y, S[p][1].y, S[p][2].y, S[p][3].y);
     }
 }
 
