@@ -1187,7 +1187,7 @@ def main():
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms else None
         # DRAM read + write bytes of one launch at this workload, from an ncu capture made
         # outside the bench (ncu cannot run inside a timed region); None for other shapes.
-        ncu_traffic = {"sq_step (fused)": 153.8e6, "sq_writeback": 157.9e6, "sq_readout": 125.3e6}
+        ncu_traffic = {"sq_step (fused)": 153.8e6, "sq_writeback": 157.9e6, "sq_readout": 113.5e6}
         default_shape = (not kda, batch, heads, qk_heads, args.dim, world, args.pivot_heads, args.two_bit_heads) == \
             (True, 256, 32, 16, 128, 1, 1, 0)
         name = ("kda-decode-b%d-h%d-k128 (config 2)" if kda else "gdn-decode-b%d-h%d-k128 (config 1)") % (batch, heads)
@@ -1214,8 +1214,8 @@ def main():
                          "algorithmic_bytes_per_launch": dom_bytes},
             "e2e": {"value": units / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"]},
-            # readout (or fused step; pivot heads are its items) and writeback; the 2-bit heads' readout and writeback
-            "gpu_launches": args.steps * ((2 if args.mode == "async" else 1) +
+            # readout (or fused step), writeback; the pivot-head readout; the 2-bit heads' readout and writeback
+            "gpu_launches": args.steps * ((2 if args.mode == "async" else 1) + (1 if res["pivot_heads_local"] else 0) +
                                           ((2 if args.mode == "async" else 1) if res["two_bit_heads_local"] else 0)),
         })
     line["clocks"] = clocks.summary()

@@ -100,13 +100,9 @@ int32_t run(int mode, sq::TileParams t, int32_t batch, cudaStream_t stream) {
         t.skip_fast = 1;
     } else if ((fast_mode || gdn_codec) && sq::fast_eligible(t.plan, t.pages)) {
         if (cudaError_t e = sq::launch_fast(mode, t, batch, stream)) return cuda_status(e);
-        // launch_fast takes every fp16 pivot head in the readout and step (items
-        // of the persistent kernel; the writeback has nothing to do for them) and
-        // the listed ones in encode and decode, and the listed 2-bit heads.
         sq::PivotHeads ph;
         sq::TwoHeads th;
-        const bool pivots = mode == sq::kStep || mode == sq::kReadout || mode == sq::kWriteback ||
-                            sq::pivot_heads(t.plan, &ph);
+        const bool pivots = sq::pivot_heads(t.plan, &ph);  // pivot and 2-bit heads run in launch_fast
         const bool twos = sq::two_heads(t.plan, &th);
         bool rest = true;
         if (t.plan.bits_host) {

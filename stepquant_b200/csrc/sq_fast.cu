@@ -653,30 +653,19 @@ __device__ __forceinline__ void halves4(uint2 raw, float2 &lo, float2 &hi) {
     hi = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
 }
 
-// A pivot item of the persistent readout / step in two passes over the warp's
-// 16 rows, streamed from global memory (the head is not staged, and the kernel
-// keeps no registers for it): the column partials of k_raw^T Y and q_raw^T Y
-// over the rows in order (as readout_rows), then -- after the column results --
-// the update in place, x' = Y (c decay) + k delta per value (the integer
-// heads' operations with unit scales) stored as fp16, the fp32 x' also to
-// `dense` ([K, V] of this item) when given.  Each lane rewrites the 8 bytes it
-// read; the second read hits L2.  As in the reference (its readout stores
-// pivot rows itself, readout.py:118-121), the writeback skips pivot heads.
-// (AHEAD: every row load in flight at once -- the readout, whose registers
-// allow it; the fused step issues them four at a time.)
-template <bool AHEAD>
-__device__ __forceinline__ void pivot_pass1(FastSmem &s, const uint8_t *head, int warp, int lane) {
-    const uint8_t *src = pivot_lane(const_cast<uint8_t *>(head), warp, lane);
+// The pivot head's two passes on the warp's 16 rows, held in registers (the
+// pivot kernel loads them once, ahead of its inputs): the column partials of
+// k_raw^T Y and q_raw^T Y over the rows in order (as readout_rows), then the
+// update in place, x' = Y (c decay) + k delta per value (the same operations
+// as the integer heads' update) stored as fp16, the fp32 x' also to `dense`
+// ([K, V] of this item) when given.
+template <class Smem>
+__device__ __forceinline__ void pivot_rows_held(Smem &s, const uint2 (&raw)[16], int warp, int lane) {
     float2 kx01 = make_float2(0.f, 0.f), kx23 = kx01, qx01 = kx01, qx23 = kx01;
-    constexpr int kAhead = AHEAD ? 16 : 4;
-    uint2 raw[16];
-#pragma unroll
-    for (int r = 0; r < kAhead; ++r) raw[r] = *reinterpret_cast<const uint2 *>(src + r * 32);
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
         float2 y01, y23;
-        if (r + kAhead < 16) raw[r + kAhead] = *reinterpret_cast<const uint2 *>(src + (r + kAhead) * 32);
         halves4(raw[r], y01, y23);
         const float4 a = s.rowa[k], b = s.rowb[k];
         kx01 = pfma2(hi2(a), y01, kx01);
@@ -687,16 +676,19 @@ __device__ __forceinline__ void pivot_pass1(FastSmem &s, const uint8_t *head, in
     *reinterpret_cast<float4 *>(&s.red[0][warp][4 * lane]) = make_float4(kx01.x, kx01.y, kx23.x, kx23.y);
     *reinterpret_cast<float4 *>(&s.red[1][warp][4 * lane]) = make_float4(qx01.x, qx01.y, qx23.x, qx23.y);
 }
-__device__ __forceinline__ void pivot_pass2(const FastSmem &s, uint8_t *head, int warp, int lane, float *dense) {
+
+template <class Smem>
+__device__ __forceinline__ void pivot_update_held(const Smem &s, const uint2 (&raw)[16], uint8_t *head, int warp,
+                                                  int lane, float *dense) {
     uint8_t *dst = pivot_lane(head, warp, lane);
     const float4 d = *reinterpret_cast<const float4 *>(&s.colc[0][4 * lane]);
     const float4 cd = *reinterpret_cast<const float4 *>(&s.colc[3][4 * lane]);
     const float2 d01 = lo2(d), d23 = hi2(d), cd01 = lo2(cd), cd23 = hi2(cd);
-#pragma unroll 4
+#pragma unroll
     for (int r = 0; r < 16; ++r) {
         const int k = warp * 16 + r;
         float2 y01, y23;
-        halves4(*reinterpret_cast<const uint2 *>(dst + r * 32), y01, y23);
+        halves4(raw[r], y01, y23);
         const float2 kk = hi2(s.rowa[k]);
         const float2 x01 = pfma2(kk, d01, pmul2(y01, cd01));
         const float2 x23 = pfma2(kk, d23, pmul2(y23, cd23));
@@ -736,14 +728,6 @@ struct WorkItem {
     bool active;  // 0 < slot < num_slots
 };
 
-// fp16 pivot heads are items of the readout and the fused step (streamed from
-// global memory; the writeback has nothing to do for them); encode and decode
-// leave them to the pivot kernel.
-template <int MODE>
-__device__ __forceinline__ bool pivot_item(const WorkItem &it) {
-    return (MODE == kReadout || MODE == kStep) && it.width == 16;
-}
-
 __device__ __forceinline__ WorkItem describe(const TileParams &p, const FastSmem &s, int req, int head, long long slot) {
     WorkItem it;
     it.req = req;
@@ -766,7 +750,7 @@ __device__ __forceinline__ void prefetch(const TileParams &p, const FastSmem &s,
     const HeadInfo &hi = s.head[it.head];
     const uint8_t *page = p.pages + it.slot * P.page_bytes;
     const uint8_t *src = page + hi.off_head;
-    if (MODE != kEncode && it.width != 16) {
+    if (MODE != kEncode) {
         if (it.width == 4) stage_codes<4>(st, src, tid);
         else if (it.width == 6) stage_codes<6>(st, src, tid);
         else stage_codes<8>(st, src, tid);
@@ -856,7 +840,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
                 kraw = load_as_float(a.k, a.io_dtype, int64_t(c.req) * a.k_stride + int64_t(qh) * FK + tid);
                 vin = load_as_float(a.v, a.io_dtype, int64_t(c.req) * a.v_stride + int64_t(c.head) * FV + tid);
             }
-            const float ro = width == 16 ? 1.f : __half2float(st.rold[tid]);  // fp16 pivot values: unit scales
+            const float ro = __half2float(st.rold[tid]);
             s.rowa[tid] = make_float4(ro, ro, kraw, kraw);
             s.rowb[tid] = make_float4(qraw, qraw, 0.f, 0.f);
         }
@@ -898,9 +882,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
         else if (width == 6) unpack_update_tm<6>(s, st, warp, lane, c.tm);
         else unpack_update_tm<8>(s, st, warp, lane, c.tm);
     } else {
-        if (width == 16) {
-            pivot_pass1<MODE == kReadout>(s, c.page + c.off_head, warp, lane);
-        } else if (MODE == kReadout) {
+        if (MODE == kReadout) {
             if (width == 4) readout_rows<4>(s, st, warp, lane);
             else if (width == 6) readout_rows<6>(s, st, warp, lane);
             else readout_rows<8>(s, st, warp, lane);
@@ -942,7 +924,7 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
                     ks = __fadd_rn(ks, s.red[0][w][tid]);
                     qs = __fadd_rn(qs, s.red[1][w][tid]);
                 }
-                const float cd = __fmul_rn(width == 16 ? 1.f : __half2float(st.cold[tid]), decay);
+                const float cd = __fmul_rn(__half2float(st.cold[tid]), decay);
                 const float kS = __fmul_rn(__fmul_rn(ks, kn), cd);      // k^T (D S)
                 const float qS = __fmul_rn(__fmul_rn(qs, qscale), cd);  // q^T (D S)
                 const float delta = __fmul_rn(beta, __fsub_rn(vin, kS));
@@ -958,13 +940,6 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
                     sc[FV + tid] = kx;
                     sc[FV + FK + tid] = decay;
                 }
-            }
-            if (width == 16) {  // pivot item: the update in place, then done
-                group_sync(c.bar);
-                consumed();  // the item's staged inputs were read in the prologue
-                pivot_pass2(s, c.page + c.off_head, warp, lane,
-                            MODE == kStep && p.dense_out ? p.dense_out + (int64_t(c.req) * H + c.head) * FK * FV : nullptr);
-                return;
             }
             if (MODE == kReadout) return;
             group_sync(c.bar);
@@ -1106,7 +1081,7 @@ __global__ void __launch_bounds__(groups_of<MODE>() * kThreads, 1) fast_kernel(T
     if (item < hi) {
         const int req = request_of(item);
         const WorkItem first = describe(p, s, req, item - req * H, slot);
-        if ((first.fast || pivot_item<MODE>(first)) && first.active) prefetch<MODE>(p, s, s.st0, first, c.tid);
+        if (first.fast && first.active) prefetch<MODE>(p, s, s.st0, first, c.tid);
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -1124,8 +1099,7 @@ __global__ void __launch_bounds__(groups_of<MODE>() * kThreads, 1) fast_kernel(T
             if (next_item < hi) {
                 const int nreq = request_of(next_item);
                 const WorkItem nxt = describe(p, s, nreq, next_item - nreq * H, s.slot_ring[ring1]);
-                if ((nxt.fast || pivot_item<MODE>(nxt)) && nxt.active)
-                    prefetch<MODE>(p, s, s.stage(kOneStage ? 0 : buf ^ 1), nxt, c.tid);
+                if (nxt.fast && nxt.active) prefetch<MODE>(p, s, s.stage(kOneStage ? 0 : buf ^ 1), nxt, c.tid);
                 if (c.tid == 0) {
                     const int after = atomicAdd(&cta.next, 1);
                     s.item_ring[ring2] = after;
@@ -1143,10 +1117,9 @@ __global__ void __launch_bounds__(groups_of<MODE>() * kThreads, 1) fast_kernel(T
         c.head = cur.head;
         c.slot = cur.slot;
         if (MODE == kReadout && c.head == 0 && c.tid == 0) p.stable_slots[c.req] = c.slot;
-        const bool handled = cur.fast || pivot_item<MODE>(cur);
-        const bool body = handled && cur.active;
+        const bool body = cur.fast && cur.active;
         if (kOneStage && !body) issue_next();
-        if (handled) {
+        if (cur.fast) {
             if (cur.active) {
                 c.page = p.pages + c.slot * P.page_bytes;
                 c.off_head = s.head[c.head].off_head;
@@ -1178,13 +1151,24 @@ __global__ void __launch_bounds__(groups_of<MODE>() * kThreads, 1) fast_kernel(T
 }
 
 // ---------------------------------------------------------------------------
-// Encode / decode of fp16 pivot heads: one CTA per (request, pivot head),
-// converting between fp32 and fp16 (the readout and step take pivot heads as
-// items of the persistent kernel).
+// fp16 pivot heads: one CTA per (request, pivot head).  Step and readout alike
+// read the head's values, form the column partials of k^T Y and q^T Y, the
+// gates and the readout (the operations of fast_body with unit row and column
+// scales), and write the updated values back as fp16 -- the reference's
+// readout stores pivot rows itself, so the writeback has nothing to do for
+// them.  Encode and decode convert between fp32 and fp16.
 // ---------------------------------------------------------------------------
+struct PivotSmem {
+    float4 rowa[FK];  // {1, 1, k, k}: raw k, then the normalised k
+    float4 rowb[FK];  // {q, q, -, -} raw q
+    float red[2][8][FV];
+    float colc[4][FV];  // [0] delta, [3] decay (c = 1)
+    float misc[64];
+};
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) pivot_kernel(TileParams p, PivotHeads ph) {
-    static_assert(MODE == kEncode || MODE == kDecode, "pivot_kernel converts pivot heads");
+    __shared__ PivotSmem s;
     const sq_plan &P = p.plan;
     const int H = P.heads;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1193,13 +1177,88 @@ __global__ void __launch_bounds__(kThreads) pivot_kernel(TileParams p, PivotHead
     const long long slot = p.slots[req];
     if (!(slot > 0 && slot < p.num_slots)) {
         if (slot > 0 && tid == 0) flag(p.status, SQ_STATUS_SLOT_RANGE);
-        if (MODE == kDecode && p.dense_out)
+        if ((MODE == kStep || MODE == kReadout) && tid < FV) store_from_float(p.step.out, p.step.io_dtype, item * FV + tid, 0.f);
+        if ((MODE == kStep || MODE == kDecode) && p.dense_out)
             for (int e = tid; e < FK * FV; e += kThreads) p.dense_out[item * FK * FV + e] = 0.f;
         return;
     }
     uint8_t *values = p.pages + slot * P.page_bytes + P.offsets[head * FK];
-    if (MODE == kEncode) pivot_encode(p.dense_in + item * FK * FV, values, warp, lane);
-    else pivot_decode(values, p.dense_out + item * FK * FV, warp, lane);
+    if (MODE == kEncode) {
+        pivot_encode(p.dense_in + item * FK * FV, values, warp, lane);
+        return;
+    }
+    if (MODE == kDecode) {
+        pivot_decode(values, p.dense_out + item * FK * FV, warp, lane);
+        return;
+    }
+    // The warp's rows first: their loads overlap the input loads and norms below.
+    uint2 raw[16];
+    {
+        const uint8_t *src = pivot_lane(values, warp, lane);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) raw[r] = *reinterpret_cast<const uint2 *>(src + r * 32);
+    }
+    const sq_step_args &a = p.step;
+    float qraw = 0.f, kraw = 0.f, vin = 0.f, braw = 0.f, graw = 0.f;
+    if (tid < FK) {
+        const int qh = head / (H / a.qk_heads);
+        qraw = load_as_float(a.q, a.io_dtype, int64_t(req) * a.q_stride + int64_t(qh) * FK + tid);
+        kraw = load_as_float(a.k, a.io_dtype, int64_t(req) * a.k_stride + int64_t(qh) * FK + tid);
+        vin = load_as_float(a.v, a.io_dtype, int64_t(req) * a.v_stride + int64_t(head) * FV + tid);
+        braw = load_as_float(a.beta, a.gate_dtype, item);
+        graw = load_as_float(a.g, a.gate_dtype, item);
+        s.rowa[tid] = make_float4(1.f, 1.f, kraw, kraw);
+        s.rowb[tid] = make_float4(qraw, qraw, 0.f, 0.f);
+        float3 part = make_float3(__fmul_rn(qraw, qraw), __fmul_rn(kraw, kraw), __fmul_rn(qraw, kraw));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            part.x += __shfl_xor_sync(0xffffffffu, part.x, o);
+            part.y += __shfl_xor_sync(0xffffffffu, part.y, o);
+            part.z += __shfl_xor_sync(0xffffffffu, part.z, o);
+        }
+        if (lane == 0) *reinterpret_cast<float4 *>(&s.misc[4 * warp]) = make_float4(part.x, part.y, part.z, 0.f);
+    }
+    __syncthreads();
+    pivot_rows_held(s, raw, warp, lane);
+    __syncthreads();
+    if (tid < FV) {
+        const float beta = a.a_log ? 1.f / (1.f + expf(-braw)) : braw;
+        float g = graw;
+        if (a.a_log) {
+            const float u = g + a.dt_bias[head];
+            g = -expf(a.a_log[head]) * (u > 20.f ? u : logf(1.f + expf(fminf(u, 20.f))));
+        }
+        const float decay = expf(g);
+        float qq = 0.f, kk = 0.f, dot = 0.f;
+#pragma unroll
+        for (int w = 0; w < FK / 32; ++w) {
+            const float4 m = reinterpret_cast<const float4 *>(s.misc)[w];
+            qq += m.x;
+            kk += m.y;
+            dot += m.z;
+        }
+        const float qn = a.normalize ? __frsqrt_rn(qq + 1e-6f) : 1.f;
+        const float kn = a.normalize ? __frsqrt_rn(kk + 1e-6f) : 1.f;
+        const float qscale = __fmul_rn(qn, a.scale);
+        const float qk = __fmul_rn(__fmul_rn(__fmul_rn(dot, qn), kn), a.scale);
+        float ks = 0.f, qs = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            ks = __fadd_rn(ks, s.red[0][w][tid]);
+            qs = __fadd_rn(qs, s.red[1][w][tid]);
+        }
+        const float kS = __fmul_rn(__fmul_rn(ks, kn), decay);
+        const float qS = __fmul_rn(__fmul_rn(qs, qscale), decay);
+        const float delta = __fmul_rn(beta, __fsub_rn(vin, kS));
+        const float kx = __fmul_rn(kraw, kn);
+        s.colc[0][tid] = delta;
+        s.colc[3][tid] = decay;
+        s.rowa[tid].z = kx;
+        s.rowa[tid].w = kx;
+        store_from_float(a.out, a.io_dtype, item * FV + tid, __fmaf_rn(qk, delta, qS));
+    }
+    __syncthreads();
+    pivot_update_held(s, raw, values, warp, lane, MODE == kStep && p.dense_out ? p.dense_out + item * FK * FV : nullptr);
 }
 
 // Resident CTAs per SM for each mode, and SMs, per device (set up on the first
@@ -1302,12 +1361,16 @@ cudaError_t launch_fast(int mode, const TileParams &params, int batch, cudaStrea
     TwoHeads th;
     if (two_heads(p.plan, &th) && th.count > 0 && (err = launch_two(mode, p, th, batch, stream)) != cudaSuccess)
         return err;
-    if (mode != kEncode && mode != kDecode) return cudaSuccess;  // the readout and step take pivot items themselves
+    if (mode == kWriteback) return cudaSuccess;
     PivotHeads ph;
     if (!pivot_heads(p.plan, &ph) || ph.count == 0) return cudaSuccess;
     const int grid = batch * ph.count;
-    if (mode == kEncode) pivot_kernel<kEncode><<<grid, kThreads, 0, stream>>>(p, ph);
-    else pivot_kernel<kDecode><<<grid, kThreads, 0, stream>>>(p, ph);
+    switch (mode) {
+        case kStep: pivot_kernel<kStep><<<grid, kThreads, 0, stream>>>(p, ph); break;
+        case kReadout: pivot_kernel<kReadout><<<grid, kThreads, 0, stream>>>(p, ph); break;
+        case kEncode: pivot_kernel<kEncode><<<grid, kThreads, 0, stream>>>(p, ph); break;
+        default: pivot_kernel<kDecode><<<grid, kThreads, 0, stream>>>(p, ph); break;
+    }
     return cudaGetLastError();
 }
 

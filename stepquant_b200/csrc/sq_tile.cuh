@@ -40,13 +40,11 @@ cudaError_t launch_tile(int mode, const TileParams &p, int items, cudaStream_t s
 // (sq_fast.cu) for the step, readout, writeback, encode and decode modes.
 // fast_eligible(): the plan's shape and the page alignment allow them;
 // fast_head(): a head of that width is handled by them.  launch_fast also
-// takes every fp16 pivot head in the readout and the step (items of the
-// persistent kernel; the writeback has nothing to do for them, the readout
-// already wrote their values), the pivot heads that pivot_heads() lists in
-// encode and decode (a second kernel), and the 2-bit heads that two_heads()
-// lists.  The tile kernel handles the other heads (pivot heads of encode and
-// decode, or 2-bit heads, when the plan has no host copy of its bits or more
-// than 32 of them; 2-bit heads with value groups other than 32).
+// runs the fp16 pivot heads that pivot_heads() lists (a second kernel; none
+// in the writeback, whose pivot values the readout already wrote) and the
+// 2-bit heads that two_heads() lists.  The tile kernel handles the other heads
+// (pivot or 2-bit heads when the plan has no host copy of its bits or more than
+// 32 of them; 2-bit heads with value groups other than 32).
 bool fast_eligible(const sq_plan &plan, const void *pages);
 __host__ __device__ inline bool fast_head(const sq_plan &plan, int width) {
     return plan.architecture == SQ_GDN && plan.keys == 128 && plan.values == 128 &&
