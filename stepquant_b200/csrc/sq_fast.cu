@@ -1031,6 +1031,9 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 template <int MODE>
 __global__ void __launch_bounds__(groups_of<MODE>() * kThreads, 1) fast_kernel(TileParams p, int items) {
     constexpr int kGroups = groups_of<MODE>();
+    // The pivot-head kernel launched after this one may start its CTAs on SMs
+    // this grid leaves (it shares no data with it).
+    if (MODE == kReadout || MODE == kStep) asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FastCta<kGroups> &cta = *reinterpret_cast<FastCta<kGroups> *>(smem_raw);
     const int group = threadIdx.x / kThreads;
@@ -1168,6 +1171,13 @@ struct PivotSmem {
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) pivot_kernel(TileParams p, PivotHeads ph) {
+    // Launched as a programmatic dependent of the readout's (step's) persistent
+    // kernel, whose heads it does not touch, its CTAs fill SMs as that kernel's
+    // CTAs leave; each still waits for that kernel's completion before it
+    // exits, so work after it in the stream sees both (a no-op otherwise).
+    struct AfterPrimary {
+        __device__ ~AfterPrimary() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+    } after_primary;
     __shared__ PivotSmem s;
     const sq_plan &P = p.plan;
     const int H = P.heads;
@@ -1359,12 +1369,27 @@ cudaError_t launch_fast(int mode, const TileParams &params, int batch, cudaStrea
     }
     if (err != cudaSuccess) return err;
     TwoHeads th;
-    if (two_heads(p.plan, &th) && th.count > 0 && (err = launch_two(mode, p, th, batch, stream)) != cudaSuccess)
-        return err;
+    const bool twos = two_heads(p.plan, &th) && th.count > 0;
+    if (twos && (err = launch_two(mode, p, th, batch, stream)) != cudaSuccess) return err;
     if (mode == kWriteback) return cudaSuccess;
     PivotHeads ph;
     if (!pivot_heads(p.plan, &ph) || ph.count == 0) return cudaSuccess;
     const int grid = batch * ph.count;
+    if ((mode == kReadout || mode == kStep) && !twos) {
+        // Directly after the persistent kernel: a programmatic dependent launch.
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(unsigned(grid));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return mode == kReadout ? cudaLaunchKernelEx(&cfg, pivot_kernel<kReadout>, p, ph)
+                                : cudaLaunchKernelEx(&cfg, pivot_kernel<kStep>, p, ph);
+    }
     switch (mode) {
         case kStep: pivot_kernel<kStep><<<grid, kThreads, 0, stream>>>(p, ph); break;
         case kReadout: pivot_kernel<kReadout><<<grid, kThreads, 0, stream>>>(p, ph); break;
