@@ -1031,9 +1031,9 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 template <int MODE>
 __global__ void __launch_bounds__(groups_of<MODE>() * kThreads, 1) fast_kernel(TileParams p, int items) {
     constexpr int kGroups = groups_of<MODE>();
-    // The pivot-head kernel launched after this one may start its CTAs on SMs
-    // this grid leaves (it shares no data with it).
-    if (MODE == kReadout || MODE == kStep) asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+    // The pivot-head or 2-bit-head kernel launched after this one may start its
+    // CTAs on SMs this grid leaves (it shares no data with it).
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FastCta<kGroups> &cta = *reinterpret_cast<FastCta<kGroups> *>(smem_raw);
     const int group = threadIdx.x / kThreads;

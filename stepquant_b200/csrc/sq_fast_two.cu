@@ -295,6 +295,12 @@ __device__ __forceinline__ void two_store(const TwoSmem &s, uint8_t *page, int o
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) two_kernel(TileParams p, TwoHeads th) {
+    // A programmatic dependent of the persistent kernel launched before it
+    // (disjoint heads): its CTAs fill SMs as that kernel's CTAs leave, and each
+    // waits for that kernel's completion before it exits.
+    struct AfterPrimary {
+        __device__ ~AfterPrimary() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+    } after_primary;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     TwoSmem &s = *reinterpret_cast<TwoSmem *>(smem_raw);
     constexpr bool kTm = MODE == kStep || MODE == kWriteback || MODE == kEncode;
@@ -586,15 +592,24 @@ cudaError_t launch_two(int mode, const TileParams &p, const TwoHeads &th, int ba
     const int grid = batch * th.count;
     constexpr int smem = int(sizeof(TwoSmem));  // below the 48 KB default limit
     static_assert(smem <= 48 * 1024, "two_kernel shared memory");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(grid));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     switch (mode) {
-        case kStep: two_kernel<kStep><<<grid, kThreads, smem, stream>>>(p, th); break;
-        case kReadout: two_kernel<kReadout><<<grid, kThreads, smem, stream>>>(p, th); break;
-        case kWriteback: two_kernel<kWriteback><<<grid, kThreads, smem, stream>>>(p, th); break;
-        case kEncode: two_kernel<kEncode><<<grid, kThreads, smem, stream>>>(p, th); break;
-        case kDecode: two_kernel<kDecode><<<grid, kThreads, smem, stream>>>(p, th); break;
+        case kStep: return cudaLaunchKernelEx(&cfg, two_kernel<kStep>, p, th);
+        case kReadout: return cudaLaunchKernelEx(&cfg, two_kernel<kReadout>, p, th);
+        case kWriteback: return cudaLaunchKernelEx(&cfg, two_kernel<kWriteback>, p, th);
+        case kEncode: return cudaLaunchKernelEx(&cfg, two_kernel<kEncode>, p, th);
+        case kDecode: return cudaLaunchKernelEx(&cfg, two_kernel<kDecode>, p, th);
         default: return cudaErrorNotSupported;
     }
-    return cudaGetLastError();
 }
 
 }  // namespace sq
