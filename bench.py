@@ -959,10 +959,10 @@ def measure_stack(args, batch, heads_total, qk_total, steps, warmup, world, rank
         name, ms = ev.key, ev.device_time_total / 1e3
         if ms <= 0:
             continue
-        if "fast_kernel<3>" in name or "fast_kernel<(int)3>" in name:
+        if "fast_kernel<3," in name or "fast_kernel<(int)3," in name:
             fam["state_readout"] += ms
             launches += ev.count
-        elif "fast_kernel<4>" in name or "fast_kernel<(int)4>" in name or "tile_kernel" in name:
+        elif "fast_kernel<4," in name or "fast_kernel<(int)4," in name or "tile_kernel" in name:
             fam["state_writeback"] += ms
             launches += ev.count
         elif "sq::" in name:

@@ -1028,9 +1028,9 @@ __device__ void fast_body(const TileParams &p, FastSmem &s, const FastStage &st,
 // first; the step, writeback and encode keep one (the other's space holds their
 // row partials and code bytes) and refill it once the item's staged data is
 // consumed, before the quantizer's column passes.
-template <int MODE>
-__global__ void __launch_bounds__(groups_of<MODE>() * kThreads, 1) fast_kernel(TileParams p, int items) {
-    constexpr int kGroups = groups_of<MODE>();
+template <int MODE, int G>
+__global__ void __launch_bounds__(G * kThreads, 1) fast_kernel(TileParams p, int items) {
+    constexpr int kGroups = G;
     // The pivot-head or 2-bit-head kernel launched after this one may start its
     // CTAs on SMs this grid leaves (it shares no data with it).
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
@@ -1274,7 +1274,7 @@ __global__ void __launch_bounds__(kThreads) pivot_kernel(TileParams p, PivotHead
 // Resident CTAs per SM for each mode, and SMs, per device (set up on the first
 // launch on a device).
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_ready[kFit + 1][kMaxDevices];  // kernel attributes set, indexed by Mode
+std::atomic<int> g_ready[kFit + 1][2][kMaxDevices];  // kernel attributes set, by Mode and group-count variant
 std::atomic<int> g_sms[kMaxDevices];
 
 // SMs the kernels of `stream` run on: its green context's SM partition (a
@@ -1305,27 +1305,50 @@ int stream_sms(cudaStream_t stream, int device_sms) {
     return std::max(1, std::min(device_sms, int(res.sm.smCount)));
 }
 
-template <int MODE>
-cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream) {
-    constexpr int kGroups = groups_of<MODE>();
-    constexpr int smem = int(sizeof(FastCta<kGroups>));
-    int device = 0;
-    cudaError_t err = cudaGetDevice(&device);
-    if (err != cudaSuccess) return err;
-    std::atomic<int> *ready = device < kMaxDevices ? &g_ready[MODE][device] : nullptr;
-    int sms = device < kMaxDevices ? g_sms[device].load(std::memory_order_relaxed) : 0;
-    if (!ready || !ready->load(std::memory_order_relaxed) || sms == 0) {
-        err = cudaFuncSetAttribute(fast_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+// The writeback's per-SM item counts at which four 64-register item groups
+// end sooner than three 80-register ones.  With n items on an SM, three groups
+// leave one item to run alone at the end when n = 3m + 1; four groups run that
+// last round three wide instead (n = 4, 7, 10).  Beyond a dozen items the
+// four-group build's extra spills cost more than the tail it saves.  Per-rank
+// item counts this small come from sharding value heads over many GPUs
+// (1,024 items on 148 SMs at 8 GPUs of config 1: 7 on most SMs).
+inline bool writeback_four_groups(int items, int grid) {
+    const int n = (items + grid - 1) / grid;
+    return n == 4 || n == 7 || n == 10;
+}
+
+template <int MODE, int G>
+cudaError_t launch_fast_groups(const TileParams &p, int items, int device, int sms, cudaStream_t stream) {
+    constexpr int smem = int(sizeof(FastCta<G>));
+    std::atomic<int> *ready = device < kMaxDevices ? &g_ready[MODE][G == groups_of<MODE>() ? 0 : 1][device] : nullptr;
+    if (!ready || !ready->load(std::memory_order_relaxed)) {
+        const cudaError_t err = cudaFuncSetAttribute(fast_kernel<MODE, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (err != cudaSuccess) return err;
-        if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return err;
         if (ready) ready->store(1, std::memory_order_relaxed);
-        if (device < kMaxDevices) g_sms[device].store(sms, std::memory_order_relaxed);
     }
     // One CTA per SM of the stream (its green context's SMs, if it has one),
     // each with a contiguous share of the items.
-    const int grid = std::max(1, std::min(items, stream_sms(stream, sms)));
-    fast_kernel<MODE><<<grid, kGroups * kThreads, smem, stream>>>(p, items);
+    const int grid = std::max(1, std::min(items, sms));
+    fast_kernel<MODE, G><<<grid, G * kThreads, smem, stream>>>(p, items);
     return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_fast_mode(const TileParams &p, int items, cudaStream_t stream) {
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return err;
+    int sms = device < kMaxDevices ? g_sms[device].load(std::memory_order_relaxed) : 0;
+    if (sms == 0) {
+        if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return err;
+        if (device < kMaxDevices) g_sms[device].store(sms, std::memory_order_relaxed);
+    }
+    sms = stream_sms(stream, sms);
+    if constexpr (MODE == kWriteback) {
+        if (writeback_four_groups(items, std::max(1, std::min(items, sms))))
+            return launch_fast_groups<MODE, 4>(p, items, device, sms, stream);
+    }
+    return launch_fast_groups<MODE, groups_of<MODE>()>(p, items, device, sms, stream);
 }
 
 }  // namespace

@@ -115,3 +115,23 @@ def test_kda_config2_async_full_size():
     bits = S.kda_widths(32, 128, gen)
     plan, oplan = _plan("kda", bits, 3)
     _run("kda", plan, oplan, 512, 32, 32, 3, [0, 5, 300, 511])
+
+
+@pytest.mark.parametrize("per_sm, widths", [
+    (7, [16, 6, 8, 4]),           # rank 0 of config 1 at 8 GPUs: three integer heads and the pivot head
+    (4, [4, 6, 8, 6]),
+    (10, [6, 4, 8, 6, 6, 4]),     # six heads: the item index split by division
+])
+def test_gdn_rank_sized_async(per_sm, widths):
+    """Per-rank launches of a value-head-sharded config 1 (a few items per SM).
+    When the busiest SM holds 4, 7 or 10 items the writeback runs four item
+    groups per SM instead of three; the batch is chosen from this GPU's SM
+    count so that it does, and the bytes must still equal the fused step's."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    heads = len(widths)
+    batch = (per_sm * sms - heads + 1) // heads
+    items = batch * heads
+    assert -(-items // sms) == per_sm and items <= per_sm * sms
+    bits = torch.tensor(widths)[:, None].expand(heads, 128).clone()
+    plan, oplan = _plan("gdn", bits, 4 + per_sm)
+    _run("gdn", plan, oplan, batch, heads, heads // 2, 4 + per_sm, [0, batch // 2, batch - 1])
