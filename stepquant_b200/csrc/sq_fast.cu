@@ -1047,6 +1047,19 @@ __global__ void __launch_bounds__(G * kThreads, 1) fast_kernel(TileParams p, int
     c.bar = 1 + group;
     const int lo = int(int64_t(blockIdx.x) * items / gridDim.x);
     const int hi = int(int64_t(blockIdx.x + 1) * items / gridDim.x);
+    const int hshift = (H & (H - 1)) == 0 ? __ffs(H) - 1 : -1;
+    auto request_of = [&](int it) { return hshift >= 0 ? it >> hshift : it / H; };
+    // The group's first two items are lo + group and lo + kGroups + group; the
+    // rest come from the counter.  Their slots are requested before the head
+    // table is read so the two global round trips overlap.
+    if (c.tid == 0) {
+        const int i0 = lo + group, i1 = lo + kGroups + group;
+        s.item_ring[0] = i0;
+        s.item_ring[1] = i1;
+        if (i0 < hi) cp_async8(&s.slot_ring[0], p.slots + request_of(i0));
+        if (i1 < hi) cp_async8(&s.slot_ring[1], p.slots + request_of(i1));
+    }
+    cp_async_commit();
     for (int h = c.tid; h < H; h += kThreads) {
         HeadInfo hi;
         hi.width = P.bits[h * FK];
@@ -1060,18 +1073,6 @@ __global__ void __launch_bounds__(G * kThreads, 1) fast_kernel(TileParams p, int
     }
     if (threadIdx.x == 0) cta.next = lo + 2 * kGroups;
     if (tm_mode<MODE>() && threadIdx.x < 32) tm_alloc(&cta.grp[0].tmem_slot, 512);
-    const int hshift = (H & (H - 1)) == 0 ? __ffs(H) - 1 : -1;
-    auto request_of = [&](int it) { return hshift >= 0 ? it >> hshift : it / H; };
-    // The group's first two items are lo + group and lo + kGroups + group; the
-    // rest come from the counter.
-    if (c.tid == 0) {
-        const int i0 = lo + group, i1 = lo + kGroups + group;
-        s.item_ring[0] = i0;
-        s.item_ring[1] = i1;
-        if (i0 < hi) cp_async8(&s.slot_ring[0], p.slots + request_of(i0));
-        if (i1 < hi) cp_async8(&s.slot_ring[1], p.slots + request_of(i1));
-    }
-    cp_async_commit();
     cp_async_wait<0>();
     if (tm_mode<MODE>()) tm_fence_before();
     __syncthreads();
