@@ -1308,14 +1308,15 @@ int stream_sms(cudaStream_t stream, int device_sms) {
 
 // The writeback's per-SM item counts at which four 64-register item groups
 // end sooner than three 80-register ones.  With n items on an SM, three groups
-// leave one item to run alone at the end when n = 3m + 1; four groups run that
-// last round three wide instead (n = 4, 7, 10).  Beyond a dozen items the
-// four-group build's extra spills cost more than the tail it saves.  Per-rank
-// item counts this small come from sharding value heads over many GPUs
-// (1,024 items on 148 SMs at 8 GPUs of config 1: 7 on most SMs).
+// end on a round one or two items wide when n = 3m + 1 or 3m + 2; four groups
+// run that tail wider (n = 4, 7, 8, 10, 11; measured at 7, 8 and 11).  Beyond
+// a dozen items the four-group build's extra instructions (rematerialised
+// addresses, a few spills) cost more than the tail it saves (measured at 14).
+// Per-rank item counts this small come from sharding value heads over many
+// GPUs (1,024 items on 148 SMs at 8 GPUs of config 1: 7 on most SMs).
 inline bool writeback_four_groups(int items, int grid) {
     const int n = (items + grid - 1) / grid;
-    return n == 4 || n == 7 || n == 10;
+    return n == 4 || n == 7 || n == 8 || n == 10 || n == 11;
 }
 
 template <int MODE, int G>

@@ -120,12 +120,13 @@ def test_kda_config2_async_full_size():
 @pytest.mark.parametrize("per_sm, widths", [
     (7, [16, 6, 8, 4]),           # rank 0 of config 1 at 8 GPUs: three integer heads and the pivot head
     (4, [4, 6, 8, 6]),
+    (8, [8, 4, 6, 6]),
     (10, [6, 4, 8, 6, 6, 4]),     # six heads: the item index split by division
 ])
 def test_gdn_rank_sized_async(per_sm, widths):
     """Per-rank launches of a value-head-sharded config 1 (a few items per SM).
-    When the busiest SM holds 4, 7 or 10 items the writeback runs four item
-    groups per SM instead of three; the batch is chosen from this GPU's SM
+    When the busiest SM holds 4, 7, 8, 10 or 11 items the writeback runs four
+    item groups per SM instead of three; the batch is chosen from this GPU's SM
     count so that it does, and the bytes must still equal the fused step's."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     heads = len(widths)
